@@ -1,0 +1,370 @@
+"""Batch-1 greedy decode throughput of the Qwen3-32B-shaped 4-bit model on B200.
+
+`python bench.py [--gpus N] [--steps K] [--warmup W] [--impl m5|reference]`
+
+A step is one decode token (one full forward of the 64-layer model at the
+current context, 8-bit KV, greedy argmax) replayed from a CUDA graph; weights
+(18.43 GB) and the 32K-token KV cache are resident in HBM before timing.
+Weights and KV are synthetic (seeded random, MLX 4-bit g64 / 8-bit g64
+layouts).  Inputs are larger than L2 (every step streams ~22.6 GB).
+
+Printed JSON (rank 0): value = tokens/s of the whole job; roofline = the
+dominant kernel (w4 dequant-GEMV) timed alone with CUDA events;
+cpu_baseline = the CPU oracle on a bounded sample of the same step.
+`--impl reference` times the CPU restatement of the reference path (MLX is
+not installable here) on the same workload and prints the same line shape.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "qwen3-32b": dict(model_type="qwen3", hidden_size=5120, num_hidden_layers=64, num_attention_heads=64,
+                      num_key_value_heads=8, head_dim=128, intermediate_size=25600, vocab_size=151936,
+                      tie_word_embeddings=False, max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6),
+    "qwen3-0.6b": dict(model_type="qwen3", hidden_size=1024, num_hidden_layers=28, num_attention_heads=16,
+                       num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=151936,
+                       tie_word_embeddings=True, max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6),
+}
+
+
+def weight_bytes_per_token(cfg: dict) -> int:
+    """Packed weight bytes one decode token streams (0.5625 B per weight + norms)."""
+    H, L, D = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["head_dim"]
+    Hq, Hkv, I, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["intermediate_size"], cfg["vocab_size"]
+    per_layer = (Hq * D * H + 2 * Hkv * D * H + H * Hq * D + 3 * I * H) * 0.5625 + (2 * H + 2 * D) * 2
+    head = V * H * 0.5625
+    return int(L * per_layer + head + H * 2)
+
+
+def kv_bytes_per_token(cfg: dict, ctx: int, bits: int = 8) -> int:
+    per_elem = bits / 8 + 4 / 64
+    return int(2 * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * per_elem * ctx)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        def run():
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            try:
+                p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                      "-lms", "200"], stdout=subprocess.PIPE, text=True)
+            except Exception:
+                return
+            while not self._stop.is_set():
+                line = p.stdout.readline()
+                if not line:
+                    break
+                self.samples.append([s.strip() for s in line.split(",")])
+            p.terminate()
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm = [float(s[0]) for s in self.samples if s and s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if len(s) > 1 and s[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            for i, n in enumerate(names):
+                if len(s) > 3 + i and s[3 + i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------- CPU legs
+def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0) -> dict:
+    """Time the CPU oracle's decode step on `layers` decoder layers (+ a vocab
+    slice of the lm_head) and scale to one full token.  Returns tok/s."""
+    import numpy as np
+    import torch
+
+    from oracle import model as om
+    from oracle.quant import affine_quantize
+
+    if threads:
+        torch.set_num_threads(threads)
+    c = om.Config.from_dict(dict(cfg, num_hidden_layers=layers))
+    # The oracle multiplies by dequantized fp32 weights; for timing, those are
+    # drawn directly (their values do not change the work), norms are ones.
+    m = om.Model(c, {})
+    g = torch.Generator().manual_seed(7)
+    for name, shape, kind in om.weight_specs(c):
+        if kind == "norm":
+            m.w[name + ".weight"] = np.full(shape, 0x3F80, dtype=np.uint16)
+        elif name.startswith("model.layers."):
+            m._deq[name] = 0.02 * torch.randn(shape, generator=g)
+    rng = np.random.default_rng(1)
+    cache = []
+    for _ in range(layers):
+        qc = om.QuantizedKVCache(64, 8)
+        k = rng.standard_normal((c.num_key_value_heads, ctx, c.head_dim)).astype(np.float32)
+        v = rng.standard_normal((c.num_key_value_heads, ctx, c.head_dim)).astype(np.float32)
+        qc.k_parts.append(affine_quantize(k, 64, 8))
+        qc.v_parts.append(affine_quantize(v, 64, 8))
+        qc.offset = ctx
+        cache.append(qc)
+    x = om.rb(torch.randn(1, cfg["hidden_size"], generator=g))
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        h = x
+        for i in range(layers):
+            p = f"model.layers.{i}."
+            r = m.attention(i, om.rms_norm(h, m.norm_w(p + "input_layernorm"), c.rms_norm_eps), cache[i])
+            h = om.rb(h + r)
+            r = m.mlp(i, om.rms_norm(h, m.norm_w(p + "post_attention_layernorm"), c.rms_norm_eps))
+            h = om.rb(h + r)
+            qc = cache[i]  # drop the appended position so every repetition sees ctx keys
+            qc.k_parts, qc.v_parts, qc.offset = qc.k_parts[:1], qc.v_parts[:1], ctx
+        reps += 1
+        if time.perf_counter() - t0 > 5.0 or reps >= 3:
+            break
+    layer_s = (time.perf_counter() - t0) / reps / layers
+    # lm_head: a 16384-row slice of the vocab, scaled
+    rows = 16384
+    head = torch.randn(rows, cfg["hidden_size"])
+    t1 = time.perf_counter()
+    _ = om.rb(h @ head.T)
+    head_s = (time.perf_counter() - t1) * cfg["vocab_size"] / rows
+    tok_s = cfg["num_hidden_layers"] * layer_s + head_s
+    return {"value": 1.0 / tok_s, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{layers} of {cfg['num_hidden_layers']} decoder layers at ctx {ctx} (8-bit KV) + "
+                      f"{rows}/{cfg['vocab_size']} lm_head rows, scaled to one token; oracle weights "
+                      f"pre-dequantized to fp32"}
+
+
+# ----------------------------------------------------------------- GPU leg
+def fill_kv_synthetic(cache, ctx: int, seed: int):
+    """Random N(0,1) K/V for positions [0, ctx) quantized into every layer."""
+    import torch
+
+    from myinfer_b200 import ops
+    g = torch.Generator(device=cache.d_len.device).manual_seed(seed)
+    for c in cache:
+        H, D = c.n_kv_heads, c.head_dim
+        for which in ("k", "v"):
+            x = torch.randn(H, ctx, D, generator=g, device=c.device).to(torch.bfloat16)
+            q, s, b = ops.quantize(x, 64, c.bits)
+            tq, ts, tb = (c._kq, c._ks, c._kb) if which == "k" else (c._vq, c._vs, c._vb)
+            tq[0, :, :ctx].copy_(q)
+            ts[0, :, :ctx].copy_(s)
+            tb[0, :, :ctx].copy_(b)
+        c.offset = ctx
+    cache.d_len.fill_(ctx)
+
+
+def gemv_roofline(model, cfg, peak_gbs) -> dict:
+    """Dominant kernel (gate/up dequant-GEMV with SwiGLU... measured as the
+    plain projection GEMVs of every layer) timed alone with CUDA events."""
+    import torch
+
+    from myinfer_b200 import ops
+    H = cfg["hidden_size"]
+    L = cfg["num_hidden_layers"]
+    x = torch.randn(1, H, device=model.device).to(torch.bfloat16)
+    names = [f"model.layers.{i}.mlp.up_proj" for i in range(L)]
+    w = model.weights
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in names]
+    for _ in range(2):
+        for n in names[:4]:
+            ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"])
+    torch.cuda.synchronize()
+    for (a, b), n in zip(ev, names):
+        a.record()
+        ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"])
+        b.record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    N, K = cfg["intermediate_size"], H
+    alg = N * K * 0.5625 + K * 2 + N * 2
+    ach = alg / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": "gemv_kernel<1,EPI_STORE> (up_proj 25600x5120 w4g64)", "achieved": round(ach, 1),
+            "peak": peak_gbs, "unit": "GB/s", "frac": round(ach / peak_gbs, 4), "traffic": None,
+            "alg_bytes_per_launch": int(alg), "avg_launch_us": round(ms * 1e3, 2)}
+
+
+def run_gpu(args) -> dict:
+    import torch
+
+    from myinfer_b200 import _lib
+    from myinfer_b200.cache import QuantizedKVCache, PromptCache
+    from myinfer_b200.generate import DecodeGraph
+    from myinfer_b200.model import Model, ModelArgs, random_weights
+
+    rank = int(os.environ.get("RANK", 0))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    cfg = CONFIGS[args.config]
+    a = ModelArgs.from_dict(cfg)
+    t0 = time.perf_counter()
+    w = random_weights(a, seed=args.seed, device=dev)
+    model = Model(a, w, dev, max_tokens=8)
+    torch.cuda.synchronize()
+    load_s = time.perf_counter() - t0
+    ctx = args.ctx
+    total = ctx + args.warmup + args.steps * 2 + 8
+    cache = PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, 8, capacity=total)
+                         for _ in range(a.num_hidden_layers)], dev)
+    fill_kv_synthetic(cache, ctx, seed=args.seed + 1)
+    # one eager step (configures kernels), then capture the decode graph
+    tok = torch.tensor([1], dtype=torch.int32, device=dev)
+    model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
+    g = DecodeGraph(model, cache, with_logits=False)
+    g.tok.copy_(tok)
+    for _ in range(args.warmup):
+        g.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            g.step()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t)
+    ms_step = ms / args.steps
+    mean_ctx = ctx + args.warmup + args.steps / 2
+    bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_per_token(cfg, int(mean_ctx))
+    peaks = measured_peaks()
+    tok_s = 1000.0 / ms_step * world
+
+    # e2e through the public decode step: pinned host token in, token out, every step
+    host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    host[0] = 1
+    torch.cuda.synchronize()
+    e_start = time.perf_counter()
+    e_steps = max(4, args.steps // 2)
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    for _ in range(e_steps):
+        g.tok.copy_(host, non_blocking=True)
+        g.step()
+        host.copy_(g.tok, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    ee.record()
+    torch.cuda.synchronize()
+    e2e_ms = es.elapsed_time(ee) / e_steps
+    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"])
+    out = {
+        "metric": "batch-1 decode tok/s (Qwen3-32B-shaped, w4g64, 8-bit KV)",
+        "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "replicas" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "w4a16 (bf16 activations, fp32 accumulate), 8-bit KV",
+        "data": "synthetic (seeded random weights and KV)",
+        "config": {"workload": f"{args.config} decode, batch 1, context {ctx}", "model": args.config,
+                   "global_batch": world, "seq_len": ctx, "parallelism": f"replicas{world}",
+                   "kv_fill": "synthetic quantized N(0,1) K/V for the 32K prompt positions",
+                   "l2": "inputs larger than L2 (>=18 GB streamed per step)"},
+        "hbm": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok / (ms_step * 1e-3) / 1e9, 1),
+                "peak_gbs": peaks["hbm_gbs"], "frac_of_measured": round(bytes_tok / (ms_step * 1e-3) / 1e9 /
+                                                                       peaks["hbm_gbs"], 4),
+                "frac_of_8tbs_nominal": round(bytes_tok / (ms_step * 1e-3) / 8e12, 4)},
+        "roofline": roof,
+        "e2e": {"value": round(1000.0 / e2e_ms * world, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+        "load_seconds": round(load_s, 1),
+    }
+    # kernels per step: 7 per layer + embed + lm_head + argmax + length update
+    out["gpu_launches"] = args.steps * (a.num_hidden_layers * 7 + 4)
+    if rank == 0 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_decode_sample(cfg, min(ctx, 4096), layers=1, threads=os.cpu_count() or 1)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return out if rank == 0 else None
+
+
+def run_reference(args) -> dict:
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return None
+    cfg = CONFIGS[args.config]
+    vals = []
+    base = None
+    for _ in range(max(1, args.steps // 8) if args.steps else 1):
+        base = cpu_decode_sample(cfg, min(args.ctx, 4096), layers=1, threads=os.cpu_count() or 1)
+        vals.append(base["value"])
+    v = statistics.mean(vals)
+    return {"impl": "reference", "metric": "batch-1 decode tok/s (Qwen3-32B-shaped, w4g64, 8-bit KV)",
+            "value": round(v, 5), "unit": "tok/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / v, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (CPU oracle)",
+            "data": "synthetic (seeded random weights and KV)",
+            "config": {"workload": f"{args.config} decode, batch 1, context {args.ctx}", "model": args.config},
+            "cpu_baseline": dict(base, value=round(v, 5)),
+            "e2e": {"value": round(v, 5), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "MLX/mlx-lm (the reference's own CPU path) is not installable here; the CPU restatement "
+                    "in oracle/ stands in for it"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="m5", choices=["m5", "reference"])
+    ap.add_argument("--config", default="qwen3-32b", choices=sorted(CONFIGS))
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    out = run_reference(args) if args.impl == "reference" else run_gpu(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

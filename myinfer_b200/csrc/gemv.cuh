@@ -1,0 +1,46 @@
+// Streaming w4g64 dequant-GEMV for decode (M <= 8 tokens per launch).
+#pragma once
+
+#include "common.cuh"
+
+namespace m5 {
+
+enum GemvEpi {
+  EPI_STORE = 0,     // y = bf16(acc)
+  EPI_RESIDUAL = 1,  // y = bf16(y + bf16(acc))      (residual add in place)
+  EPI_SWIGLU = 2,    // y = bf16(bf16(g * bf16(sigmoid(g))) * u), g/u = bf16(acc) of gate/up rows
+  EPI_F32 = 3        // yf = acc (fp32; partial sums before a tensor-parallel reduce)
+};
+
+// A run of weight rows that share one output buffer.  Several segments let one
+// launch cover q/k/v (or several experts) without repacking MLX tensors.
+struct GemvSeg {
+  const uint32_t* w;  // [rows, K/8]
+  const bf16* s;      // [rows, K/64]
+  const bf16* b;
+  int rows;
+  bf16* y;            // output column base: y[t * ldy + r]
+  float* yf;          // fp32 output base (EPI_F32)
+};
+
+struct GemvArgs {
+  const bf16* x;      // [MT, ldx]
+  int64_t ldx;
+  int K;
+  int nseg;
+  GemvSeg seg[4];     // SWIGLU: seg[0] gate, seg[1] up (same rows), output seg[0].y
+  int64_t ldy;
+  int total_rows;     // rows to produce (SWIGLU: gate rows)
+  int rows_per_warp;
+  const bf16* norm_w; // fused RMSNorm of x when non-null
+  float eps;
+};
+
+// Launch y = epi(x @ W^T) for up to 8 tokens.  Chooses rows per warp so the
+// grid fits the device in one wave.  Returns an M5 status.
+int gemv_launch(const GemvArgs& a, int MT, int epi, cudaStream_t stream);
+
+// Largest number of tokens one launch can stage for this K (shared memory).
+int gemv_max_tokens(int K);
+
+}  // namespace m5

@@ -1,0 +1,123 @@
+// Routed experts of a Qwen3-MoE layer as two grouped streaming GEMVs.
+//
+// The router (GEMV + moe_topk) leaves ids/scores [T, k] on the device, so no
+// host sync happens inside the layer (the reference's streaming wrapper syncs
+// at m5engine/expert_stream.py:384-389).  Then:
+//   gate/up - grid.y = (token, slot); a CTA stages RMSNorm(x_t) once and its
+//             warps stream rows of expert ids[t, slot]'s gate and up matrices,
+//             writing bf16(bf16(g*bf16(sigmoid g)) * u) (mlx-lm SwiGLU);
+//   down    - grid.y = token; a CTA stages the k SwiGLU rows of its token and
+//             every warp computes one output row for all k experts, then
+//             h += bf16(sum_j bf16(bf16(y_j) * score_j)) (the score-weighted
+//             sum of mlx-lm Qwen3MoeSparseMoeBlock) in its epilogue.
+// Experts outside [e_first, e_first + e_local) are skipped, which is what an
+// expert-parallel rank needs; it then writes fp32 partial sums for a reduce.
+#include <algorithm>
+
+#include "gemv_impl.cuh"
+#include "moe.cuh"
+
+namespace m5 {
+
+constexpr int MOE_WARPS = 4;
+
+__global__ void __launch_bounds__(MOE_WARPS * 32) moe_gate_up_kernel(const MoeArgs a, int rpw) {
+  extern __shared__ __align__(16) float smem[];
+  const int slot = blockIdx.y;
+  const int t = slot / a.k;
+  const int e = a.ids[slot] - a.e_first;
+  if (e < 0 || e >= a.e_local) return;
+  const int H = a.H, I = a.I;
+  float* xs = smem;
+  float* xsum = xs + H;
+  float* red = xsum + (H >> 5);
+  stage_rows<1>(a.x + size_t(t) * H, H, H, a.norm_w, a.eps, xs, xsum, red);
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * MOE_WARPS + (threadIdx.x >> 5);
+  const size_t H8 = H >> 3, H64 = H >> 6;
+  for (int rr = 0; rr < rpw; ++rr) {
+    const int row = gw * rpw + rr;
+    if (row >= I) break;
+    const size_t er = size_t(e) * I + row;
+    float g[1] = {0.f}, u[1] = {0.f};
+    row_dot<1, 4>(a.gate.w + er * H8, a.gate.s + er * H64, a.gate.b + er * H64, H, xs, xsum, g);
+    row_dot<1, 4>(a.up.w + er * H8, a.up.s + er * H64, a.up.b + er * H64, H, xs, xsum, u);
+    const float gv = rbf(warp_sum(g[0])), uv = rbf(warp_sum(u[0]));
+    if (lane == 0) {
+      const float sg = rbf(1.f / (1.f + expf(-gv)));
+      a.act[size_t(slot) * I + row] = f2bf(rbf(gv * sg) * uv);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(MOE_WARPS * 32) moe_down_kernel(const MoeArgs a, int rpw) {
+  extern __shared__ __align__(16) float smem[];
+  const int t = blockIdx.y;
+  const int H = a.H, I = a.I, k = a.k;
+  float* xs = smem;
+  float* xsum = xs + size_t(k) * I;
+  float* red = xsum + size_t(k) * (I >> 5);
+  for (int j = 0; j < k; ++j) {
+    const int e = a.ids[t * k + j] - a.e_first;
+    if (e < 0 || e >= a.e_local) continue;  // uniform across the CTA
+    stage_rows<1>(a.act + size_t(t * k + j) * I, I, I, nullptr, 0.f, xs + size_t(j) * I, xsum + size_t(j) * (I >> 5),
+                  red);
+  }
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * MOE_WARPS + (threadIdx.x >> 5);
+  const size_t I8 = I >> 3, I64 = I >> 6;
+  for (int rr = 0; rr < rpw; ++rr) {
+    const int n = gw * rpw + rr;
+    if (n >= H) break;
+    float sum = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int e = a.ids[t * k + j] - a.e_first;
+      if (e < 0 || e >= a.e_local) continue;
+      const size_t er = size_t(e) * H + n;
+      float acc[1] = {0.f};
+      row_dot<1, 4>(a.down.w + er * I8, a.down.s + er * I64, a.down.b + er * I64, I, xs + size_t(j) * I,
+                    xsum + size_t(j) * (I >> 5), acc);
+      const float y = rbf(warp_sum(acc[0]));
+      sum += rbf(y * bf2f(a.scores[t * k + j]));
+    }
+    if (lane == 0) {
+      if (a.partial) {
+        a.partial[size_t(t) * H + n] = sum;
+      } else {
+        bf16* p = a.h + size_t(t) * H + n;
+        *p = f2bf(bf2f(*p) + rbf(sum));
+      }
+    }
+  }
+}
+
+int moe_launch(const MoeArgs& a, cudaStream_t st) {
+  if (a.H % 64 || a.I % 64) return fail(M5_ERR_INVALID, "moe: hidden and expert sizes must be multiples of 64");
+  if (a.T <= 0) return M5_OK;
+  static bool configured = false;
+  if (!configured) {
+    M5_CUDA(cudaFuncSetAttribute(moe_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    M5_CUDA(cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    configured = true;
+  }
+  const int resident = sm_count() * 48;
+  {
+    const size_t smem = size_t(a.H) * 4 + size_t(a.H / 32) * 4 + 33 * 4;
+    const long long slots = (long long)a.T * a.k;
+    const int rpw = std::max(1, (int)((a.I * slots + resident - 1) / resident));
+    dim3 grid(ceil_div(a.I, MOE_WARPS * rpw), (unsigned)slots);
+    moe_gate_up_kernel<<<grid, MOE_WARPS * 32, smem, st>>>(a, rpw);
+    M5_LAUNCH_CHECK("moe gate/up launch");
+  }
+  {
+    const size_t smem = size_t(a.k) * a.I * 4 + size_t(a.k) * (a.I / 32) * 4 + 33 * 4;
+    if (smem > 200 * 1024) return fail(M5_ERR_UNSUPPORTED, "moe: k * moe_intermediate_size too large");
+    const int rpw = std::max(1, (int)(((long long)a.H * a.T + resident - 1) / resident));
+    dim3 grid(ceil_div(a.H, MOE_WARPS * rpw), (unsigned)a.T);
+    moe_down_kernel<<<grid, MOE_WARPS * 32, smem, st>>>(a, rpw);
+    M5_LAUNCH_CHECK("moe down launch");
+  }
+  return M5_OK;
+}
+
+}  // namespace m5

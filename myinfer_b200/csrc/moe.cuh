@@ -1,0 +1,31 @@
+// Routed-expert MLP of a Qwen3-MoE layer (mlx-lm SwitchGLU via gather_qmm;
+// the reference's wrapper contract is m5engine/expert_stream.py:381-403).
+#pragma once
+
+#include "common.cuh"
+
+namespace m5 {
+
+struct QW {
+  const uint32_t* w;  // stacked local experts [E_local, N, K/8]
+  const bf16* s;      // [E_local, N, K/64]
+  const bf16* b;
+};
+
+struct MoeArgs {
+  const bf16* x;        // [T, H] residual stream (normalised inside with norm_w)
+  int T, H, I, k;
+  int e_first, e_local; // global id of local expert 0, number of local experts
+  const int32_t* ids;   // [T, k] global expert ids from the router
+  const bf16* scores;   // [T, k]
+  QW gate, up, down;
+  const bf16* norm_w;
+  float eps;
+  bf16* act;            // scratch [T * k, I]
+  bf16* h;              // [T, H], h += sum_j bf16(y_j * score_j)
+  float* partial;       // when non-null: write fp32 sums here instead of h (expert parallel)
+};
+
+int moe_launch(const MoeArgs& a, cudaStream_t stream);
+
+}  // namespace m5

@@ -1,0 +1,652 @@
+// The model handle and the forward pass of the token loop (C ABI).
+//
+// m5_forward is the device-side body of one mlx-lm model call
+// (model(tokens[1, L], cache) at m5engine/context.py:53, driven by
+// generate_step behind m5engine/engine.py:420-423): embedding, then per layer
+//   fused-RMSNorm q|k|v GEMV -> QK-norm + RoPE/YaRN + KV quantize-append ->
+//   split-KV attention -> o_proj GEMV (+ residual) -> fused-RMSNorm gate|up
+//   GEMV with SwiGLU -> down GEMV (+ residual)      [dense layers]
+//   fused-RMSNorm router GEMV -> top-k -> grouped expert GEMVs  [MoE layers]
+// then the final norm fused into the lm_head GEMV and a greedy argmax.
+// Positions come from a device counter so one captured CUDA graph replays
+// every decode step; every launch shape depends only on L and capacities.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "attn.cuh"
+#include "gemv.cuh"
+#include "moe.cuh"
+#include "ops.cuh"
+
+namespace m5 {
+
+struct Linear {
+  const uint32_t* w = nullptr;
+  const bf16* s = nullptr;
+  const bf16* b = nullptr;
+  bool ok() const { return w && s && b; }
+};
+
+struct Layer {
+  const bf16* in_norm = nullptr;
+  const bf16* post_norm = nullptr;
+  const bf16* q_norm = nullptr;
+  const bf16* k_norm = nullptr;
+  Linear q, k, v, o;
+  Linear gate, up, down;        // dense MLP
+  Linear router;                // MoE: mlp.gate
+  Linear e_gate, e_up, e_down;  // MoE: stacked local experts
+};
+
+struct Model {
+  m5_model_cfg cfg{};
+  int Hq = 0, Hkv = 0, I = 0, E_local = 0, e_first = 0;  // this rank's shard
+  Linear embed, lm_head;
+  const bf16* final_norm = nullptr;
+  std::vector<Layer> layers;
+  float* d_inv_freq = nullptr;
+  float mscale = 1.f;
+  bool rope_set = false;
+  // scratch arena
+  int max_tokens = 0;
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+  bf16 *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits_last = nullptr;
+  bf16 *rlogits = nullptr, *rscores = nullptr;
+  int32_t* rids = nullptr;
+  float* attn_part = nullptr;
+  size_t attn_part_bytes = 0;
+  void* argmax_scratch = nullptr;
+};
+
+static bool parse_layer(const char* name, int& idx, const char*& rest) {
+  const char* p = "model.layers.";
+  if (strncmp(name, p, strlen(p)) != 0) return false;
+  const char* s = name + strlen(p);
+  char* end = nullptr;
+  long v = strtol(s, &end, 10);
+  if (end == s || *end != '.') return false;
+  idx = (int)v;
+  rest = end + 1;
+  return true;
+}
+
+static bool bind_linear(Linear& l, const char* suffix, const void* ptr) {
+  if (!strcmp(suffix, "weight")) l.w = (const uint32_t*)ptr;
+  else if (!strcmp(suffix, "scales")) l.s = (const bf16*)ptr;
+  else if (!strcmp(suffix, "biases")) l.b = (const bf16*)ptr;
+  else return false;
+  return true;
+}
+
+// `base` names a module ("self_attn.q_proj"); the tensor is base + "." + suffix.
+static bool match(const char* rest, const char* base, const char*& suffix) {
+  size_t n = strlen(base);
+  if (strncmp(rest, base, n) != 0 || rest[n] != '.') return false;
+  suffix = rest + n + 1;
+  return true;
+}
+
+static int bind(Model* m, const char* name, const void* ptr) {
+  const char* suffix = nullptr;
+  if (match(name, "model.embed_tokens", suffix)) return bind_linear(m->embed, suffix, ptr) ? M5_OK : -1;
+  if (match(name, "lm_head", suffix)) return bind_linear(m->lm_head, suffix, ptr) ? M5_OK : -1;
+  if (!strcmp(name, "model.norm.weight")) { m->final_norm = (const bf16*)ptr; return M5_OK; }
+  int li;
+  const char* rest;
+  if (!parse_layer(name, li, rest) || li < 0 || li >= (int)m->layers.size()) return -1;
+  Layer& L = m->layers[li];
+  if (!strcmp(rest, "input_layernorm.weight")) { L.in_norm = (const bf16*)ptr; return M5_OK; }
+  if (!strcmp(rest, "post_attention_layernorm.weight")) { L.post_norm = (const bf16*)ptr; return M5_OK; }
+  if (!strcmp(rest, "self_attn.q_norm.weight")) { L.q_norm = (const bf16*)ptr; return M5_OK; }
+  if (!strcmp(rest, "self_attn.k_norm.weight")) { L.k_norm = (const bf16*)ptr; return M5_OK; }
+  struct { const char* base; Linear* l; } table[] = {
+      {"self_attn.q_proj", &L.q}, {"self_attn.k_proj", &L.k}, {"self_attn.v_proj", &L.v},
+      {"self_attn.o_proj", &L.o}, {"mlp.gate_proj", &L.gate}, {"mlp.up_proj", &L.up},
+      {"mlp.down_proj", &L.down}, {"mlp.gate", &L.router}, {"mlp.switch_mlp.gate_proj", &L.e_gate},
+      {"mlp.switch_mlp.up_proj", &L.e_up}, {"mlp.switch_mlp.down_proj", &L.e_down},
+  };
+  for (auto& t : table)
+    if (match(rest, t.base, suffix)) return bind_linear(*t.l, suffix, ptr) ? M5_OK : -1;
+  return -1;
+}
+
+static std::string missing(const Model* m) {
+  const bool moe = m->cfg.num_experts > 0;
+  if (!m->embed.ok()) return "model.embed_tokens";
+  if (!m->final_norm) return "model.norm.weight";
+  if (!m->cfg.tie_word_embeddings && !m->lm_head.ok()) return "lm_head";
+  for (size_t i = 0; i < m->layers.size(); ++i) {
+    const Layer& L = m->layers[i];
+    std::string p = "model.layers." + std::to_string(i) + ".";
+    if (!L.in_norm) return p + "input_layernorm.weight";
+    if (!L.post_norm) return p + "post_attention_layernorm.weight";
+    if (!L.q_norm) return p + "self_attn.q_norm.weight";
+    if (!L.k_norm) return p + "self_attn.k_norm.weight";
+    if (!L.q.ok()) return p + "self_attn.q_proj";
+    if (!L.k.ok()) return p + "self_attn.k_proj";
+    if (!L.v.ok()) return p + "self_attn.v_proj";
+    if (!L.o.ok()) return p + "self_attn.o_proj";
+    if (moe) {
+      if (!L.router.ok()) return p + "mlp.gate";
+      if (!L.e_gate.ok()) return p + "mlp.switch_mlp.gate_proj";
+      if (!L.e_up.ok()) return p + "mlp.switch_mlp.up_proj";
+      if (!L.e_down.ok()) return p + "mlp.switch_mlp.down_proj";
+    } else {
+      if (!L.gate.ok()) return p + "mlp.gate_proj";
+      if (!L.up.ok()) return p + "mlp.up_proj";
+      if (!L.down.ok()) return p + "mlp.down_proj";
+    }
+  }
+  return "";
+}
+
+static char* carve(char*& p, size_t bytes) {
+  char* r = p;
+  p += (bytes + 255) & ~size_t(255);
+  return r;
+}
+
+// y rows for x [T, K] through one or more weight segments, in chunks of the
+// largest token count the GEMV can stage.
+static int linear_tokens(const GemvArgs& proto, int T, int epi, cudaStream_t st) {
+  const int cap = gemv_max_tokens(proto.K);
+  if (cap <= 0) return fail(M5_ERR_UNSUPPORTED, "linear: K too large for the decode GEMV");
+  for (int t0 = 0; t0 < T;) {
+    int mt = 1;
+    while (mt * 2 <= std::min(cap, T - t0)) mt *= 2;
+    GemvArgs a = proto;
+    a.x = proto.x + size_t(t0) * proto.ldx;
+    for (int i = 0; i < a.nseg; ++i) {
+      if (a.seg[i].y) a.seg[i].y = proto.seg[i].y + size_t(t0) * proto.ldy;
+      if (a.seg[i].yf) a.seg[i].yf = proto.seg[i].yf + size_t(t0) * proto.ldy;
+    }
+    int rc = gemv_launch(a, mt, epi, st);
+    if (rc) return rc;
+    t0 += mt;
+  }
+  return M5_OK;
+}
+
+static GemvSeg seg_of(const Linear& l, int rows, bf16* y) {
+  GemvSeg s{};
+  s.w = l.w;
+  s.s = l.s;
+  s.b = l.b;
+  s.rows = rows;
+  s.y = y;
+  return s;
+}
+
+__global__ void add_len_kernel(int32_t* d_len, int L) { *d_len += L; }
+
+static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int L, void* logits,
+                   int logits_mode, int32_t* d_argmax, cudaStream_t st) {
+  const m5_model_cfg& c = m->cfg;
+  const int H = c.hidden_size, D = c.head_dim;
+  const int Hq = m->Hq, Hkv = m->Hkv;
+  const int QKV = (Hq + 2 * Hkv) * D;
+  int rc = embed_launch(d_tokens, L, m->embed.w, m->embed.s, m->embed.b, H, c.vocab_size, m->h, st);
+  if (rc) return rc;
+  for (int li = 0; li < c.num_layers; ++li) {
+    const Layer& ly = m->layers[li];
+    const m5_layer_kv& lk = kv[li];
+    // q | k | v projections of RMSNorm(h)
+    GemvArgs a{};
+    a.x = m->h;
+    a.ldx = H;
+    a.K = H;
+    a.nseg = 3;
+    a.seg[0] = seg_of(ly.q, Hq * D, m->qkv);
+    a.seg[1] = seg_of(ly.k, Hkv * D, m->qkv + Hq * D);
+    a.seg[2] = seg_of(ly.v, Hkv * D, m->qkv + (Hq + Hkv) * D);
+    a.ldy = QKV;
+    a.total_rows = QKV;
+    a.norm_w = ly.in_norm;
+    a.eps = c.rms_norm_eps;
+    if ((rc = linear_tokens(a, L, EPI_STORE, st))) return rc;
+    // QK-norm + RoPE + KV append
+    RopeAppendArgs r{};
+    r.qkv = m->qkv;
+    r.L = L;
+    r.Hq = Hq;
+    r.Hkv = Hkv;
+    r.q_norm = ly.q_norm;
+    r.k_norm = ly.k_norm;
+    r.eps = c.rms_norm_eps;
+    r.inv_freq = m->d_inv_freq;
+    r.mscale = m->mscale;
+    r.d_len = d_len;
+    r.q_out = m->q;
+    r.kv = lk;
+    if ((rc = rope_append_launch(r, st))) return rc;
+    // attention over the cache (S = *d_len + L keys after the append)
+    AttnArgs at{};
+    at.q = m->q;
+    at.B = 1;
+    at.Hq = Hq;
+    at.L = L;
+    at.D = D;
+    at.k = m5_kv_view{lk.k, lk.k_scales, lk.k_biases, 0, lk.capacity};
+    at.v = m5_kv_view{lk.v, lk.v_scales, lk.v_biases, 0, lk.capacity};
+    at.bits = lk.bits;
+    at.Hkv = Hkv;
+    at.d_S = d_len;
+    at.S_add = L;
+    at.scale = 1.f / sqrtf(float(D));
+    at.mask_kind = L > 1 ? M5_MASK_CAUSAL : M5_MASK_NONE;
+    attn_plan(1, Hq, Hkv, L, (int)lk.capacity, at.QB, at.nsplit);
+    if (attn_scratch_bytes(1, Hq, L, D, at.nsplit) > m->attn_part_bytes) at.nsplit = 1;
+    at.part_o = m->attn_part;
+    at.part_ml = m->attn_part + size_t(Hq) * L * at.nsplit * D;
+    at.out = m->attn;
+    at.out_tokens_major = 1;
+    if ((rc = attn_launch(at, st))) return rc;
+    // o_proj, residual add into h
+    GemvArgs o{};
+    o.x = m->attn;
+    o.ldx = Hq * D;
+    o.K = Hq * D;
+    o.nseg = 1;
+    o.seg[0] = seg_of(ly.o, H, m->h);
+    o.ldy = H;
+    o.total_rows = H;
+    if ((rc = linear_tokens(o, L, EPI_RESIDUAL, st))) return rc;
+    if (c.num_experts == 0) {
+      GemvArgs g{};
+      g.x = m->h;
+      g.ldx = H;
+      g.K = H;
+      g.nseg = 2;
+      g.seg[0] = seg_of(ly.gate, m->I, m->act);
+      g.seg[1] = seg_of(ly.up, m->I, nullptr);
+      g.ldy = m->I;
+      g.total_rows = m->I;
+      g.norm_w = ly.post_norm;
+      g.eps = c.rms_norm_eps;
+      if ((rc = linear_tokens(g, L, EPI_SWIGLU, st))) return rc;
+      GemvArgs d{};
+      d.x = m->act;
+      d.ldx = m->I;
+      d.K = m->I;
+      d.nseg = 1;
+      d.seg[0] = seg_of(ly.down, H, m->h);
+      d.ldy = H;
+      d.total_rows = H;
+      if ((rc = linear_tokens(d, L, EPI_RESIDUAL, st))) return rc;
+    } else {
+      // router logits of RMSNorm(h), top-k, then the routed experts
+      GemvArgs g{};
+      g.x = m->h;
+      g.ldx = H;
+      g.K = H;
+      g.nseg = 1;
+      g.seg[0] = seg_of(ly.router, c.num_experts, m->rlogits);
+      g.ldy = c.num_experts;
+      g.total_rows = c.num_experts;
+      g.norm_w = ly.post_norm;
+      g.eps = c.rms_norm_eps;
+      if ((rc = linear_tokens(g, L, EPI_STORE, st))) return rc;
+      if ((rc = moe_topk_launch(m->rlogits, L, c.num_experts, c.experts_per_tok, c.norm_topk_prob, m->rids,
+                                m->rscores, st)))
+        return rc;
+      MoeArgs me{};
+      me.x = m->h;
+      me.T = L;
+      me.H = H;
+      me.I = c.moe_intermediate_size;
+      me.k = c.experts_per_tok;
+      me.e_first = m->e_first;
+      me.e_local = m->E_local;
+      me.ids = m->rids;
+      me.scores = m->rscores;
+      me.gate = {ly.e_gate.w, ly.e_gate.s, ly.e_gate.b};
+      me.up = {ly.e_up.w, ly.e_up.s, ly.e_up.b};
+      me.down = {ly.e_down.w, ly.e_down.s, ly.e_down.b};
+      me.norm_w = ly.post_norm;
+      me.eps = c.rms_norm_eps;
+      me.act = m->act;
+      me.h = m->h;
+      if ((rc = moe_launch(me, st))) return rc;
+    }
+  }
+  // final norm + lm_head (+ argmax)
+  const Linear& head = c.tie_word_embeddings ? m->embed : m->lm_head;
+  const int V = c.vocab_size;
+  GemvArgs hd{};
+  hd.ldx = H;
+  hd.K = H;
+  hd.nseg = 1;
+  hd.ldy = V;
+  hd.total_rows = V;
+  hd.norm_w = m->final_norm;
+  hd.eps = c.rms_norm_eps;
+  bf16* last_row = nullptr;
+  if (logits_mode == M5_LOGITS_ALL) {
+    hd.x = m->h;
+    hd.seg[0] = seg_of(head, V, (bf16*)logits);
+    if ((rc = linear_tokens(hd, L, EPI_STORE, st))) return rc;
+    last_row = (bf16*)logits + size_t(L - 1) * V;
+  } else if (logits_mode == M5_LOGITS_LAST || d_argmax) {
+    hd.x = m->h + size_t(L - 1) * H;
+    last_row = logits_mode == M5_LOGITS_LAST ? (bf16*)logits : m->logits_last;
+    hd.seg[0] = seg_of(head, V, last_row);
+    if ((rc = linear_tokens(hd, 1, EPI_STORE, st))) return rc;
+  }
+  if (d_argmax && last_row) {
+    if ((rc = argmax_launch(last_row, V, d_argmax, m->argmax_scratch, st))) return rc;
+  }
+  add_len_kernel<<<1, 1, 0, st>>>(d_len, L);
+  M5_LAUNCH_CHECK("length update");
+  return M5_OK;
+}
+
+// --------------------------------------------------- standalone scratch
+// Grow-only per-device arena for the standalone attention entry point.
+struct Arena {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+static std::mutex g_arena_mu;
+static Arena g_arena[64];
+
+static int arena_get(size_t bytes, void** out) {
+  int dev = 0;
+  M5_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(M5_ERR_INVALID, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  Arena& a = g_arena[dev];
+  if (a.bytes < bytes) {
+    if (a.ptr) {
+      M5_CUDA(cudaDeviceSynchronize());
+      M5_CUDA(cudaFree(a.ptr));
+      a.ptr = nullptr;
+      a.bytes = 0;
+    }
+    M5_CUDA(cudaMalloc(&a.ptr, bytes));
+    a.bytes = bytes;
+  }
+  *out = a.ptr;
+  return M5_OK;
+}
+
+}  // namespace m5
+
+using namespace m5;
+
+extern "C" int m5_quantized_matmul(const void* x, int64_t M, int64_t K, const uint32_t* wq, const void* scales,
+                                   const void* biases, int64_t N, int group_size, int bits, void* y, void* stream) {
+  M5_CHECK_ARG(x && wq && scales && biases && y, "m5_quantized_matmul: null pointer");
+  M5_CHECK_ARG(bits == 4 && group_size == 64, "m5_quantized_matmul: only 4-bit group-64 weights");
+  M5_CHECK_ARG(K > 0 && K % 64 == 0 && N > 0 && M >= 0, "m5_quantized_matmul: K must be a multiple of 64");
+  M5_CHECK_ARG(N < (1LL << 31) && K < (1LL << 31) && M < (1LL << 31), "m5_quantized_matmul: size too large");
+  if (M == 0) return M5_OK;
+  GemvArgs a{};
+  a.x = (const bf16*)x;
+  a.ldx = K;
+  a.K = (int)K;
+  a.nseg = 1;
+  a.seg[0].w = wq;
+  a.seg[0].s = (const bf16*)scales;
+  a.seg[0].b = (const bf16*)biases;
+  a.seg[0].rows = (int)N;
+  a.seg[0].y = (bf16*)y;
+  a.ldy = N;
+  a.total_rows = (int)N;
+  return linear_tokens(a, (int)M, EPI_STORE, (cudaStream_t)stream);
+}
+
+extern "C" int m5_rms_norm(const void* x, const void* w, int64_t rows, int64_t dim, float eps, void* y, void* stream) {
+  M5_CHECK_ARG(x && w && y, "m5_rms_norm: null pointer");
+  M5_CHECK_ARG(dim > 0 && rows >= 0, "m5_rms_norm: bad shape");
+  return rms_norm_launch((const bf16*)x, (const bf16*)w, rows, (int)dim, eps, (bf16*)y, (cudaStream_t)stream);
+}
+
+extern "C" int m5_quantized_sdpa(const void* q, int B, int Hq, int L, int D, m5_kv_view keys, m5_kv_view values,
+                                 int Hkv, int S, float scale, int mask_kind, const void* mask,
+                                 const int64_t* mask_strides, int group_size, int bits, void* out, void* stream) {
+  M5_CHECK_ARG(q && out && keys.data && values.data, "m5_quantized_sdpa: null pointer");
+  M5_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && L > 0 && S > 0, "m5_quantized_sdpa: empty shape");
+  M5_CHECK_ARG(Hq % Hkv == 0, "m5_quantized_sdpa: Hq must be a multiple of Hkv");
+  M5_CHECK_ARG(D == 64 || D == 128, "m5_quantized_sdpa: head_dim must be 64 or 128");
+  M5_CHECK_ARG(bits == 0 || bits == 4 || bits == 8, "m5_quantized_sdpa: bits must be 0, 4 or 8");
+  M5_CHECK_ARG(bits == 0 || group_size == 64, "m5_quantized_sdpa: group_size must be 64");
+  M5_CHECK_ARG(bits == 0 || (keys.scales && keys.biases && values.scales && values.biases),
+               "m5_quantized_sdpa: packed K/V need scales and biases");
+  M5_CHECK_ARG(mask_kind >= M5_MASK_NONE && mask_kind <= M5_MASK_ADDITIVE, "m5_quantized_sdpa: mask kind");
+  M5_CHECK_ARG(mask_kind < M5_MASK_BOOL || (mask && mask_strides), "m5_quantized_sdpa: mask pointer/strides");
+  M5_CHECK_ARG(mask_kind != M5_MASK_CAUSAL || L <= S, "m5_quantized_sdpa: causal mask needs L <= S");
+  M5_CHECK_ARG(Hq / Hkv <= 16, "m5_quantized_sdpa: GQA group larger than 16");
+  AttnArgs a{};
+  a.q = (const bf16*)q;
+  a.B = B;
+  a.Hq = Hq;
+  a.L = L;
+  a.D = D;
+  a.k = keys;
+  a.v = values;
+  a.bits = bits;
+  a.Hkv = Hkv;
+  a.S_host = S;
+  a.scale = scale;
+  a.mask_kind = mask_kind;
+  a.mask = mask;
+  if (mask_kind >= M5_MASK_BOOL) {
+    a.ms_b = mask_strides[0];
+    a.ms_h = mask_strides[1];
+    a.ms_l = mask_strides[2];
+  }
+  attn_plan(B, Hq, Hkv, L, S, a.QB, a.nsplit);
+  a.out = (bf16*)out;
+  const size_t need = attn_scratch_bytes(B, Hq, L, D, a.nsplit);
+  if (need) {
+    void* p = nullptr;
+    int rc = arena_get(need, &p);
+    if (rc) return rc;
+    a.part_o = (float*)p;
+    a.part_ml = a.part_o + size_t(B) * Hq * L * a.nsplit * D;
+  }
+  return attn_launch(a, (cudaStream_t)stream);
+}
+
+extern "C" int m5_argmax_bf16(const void* x, int64_t n, int32_t* out, void* stream) {
+  M5_CHECK_ARG(x && out, "m5_argmax_bf16: null pointer");
+  M5_CHECK_ARG(n > 0 && n < (1LL << 31), "m5_argmax_bf16: bad length");
+  void* p = nullptr;
+  int dev = 0;
+  M5_CUDA(cudaGetDevice(&dev));
+  static std::mutex mu;
+  static void* scratch[64] = {nullptr};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!scratch[dev]) {
+      M5_CUDA(cudaMalloc(&scratch[dev], argmax_scratch_bytes()));
+      M5_CUDA(cudaMemset(scratch[dev], 0, argmax_scratch_bytes()));
+    }
+    p = scratch[dev];
+  }
+  return argmax_launch((const bf16*)x, n, out, p, (cudaStream_t)stream);
+}
+
+extern "C" int m5_kv_quantize_layer(const m5_layer_kv* src, const m5_layer_kv* dst, int num_kv_heads, int head_dim,
+                                    int len, void* stream) {
+  M5_CHECK_ARG(src && dst && src->k && src->v && dst->k && dst->v, "m5_kv_quantize_layer: null pointer");
+  M5_CHECK_ARG(dst->k_scales && dst->k_biases && dst->v_scales && dst->v_biases, "m5_kv_quantize_layer: scales");
+  M5_CHECK_ARG(dst->group_size == 64, "m5_kv_quantize_layer: group_size must be 64");
+  return kv_quantize_layer_launch(*src, *dst, num_kv_heads, head_dim, len, (cudaStream_t)stream);
+}
+
+extern "C" int m5_moe_route(const void* x, int T, int H, const uint32_t* gate_w, const void* gate_s, const void* gate_b,
+                            int E, int k, int norm_topk_prob, int32_t* ids, void* scores, void* logits_out,
+                            void* stream) {
+  M5_CHECK_ARG(x && gate_w && gate_s && gate_b && ids && scores, "m5_moe_route: null pointer");
+  M5_CHECK_ARG(T >= 0 && H > 0 && H % 64 == 0 && E > 0 && E <= 256 && k > 0 && k <= E && k <= 32,
+               "m5_moe_route: bad shape");
+  if (T == 0) return M5_OK;
+  void* lg = logits_out;
+  if (!lg) {
+    int rc = arena_get(size_t(T) * E * sizeof(bf16), &lg);
+    if (rc) return rc;
+  }
+  GemvArgs a{};
+  a.x = (const bf16*)x;
+  a.ldx = H;
+  a.K = H;
+  a.nseg = 1;
+  a.seg[0].w = gate_w;
+  a.seg[0].s = (const bf16*)gate_s;
+  a.seg[0].b = (const bf16*)gate_b;
+  a.seg[0].rows = E;
+  a.seg[0].y = (bf16*)lg;
+  a.ldy = E;
+  a.total_rows = E;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = linear_tokens(a, T, EPI_STORE, st);
+  if (rc) return rc;
+  return moe_topk_launch((const bf16*)lg, T, E, k, norm_topk_prob, ids, (bf16*)scores, st);
+}
+
+extern "C" int m5_model_create(const m5_model_cfg* cfg, void** out) {
+  M5_CHECK_ARG(cfg && out, "m5_model_create: null pointer");
+  const m5_model_cfg& c = *cfg;
+  M5_CHECK_ARG(c.head_dim == 128, "m5_model_create: head_dim must be 128");
+  M5_CHECK_ARG(c.bits == 4 && c.group_size == 64, "m5_model_create: weights must be 4-bit group-64");
+  M5_CHECK_ARG(c.hidden_size > 0 && c.hidden_size % 64 == 0, "m5_model_create: hidden_size % 64");
+  M5_CHECK_ARG(c.num_layers > 0 && c.num_heads > 0 && c.num_kv_heads > 0 && c.num_heads % c.num_kv_heads == 0,
+               "m5_model_create: heads");
+  M5_CHECK_ARG(c.vocab_size > 0, "m5_model_create: vocab_size");
+  const int tp = std::max(1, c.tp_size), ep = std::max(1, c.ep_size);
+  M5_CHECK_ARG(c.tp_rank >= 0 && c.tp_rank < tp && c.ep_rank >= 0 && c.ep_rank < ep, "m5_model_create: rank");
+  M5_CHECK_ARG(c.num_heads % tp == 0 && c.num_kv_heads % tp == 0, "m5_model_create: heads not divisible by tp_size");
+  Model* m = new Model();
+  m->cfg = c;
+  m->cfg.tp_size = tp;
+  m->cfg.ep_size = ep;
+  m->Hq = c.num_heads / tp;
+  m->Hkv = c.num_kv_heads / tp;
+  if (c.num_experts > 0) {
+    if (c.num_experts % ep || c.moe_intermediate_size % 64 || c.experts_per_tok <= 0) {
+      delete m;
+      return fail(M5_ERR_INVALID, "m5_model_create: experts not divisible by ep_size or bad MoE sizes");
+    }
+    m->E_local = c.num_experts / ep;
+    m->e_first = c.ep_rank * m->E_local;
+    m->I = c.moe_intermediate_size;
+  } else {
+    if (c.intermediate_size % (64 * tp)) {
+      delete m;
+      return fail(M5_ERR_INVALID, "m5_model_create: intermediate_size not divisible by 64 * tp_size");
+    }
+    m->I = c.intermediate_size / tp;
+  }
+  if (tp > 1 || ep > 1) {
+    delete m;
+    return fail(M5_ERR_UNSUPPORTED, "m5_model_create: multi-rank models need m5_model_set_comm (not in this build)");
+  }
+  m->layers.resize(c.num_layers);
+  *out = m;
+  return M5_OK;
+}
+
+extern "C" int m5_model_destroy(void* model) {
+  Model* m = (Model*)model;
+  if (!m) return M5_OK;
+  if (m->arena) cudaFree(m->arena);
+  if (m->d_inv_freq) cudaFree(m->d_inv_freq);
+  delete m;
+  return M5_OK;
+}
+
+extern "C" int m5_model_bind(void* model, const char* name, const void* ptr) {
+  M5_CHECK_ARG(model && name && ptr, "m5_model_bind: null argument");
+  if (bind((Model*)model, name, ptr) != M5_OK)
+    return fail(M5_ERR_INVALID, std::string("m5_model_bind: unknown tensor name '") + name + "'");
+  return M5_OK;
+}
+
+extern "C" int m5_model_check(void* model) {
+  M5_CHECK_ARG(model, "m5_model_check: null model");
+  Model* m = (Model*)model;
+  std::string miss = missing(m);
+  if (!miss.empty()) return fail(M5_ERR_STATE, "model tensor not bound: " + miss);
+  if (!m->rope_set) return fail(M5_ERR_STATE, "model RoPE table not set (m5_model_set_rope)");
+  return M5_OK;
+}
+
+extern "C" int m5_model_set_rope(void* model, const float* inv_freq, float mscale) {
+  M5_CHECK_ARG(model && inv_freq, "m5_model_set_rope: null argument");
+  Model* m = (Model*)model;
+  const int half = m->cfg.head_dim / 2;
+  if (!m->d_inv_freq) M5_CUDA(cudaMalloc(&m->d_inv_freq, half * sizeof(float)));
+  M5_CUDA(cudaMemcpy(m->d_inv_freq, inv_freq, half * sizeof(float), cudaMemcpyHostToDevice));
+  m->mscale = mscale;
+  m->rope_set = true;
+  return M5_OK;
+}
+
+extern "C" int m5_model_reserve(void* model, int max_tokens) {
+  M5_CHECK_ARG(model && max_tokens > 0, "m5_model_reserve: bad argument");
+  Model* m = (Model*)model;
+  if (max_tokens <= m->max_tokens) return M5_OK;
+  const m5_model_cfg& c = m->cfg;
+  const size_t T = max_tokens, H = c.hidden_size, D = c.head_dim;
+  const size_t QKV = size_t(m->Hq + 2 * m->Hkv) * D;
+  const size_t k = std::max(1, c.experts_per_tok);
+  const size_t act = c.num_experts ? T * k * m->I : T * m->I;
+  // Attention partials for decode-sized calls (L <= 16): nsplit <= 2 * SMs.
+  const size_t part = attn_scratch_bytes(1, m->Hq, (int)std::min<size_t>(T, 4), (int)D, 2 * sm_count());
+  size_t total = 0;
+  const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
+                          size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,
+                          part, argmax_scratch_bytes()};
+  for (size_t s : sizes) total += (s + 255) & ~size_t(255);
+  char* buf = nullptr;
+  M5_CUDA(cudaMalloc(&buf, total));
+  M5_CUDA(cudaMemset(buf, 0, total));
+  if (m->arena) {
+    cudaDeviceSynchronize();
+    cudaFree(m->arena);
+  }
+  m->arena = buf;
+  m->arena_bytes = total;
+  char* p = buf;
+  m->h = (bf16*)carve(p, sizes[0]);
+  m->qkv = (bf16*)carve(p, sizes[1]);
+  m->q = (bf16*)carve(p, sizes[2]);
+  m->attn = (bf16*)carve(p, sizes[3]);
+  m->act = (bf16*)carve(p, sizes[4]);
+  m->logits_last = (bf16*)carve(p, sizes[5]);
+  m->rlogits = (bf16*)carve(p, sizes[6]);
+  m->rscores = (bf16*)carve(p, sizes[7]);
+  m->rids = (int32_t*)carve(p, sizes[8]);
+  m->attn_part = (float*)carve(p, sizes[9]);
+  m->attn_part_bytes = sizes[9];
+  m->argmax_scratch = carve(p, sizes[10]);
+  m->max_tokens = max_tokens;
+  return M5_OK;
+}
+
+extern "C" int m5_forward(void* model, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int L,
+                          void* logits, int logits_mode, int32_t* d_argmax, void* stream) {
+  M5_CHECK_ARG(model && kv && d_len && d_tokens, "m5_forward: null argument");
+  Model* m = (Model*)model;
+  M5_CHECK_ARG(L > 0, "m5_forward: L must be positive");
+  M5_CHECK_ARG(logits_mode >= M5_LOGITS_NONE && logits_mode <= M5_LOGITS_ALL, "m5_forward: logits_mode");
+  M5_CHECK_ARG(logits_mode == M5_LOGITS_NONE || logits, "m5_forward: logits buffer required");
+  if (L > m->max_tokens) return fail(M5_ERR_STATE, "m5_forward: L exceeds m5_model_reserve size");
+  std::string miss = missing(m);
+  if (!miss.empty()) return fail(M5_ERR_STATE, "model tensor not bound: " + miss);
+  if (!m->rope_set) return fail(M5_ERR_STATE, "model RoPE table not set");
+  for (int i = 0; i < m->cfg.num_layers; ++i) {
+    const m5_layer_kv& l = kv[i];
+    if (!l.k || !l.v || l.capacity <= 0) return fail(M5_ERR_INVALID, "m5_forward: cache layer " + std::to_string(i));
+    if (l.bits != 0 && l.bits != 4 && l.bits != 8) return fail(M5_ERR_INVALID, "m5_forward: cache bits");
+    if (l.bits && (!l.k_scales || !l.k_biases || !l.v_scales || !l.v_biases || l.group_size != 64))
+      return fail(M5_ERR_INVALID, "m5_forward: packed cache needs scales/biases and group 64");
+  }
+  return forward(m, kv, d_len, d_tokens, L, logits, logits_mode, d_argmax, (cudaStream_t)stream);
+}

@@ -1,0 +1,186 @@
+"""The token loop: chunked prefill + greedy decode on the device.
+
+Replaces mlx-lm ``stream_generate`` / ``generate_step`` as the reference calls
+them at m5engine/engine.py:396-423: the prompt minus its last token runs in
+chunks of ``prefill_step_size``; after every model call the cache is
+quantized once ``offset >= quantized_kv_start`` (m5engine/attention.py:106-112);
+the last prompt token produces the first sampled token; then every decode step
+feeds the previous token.  Like ``generate_step`` the next step is computed
+before the current token is yielded, so the cache ends holding prompt +
+max_tokens positions.
+
+Greedy decode steps run as one replayed CUDA graph per cache layout: the graph
+reads the previous token and the cache length from device memory and writes
+the argmax back, so the host only copies 4 bytes per token out.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+from typing import Callable, Iterator, List, Optional
+
+import torch
+
+from . import _lib
+from .attention import safe_maybe_quantize_kv_cache
+from .cache import PromptCache, make_prompt_cache
+
+
+@dataclass
+class GenerationResponse:
+    """Fields the reference reads from mlx-lm responses (m5engine/engine.py:424-432)."""
+    text: str
+    token: int
+    logprobs: Optional[torch.Tensor]
+    from_draft: bool
+    prompt_tokens: int
+    prompt_tps: float
+    generation_tokens: int
+    generation_tps: float
+    peak_memory: float
+    finish_reason: Optional[str] = None
+
+
+class DecodeGraph:
+    """One captured L=1 forward: token buffer in, argmax into the same buffer."""
+
+    def __init__(self, model, cache: PromptCache, with_logits: bool):
+        self.model, self.cache = model, cache
+        dev = model.device
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.logits = torch.empty(model.args.vocab_size, dtype=torch.bfloat16, device=dev) if with_logits else None
+        self.sig = cache.signature()
+        self.graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        offsets = [c.offset for c in cache]
+        with torch.cuda.stream(s):
+            self.graph.capture_begin()
+            try:
+                model.forward(self.tok, cache, _lib.M5_LOGITS_LAST if with_logits else _lib.M5_LOGITS_NONE,
+                              self.logits, self.tok, sync_len=False)
+            finally:
+                self.graph.capture_end()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for c, o in zip(cache, offsets):  # capture did not run anything
+            c.offset = o
+
+    def valid_for(self, cache: PromptCache) -> bool:
+        return cache is self.cache and cache.signature() == self.sig
+
+    def step(self) -> None:
+        self.graph.replay()
+        for c in self.cache:
+            c.offset += 1
+
+
+def _step_eager(model, cache: PromptCache, tokens: torch.Tensor, want_logits: bool):
+    out_tok = torch.empty(1, dtype=torch.int32, device=model.device)
+    logits = torch.empty(model.args.vocab_size, dtype=torch.bfloat16, device=model.device) if want_logits else None
+    model.forward(tokens, cache, _lib.M5_LOGITS_LAST if want_logits else _lib.M5_LOGITS_NONE, logits, out_tok)
+    return out_tok, logits
+
+
+def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Optional[Callable] = None,
+                  prompt_cache: Optional[PromptCache] = None, prefill_step_size: int = 2048,
+                  kv_bits: Optional[int] = None, kv_group_size: int = 64, quantized_kv_start: int = 0,
+                  use_graph: bool = True, return_logits: bool = False,
+                  stats: Optional[dict] = None) -> Iterator[tuple]:
+    """Yields (token, logits-or-None) pairs; ``sampler`` None means greedy on the device."""
+    if not prompt:
+        raise ValueError("empty prompt")
+    V = model.args.vocab_size
+    if min(prompt) < 0 or max(prompt) >= V:
+        raise ValueError(f"token id out of range [0, {V})")
+    dev = model.device
+    cache = prompt_cache if prompt_cache is not None else make_prompt_cache(model)
+    total = cache.offset + len(prompt) + max_tokens
+    prompt_t = torch.as_tensor(prompt, dtype=torch.int32).to(dev, non_blocking=True)
+    model.reserve(min(prefill_step_size, max(1, len(prompt) - 1)))
+
+    def maybe_quantize():
+        safe_maybe_quantize_kv_cache(cache, quantized_kv_start, kv_group_size, kv_bits)
+        for c in cache:  # pre-size so decode never reallocates under a captured graph
+            if c.capacity < total:
+                c.reserve(total)
+
+    t0 = time.perf_counter()
+    pos = 0
+    n = len(prompt)
+    while n - pos > 1:
+        m = min(prefill_step_size, n - pos - 1)
+        model.forward(prompt_t[pos:pos + m], cache)
+        maybe_quantize()
+        pos += m
+    greedy = sampler is None
+    tok, logits = _step_eager(model, cache, prompt_t[pos:], return_logits or not greedy)
+    maybe_quantize()
+    if not greedy:
+        tok = sampler(logits.float()[None]).to(torch.int32).reshape(1)
+    host = torch.empty(2, dtype=torch.int32, pin_memory=True)
+    host[0:1].copy_(tok, non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record()
+    ev.synchronize()
+    if stats is not None:
+        stats["prompt_time"] = time.perf_counter() - t0
+        stats["prompt_tokens"] = n
+    y = int(host[0])
+    y_logits = logits
+    graph: Optional[DecodeGraph] = None
+    t1 = time.perf_counter()
+    for i in range(max_tokens):
+        # compute the next step before yielding y (mlx-lm generate_step order)
+        if greedy and use_graph:
+            if graph is None or not graph.valid_for(cache):
+                graph = DecodeGraph(model, cache, return_logits)
+            graph.tok.copy_(tok)
+            graph.step()
+            tok = graph.tok
+            nxt_logits = graph.logits.clone() if return_logits else None
+        else:
+            tok_in = torch.tensor([y], dtype=torch.int32, device=dev)
+            tok, nxt_logits = _step_eager(model, cache, tok_in, return_logits or not greedy)
+            if not greedy:
+                tok = sampler(nxt_logits.float()[None]).to(torch.int32).reshape(1)
+            maybe_quantize()
+        slot = (i + 1) & 1
+        host[slot:slot + 1].copy_(tok, non_blocking=True)
+        ev.record()
+        yield y, y_logits
+        ev.synchronize()
+        y, y_logits = int(host[slot]), nxt_logits
+    if stats is not None:
+        stats["decode_time"] = time.perf_counter() - t1
+
+
+def stream_generate(model, tokenizer, prompt, max_tokens: int = 256, draft_model=None,
+                    **kwargs) -> Iterator[GenerationResponse]:
+    """mlx-lm ``stream_generate`` surface used by the engine (greedy or sampler)."""
+    if draft_model is not None:
+        raise NotImplementedError("speculative decoding with a draft model is not implemented")
+    if isinstance(prompt, str):
+        prompt = tokenizer.encode(prompt)
+    prompt = [int(t) for t in (prompt.tolist() if hasattr(prompt, "tolist") else prompt)]
+    kwargs.pop("logits_processors", None)
+    eos = set(getattr(tokenizer, "eos_token_ids", []) or [])
+    stats: dict = {}
+    t_start = time.perf_counter()
+    n = 0
+    for token, _ in generate_step(prompt, model, max_tokens, stats=stats, **kwargs):
+        n += 1
+        prompt_tps = stats.get("prompt_tokens", len(prompt)) / max(stats.get("prompt_time", 1e-9), 1e-9)
+        gen_time = time.perf_counter() - t_start - stats.get("prompt_time", 0.0)
+        finish = None
+        if token in eos:
+            finish = "stop"
+        elif n == max_tokens:
+            finish = "length"
+        yield GenerationResponse(
+            text="" if finish == "stop" else tokenizer.decode([token]), token=token, logprobs=None,
+            from_draft=False, prompt_tokens=len(prompt), prompt_tps=prompt_tps, generation_tokens=n,
+            generation_tps=n / max(gen_time, 1e-9),
+            peak_memory=torch.cuda.max_memory_allocated(model.device) / 1e9, finish_reason=finish)
+        if finish:
+            break

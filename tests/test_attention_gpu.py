@@ -1,0 +1,107 @@
+"""Quantized-KV attention (m5_quantized_sdpa through blocked_quantized_sdpa)
+against the CPU restatement of m5engine/attention.py.
+
+Tolerances: the device kernel rounds scores and p to bf16 at the reference's
+points but accumulates in a different order and block size, and rounds the
+output to bf16, so it is compared at max-abs 2e-2 on N(0,1) data (output
+values are O(1); one bf16 step at 1.0 is 7.8e-3)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.quant import affine_dequantize, affine_quantize, bf16_bits_to_f32, f32_to_bf16_bits
+from oracle.sdpa import blocked_quantized_sdpa as ref_blocked
+from oracle.sdpa import dense_quantized_sdpa as ref_dense
+from oracle.sdpa import reference_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16(a):
+    return bf16_bits_to_f32(f32_to_bf16_bits(a.astype(np.float32)))
+
+
+def _kv(rng, B, Hkv, S, D, bits):
+    k = _bf16(rng.standard_normal((B, Hkv, S, D)))
+    v = _bf16(rng.standard_normal((B, Hkv, S, D)))
+    if bits == 0:
+        return k, v, torch.from_numpy(k), torch.from_numpy(v)
+    qk = affine_quantize(k, 64, bits)
+    qv = affine_quantize(v, 64, bits)
+    return qk, qv, None, None
+
+
+def _dev(t):
+    wq, s, b = t
+    return (torch.from_numpy(wq.view(np.int32)).cuda(), torch.from_numpy(s.view(np.int16)).view(torch.bfloat16).cuda(),
+            torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).cuda())
+
+
+@pytest.mark.parametrize("hq,hk", [(4, 4), (8, 2)])
+@pytest.mark.parametrize("mask_kind", ["causal", "bool", None])
+def test_reference_grid(hq, hk, mask_kind):
+    """The grid of tests/test_core.py:23-40 (L=6, S=700, D=64, 8-bit g64)."""
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    rng = np.random.default_rng(0)
+    L, S, D = 6, 700, 64
+    q = _bf16(rng.standard_normal((1, hq, L, D)))
+    qk, qv, _, _ = _kv(rng, 1, hk, S, D, 8)
+    causal = torch.arange(S - L, S)[:, None] >= torch.arange(S)[None]
+    mask = {"causal": "causal", "bool": causal, None: None}[mask_kind]
+    dmask = mask.cuda() if isinstance(mask, torch.Tensor) else mask
+    out = blocked_quantized_sdpa(torch.from_numpy(q).to(torch.bfloat16).cuda(), _dev(qk), _dev(qv), 0.125, dmask,
+                                 64, 8).float().cpu()
+    oracle = ref_blocked(torch.from_numpy(q), qk, qv, 0.125, mask, 64, 8, score_budget_bytes=1, min_block=128)
+    kd = torch.from_numpy(affine_dequantize(*qk, 64, 8)).repeat_interleave(hq // hk, dim=1)
+    vd = torch.from_numpy(affine_dequantize(*qv, 64, 8)).repeat_interleave(hq // hk, dim=1)
+    dense = reference_attention(torch.from_numpy(q), kd, vd, 0.125, None if mask_kind is None else causal)
+    assert (out - oracle).abs().max().item() < 2e-2
+    assert (out - dense).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("bits", [8, 4, 0])
+@pytest.mark.parametrize("hq,hk,S", [(64, 8, 4096), (16, 8, 700), (32, 4, 2500), (64, 4, 1500)])
+def test_decode(bits, hq, hk, S):
+    """L == 1 (mlx-lm's dense quantized SDPA path), GQA groups of the BASELINE configs."""
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    rng = np.random.default_rng(S + hq)
+    D = 128
+    q = _bf16(rng.standard_normal((1, hq, 1, D)))
+    k, v, kt, vt = _kv(rng, 1, hk, S, D, bits)
+    qd = torch.from_numpy(q).to(torch.bfloat16).cuda()
+    if bits:
+        out = blocked_quantized_sdpa(qd, _dev(k), _dev(v), D ** -0.5, None, 64, bits)
+        oracle = ref_dense(torch.from_numpy(q), k, v, D ** -0.5, None, 64, bits)
+    else:
+        out = blocked_quantized_sdpa(qd, kt.to(torch.bfloat16).cuda(), vt.to(torch.bfloat16).cuda(), D ** -0.5, None)
+        oracle = ref_dense(torch.from_numpy(q), kt, vt, D ** -0.5, None)
+    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_prefill_chunk_causal(bits):
+    """L > 1 causal chunk at the end of a longer cache (blocked path)."""
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    rng = np.random.default_rng(11)
+    hq, hk, L, S, D = 16, 8, 200, 1200, 128
+    q = _bf16(rng.standard_normal((1, hq, L, D)))
+    k, v, _, _ = _kv(rng, 1, hk, S, D, bits)
+    out = blocked_quantized_sdpa(torch.from_numpy(q).to(torch.bfloat16).cuda(), _dev(k), _dev(v), D ** -0.5,
+                                 "causal", 64, bits)
+    oracle = ref_blocked(torch.from_numpy(q), k, v, D ** -0.5, "causal", 64, bits, score_budget_bytes=1,
+                         min_block=256)
+    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
+
+
+def test_additive_mask():
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    rng = np.random.default_rng(3)
+    hq, hk, L, S, D = 8, 2, 4, 300, 128
+    q = _bf16(rng.standard_normal((1, hq, L, D)))
+    k, v, _, _ = _kv(rng, 1, hk, S, D, 8)
+    add = torch.from_numpy(rng.standard_normal((1, 1, L, S)).astype(np.float32))
+    out = blocked_quantized_sdpa(torch.from_numpy(q).to(torch.bfloat16).cuda(), _dev(k), _dev(v), D ** -0.5,
+                                 add.cuda(), 64, 8)
+    oracle = ref_blocked(torch.from_numpy(q), k, v, D ** -0.5, add, 64, 8, score_budget_bytes=1, min_block=128)
+    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2

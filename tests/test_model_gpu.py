@@ -1,0 +1,111 @@
+"""Full token loop on the device (m5_forward through generate_step) vs the CPU
+restatement of mlx-lm Qwen3 / Qwen3-MoE driven as m5engine/engine.py does.
+
+Bar: greedy tokens identical, per-step logits cosine
+>= 0.9999 and max-abs error <= 0.05, KV cache bytes bit-exact where both
+sides quantize the same bf16 K/V (checked in test_quant_gpu / kv tests)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=2,
+            head_dim=128, intermediate_size=1024, vocab_size=4096, tie_word_embeddings=False,
+            max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+TINY_MOE = dict(TINY, model_type="qwen3_moe", num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
+                norm_topk_prob=True, intermediate_size=0)
+QWEN3_06B = dict(model_type="qwen3", hidden_size=1024, num_hidden_layers=28, num_attention_heads=16,
+                 num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=151936,
+                 tie_word_embeddings=True, max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+
+
+def _build(cfg_dict, seed):
+    from myinfer_b200.model import Model, ModelArgs, upload_weights
+    host = om.generate_weights(om.Config.from_dict(cfg_dict), seed)
+    dev_model = Model(ModelArgs.from_dict(cfg_dict), upload_weights(host, "cuda"), "cuda", max_tokens=64)
+    ora = om.Model(om.Config.from_dict(cfg_dict), host)
+    return dev_model, ora
+
+
+def _run(dev_model, ora, prompt, n, prefill_step, kv_bits, qstart, yarn=1.0):
+    from myinfer_b200.generate import generate_step
+    if yarn > 1:
+        dev_model.set_rope(yarn, 32768)
+        ora.set_rope(yarn, 32768)
+    toks_o, _, logits_o = om.generate(ora, prompt, n, prefill_step=prefill_step, kv_bits=kv_bits,
+                                      quantized_kv_start=qstart, return_logits=True)
+    out = list(generate_step(prompt, dev_model, n, prefill_step_size=prefill_step, kv_bits=kv_bits,
+                             quantized_kv_start=qstart, return_logits=True))
+    toks_d = [t for t, _ in out]
+    logits_d = torch.stack([l.float().cpu() for _, l in out])
+    return toks_o, logits_o, toks_d, logits_d
+
+
+def _check(toks_o, logits_o, toks_d, logits_d, n_equal):
+    assert toks_d[:n_equal] == toks_o[:n_equal], (toks_d, toks_o)
+    k = next((i for i in range(len(toks_o)) if toks_o[i] != toks_d[i]), len(toks_o))
+    k = max(k, 1)
+    a, b = logits_d[:k], logits_o[:k]
+    cos = torch.nn.functional.cosine_similarity(a, b, dim=-1)
+    assert cos.min().item() >= 0.9999, cos.min().item()
+    assert (a - b).abs().max().item() <= 0.05, (a - b).abs().max().item()
+
+
+@pytest.mark.parametrize("kv_bits,qstart", [(8, 0), (4, 0), (8, 24), (None, 0)])
+def test_tiny_dense(kv_bits, qstart):
+    dev_model, ora = _build(TINY, seed=3)
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, TINY["vocab_size"], 45).tolist()
+    r = _run(dev_model, ora, prompt, 12, 16, kv_bits, qstart)
+    _check(*r, n_equal=12)
+
+
+def test_tiny_dense_yarn():
+    dev_model, ora = _build(TINY, seed=4)
+    prompt = list(range(7, 40))
+    _check(*_run(dev_model, ora, prompt, 8, 64, 8, 0, yarn=4.0), n_equal=8)
+
+
+def test_tiny_moe():
+    dev_model, ora = _build(TINY_MOE, seed=6)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, TINY_MOE["vocab_size"], 20).tolist()
+    _check(*_run(dev_model, ora, prompt, 6, 8, 8, 0), n_equal=6)
+
+
+def test_moe_router_matches_oracle():
+    """Router top-k ids equal except at probability ties within 1e-3."""
+    from myinfer_b200 import ops
+    cfg = om.Config.from_dict(TINY_MOE)
+    host = om.generate_weights(cfg, 6)
+    ora = om.Model(cfg, host)
+    rng = np.random.default_rng(2)
+    x = torch.from_numpy(rng.standard_normal((33, cfg.hidden_size)).astype(np.float32)).to(torch.bfloat16).float()
+    inds, scores, gates = ora.route(0, x)
+    name = "model.layers.0.mlp.gate"
+    g = (torch.from_numpy(host[name + ".weight"].view(np.int32)).cuda(),
+         torch.from_numpy(host[name + ".scales"].view(np.int16)).view(torch.bfloat16).cuda(),
+         torch.from_numpy(host[name + ".biases"].view(np.int16)).view(torch.bfloat16).cuda())
+    ids, sc, logits = ops.moe_route(x.to(torch.bfloat16).cuda(), g, cfg.num_experts_per_tok, True)
+    ids = ids.cpu()
+    probs = torch.softmax(gates, -1)
+    for t in range(x.shape[0]):
+        a, b = set(ids[t].tolist()), set(inds[t].tolist())
+        if a != b:
+            kth = probs[t].sort(descending=True).values[cfg.num_experts_per_tok - 1:cfg.num_experts_per_tok + 1]
+            assert (kth[0] - kth[1]).abs() < 1e-3
+        else:
+            assert torch.allclose(sc[t].float().cpu().sort().values, scores[t].sort().values, atol=1e-2)
+
+
+@pytest.mark.slow
+def test_qwen3_06b_config():
+    """0.6B shape, 512-token prompt, greedy, 8-bit KV from position 0."""
+    dev_model, ora = _build(QWEN3_06B, seed=0)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, QWEN3_06B["vocab_size"], 512).tolist()
+    _check(*_run(dev_model, ora, prompt, 32, 2048, 8, 0), n_equal=32)
