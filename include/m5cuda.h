@@ -66,6 +66,11 @@ M5_API int m5_version(void);
  * returns the full length of the message. */
 M5_API size_t m5_last_error(char* buf, size_t n);
 
+/* Sticky device-side error word: nonzero when a bounded wait inside a kernel
+ * gave up (the kernel then returned early and its output is invalid).
+ * Synchronises the device.  reset != 0 clears it. */
+M5_API int m5_device_status(int* code, int reset);
+
 /* ------------------------------------------------------------ quantization */
 /* Affine group quantization of x [rows, cols] (row stride ld_x elements,
  * x_dtype M5_DTYPE_BF16 or M5_DTYPE_F32) into wq [rows, cols*bits/32] uint32,

@@ -50,6 +50,7 @@ class M5ModelCfg(ctypes.Structure):
 _SIGS = {
     "m5_version": (c_int, []),
     "m5_last_error": (c_size_t, [c_char_p, c_size_t]),
+    "m5_device_status": (c_int, [POINTER(c_int), c_int]),
     "m5_affine_quantize": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_int, c_void_p,
                                    c_void_p, c_void_p, c_void_p]),
     "m5_affine_dequantize": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,

@@ -34,6 +34,12 @@ struct GemvArgs {
   int rows_per_warp;
   const bf16* norm_w; // fused RMSNorm of x when non-null
   float eps;
+  // Zero-initialised fp32 [8][mma_rows] + int [mma_rows/16] scratch for the
+  // tensor-core GEMV's split tiles (left zeroed after every launch); when null
+  // the launcher uses its own per-device scratch.
+  float* mma_acc;
+  int* mma_cnt;
+  int mma_rows;
 };
 
 // Launch y = epi(x @ W^T) for up to 8 tokens.  Chooses rows per warp so the
@@ -42,5 +48,17 @@ int gemv_launch(const GemvArgs& a, int MT, int epi, cudaStream_t stream);
 
 // Largest number of tokens one launch can stage for this K (shared memory).
 int gemv_max_tokens(int K);
+
+// Tensor-core variant (gemv_mma.cu): K % 64 == 0, segments of 16-row multiples.
+bool gemv_mma_eligible(const GemvArgs& a, int MT, int epi);
+int gemv_mma_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, int acc_rows, cudaStream_t stream);
+// Bytes of zeroed scratch gemv_mma needs for matrices of up to `rows` rows.
+size_t gemv_mma_scratch_bytes(int rows);
+
+// TMA-fed variant (gemv_tma.cu): K % 512 == 0 and MT <= 2.
+bool gemv_tma_eligible(int K, int MT, int epi);
+int gemv_tma_launch(const GemvArgs& a, int MT, int epi, cudaStream_t stream);
+// Sticky device error word of the bounded waits in gemv_tma.cu (-1 if unreadable).
+int gemv_tma_error(int reset);
 
 }  // namespace m5

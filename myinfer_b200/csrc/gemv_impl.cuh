@@ -6,8 +6,6 @@
 
 namespace m5 {
 
-constexpr int GEMV_WARPS = 16;  // 512-thread CTAs amortise the activation staging
-
 // Element e of a token row lives at this float offset of the staged row.
 __device__ __forceinline__ int xs_index(int e) {
   const int blk = e >> 5, piece = (e >> 2) & 7;

@@ -61,6 +61,9 @@ struct Model {
   float* attn_part = nullptr;
   size_t attn_part_bytes = 0;
   void* argmax_scratch = nullptr;
+  float* mma_acc = nullptr;  // zeroed split-tile scratch of the tensor-core GEMV
+  int* mma_cnt = nullptr;
+  int mma_rows = 0;
 };
 
 static bool parse_layer(const char* name, int& idx, const char*& rest) {
@@ -157,8 +160,11 @@ static int linear_tokens(const GemvArgs& proto, int T, int epi, cudaStream_t st)
   const int cap = gemv_max_tokens(proto.K);
   if (cap <= 0) return fail(M5_ERR_UNSUPPORTED, "linear: K too large for the decode GEMV");
   for (int t0 = 0; t0 < T;) {
-    int mt = 1;
-    while (mt * 2 <= std::min(cap, T - t0)) mt *= 2;
+    int mt = std::min(8, T - t0);
+    if (!gemv_mma_eligible(proto, mt, epi)) {
+      mt = 1;
+      while (mt * 2 <= std::min(cap, T - t0)) mt *= 2;
+    }
     GemvArgs a = proto;
     a.x = proto.x + size_t(t0) * proto.ldx;
     for (int i = 0; i < a.nseg; ++i) {
@@ -170,6 +176,12 @@ static int linear_tokens(const GemvArgs& proto, int T, int epi, cudaStream_t st)
     t0 += mt;
   }
   return M5_OK;
+}
+
+static void attach(const Model* m, GemvArgs& a) {
+  a.mma_acc = m->mma_acc;
+  a.mma_cnt = m->mma_cnt;
+  a.mma_rows = m->mma_rows;
 }
 
 static GemvSeg seg_of(const Linear& l, int rows, bf16* y) {
@@ -208,6 +220,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     a.total_rows = QKV;
     a.norm_w = ly.in_norm;
     a.eps = c.rms_norm_eps;
+    attach(m, a);
     if ((rc = linear_tokens(a, L, EPI_STORE, st))) return rc;
     // QK-norm + RoPE + KV append
     RopeAppendArgs r{};
@@ -255,6 +268,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     o.seg[0] = seg_of(ly.o, H, m->h);
     o.ldy = H;
     o.total_rows = H;
+    attach(m, o);
     if ((rc = linear_tokens(o, L, EPI_RESIDUAL, st))) return rc;
     if (c.num_experts == 0) {
       GemvArgs g{};
@@ -268,6 +282,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       g.total_rows = m->I;
       g.norm_w = ly.post_norm;
       g.eps = c.rms_norm_eps;
+      attach(m, g);
       if ((rc = linear_tokens(g, L, EPI_SWIGLU, st))) return rc;
       GemvArgs d{};
       d.x = m->act;
@@ -277,6 +292,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       d.seg[0] = seg_of(ly.down, H, m->h);
       d.ldy = H;
       d.total_rows = H;
+      attach(m, d);
       if ((rc = linear_tokens(d, L, EPI_RESIDUAL, st))) return rc;
     } else {
       // router logits of RMSNorm(h), top-k, then the routed experts
@@ -290,6 +306,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       g.total_rows = c.num_experts;
       g.norm_w = ly.post_norm;
       g.eps = c.rms_norm_eps;
+      attach(m, g);
       if ((rc = linear_tokens(g, L, EPI_STORE, st))) return rc;
       if ((rc = moe_topk_launch(m->rlogits, L, c.num_experts, c.experts_per_tok, c.norm_topk_prob, m->rids,
                                 m->rscores, st)))
@@ -325,6 +342,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
   hd.total_rows = V;
   hd.norm_w = m->final_norm;
   hd.eps = c.rms_norm_eps;
+  attach(m, hd);
   bf16* last_row = nullptr;
   if (logits_mode == M5_LOGITS_ALL) {
     hd.x = m->h;
@@ -377,6 +395,15 @@ static int arena_get(size_t bytes, void** out) {
 }  // namespace m5
 
 using namespace m5;
+
+extern "C" int m5_device_status(int* code, int reset) {
+  M5_CHECK_ARG(code, "m5_device_status: null pointer");
+  M5_CUDA(cudaDeviceSynchronize());
+  const int g = gemv_tma_error(reset);
+  if (g < 0) return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error word");
+  *code = g;
+  return M5_OK;
+}
 
 extern "C" int m5_quantized_matmul(const void* x, int64_t M, int64_t K, const uint32_t* wq, const void* scales,
                                    const void* biases, int64_t N, int group_size, int bits, void* y, void* stream) {
@@ -600,9 +627,12 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   // Attention partials for decode-sized calls (L <= 16): nsplit <= 2 * SMs.
   const size_t part = attn_scratch_bytes(1, m->Hq, (int)std::min<size_t>(T, 4), (int)D, 2 * sm_count());
   size_t total = 0;
+  const int mrows = (int)std::max<size_t>({QKV, H, size_t(2) * m->I, size_t(c.vocab_size),
+                                            size_t(std::max(1, c.num_experts)), size_t(16)});
+  const int mrows16 = (mrows + 15) / 16 * 16;
   const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
                           size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,
-                          part, argmax_scratch_bytes()};
+                          part, argmax_scratch_bytes(), gemv_mma_scratch_bytes(mrows16)};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -626,6 +656,10 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->attn_part = (float*)carve(p, sizes[9]);
   m->attn_part_bytes = sizes[9];
   m->argmax_scratch = carve(p, sizes[10]);
+  char* mma = carve(p, sizes[11]);
+  m->mma_acc = reinterpret_cast<float*>(mma);
+  m->mma_cnt = reinterpret_cast<int*>(mma + size_t(8) * mrows16 * sizeof(float));
+  m->mma_rows = mrows16;
   m->max_tokens = max_tokens;
   return M5_OK;
 }

@@ -86,8 +86,11 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
                   prompt_cache: Optional[PromptCache] = None, prefill_step_size: int = 2048,
                   kv_bits: Optional[int] = None, kv_group_size: int = 64, quantized_kv_start: int = 0,
                   use_graph: bool = True, return_logits: bool = False,
-                  stats: Optional[dict] = None) -> Iterator[tuple]:
-    """Yields (token, logits-or-None) pairs; ``sampler`` None means greedy on the device."""
+                  stats: Optional[dict] = None, feed: Optional[List[int]] = None) -> Iterator[tuple]:
+    """Yields (token, logits-or-None) pairs; ``sampler`` None means greedy on the device.
+
+    ``feed`` (testing) replaces the token fed at decode step i with feed[i] while
+    the yielded tokens stay the device's own argmax (teacher forcing)."""
     if not prompt:
         raise ValueError("empty prompt")
     V = model.args.vocab_size
@@ -129,18 +132,25 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
     y = int(host[0])
     y_logits = logits
     graph: Optional[DecodeGraph] = None
+    feed_t = None if feed is None else torch.as_tensor(feed, dtype=torch.int32).to(dev)
     t1 = time.perf_counter()
     for i in range(max_tokens):
         # compute the next step before yielding y (mlx-lm generate_step order)
+        if feed_t is not None:
+            tok = feed_t[i:i + 1]
+            y_in = int(feed[i])
+        else:
+            y_in = y
         if greedy and use_graph:
             if graph is None or not graph.valid_for(cache):
                 graph = DecodeGraph(model, cache, return_logits)
-            graph.tok.copy_(tok)
+            if tok is not graph.tok:
+                graph.tok.copy_(tok)
             graph.step()
             tok = graph.tok
             nxt_logits = graph.logits.clone() if return_logits else None
         else:
-            tok_in = torch.tensor([y], dtype=torch.int32, device=dev)
+            tok_in = torch.tensor([y_in], dtype=torch.int32, device=dev)
             tok, nxt_logits = _step_eager(model, cache, tok_in, return_logits or not greedy)
             if not greedy:
                 tok = sampler(nxt_logits.float()[None]).to(torch.int32).reshape(1)

@@ -1,0 +1,105 @@
+"""Kernel microbenchmarks (CUDA-event timed) for the token loop's hot kernels.
+
+    python -m myinfer_b200.microbench gemv --n 25600 --k 5120 [--m 1] [--iters 20]
+    python -m myinfer_b200.microbench attention --s 32768 --l 1 --bits 8 [--hq 64 --hkv 8]
+
+``gemv`` cycles over enough distinct weight matrices that every launch reads
+from HBM (more than L2 in total); ``attention`` is the standalone
+attention.py-op microbench of the BASELINE config (B=1, 64 q / 8 kv heads,
+D=128, bf16 Q, N(0,1) K/V quantized 8/4-bit g64).  One JSON line per run.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+import torch
+
+
+def _timed(fn, iters: int) -> float:
+    """Mean device microseconds per call: `iters` back-to-back launches between
+    two events, enqueued ahead of the GPU (a host-side delay gate keeps the
+    queue full so host launch overhead is not measured)."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(2_000_000)  # ~1 ms of GPU spin so the launches below queue up behind it
+    start.record()
+    for i in range(iters):
+        fn(i)
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) * 1e3 / iters
+
+
+def bench_gemv(n: int, k: int, m: int, iters: int) -> dict:
+    from myinfer_b200 import ops
+    per = n * k // 2 + n * k // 32
+    copies = max(2, (3 << 28) // per + 1)  # > 768 MB of weights in rotation (L2 is 126 MB)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    mats = []
+    for _ in range(copies):
+        w = (0.02 * torch.randn(n, k, generator=g, device="cuda")).to(torch.bfloat16)
+        mats.append(ops.quantize(w, 64, 4))
+        del w
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    for i in range(3):
+        ops.quantized_matmul(x, *mats[i % copies])
+    torch.cuda.synchronize()
+    us = _timed(lambda i: ops.quantized_matmul(x, *mats[i % copies]), iters)
+    alg = n * k * 0.5625 + m * k * 2 + m * n * 2
+    return {"kernel": "gemv", "n": n, "k": k, "m": m, "us": round(us, 2), "alg_bytes": int(alg),
+            "gbs": round(alg / us / 1e3, 1)}
+
+
+def bench_attention(s: int, l: int, bits: int, hq: int, hkv: int, iters: int) -> dict:
+    from myinfer_b200 import ops
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    D = 128
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.randn(1, hq, l, D, generator=g, device="cuda").to(torch.bfloat16)
+    reps = max(1, min(8, (1 << 29) // max(1, 2 * hkv * s * D)))
+    kvs = []
+    for _ in range(reps):
+        k = torch.randn(1, hkv, s, D, generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn(1, hkv, s, D, generator=g, device="cuda").to(torch.bfloat16)
+        kvs.append((ops.quantize(k, 64, bits), ops.quantize(v, 64, bits)) if bits else (k, v))
+        del k, v
+    mask = "causal" if l > 1 else None
+    for i in range(2):
+        blocked_quantized_sdpa(q, *kvs[i % reps], D ** -0.5, mask, 64, bits)
+    torch.cuda.synchronize()
+    us = _timed(lambda i: blocked_quantized_sdpa(q, *kvs[i % reps], D ** -0.5, mask, 64, bits), iters)
+    per_elem = bits / 8 + 4 / 64 if bits else 2
+    kv_bytes = 2 * hkv * D * s * per_elem
+    alg = kv_bytes + 2 * hq * l * D * 2
+    flops = 4 * hq * D * (l * s - (l * (l - 1) // 2 if l > 1 else 0))
+    return {"kernel": "attention", "s": s, "l": l, "bits": bits, "hq": hq, "hkv": hkv, "us": round(us, 2),
+            "alg_bytes": int(alg), "gbs": round(alg / us / 1e3, 1), "tflops": round(flops / us / 1e6, 2)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    g = sub.add_parser("gemv")
+    g.add_argument("--n", type=int, default=25600)
+    g.add_argument("--k", type=int, default=5120)
+    g.add_argument("--m", type=int, default=1)
+    g.add_argument("--iters", type=int, default=20)
+    a = sub.add_parser("attention")
+    a.add_argument("--s", type=int, default=32768)
+    a.add_argument("--l", type=int, default=1)
+    a.add_argument("--bits", type=int, default=8)
+    a.add_argument("--hq", type=int, default=64)
+    a.add_argument("--hkv", type=int, default=8)
+    a.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    if args.cmd == "gemv":
+        r = bench_gemv(args.n, args.k, args.m, args.iters)
+    else:
+        r = bench_attention(args.s, args.l, args.bits, args.hq, args.hkv, args.iters)
+    print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
