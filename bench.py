@@ -207,13 +207,23 @@ def gemv_roofline(model, cfg, peak_gbs) -> dict:
         for n in names[:4]:
             ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"])
     torch.cuda.synchronize()
-    # all layers' up_proj back to back (distinct weights, no L2 reuse); the
-    # leading GPU sleep lets the launches queue so host overhead is not timed
+    # all layers' up_proj back to back (distinct weights, no L2 reuse),
+    # captured in one CUDA graph so host launch overhead is not timed
+    s = torch.cuda.Stream(device=model.device)
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    outs = [torch.empty(1, cfg["intermediate_size"], dtype=torch.bfloat16, device=model.device) for _ in names]
+    with torch.cuda.stream(s):
+        graph.capture_begin()
+        for n, o in zip(names, outs):
+            o.copy_(ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"]))
+        graph.capture_end()
+    torch.cuda.current_stream().wait_stream(s)
+    graph.replay()
+    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda._sleep(2_000_000)
     a.record()
-    for n in names:
-        ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"])
+    graph.replay()
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / len(names)

@@ -292,22 +292,45 @@ __global__ void __launch_bounds__(D) attn_combine_kernel(const float* __restrict
                                                          bf16* __restrict__ out) {
   const size_t row = blockIdx.x;  // (b * Hq + h) * L + qi
   const int d = threadIdx.x;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[(row * nsplit + s) * 2]);
-  float num = 0.f, den = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const float m = part_ml[(row * nsplit + s) * 2];
-    if (m == -INFINITY) continue;
-    const float w = expf(m - M);
-    num = fmaf(w, part_o[(row * nsplit + s) * D + d], num);
+  __shared__ float w_s[1024];
+  __shared__ float stat[2];
+  // split weights exp(m_s - M): one thread per split, loads issued in parallel
+  float m = -INFINITY;
+  for (int s = d; s < nsplit; s += D) m = fmaxf(m, part_ml[(row * nsplit + s) * 2]);
+  m = warp_max(m);
+  __shared__ float wmax[D / 32];
+  if ((d & 31) == 0) wmax[d >> 5] = m;
+  __syncthreads();
+  if (d == 0) {
+    float M = -INFINITY;
+    for (int i = 0; i < D / 32; ++i) M = fmaxf(M, wmax[i]);
+    stat[0] = M;
+  }
+  __syncthreads();
+  const float M = stat[0];
+  float den = 0.f;
+  for (int s = d; s < nsplit; s += D) {
+    const float ms = part_ml[(row * nsplit + s) * 2];
+    const float w = (ms == -INFINITY) ? 0.f : expf(ms - M);
+    w_s[s] = w;
     den = fmaf(w, part_ml[(row * nsplit + s) * 2 + 1], den);
   }
+  den = warp_sum(den);
+  __shared__ float wden[D / 32];
+  if ((d & 31) == 0) wden[d >> 5] = den;
+  __syncthreads();
+  float dsum = 0.f;
+  for (int i = 0; i < D / 32; ++i) dsum += wden[i];
+  // numerator: independent loads over the splits (unrolled by the compiler)
+  float num = 0.f;
+#pragma unroll 8
+  for (int s = 0; s < nsplit; ++s) num = fmaf(w_s[s], part_o[(row * nsplit + s) * D + d], num);
   size_t od = row;
   if (tokens_major) {
     const size_t qi = row % L, bh = row / L, h = bh % Hq, b = bh / Hq;
     od = (b * L + qi) * Hq + h;
   }
-  out[od * D + d] = f2bf(num / fmaxf(den, 1e-30f));
+  out[od * D + d] = f2bf(num / fmaxf(dsum, 1e-30f));
 }
 
 size_t attn_scratch_bytes(int B, int Hq, int L, int D, int nsplit) {
@@ -324,7 +347,7 @@ void attn_plan(int B, int Hq, int Hkv, int L, int S_max, int& QB, int& nsplit) {
   const int tiles = std::max(1, (S_max + ATT_TK - 1) / ATT_TK);
   // Enough CTAs for ~2 per SM, each with at least one key tile.
   long long want = (2LL * sm_count() + ctas - 1) / ctas;
-  nsplit = (int)std::max(1LL, std::min<long long>(want, tiles));
+  nsplit = (int)std::max(1LL, std::min<long long>(std::min<long long>(want, tiles), 1024));
 }
 
 template <int BITS, int D, int R>
@@ -348,7 +371,9 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream) {
   const int R = a.QB * rep;
   if (R > ATT_RMAX) return fail(M5_ERR_INVALID, "attention: queries-per-CTA x GQA group exceeds 16");
   int rc;
-  if (a.D == 128) {
+  if (attn_mma_eligible(a)) {
+    rc = attn_mma_launch(a, stream);
+  } else if (a.D == 128) {
     if (a.bits == 8) rc = launch_r<8, 128>(a, R, stream);
     else if (a.bits == 4) rc = launch_r<4, 128>(a, R, stream);
     else rc = launch_r<0, 128>(a, R, stream);

@@ -35,4 +35,10 @@ void attn_plan(int B, int Hq, int Hkv, int L, int S_max, int& QB, int& nsplit);
 // Launch (and combine when nsplit > 1).  part_* must hold attn_scratch_bytes.
 int attn_launch(const AttnArgs& a, cudaStream_t stream);
 
+// Tensor-core split-KV decode kernel (attn_mma.cu): 8/4-bit K/V, D = 128,
+// rows (GQA group x queries per CTA) <= 16, no / causal mask, aligned views.
+bool attn_mma_eligible(const AttnArgs& a);
+int attn_mma_launch(const AttnArgs& a, cudaStream_t stream);
+int attn_mma_error(int reset);
+
 }  // namespace m5

@@ -307,15 +307,17 @@ int gemv_launch(const GemvArgs& a_in, int MT, int epi, cudaStream_t stream) {
   GemvArgs a = a_in;
   if (a.K % 64 != 0 || a.K <= 0) return fail(M5_ERR_INVALID, "gemv: K must be a positive multiple of 64");
   if (a.total_rows <= 0) return M5_OK;
-  if (gemv_mma_eligible(a, MT, epi)) {
+  const bool tmap = gemv_tmap_eligible(a, MT, epi);
+  if (tmap || gemv_mma_eligible(a, MT, epi)) {
     const int vrows = a.total_rows * (epi == EPI_SWIGLU ? 2 : 1);
-    if (a.mma_acc && a.mma_cnt && a.mma_rows >= vrows)
-      return gemv_mma_launch(a, MT, epi, a.mma_acc, a.mma_cnt, a.mma_rows, stream);
-    float* acc = nullptr;
-    int* cnt = nullptr;
-    int rows = 0;
-    int rc = gemv_default_scratch(vrows, &acc, &cnt, &rows);
-    if (rc) return rc;
+    float* acc = a.mma_acc;
+    int* cnt = a.mma_cnt;
+    int rows = a.mma_rows;
+    if (!(acc && cnt && rows >= vrows)) {
+      int rc = gemv_default_scratch(vrows, &acc, &cnt, &rows);
+      if (rc) return rc;
+    }
+    if (tmap) return gemv_tmap_launch(a, MT, epi, acc, cnt, rows, stream);
     return gemv_mma_launch(a, MT, epi, acc, cnt, rows, stream);
   }
   if (gemv_tma_eligible(a.K, MT, epi)) return gemv_tma_launch(a, MT, epi, stream);

@@ -49,6 +49,11 @@ int gemv_launch(const GemvArgs& a, int MT, int epi, cudaStream_t stream);
 // Largest number of tokens one launch can stage for this K (shared memory).
 int gemv_max_tokens(int K);
 
+// TMA tensor-map + tensor-core variant (gemv_tmap.cu): K % 512 == 0.
+bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi);
+int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, int acc_rows, cudaStream_t stream);
+int gemv_tmap_error(int reset);
+
 // Tensor-core variant (gemv_mma.cu): K % 64 == 0, segments of 16-row multiples.
 bool gemv_mma_eligible(const GemvArgs& a, int MT, int epi);
 int gemv_mma_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, int acc_rows, cudaStream_t stream);

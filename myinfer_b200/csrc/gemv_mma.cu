@@ -25,12 +25,13 @@
 // Weight loads are prefetched PIPE steps ahead in registers.
 #include <algorithm>
 
+#include "frag_stage.cuh"
 #include "gemv.cuh"
 
 namespace m5 {
 
 constexpr int MW = 8;      // warps per CTA
-constexpr int PIPE_S = 6;  // steps prefetched per warp
+constexpr int PIPE_S = 12;  // steps prefetched per warp
 
 struct MmaScratch {
   float* acc;      // [8][acc_rows] fp32, zero between launches
@@ -88,46 +89,8 @@ __global__ void __launch_bounds__(MW * 32, 2) gemv_mma_kernel(const GemvArgs a, 
   float* red = xg + MT * NG;                                      // [33]
 
   // ---- stage activations (optionally RMS-normalised) in fragment order
-  const int tid = threadIdx.x, nt = blockDim.x;
-  for (int t = 0; t < MT; ++t) {
-    const bf16* xr = a.x + t * a.ldx;
-    float inv = 1.f;
-    if (a.norm_w) {
-      float ss = 0.f;
-      for (int i = tid; i < K; i += nt) {
-        const float v = bf2f(xr[i]);
-        ss += v * v;
-      }
-      ss = warp_sum(ss);
-      if ((tid & 31) == 0) red[tid >> 5] = ss;
-      __syncthreads();
-      float tot = 0.f;
-      for (int w = 0; w < (nt >> 5); ++w) tot += red[w];
-      inv = __frsqrt_rn(__fadd_rn(tot / float(K), a.eps));
-      __syncthreads();
-    }
-    // one thread per (group, t, pair j): elements e0 = 64G + 16t + 8(j>>2) + (j&3), e1 = e0 + 4
-    for (int p = tid; p < NG * 32; p += nt) {
-      const int G = p >> 5, tq = (p >> 3) & 3, j = p & 7;
-      const int e0 = G * 64 + tq * 16 + (j >> 2) * 8 + (j & 3);
-      float v0 = bf2f(xr[e0]), v1 = bf2f(xr[e0 + 4]);
-      if (a.norm_w) {
-        v0 = rbf(__fmul_rn(bf2f(a.norm_w[e0]), rbf(__fmul_rn(v0, inv))));
-        v1 = rbf(__fmul_rn(bf2f(a.norm_w[e0 + 4]), rbf(__fmul_rn(v1, inv))));
-      }
-      xf[(t * NG + G) * 32 + tq * 8 + j] =
-          uint32_t(__bfloat16_as_ushort(f2bf(v0))) | (uint32_t(__bfloat16_as_ushort(f2bf(v1))) << 16);
-    }
-  }
-  __syncthreads();
-  for (int q = tid; q < MT * NG; q += nt) {
-    const uint32_t* p = xf + q * 32;
-    float s = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < 32; ++j) s += bf16_lo(p[j]) + bf16_hi(p[j]);
-    xg[q] = s;
-  }
-  __syncthreads();
+  const int tid = threadIdx.x;
+  stage_frag<MT, MW * 32>(a.x, a.ldx, K, a.norm_w, a.eps, xf, xg, red, 0);
 
   // ---- this warp's range of (tile, group) steps
   const int lane = tid & 31, g = lane >> 2, tq = lane & 3;

@@ -1,0 +1,386 @@
+// Decode dequant-GEMV: 2-D TMA tiles into shared memory + tensor-core dot
+// products (kernel K1, M <= 8 tokens, K % 512 == 0).
+//
+// The register-prefetch tensor-core GEMV (gemv_mma.cu) spends ~3.6 issue
+// slots per weight and stalls on L1 load latency with 16 warps per SM; the
+// TMA-fed CUDA-core GEMV (gemv_tma.cu) keeps enough bytes in flight but is
+// issue-bound at ~5.3 slots per weight.  This kernel takes the best of both:
+//   * a producer warp streams units of (16 weight rows x 512 columns) with
+//     2-D tensor-map TMA loads (weights with 128-byte swizzle so the 8 rows a
+//     fragment load touches hit different banks; bf16 scales and biases) into
+//     a 12-stage ring (~54 KB in flight per CTA), no registers involved;
+//   * four consumer warps each take two 64-column scale groups of every unit
+//     and run the same mma.sync m16n8k16 bf16 dot products as gemv_mma.cu:
+//     codes -> (128 + q) bf16 pairs with one LOP3 per two codes, per-group
+//     fold  s * D + (b - 128 s) * sum(x);
+//   * units are dealt to CTAs as equal contiguous ranges (stream-K); partial
+//     tile sums go through fp32 atomics into a zeroed scratch and the warp that
+//     completes a tile runs the epilogue and re-zeroes the scratch.
+// All mbarrier waits are bounded (tma.cuh).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "frag_stage.cuh"
+#include "gemv.cuh"
+#include "tma.cuh"
+
+namespace m5 {
+
+static __device__ int g_gemv_tmap_err = 0;
+
+constexpr int TP_CW = 4;                       // consumer warps
+constexpr int TP_THREADS = (TP_CW + 1) * 32;
+constexpr int TP_STAGES = 12;
+constexpr int TP_W_STAGE = 4096;               // 16 rows x 256 bytes (2 halves x 2 swizzled 1 KB boxes)
+constexpr int TP_SB_STAGE = 256;               // 2 halves x 8 rows x 16 bytes (8 bf16 groups)
+
+struct TmapSet {
+  CUtensorMap w[3], s[3], b[3];  // per segment
+};
+
+__device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t tp_nib_pair(uint32_t w, int i) {
+  return ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
+}
+
+__device__ __forceinline__ void tp_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Half h (rows 8h..8h+7) of tile `tile`: segment and first row inside it.
+template <int EPI>
+__device__ __forceinline__ void tp_half(const GemvArgs& a, int tile, int h, int& si, int& row0) {
+  if constexpr (EPI == EPI_SWIGLU) {
+    si = h;
+    row0 = tile * 8;
+  } else {
+    int v = tile * 16 + 8 * h;
+    si = 0;
+    while (si < a.nseg - 1 && v >= a.seg[si].rows) {
+      v -= a.seg[si].rows;
+      ++si;
+    }
+    row0 = v;
+  }
+}
+
+template <int MT, int EPI>
+__global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a, const __grid_constant__ TmapSet tm,
+                                                               float* acc_buf, int* cnt_buf, int acc_rows) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 128-byte-swizzled boxes must start on 1 KB boundaries
+  unsigned char* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+  const int K = a.K, NG = K >> 6, NCH = NG >> 3;
+  unsigned char* wring = smem;                                   // [STAGES][4096], 1024-aligned boxes
+  unsigned char* sbring = wring + TP_STAGES * TP_W_STAGE;        // [STAGES][2 (s,b)][256]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbring + TP_STAGES * 2 * TP_SB_STAGE);
+  uint64_t* empty = full + TP_STAGES;
+  uint32_t* xf = reinterpret_cast<uint32_t*>(empty + TP_STAGES);  // [MT][NG][4][8] bf16 pairs
+  float* xg = reinterpret_cast<float*>(xf + MT * NG * 32);        // [MT][NG]
+  float* red = xg + MT * NG;                                      // [8]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
+  const int ntiles = vrows >> 4;
+  const long long total = (long long)ntiles * NCH;
+  const long long u0 = total * blockIdx.x / gridDim.x, u1 = total * (blockIdx.x + 1) / gridDim.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < TP_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], TP_CW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == TP_CW) {
+    // -------------------------------------------------------------- producer
+    if (lane == 0) {
+      int it = 0;
+      for (long long u = u0; u < u1; ++u, ++it) {
+        const int st = it % TP_STAGES;
+        const uint32_t par = (it / TP_STAGES) & 1;
+        if (!mbar_wait(&empty[st], par ^ 1, &g_gemv_tmap_err)) return;
+        const int tile = int(u / NCH), ch = int(u % NCH);
+        mbar_arrive_expect_tx(&full[st], TP_W_STAGE + 2 * TP_SB_STAGE);
+        unsigned char* ws = wring + st * TP_W_STAGE;
+        unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int si, row0;
+          tp_half<EPI>(a, tile, h, si, row0);
+          tma2d(ws + (2 * h + 0) * 1024, &tm.w[si], ch * 64 + 0, row0, &full[st]);
+          tma2d(ws + (2 * h + 1) * 1024, &tm.w[si], ch * 64 + 32, row0, &full[st]);
+          tma2d(ss + h * 128, &tm.s[si], ch * 8, row0, &full[st]);
+          tma2d(ss + TP_SB_STAGE + h * 128, &tm.b[si], ch * 8, row0, &full[st]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------- consumers: stage activations
+  stage_frag<MT, TP_CW * 32>(a.x, a.ldx, K, a.norm_w, a.eps, xf, xg, red, 1);
+
+  const int g = lane >> 2, tq = lane & 3;
+  const int tok = g < MT ? g : MT - 1;
+  const uint32_t* xfl = xf + tok * NG * 32 + tq * 8;
+  const float* xg0 = xg + (2 * tq < MT ? 2 * tq : MT - 1) * NG;
+  const float* xg1 = xg + (2 * tq + 1 < MT ? 2 * tq + 1 : MT - 1) * NG;
+
+  float tot[4] = {0.f, 0.f, 0.f, 0.f};
+  int cur_tile = u0 < u1 ? int(u0 / NCH) : 0, done = 0;
+
+  auto flush = [&](int tile) {
+    const int base = tile * 16;
+    const int t0 = 2 * tq, t1 = 2 * tq + 1;
+    if (t0 < MT) {
+      atomicAdd(&acc_buf[t0 * acc_rows + base + g], tot[0]);
+      atomicAdd(&acc_buf[t0 * acc_rows + base + g + 8], tot[2]);
+    }
+    if (t1 < MT) {
+      atomicAdd(&acc_buf[t1 * acc_rows + base + g], tot[1]);
+      atomicAdd(&acc_buf[t1 * acc_rows + base + g + 8], tot[3]);
+    }
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = (atomicAdd(&cnt_buf[tile], done) + done == NG);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence();
+      for (int q = lane; q < 16 * MT; q += 32) {
+        const int r16 = q & 15, t = q >> 4;
+        float* p = &acc_buf[t * acc_rows + base + r16];
+        if constexpr (EPI == EPI_SWIGLU) {
+          if (r16 < 8) {
+            float* pu = &acc_buf[t * acc_rows + base + r16 + 8];
+            const float v = __ldcg(p), u = __ldcg(pu);
+            *p = 0.f;
+            *pu = 0.f;
+            const float gv = rbf(v), uv = rbf(u);
+            const float sg = rbf(1.f / (1.f + expf(-gv)));
+            a.seg[0].y[t * a.ldy + tile * 8 + r16] = f2bf(rbf(gv * sg) * uv);
+          }
+        } else {
+          const float v = __ldcg(p);
+          *p = 0.f;
+          int si, row0;
+          tp_half<EPI>(a, tile, r16 >> 3, si, row0);
+          const int rr = row0 + (r16 & 7);
+          const GemvSeg& sg = a.seg[si];
+          if constexpr (EPI == EPI_STORE) {
+            sg.y[t * a.ldy + rr] = f2bf(v);
+          } else if constexpr (EPI == EPI_RESIDUAL) {
+            bf16* o = sg.y + t * a.ldy + rr;
+            *o = f2bf(bf2f(*o) + rbf(v));
+          } else {
+            sg.yf[t * a.ldy + rr] = v;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) cnt_buf[tile] = 0;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) tot[i] = 0.f;
+    done = 0;
+  };
+
+  int it = 0;
+  for (long long u = u0; u < u1; ++u, ++it) {
+    const int st = it % TP_STAGES;
+    const uint32_t par = (it / TP_STAGES) & 1;
+    const int tile = int(u / NCH), ch = int(u % NCH);
+    if (tile != cur_tile) {
+      flush(cur_tile);
+      cur_tile = tile;
+    }
+    if (!mbar_wait(&full[st], par, &g_gemv_tmap_err)) return;
+    const unsigned char* ws = wring + st * TP_W_STAGE;
+    const unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int j = 2 * warp + jj;        // group within the unit
+      const int G = ch * 8 + j;           // global scale group
+      // swizzled 8-byte fragment of rows g (half 0) and g (half 1 = tile row g+8)
+      const int c = 2 * (j & 3) + (tq >> 1);
+      const int off = g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
+      const uint2 w0 = *reinterpret_cast<const uint2*>(ws + (0 + (j >> 2)) * 1024 + off);
+      const uint2 w8 = *reinterpret_cast<const uint2*>(ws + (2 + (j >> 2)) * 1024 + off);
+      const uint4 xa = *reinterpret_cast<const uint4*>(xfl + G * 32);
+      const uint4 xb = *reinterpret_cast<const uint4*>(xfl + G * 32 + 4);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        uint32_t A[4] = {tp_nib_pair(w0.x, 0), tp_nib_pair(w8.x, 0), tp_nib_pair(w0.x, 1), tp_nib_pair(w8.x, 1)};
+        tp_mma(d, A, xa.x, xa.y);
+      }
+      {
+        uint32_t A[4] = {tp_nib_pair(w0.x, 2), tp_nib_pair(w8.x, 2), tp_nib_pair(w0.x, 3), tp_nib_pair(w8.x, 3)};
+        tp_mma(d, A, xa.z, xa.w);
+      }
+      {
+        uint32_t A[4] = {tp_nib_pair(w0.y, 0), tp_nib_pair(w8.y, 0), tp_nib_pair(w0.y, 1), tp_nib_pair(w8.y, 1)};
+        tp_mma(d, A, xb.x, xb.y);
+      }
+      {
+        uint32_t A[4] = {tp_nib_pair(w0.y, 2), tp_nib_pair(w8.y, 2), tp_nib_pair(w0.y, 3), tp_nib_pair(w8.y, 3)};
+        tp_mma(d, A, xb.z, xb.w);
+      }
+      const bf16* s0 = reinterpret_cast<const bf16*>(ss + g * 16) + j;
+      const bf16* s8 = reinterpret_cast<const bf16*>(ss + 128 + g * 16) + j;
+      const bf16* b0 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + g * 16) + j;
+      const bf16* b8 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + 128 + g * 16) + j;
+      const float sA = bf2f(*s0), bA = bf2f(*b0), sB = bf2f(*s8), bB = bf2f(*b8);
+      const float X0 = xg0[G], X1 = xg1[G];
+      const float oA = fmaf(-128.f, sA, bA), oB = fmaf(-128.f, sB, bB);
+      tot[0] = fmaf(sA, d[0], fmaf(oA, X0, tot[0]));
+      tot[1] = fmaf(sA, d[1], fmaf(oA, X1, tot[1]));
+      tot[2] = fmaf(sB, d[2], fmaf(oB, X0, tot[2]));
+      tot[3] = fmaf(sB, d[3], fmaf(oB, X1, tot[3]));
+    }
+    done += 2;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (u0 < u1) flush(cur_tile);
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i) {
+  auto enc = encode_fn();
+  if (!enc) return fail(M5_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t rows = (cuuint64_t)sg.rows;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)K / 8, rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K / 2};
+    cuuint32_t box[2] = {32, 8}, es[2] = {1, 1};
+    CUresult r = enc(&ts.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(sg.w), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(M5_ERR_CUDA, "tensor map (weights) encode failed");
+  }
+  const bf16* p2[2] = {sg.s, sg.b};
+  CUtensorMap* m2[2] = {&ts.s[i], &ts.b[i]};
+  for (int k = 0; k < 2; ++k) {
+    cuuint64_t dims[2] = {(cuuint64_t)K / 64, rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K / 32};
+    cuuint32_t box[2] = {8, 8}, es[2] = {1, 1};
+    CUresult r = enc(m2[k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(p2[k]), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(M5_ERR_CUDA, "tensor map (scales) encode failed");
+  }
+  return M5_OK;
+}
+
+static size_t tp_smem(int MT, int K) {
+  return TP_STAGES * (TP_W_STAGE + 2 * TP_SB_STAGE) + 2 * TP_STAGES * 8 + size_t(MT) * (K / 64) * 32 * 4 +
+         size_t(MT) * (K / 64) * 4 + 8 * 4 + 1024;
+}
+
+bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
+  if (MT < 1 || MT > 8 || a.K % 512) return false;
+  if (tp_smem(MT, a.K) > 200 * 1024) return false;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  for (int i = 0; i < a.nseg; ++i) {
+    if (!al(a.seg[i].w) || !al(a.seg[i].s) || !al(a.seg[i].b)) return false;
+    if (epi == EPI_SWIGLU ? (a.seg[i].rows % 8) : (a.seg[i].rows % 16)) return false;
+  }
+  if (epi == EPI_SWIGLU && (a.nseg < 2 || a.seg[0].rows != a.total_rows || a.seg[1].rows != a.total_rows))
+    return false;
+  return encode_fn() != nullptr;
+}
+
+template <int MT, int EPI>
+static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* acc, int* cnt, int acc_rows, cudaStream_t st) {
+  const size_t smem = tp_smem(MT, a.K);
+  static bool configured = false;
+  if (!configured) {
+    M5_CUDA(cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
+    configured = true;
+  }
+  int per_sm = 0;
+  M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tmap_kernel<MT, EPI>, TP_THREADS, smem));
+  const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
+  const long long units = (long long)(vrows / 16) * (a.K / 512);
+  const long long max_ctas = (long long)std::max(1, per_sm) * sm_count();
+  const int grid = (int)std::max(1LL, std::min(max_ctas, units));
+  gemv_tmap_kernel<MT, EPI><<<grid, TP_THREADS, smem, st>>>(a, ts, acc, cnt, acc_rows);
+  M5_LAUNCH_CHECK("gemv_tmap launch");
+  return M5_OK;
+}
+
+template <int MT>
+static int tp_launch_epi(const GemvArgs& a, int epi, const TmapSet& ts, float* acc, int* cnt, int rows,
+                         cudaStream_t st) {
+  switch (epi) {
+    case EPI_STORE: return tp_launch_t<MT, EPI_STORE>(a, ts, acc, cnt, rows, st);
+    case EPI_RESIDUAL: return tp_launch_t<MT, EPI_RESIDUAL>(a, ts, acc, cnt, rows, st);
+    case EPI_SWIGLU: return tp_launch_t<MT, EPI_SWIGLU>(a, ts, acc, cnt, rows, st);
+    case EPI_F32: return tp_launch_t<MT, EPI_F32>(a, ts, acc, cnt, rows, st);
+  }
+  return fail(M5_ERR_INVALID, "gemv_tmap: bad epilogue");
+}
+
+int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, int acc_rows, cudaStream_t st) {
+  const int vrows = a.total_rows * (epi == EPI_SWIGLU ? 2 : 1);
+  if (vrows > acc_rows) return fail(M5_ERR_INVALID, "gemv_tmap: scratch too small for this matrix");
+  TmapSet ts;
+  memset(&ts, 0, sizeof(ts));
+  for (int i = 0; i < a.nseg && i < 3; ++i) {
+    int rc = make_maps(a.seg[i], a.K, ts, i);
+    if (rc) return rc;
+  }
+  switch (MT) {
+    case 1: return tp_launch_epi<1>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 2: return tp_launch_epi<2>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 3: return tp_launch_epi<3>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 4: return tp_launch_epi<4>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 5: return tp_launch_epi<5>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 6: return tp_launch_epi<6>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 7: return tp_launch_epi<7>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 8: return tp_launch_epi<8>(a, epi, ts, acc, cnt, acc_rows, st);
+  }
+  return fail(M5_ERR_INVALID, "gemv_tmap: MT must be 1..8");
+}
+
+int gemv_tmap_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemv_tmap_err, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_gemv_tmap_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace m5

@@ -400,8 +400,10 @@ extern "C" int m5_device_status(int* code, int reset) {
   M5_CHECK_ARG(code, "m5_device_status: null pointer");
   M5_CUDA(cudaDeviceSynchronize());
   const int g = gemv_tma_error(reset);
-  if (g < 0) return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error word");
-  *code = g;
+  const int gt = gemv_tmap_error(reset);
+  const int at = attn_mma_error(reset);
+  if (g < 0 || gt < 0 || at < 0) return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error words");
+  *code = g | gt | at;
   return M5_OK;
 }
 

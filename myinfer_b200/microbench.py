@@ -19,14 +19,25 @@ import torch
 
 
 def _timed(fn, iters: int) -> float:
-    """Mean device microseconds per call: `iters` back-to-back launches between
-    two events, enqueued ahead of the GPU (a host-side delay gate keeps the
-    queue full so host launch overhead is not measured)."""
+    """Mean device microseconds per call.  The `iters` calls are captured once
+    into a CUDA graph and the graph is replayed, so host-side launch overhead
+    (Python, ctypes, descriptor setup) is not part of the measurement."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        fn(0)  # warm (lazy module load, attribute setup) outside the capture
+        torch.cuda.synchronize()
+        g.capture_begin()
+        for i in range(iters):
+            fn(i)
+        g.capture_end()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda._sleep(2_000_000)  # ~1 ms of GPU spin so the launches below queue up behind it
     start.record()
-    for i in range(iters):
-        fn(i)
+    g.replay()
     end.record()
     torch.cuda.synchronize()
     return start.elapsed_time(end) * 1e3 / iters
