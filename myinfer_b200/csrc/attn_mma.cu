@@ -242,10 +242,12 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) 
   float vb_acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [row][group] sum p * vbias
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
+  // A timed-out wait ends this warp's key loop (its state stays as is) but the
+  // warp still joins the merge barriers below.
   for (int it = 0; it < ntiles; ++it) {
     const int st = it % AM_STAGES;
     const uint32_t par = (it / AM_STAGES) & 1;
-    if (!mbar_wait(&full[st], par, &g_attn_mma_err)) return;
+    if (!mbar_wait(&full[st], par, &g_attn_mma_err)) break;
     const unsigned char* sb = smem + st * LY::STAGE;
     const int kw0 = warp * 16;  // this warp's first key within the tile
     const int key_base = k_begin + it * AM_TK + kw0;

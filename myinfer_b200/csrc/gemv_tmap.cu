@@ -1,15 +1,16 @@
 // Decode dequant-GEMV: 2-D TMA tiles into shared memory + tensor-core dot
-// products (kernel K1, M <= 8 tokens, K % 512 == 0).
+// products (kernel K1, M <= 8 tokens, K % 1024 == 0).
 //
 // The register-prefetch tensor-core GEMV (gemv_mma.cu) spends ~3.6 issue
 // slots per weight and stalls on L1 load latency with 16 warps per SM; the
 // TMA-fed CUDA-core GEMV (gemv_tma.cu) keeps enough bytes in flight but is
 // issue-bound at ~5.3 slots per weight.  This kernel takes the best of both:
-//   * a producer warp streams units of (16 weight rows x 512 columns) with
-//     2-D tensor-map TMA loads (weights with 128-byte swizzle so the 8 rows a
-//     fragment load touches hit different banks; bf16 scales and biases) into
-//     a 12-stage ring (~54 KB in flight per CTA), no registers involved;
-//   * four consumer warps each take two 64-column scale groups of every unit
+//   * a producer warp streams units of (16 weight rows x 1024 columns) with
+//     2-D tensor-map TMA loads (weights in 1 KB boxes with 128-byte swizzle so
+//     the 8 rows a fragment load touches hit different banks; bf16 scales and
+//     biases) into a 5-stage ring (~45 KB in flight per CTA, several CTAs per
+//     SM), no registers involved;
+//   * four consumer warps each take four 64-column scale groups of every unit
 //     and run the same mma.sync m16n8k16 bf16 dot products as gemv_mma.cu:
 //     codes -> (128 + q) bf16 pairs with one LOP3 per two codes, per-group
 //     fold  s * D + (b - 128 s) * sum(x);
@@ -33,9 +34,10 @@ static __device__ int g_gemv_tmap_err = 0;
 
 constexpr int TP_CW = 4;                       // consumer warps
 constexpr int TP_THREADS = (TP_CW + 1) * 32;
-constexpr int TP_STAGES = 12;
-constexpr int TP_W_STAGE = 4096;               // 16 rows x 256 bytes (2 halves x 2 swizzled 1 KB boxes)
-constexpr int TP_SB_STAGE = 256;               // 2 halves x 8 rows x 16 bytes (8 bf16 groups)
+constexpr int TP_STAGES = 5;
+constexpr int TP_UG = 16;                     // 64-column scale groups per unit (1024 columns)
+constexpr int TP_W_STAGE = 16 * TP_UG * 32;    // 16 rows x UG groups x 32 bytes (1 KB swizzled boxes)
+constexpr int TP_SB_STAGE = 16 * TP_UG * 2;    // 16 rows x UG bf16 (scales or biases)
 
 struct TmapSet {
   CUtensorMap w[3], s[3], b[3];  // per segment
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 128-byte-swizzled boxes must start on 1 KB boundaries
   unsigned char* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
-  const int K = a.K, NG = K >> 6, NCH = NG >> 3;
+  const int K = a.K, NG = K >> 6, NCH = NG / TP_UG;
   unsigned char* wring = smem;                                   // [STAGES][4096], 1024-aligned boxes
   unsigned char* sbring = wring + TP_STAGES * TP_W_STAGE;        // [STAGES][2 (s,b)][256]
   uint64_t* full = reinterpret_cast<uint64_t*>(sbring + TP_STAGES * 2 * TP_SB_STAGE);
@@ -112,11 +114,11 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
     // -------------------------------------------------------------- producer
     if (lane == 0) {
       int it = 0;
+      int tile = int(u0 / NCH), ch = int(u0 % NCH);
       for (long long u = u0; u < u1; ++u, ++it) {
         const int st = it % TP_STAGES;
         const uint32_t par = (it / TP_STAGES) & 1;
         if (!mbar_wait(&empty[st], par ^ 1, &g_gemv_tmap_err)) return;
-        const int tile = int(u / NCH), ch = int(u % NCH);
         mbar_arrive_expect_tx(&full[st], TP_W_STAGE + 2 * TP_SB_STAGE);
         unsigned char* ws = wring + st * TP_W_STAGE;
         unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
@@ -124,10 +126,15 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
         for (int h = 0; h < 2; ++h) {
           int si, row0;
           tp_half<EPI>(a, tile, h, si, row0);
-          tma2d(ws + (2 * h + 0) * 1024, &tm.w[si], ch * 64 + 0, row0, &full[st]);
-          tma2d(ws + (2 * h + 1) * 1024, &tm.w[si], ch * 64 + 32, row0, &full[st]);
-          tma2d(ss + h * 128, &tm.s[si], ch * 8, row0, &full[st]);
-          tma2d(ss + TP_SB_STAGE + h * 128, &tm.b[si], ch * 8, row0, &full[st]);
+#pragma unroll
+          for (int bx = 0; bx < TP_UG / 4; ++bx)  // 1 KB box = 8 rows x 4 groups
+            tma2d(ws + (h * (TP_UG / 4) + bx) * 1024, &tm.w[si], ch * TP_UG * 8 + bx * 32, row0, &full[st]);
+          tma2d(ss + h * (TP_SB_STAGE / 2), &tm.s[si], ch * TP_UG, row0, &full[st]);
+          tma2d(ss + TP_SB_STAGE + h * (TP_SB_STAGE / 2), &tm.b[si], ch * TP_UG, row0, &full[st]);
+        }
+        if (++ch == NCH) {
+          ch = 0;
+          ++tile;
         }
       }
     }
@@ -146,56 +153,95 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
   float tot[4] = {0.f, 0.f, 0.f, 0.f};
   int cur_tile = u0 < u1 ? int(u0 / NCH) : 0, done = 0;
 
+  // Epilogue of one finished tile row r16 / token t with its complete sum v.
+  auto epilogue = [&](int tile, int r16, int t, float v, float vu) {
+    if constexpr (EPI == EPI_SWIGLU) {
+      const float gv = rbf(v), uv = rbf(vu);
+      const float sg = rbf(1.f / (1.f + expf(-gv)));
+      a.seg[0].y[t * a.ldy + tile * 8 + r16] = f2bf(rbf(gv * sg) * uv);
+    } else {
+      int si, row0;
+      tp_half<EPI>(a, tile, r16 >> 3, si, row0);
+      const int rr = row0 + (r16 & 7);
+      const GemvSeg& sg = a.seg[si];
+      if constexpr (EPI == EPI_STORE) {
+        sg.y[t * a.ldy + rr] = f2bf(v);
+      } else if constexpr (EPI == EPI_RESIDUAL) {
+        bf16* o = sg.y + t * a.ldy + rr;
+        *o = f2bf(bf2f(*o) + rbf(v));
+      } else {
+        sg.yf[t * a.ldy + rr] = v;
+      }
+    }
+  };
+  float* tred = reinterpret_cast<float*>(red + 8);  // [CW][MT][16] partial tile sums
+  // A tile whose units all lie in this CTA's range is reduced in shared memory
+  // by the four consumer warps (no global atomics, no fence); a tile shared
+  // with a neighbouring CTA goes through the zeroed global scratch and the
+  // last contributor finishes it.
   auto flush = [&](int tile) {
-    const int base = tile * 16;
     const int t0 = 2 * tq, t1 = 2 * tq + 1;
-    if (t0 < MT) {
-      atomicAdd(&acc_buf[t0 * acc_rows + base + g], tot[0]);
-      atomicAdd(&acc_buf[t0 * acc_rows + base + g + 8], tot[2]);
-    }
-    if (t1 < MT) {
-      atomicAdd(&acc_buf[t1 * acc_rows + base + g], tot[1]);
-      atomicAdd(&acc_buf[t1 * acc_rows + base + g + 8], tot[3]);
-    }
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = (atomicAdd(&cnt_buf[tile], done) + done == NG);
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      __threadfence();
-      for (int q = lane; q < 16 * MT; q += 32) {
-        const int r16 = q & 15, t = q >> 4;
-        float* p = &acc_buf[t * acc_rows + base + r16];
-        if constexpr (EPI == EPI_SWIGLU) {
-          if (r16 < 8) {
-            float* pu = &acc_buf[t * acc_rows + base + r16 + 8];
-            const float v = __ldcg(p), u = __ldcg(pu);
-            *p = 0.f;
-            *pu = 0.f;
-            const float gv = rbf(v), uv = rbf(u);
-            const float sg = rbf(1.f / (1.f + expf(-gv)));
-            a.seg[0].y[t * a.ldy + tile * 8 + r16] = f2bf(rbf(gv * sg) * uv);
+    const bool whole = (long long)tile * NCH >= u0 && (long long)(tile + 1) * NCH <= u1;
+    if (whole) {
+      if (t0 < MT) {
+        tred[(warp * MT + t0) * 16 + g] = tot[0];
+        tred[(warp * MT + t0) * 16 + g + 8] = tot[2];
+      }
+      if (t1 < MT) {
+        tred[(warp * MT + t1) * 16 + g] = tot[1];
+        tred[(warp * MT + t1) * 16 + g + 8] = tot[3];
+      }
+      named_sync(2, TP_CW * 32);
+      if (warp == 0) {
+        for (int q = lane; q < 16 * MT; q += 32) {
+          const int r16 = q & 15, t = q >> 4;
+          float v = 0.f, vu = 0.f;
+#pragma unroll
+          for (int w = 0; w < TP_CW; ++w) {
+            v += tred[(w * MT + t) * 16 + r16];
+            if (EPI == EPI_SWIGLU && r16 < 8) vu += tred[(w * MT + t) * 16 + r16 + 8];
           }
-        } else {
-          const float v = __ldcg(p);
-          *p = 0.f;
-          int si, row0;
-          tp_half<EPI>(a, tile, r16 >> 3, si, row0);
-          const int rr = row0 + (r16 & 7);
-          const GemvSeg& sg = a.seg[si];
-          if constexpr (EPI == EPI_STORE) {
-            sg.y[t * a.ldy + rr] = f2bf(v);
-          } else if constexpr (EPI == EPI_RESIDUAL) {
-            bf16* o = sg.y + t * a.ldy + rr;
-            *o = f2bf(bf2f(*o) + rbf(v));
-          } else {
-            sg.yf[t * a.ldy + rr] = v;
-          }
+          if (EPI != EPI_SWIGLU || r16 < 8) epilogue(tile, r16, t, v, vu);
         }
       }
+      named_sync(2, TP_CW * 32);
+    } else {
+      const int base = tile * 16;
+      if (t0 < MT) {
+        atomicAdd(&acc_buf[t0 * acc_rows + base + g], tot[0]);
+        atomicAdd(&acc_buf[t0 * acc_rows + base + g + 8], tot[2]);
+      }
+      if (t1 < MT) {
+        atomicAdd(&acc_buf[t1 * acc_rows + base + g], tot[1]);
+        atomicAdd(&acc_buf[t1 * acc_rows + base + g + 8], tot[3]);
+      }
+      __threadfence();
       __syncwarp();
-      if (lane == 0) cnt_buf[tile] = 0;
+      int last = 0;
+      if (lane == 0) last = (atomicAdd(&cnt_buf[tile], done) + done == NG);
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        for (int q = lane; q < 16 * MT; q += 32) {
+          const int r16 = q & 15, t = q >> 4;
+          float* p = &acc_buf[t * acc_rows + base + r16];
+          if (EPI == EPI_SWIGLU) {
+            if (r16 < 8) {
+              float* pu = &acc_buf[t * acc_rows + base + r16 + 8];
+              const float v = __ldcg(p), u = __ldcg(pu);
+              *p = 0.f;
+              *pu = 0.f;
+              epilogue(tile, r16, t, v, u);
+            }
+          } else {
+            const float v = __ldcg(p);
+            *p = 0.f;
+            epilogue(tile, r16, t, v, 0.f);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) cnt_buf[tile] = 0;
+      }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) tot[i] = 0.f;
@@ -203,26 +249,37 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
   };
 
   int it = 0;
+  bool failed = false;
+  int tile = cur_tile, ch = u0 < u1 ? int(u0 % NCH) : 0;
   for (long long u = u0; u < u1; ++u, ++it) {
     const int st = it % TP_STAGES;
     const uint32_t par = (it / TP_STAGES) & 1;
-    const int tile = int(u / NCH), ch = int(u % NCH);
     if (tile != cur_tile) {
       flush(cur_tile);
       cur_tile = tile;
     }
-    if (!mbar_wait(&full[st], par, &g_gemv_tmap_err)) return;
+    // On a timed-out wait the warp stops computing but keeps walking the units
+    // so that every consumer warp still reaches the tile barriers in flush().
+    if (!failed && !mbar_wait(&full[st], par, &g_gemv_tmap_err)) failed = true;
+    if (failed) {
+      done += TP_UG / TP_CW;
+      if (++ch == NCH) {
+        ch = 0;
+        ++tile;
+      }
+      continue;
+    }
     const unsigned char* ws = wring + st * TP_W_STAGE;
     const unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int j = 2 * warp + jj;        // group within the unit
-      const int G = ch * 8 + j;           // global scale group
+    for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
+      const int j = (TP_UG / TP_CW) * warp + jj;  // group within the unit
+      const int G = ch * TP_UG + j;               // global scale group
       // swizzled 8-byte fragment of rows g (half 0) and g (half 1 = tile row g+8)
       const int c = 2 * (j & 3) + (tq >> 1);
       const int off = g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
-      const uint2 w0 = *reinterpret_cast<const uint2*>(ws + (0 + (j >> 2)) * 1024 + off);
-      const uint2 w8 = *reinterpret_cast<const uint2*>(ws + (2 + (j >> 2)) * 1024 + off);
+      const uint2 w0 = *reinterpret_cast<const uint2*>(ws + (0 * (TP_UG / 4) + (j >> 2)) * 1024 + off);
+      const uint2 w8 = *reinterpret_cast<const uint2*>(ws + (1 * (TP_UG / 4) + (j >> 2)) * 1024 + off);
       const uint4 xa = *reinterpret_cast<const uint4*>(xfl + G * 32);
       const uint4 xb = *reinterpret_cast<const uint4*>(xfl + G * 32 + 4);
       float d[4] = {0.f, 0.f, 0.f, 0.f};
@@ -242,10 +299,10 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
         uint32_t A[4] = {tp_nib_pair(w0.y, 2), tp_nib_pair(w8.y, 2), tp_nib_pair(w0.y, 3), tp_nib_pair(w8.y, 3)};
         tp_mma(d, A, xb.z, xb.w);
       }
-      const bf16* s0 = reinterpret_cast<const bf16*>(ss + g * 16) + j;
-      const bf16* s8 = reinterpret_cast<const bf16*>(ss + 128 + g * 16) + j;
-      const bf16* b0 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + g * 16) + j;
-      const bf16* b8 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + 128 + g * 16) + j;
+      const bf16* s0 = reinterpret_cast<const bf16*>(ss + g * (TP_UG * 2)) + j;
+      const bf16* s8 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE / 2 + g * (TP_UG * 2)) + j;
+      const bf16* b0 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + g * (TP_UG * 2)) + j;
+      const bf16* b8 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + TP_SB_STAGE / 2 + g * (TP_UG * 2)) + j;
       const float sA = bf2f(*s0), bA = bf2f(*b0), sB = bf2f(*s8), bB = bf2f(*b8);
       const float X0 = xg0[G], X1 = xg1[G];
       const float oA = fmaf(-128.f, sA, bA), oB = fmaf(-128.f, sB, bB);
@@ -254,9 +311,13 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
       tot[2] = fmaf(sB, d[2], fmaf(oB, X0, tot[2]));
       tot[3] = fmaf(sB, d[3], fmaf(oB, X1, tot[3]));
     }
-    done += 2;
+    done += TP_UG / TP_CW;
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
+    if (++ch == NCH) {
+      ch = 0;
+      ++tile;
+    }
   }
   if (u0 < u1) flush(cur_tile);
 }
@@ -293,7 +354,7 @@ static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i) {
   for (int k = 0; k < 2; ++k) {
     cuuint64_t dims[2] = {(cuuint64_t)K / 64, rows};
     cuuint64_t strides[1] = {(cuuint64_t)K / 32};
-    cuuint32_t box[2] = {8, 8}, es[2] = {1, 1};
+    cuuint32_t box[2] = {TP_UG, 8}, es[2] = {1, 1};
     CUresult r = enc(m2[k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(p2[k]), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -304,11 +365,11 @@ static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i) {
 
 static size_t tp_smem(int MT, int K) {
   return TP_STAGES * (TP_W_STAGE + 2 * TP_SB_STAGE) + 2 * TP_STAGES * 8 + size_t(MT) * (K / 64) * 32 * 4 +
-         size_t(MT) * (K / 64) * 4 + 8 * 4 + 1024;
+         size_t(MT) * (K / 64) * 4 + 8 * 4 + size_t(TP_CW) * MT * 16 * 4 + 1024;
 }
 
 bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
-  if (MT < 1 || MT > 8 || a.K % 512) return false;
+  if (MT < 1 || MT > 8 || a.K % (64 * TP_UG)) return false;
   if (tp_smem(MT, a.K) > 200 * 1024) return false;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   for (int i = 0; i < a.nseg; ++i) {
@@ -331,7 +392,7 @@ static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* acc, int* cn
   int per_sm = 0;
   M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tmap_kernel<MT, EPI>, TP_THREADS, smem));
   const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
-  const long long units = (long long)(vrows / 16) * (a.K / 512);
+  const long long units = (long long)(vrows / 16) * (a.K / (64 * TP_UG));
   const long long max_ctas = (long long)std::max(1, per_sm) * sm_count();
   const int grid = (int)std::max(1LL, std::min(max_ctas, units));
   gemv_tmap_kernel<MT, EPI><<<grid, TP_THREADS, smem, st>>>(a, ts, acc, cnt, acc_rows);

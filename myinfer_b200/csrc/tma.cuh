@@ -9,7 +9,7 @@
 
 namespace m5 {
 
-constexpr uint32_t M5_WAIT_LIMIT = 1u << 26;  // polls (each ~tens of ns) before a wait gives up
+constexpr uint32_t M5_WAIT_LIMIT = 1u << 20;  // polls (each up to ~2 us of suspension) before a wait gives up
 enum { M5_DEV_ERR_WAIT_TIMEOUT = 1 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -35,12 +35,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// One poll; the thread may be suspended by the hardware for up to ~2 us
+// while the phase is incomplete, so a waiting warp does not burn issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(2000u)
       : "memory");
   return ok != 0;
 }
