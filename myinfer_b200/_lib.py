@@ -57,6 +57,8 @@ _SIGS = {
                                      c_void_p, c_void_p]),
     "m5_quantized_matmul": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
                                     c_int, c_int, c_void_p, c_void_p]),
+    "m5_quantized_matmul_noalloc": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
+                                            c_int, c_int, c_void_p, c_void_p]),
     "m5_rms_norm": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p, c_void_p]),
     "m5_quantized_sdpa": (c_int, [c_void_p, c_int, c_int, c_int, c_int, M5KvView, M5KvView, c_int, c_int,
                                   c_float, c_int, c_void_p, POINTER(c_int64), c_int, c_int, c_void_p,
