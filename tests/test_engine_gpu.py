@@ -1,0 +1,88 @@
+"""Engine surface on the device: load a seeded random model, generate, reuse a
+prefix, plan the context, benchmark (m5engine/engine.py:192-553 contract)."""
+
+import json
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=2,
+            head_dim=128, intermediate_size=1024, vocab_size=4096, tie_word_embeddings=False,
+            max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+
+
+@pytest.fixture(scope="module")
+def engine(tmp_path_factory):
+    from myinfer_b200.engine import Engine, LoadOptions
+    p = tmp_path_factory.mktemp("cfg") / "config.json"
+    p.write_text(json.dumps(TINY))
+    eng = Engine()
+    info = eng.load(LoadOptions(model=f"random:{p}", kv_bits=8, quantized_kv_start=0, memory_budget_gb=4.0,
+                                prefill_step=64, seed=5))
+    assert info["state"] == "ready" and info["context"]["max_context"] >= 512
+    yield eng
+    eng.unload()
+
+
+def _run(eng, tokens, n, **kw):
+    from myinfer_b200.engine import GenerationParams
+    chunks = list(eng.generate(tokens, GenerationParams(max_tokens=n, temperature=0.0, **kw)))
+    assert chunks[-1].finish_reason in ("length", "stop")
+    return "".join(c.text for c in chunks), chunks[-1].metrics
+
+
+def test_generate_matches_token_loop(engine):
+    from myinfer_b200.cache import make_prompt_cache
+    from myinfer_b200.generate import generate_step
+    prompt = engine.encode_text("The quick brown fox jumps over the lazy dog. " * 3)
+    text, m = _run(engine, prompt, 12, use_prefix_cache=False)
+    assert m.prompt_tokens == len(prompt) and m.completion_tokens == 12 and m.cached_tokens == 0
+    assert m.decode_tps > 0 and m.prompt_tps > 0
+    toks = [t for t, _ in generate_step(prompt, engine.model, 12, prompt_cache=make_prompt_cache(engine.model),
+                                        prefill_step_size=64, kv_bits=8, quantized_kv_start=0)]
+    assert text == engine.tokenizer.decode(toks)
+
+
+def test_prefix_cache_reuse(engine):
+    engine.prefix.clear()
+    base = engine.encode_text("A long shared system prompt that both requests start with. " * 2)
+    _, m1 = _run(engine, base, 8)
+    assert m1.cached_tokens == 0 and len(engine.prefix) == 1
+    follow = base + engine.encode_text(" And a follow-up question?")
+    _, m2 = _run(engine, follow, 8)
+    # the first request's prompt is a prefix of the second: reused without re-prefill
+    assert m2.cached_tokens == len(base)
+    assert engine.prefix.total_hit_tokens >= len(base)
+    # the reused cache was trimmed back, not copied: one entry per key
+    assert len(engine.prefix) == 1
+
+
+def test_stop_strings_and_errors(engine):
+    from myinfer_b200.engine import ContextOverflow, GenerationParams
+    prompt = engine.encode_text("stop test")
+    full, _ = _run(engine, prompt, 10, use_prefix_cache=False)
+    if len(full) > 3:
+        cut = full[2:4]
+        chunks = list(engine.generate(prompt, GenerationParams(max_tokens=10, temperature=0.0, stop=[cut],
+                                                               use_prefix_cache=False)))
+        text = "".join(c.text for c in chunks)
+        assert cut not in text and chunks[-1].finish_reason == "stop"
+    with pytest.raises(ContextOverflow):
+        next(iter(engine.generate([5] * (engine.plan.max_context + 1), GenerationParams(max_tokens=1))))
+
+
+def test_sampling_and_benchmark(engine):
+    from myinfer_b200.engine import GenerationParams
+    prompt = engine.encode_text("sampling")
+    outs = set()
+    for seed in (1, 1, 2):
+        chunks = list(engine.generate(prompt, GenerationParams(max_tokens=6, temperature=1.0, top_p=0.9,
+                                                               seed=seed, use_prefix_cache=False)))
+        outs.add((seed, "".join(c.text for c in chunks)))
+    assert len({t for s, t in outs if s == 1}) == 1          # seeded sampling is reproducible
+    b = engine.benchmark(prompt_tokens=256, gen_tokens=16)
+    assert b["prompt_tokens"] == 256 and b["completion_tokens"] == 16 and b["decode_tps"] > 0
+    info = engine.info()
+    assert info["totals"]["requests"] >= 1 and info["model"]["type"] == "qwen3"

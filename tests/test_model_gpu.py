@@ -130,8 +130,29 @@ def test_moe_router_matches_oracle():
 
 @pytest.mark.slow
 def test_qwen3_06b_config():
-    """0.6B shape, 512-token prompt, greedy, 8-bit KV from position 0."""
+    """0.6B shape, 512-token prompt, greedy, 8-bit KV from position 0.
+
+    At 28 layers the bf16 rounding at every layer boundary turns any change of
+    fp32 summation order into a few-ulp drift of the logits: the oracle run
+    with fp32 matmuls and the same oracle with fp64 accumulation (rounded to
+    bf16 at the same points) only agree to cosine ~0.99990 / max-abs ~0.043
+    (tests/parity_floor.py prints these figures).  The device is held to the
+    same noise: its distance from the fp64-accumulating oracle may exceed the
+    fp32 oracle's own by at most 1.5x, on top of absolute guards."""
+    from parity_floor import Fp64Model
     dev_model, ora = _build(QWEN3_06B, seed=0)
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, QWEN3_06B["vocab_size"], 512).tolist()
-    _check(*_run(dev_model, ora, prompt, 32, 2048, 8, 0), n_equal=32)
+    n = 32
+    toks_o, logits_o, free, toks_f, logits_f = _run(dev_model, ora, prompt, n, 2048, 8, 0)
+    ora64 = Fp64Model(ora.cfg, ora.w)
+    ora64._deq = ora._deq
+    toks_64, _, logits_64 = om.generate(ora64, prompt, n, prefill_step=2048, kv_bits=8, quantized_kv_start=0,
+                                        return_logits=True)
+    assert toks_64 == toks_o
+    cos = torch.nn.functional.cosine_similarity
+    floor = 1 - cos(logits_o, logits_64, dim=-1).min().item()
+    dev64 = 1 - cos(logits_f, logits_64, dim=-1).min().item()
+    print(f"1-cos: oracle32 vs oracle64 {floor:.3e}, device vs oracle64 {dev64:.3e}")
+    assert dev64 <= 1.5 * floor + 1e-6, (dev64, floor)
+    _check(toks_o, logits_o, free, toks_f, logits_f, n_equal=n, cos_min=0.9998, cos_median=0.9998, max_abs=0.07)
