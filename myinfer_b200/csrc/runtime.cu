@@ -64,7 +64,14 @@ struct Model {
   float* mma_acc = nullptr;  // zeroed split-tile scratch of the tensor-core GEMV
   int* mma_cnt = nullptr;
   int mma_rows = 0;
+  bf16* xn = nullptr;        // RMSNorm(h) materialised for the prefill GEMM [T, H]
+  bf16* gxs = nullptr;       // per-token group sums of the prefill GEMM input
+  size_t gxs_bytes = 0;
 };
+
+// Token count from which a projection runs as the tensor-core GEMM instead of
+// chunks of the streaming GEMV (the GEMV re-reads the weights every 8 tokens).
+constexpr int kGemmMinTokens = 16;
 
 static bool parse_layer(const char* name, int& idx, const char*& rest) {
   const char* p = "model.layers.";
@@ -184,6 +191,28 @@ static void attach(const Model* m, GemvArgs& a) {
   a.mma_rows = m->mma_rows;
 }
 
+// One projection of T tokens: the tensor-core GEMM for prefill-sized T (with
+// the fused RMSNorm materialised first), the streaming GEMV otherwise.
+static int linear_auto(const Model* m, const GemvArgs& proto, int T, int epi, cudaStream_t st) {
+  if (T >= kGemmMinTokens && m->gxs && gemm_tc_xs_bytes(T, proto.K) <= m->gxs_bytes) {
+    GemvArgs a = proto;
+    if (proto.norm_w) {
+      a.norm_w = nullptr;
+      a.x = m->xn;
+      a.ldx = a.K;
+    }
+    const bool norm_fits = !proto.norm_w || proto.K == m->cfg.hidden_size;  // xn holds [T, H]
+    if (norm_fits && gemm_tc_eligible(a, T, epi)) {
+      if (proto.norm_w) {
+        int rc = rms_norm_launch(proto.x, proto.norm_w, T, a.K, proto.eps, m->xn, st);
+        if (rc) return rc;
+      }
+      return gemm_tc_launch(a, T, epi, m->gxs, m->gxs_bytes, st);
+    }
+  }
+  return linear_tokens(proto, T, epi, st);
+}
+
 static GemvSeg seg_of(const Linear& l, int rows, bf16* y) {
   GemvSeg s{};
   s.w = l.w;
@@ -221,7 +250,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     a.norm_w = ly.in_norm;
     a.eps = c.rms_norm_eps;
     attach(m, a);
-    if ((rc = linear_tokens(a, L, EPI_STORE, st))) return rc;
+    if ((rc = linear_auto(m, a, L, EPI_STORE, st))) return rc;
     // QK-norm + RoPE + KV append
     RopeAppendArgs r{};
     r.qkv = m->qkv;
@@ -269,7 +298,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     o.ldy = H;
     o.total_rows = H;
     attach(m, o);
-    if ((rc = linear_tokens(o, L, EPI_RESIDUAL, st))) return rc;
+    if ((rc = linear_auto(m, o, L, EPI_RESIDUAL, st))) return rc;
     if (c.num_experts == 0) {
       GemvArgs g{};
       g.x = m->h;
@@ -283,7 +312,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       g.norm_w = ly.post_norm;
       g.eps = c.rms_norm_eps;
       attach(m, g);
-      if ((rc = linear_tokens(g, L, EPI_SWIGLU, st))) return rc;
+      if ((rc = linear_auto(m, g, L, EPI_SWIGLU, st))) return rc;
       GemvArgs d{};
       d.x = m->act;
       d.ldx = m->I;
@@ -293,7 +322,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       d.ldy = H;
       d.total_rows = H;
       attach(m, d);
-      if ((rc = linear_tokens(d, L, EPI_RESIDUAL, st))) return rc;
+      if ((rc = linear_auto(m, d, L, EPI_RESIDUAL, st))) return rc;
     } else {
       // router logits of RMSNorm(h), top-k, then the routed experts
       GemvArgs g{};
@@ -307,7 +336,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       g.norm_w = ly.post_norm;
       g.eps = c.rms_norm_eps;
       attach(m, g);
-      if ((rc = linear_tokens(g, L, EPI_STORE, st))) return rc;
+      if ((rc = linear_auto(m, g, L, EPI_STORE, st))) return rc;
       if ((rc = moe_topk_launch(m->rlogits, L, c.num_experts, c.experts_per_tok, c.norm_topk_prob, m->rids,
                                 m->rscores, st)))
         return rc;
@@ -347,7 +376,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
   if (logits_mode == M5_LOGITS_ALL) {
     hd.x = m->h;
     hd.seg[0] = seg_of(head, V, (bf16*)logits);
-    if ((rc = linear_tokens(hd, L, EPI_STORE, st))) return rc;
+    if ((rc = linear_auto(m, hd, L, EPI_STORE, st))) return rc;
     last_row = (bf16*)logits + size_t(L - 1) * V;
   } else if (logits_mode == M5_LOGITS_LAST || d_argmax) {
     hd.x = m->h + size_t(L - 1) * H;
@@ -370,14 +399,15 @@ struct Arena {
   size_t bytes = 0;
 };
 static std::mutex g_arena_mu;
-static Arena g_arena[64];
+enum { ARENA_ATTN = 0, ARENA_GEMM = 1 };
+static Arena g_arena[2][64];
 
-static int arena_get(size_t bytes, void** out) {
+static int arena_get(size_t bytes, void** out, int slot = ARENA_ATTN) {
   int dev = 0;
   M5_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(M5_ERR_INVALID, "device index out of range");
   std::lock_guard<std::mutex> lk(g_arena_mu);
-  Arena& a = g_arena[dev];
+  Arena& a = g_arena[slot][dev];
   if (a.bytes < bytes) {
     if (a.ptr) {
       M5_CUDA(cudaDeviceSynchronize());
@@ -402,8 +432,10 @@ extern "C" int m5_device_status(int* code, int reset) {
   const int g = gemv_tma_error(reset);
   const int gt = gemv_tmap_error(reset);
   const int at = attn_mma_error(reset);
-  if (g < 0 || gt < 0 || at < 0) return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error words");
-  *code = g | gt | at;
+  const int gm = gemm_tc_error(reset);
+  if (g < 0 || gt < 0 || at < 0 || gm < 0)
+    return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error words");
+  *code = g | gt | at | gm;
   return M5_OK;
 }
 
@@ -426,6 +458,13 @@ extern "C" int m5_quantized_matmul(const void* x, int64_t M, int64_t K, const ui
   a.seg[0].y = (bf16*)y;
   a.ldy = N;
   a.total_rows = (int)N;
+  if (M >= kGemmMinTokens && gemm_tc_eligible(a, (int)M, EPI_STORE)) {
+    void* xs = nullptr;
+    const size_t bytes = gemm_tc_xs_bytes((int)M, (int)K);
+    int rc = arena_get(bytes, &xs, ARENA_GEMM);
+    if (rc) return rc;
+    return gemm_tc_launch(a, (int)M, EPI_STORE, (bf16*)xs, bytes, (cudaStream_t)stream);
+  }
   return linear_tokens(a, (int)M, EPI_STORE, (cudaStream_t)stream);
 }
 
@@ -632,9 +671,12 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   const int mrows = (int)std::max<size_t>({QKV, H, size_t(2) * m->I, size_t(c.vocab_size),
                                             size_t(std::max(1, c.num_experts)), size_t(16)});
   const int mrows16 = (mrows + 15) / 16 * 16;
+  const int maxK = (int)std::max<size_t>({H, size_t(m->Hq) * D, size_t(m->I)});
+  const size_t gxs = T >= kGemmMinTokens ? gemm_tc_xs_bytes((int)T, maxK) : 0;
   const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
                           size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,
-                          part, argmax_scratch_bytes(), gemv_mma_scratch_bytes(mrows16)};
+                          part, argmax_scratch_bytes(), gemv_mma_scratch_bytes(mrows16),
+                          T >= kGemmMinTokens ? T * H * 2 : 0, gxs};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -662,6 +704,9 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->mma_acc = reinterpret_cast<float*>(mma);
   m->mma_cnt = reinterpret_cast<int*>(mma + size_t(8) * mrows16 * sizeof(float));
   m->mma_rows = mrows16;
+  m->xn = sizes[12] ? (bf16*)carve(p, sizes[12]) : nullptr;
+  m->gxs = sizes[13] ? (bf16*)carve(p, sizes[13]) : nullptr;
+  m->gxs_bytes = sizes[13];
   m->max_tokens = max_tokens;
   return M5_OK;
 }

@@ -47,6 +47,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// One poll without a suspend-time hint: the hardware may still suspend the
+// thread for a short system-defined time while the phase is incomplete.
+__device__ __forceinline__ bool mbar_try_wait_fast(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with `parity` completed; false (and error recorded) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   for (uint32_t i = 0; i < M5_WAIT_LIMIT; ++i)

@@ -2,6 +2,7 @@
 
     python -m myinfer_b200.microbench gemv --n 25600 --k 5120 [--m 1] [--iters 20]
     python -m myinfer_b200.microbench attention --s 32768 --l 1 --bits 8 [--hq 64 --hkv 8]
+    python -m myinfer_b200.microbench gemm --m 2048 --n 8192 --k 5120
 
 ``gemv`` cycles over enough distinct weight matrices that every launch reads
 from HBM (more than L2 in total); ``attention`` is the standalone
@@ -63,6 +64,22 @@ def bench_gemv(n: int, k: int, m: int, iters: int) -> dict:
             "gbs": round(alg / us / 1e3, 1)}
 
 
+def bench_gemm(m: int, n: int, k: int, iters: int) -> dict:
+    """Prefill dequant-GEMM (tensor cores): M tokens x N weight rows x K."""
+    from myinfer_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = (0.02 * torch.randn(n, k, generator=g, device="cuda")).to(torch.bfloat16)
+    mat = ops.quantize(w, 64, 4)
+    del w
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    ops.quantized_matmul(x, *mat, out=y)
+    torch.cuda.synchronize()
+    us = _timed(lambda i: ops.quantized_matmul(x, *mat, out=y), iters)
+    flops = 2.0 * m * n * k
+    return {"kernel": "gemm", "m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(flops / us / 1e6, 1)}
+
+
 def bench_attention(s: int, l: int, bits: int, hq: int, hkv: int, iters: int) -> dict:
     from myinfer_b200 import ops
     from myinfer_b200.attention import blocked_quantized_sdpa
@@ -97,6 +114,11 @@ def main():
     g.add_argument("--k", type=int, default=5120)
     g.add_argument("--m", type=int, default=1)
     g.add_argument("--iters", type=int, default=20)
+    gm = sub.add_parser("gemm")
+    gm.add_argument("--m", type=int, default=2048)
+    gm.add_argument("--n", type=int, default=8192)
+    gm.add_argument("--k", type=int, default=5120)
+    gm.add_argument("--iters", type=int, default=20)
     a = sub.add_parser("attention")
     a.add_argument("--s", type=int, default=32768)
     a.add_argument("--l", type=int, default=1)
@@ -107,6 +129,8 @@ def main():
     args = ap.parse_args()
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.m, args.iters)
+    elif args.cmd == "gemm":
+        r = bench_gemm(args.m, args.n, args.k, args.iters)
     else:
         r = bench_attention(args.s, args.l, args.bits, args.hq, args.hkv, args.iters)
     print(json.dumps(r), flush=True)

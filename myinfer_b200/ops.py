@@ -60,8 +60,12 @@ def dequantize(wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, gro
 
 
 def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
-                     transpose: bool = True, group_size: int = 64, bits: int = 4) -> torch.Tensor:
-    """``mx.quantized_matmul(x, w, scales, biases, transpose=True)`` for bf16 x."""
+                     transpose: bool = True, group_size: int = 64, bits: int = 4,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``mx.quantized_matmul(x, w, scales, biases, transpose=True)`` for bf16 x.
+
+    Up to 15 tokens run on the streaming decode GEMV; 16 or more on the
+    tensor-core GEMM (K a multiple of 512, N of 128), else the GEMV in chunks."""
     if not transpose:
         raise NotImplementedError("only transpose=True (x @ W.T) is implemented")
     _need_cuda(x, wq, scales, biases)
@@ -69,7 +73,9 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
         raise ValueError("quantized_matmul expects bf16 activations")
     x2 = x.contiguous().reshape(-1, x.shape[-1])
     N = wq.shape[-2]
-    y = torch.empty(x2.shape[0], N, dtype=torch.bfloat16, device=x.device)
+    y = out if out is not None else torch.empty(x2.shape[0], N, dtype=torch.bfloat16, device=x.device)
+    if y.shape != (x2.shape[0], N) or y.dtype != torch.bfloat16 or not y.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 tensor of shape [tokens, N]")
     call("m5_quantized_matmul", x2.data_ptr(), x2.shape[0], x2.shape[1], wq.data_ptr(), scales.data_ptr(),
          biases.data_ptr(), N, group_size, bits, y.data_ptr(), _stream())
     return y.reshape(*x.shape[:-1], N)

@@ -32,6 +32,28 @@ def _build(cfg_dict, seed):
 
 
 NEAR_TIE = 0.02  # oracle top-1 minus top-2 logit below which argmax order is numerical noise
+ROUTER_TIE = 1e-3  # k-th minus (k+1)-th router probability below which expert choice may differ
+
+
+def _record_router_gaps(ora):
+    """Wrap the oracle's router to record, per model call, the smallest gap
+    between the k-th and (k+1)-th expert probability over layers and tokens."""
+    calls = []
+    orig = ora.route
+
+    def route(i, x):
+        order, scores, gates = orig(i, x)
+        srt = torch.softmax(gates, dim=-1).sort(dim=-1, descending=True).values
+        k = ora.cfg.num_experts_per_tok
+        gap = (srt[:, k - 1] - srt[:, k]).min().item()
+        if i == 0:
+            calls.append(gap)
+        else:
+            calls[-1] = min(calls[-1], gap)
+        return order, scores, gates
+
+    ora.route = route
+    return calls
 
 
 def _run(dev_model, ora, prompt, n, prefill_step, kv_bits, qstart, yarn=1.0):
@@ -42,14 +64,18 @@ def _run(dev_model, ora, prompt, n, prefill_step, kv_bits, qstart, yarn=1.0):
     if yarn > 1:
         dev_model.set_rope(yarn, 32768)
         ora.set_rope(yarn, 32768)
+    gaps = _record_router_gaps(ora) if ora.cfg.moe else None
     toks_o, _, logits_o = om.generate(ora, prompt, n, prefill_step=prefill_step, kv_bits=kv_bits,
                                       quantized_kv_start=qstart, return_logits=True)
+    # steps whose oracle forward met a router near-tie (the device may route differently there)
+    n_prefill = len(gaps) - (n + 1) if gaps is not None else 0
+    ties = {i for i in range(n) if gaps is not None and gaps[n_prefill + i] < ROUTER_TIE}
     kw = dict(prefill_step_size=prefill_step, kv_bits=kv_bits, quantized_kv_start=qstart, return_logits=True)
     free = [t for t, _ in generate_step(prompt, dev_model, n, **kw)]
     forced = list(generate_step(prompt, dev_model, n, prompt_cache=make_prompt_cache(dev_model), feed=toks_o, **kw))
     toks_f = [t for t, _ in forced]
     logits_f = torch.stack([l.float().cpu() for _, l in forced])
-    return toks_o, logits_o, free, toks_f, logits_f
+    return toks_o, logits_o, free, toks_f, logits_f, ties
 
 
 def _margins(logits):
@@ -57,24 +83,29 @@ def _margins(logits):
     return (top[:, 0] - top[:, 1]).tolist()
 
 
-def _check(toks_o, logits_o, free, toks_f, logits_f, n_equal, cos_min=0.9995, cos_median=0.9999, max_abs=0.05):
+def _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal, cos_min=0.9995, cos_median=0.9999,
+           max_abs=0.05):
     """North-star bar: logits cosine >= 0.9999 (asserted on the median step;
     every step must clear `cos_min`, the measured bf16 rounding-chaos floor of
-    a random-init model), max-abs error <= 0.05, greedy tokens identical."""
+    a random-init model), max-abs error <= 0.05, greedy tokens identical.
+    Steps in `ties` (MoE router near-ties, where expert ids may legitimately
+    differ) are exempt from the per-step bounds but count in the median."""
     cos = torch.nn.functional.cosine_similarity(logits_f, logits_o, dim=-1)
+    keep = [i for i in range(len(cos)) if i not in ties]
     print(f"logits cosine min {cos.min().item():.6f} median {cos.median().item():.6f}; "
-          f"max-abs {(logits_f - logits_o).abs().max().item():.4f}")
+          f"max-abs {(logits_f - logits_o).abs().max().item():.4f}; router-tie steps {sorted(ties)}")
     assert cos.median().item() >= cos_median, cos.tolist()
-    assert cos.min().item() >= cos_min, cos.tolist()
-    assert (logits_f - logits_o).abs().max().item() <= max_abs, (logits_f - logits_o).abs().max().item()
+    assert cos[keep].min().item() >= cos_min, cos.tolist()
+    err = (logits_f - logits_o)[keep].abs().max().item()
+    assert err <= max_abs, err
     marg = _margins(logits_o)
     # teacher-forced argmax equals the oracle's wherever the oracle is not at a near-tie
     for i, (a, b) in enumerate(zip(toks_f, toks_o)):
-        assert a == b or marg[i] < NEAR_TIE, (i, a, b, marg[i])
+        assert a == b or marg[i] < NEAR_TIE or i in ties, (i, a, b, marg[i])
     # free-running greedy tokens identical up to n_equal, unless a near-tie comes first
     for i in range(n_equal):
         if free[i] != toks_o[i]:
-            assert marg[i] < NEAR_TIE, (i, free, toks_o, marg[:i + 1])
+            assert marg[i] < NEAR_TIE or i in ties, (i, free, toks_o, marg[:i + 1])
             break
 
 
@@ -101,6 +132,22 @@ def test_tiny_moe():
     rng = np.random.default_rng(9)
     prompt = rng.integers(0, TINY_MOE["vocab_size"], 20).tolist()
     _check(*_run(dev_model, ora, prompt, 6, 8, 8, 0), n_equal=6)
+
+
+def test_tiny_moe_prefill_gemm():
+    """32-token prefill chunks: attention projections on the tensor-core GEMM."""
+    dev_model, ora = _build(TINY_MOE, seed=8)
+    rng = np.random.default_rng(10)
+    prompt = rng.integers(0, TINY_MOE["vocab_size"], 70).tolist()
+    _check(*_run(dev_model, ora, prompt, 6, 32, 8, 0), n_equal=6)
+
+
+def test_tiny_dense_long_prefill():
+    """A 256-token prefill chunk (two token tiles of the GEMM) then decode."""
+    dev_model, ora = _build(TINY, seed=12)
+    rng = np.random.default_rng(13)
+    prompt = rng.integers(0, TINY["vocab_size"], 300).tolist()
+    _check(*_run(dev_model, ora, prompt, 8, 256, 8, 0), n_equal=8)
 
 
 def test_moe_router_matches_oracle():
@@ -144,7 +191,7 @@ def test_qwen3_06b_config():
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, QWEN3_06B["vocab_size"], 512).tolist()
     n = 32
-    toks_o, logits_o, free, toks_f, logits_f = _run(dev_model, ora, prompt, n, 2048, 8, 0)
+    toks_o, logits_o, free, toks_f, logits_f, ties = _run(dev_model, ora, prompt, n, 2048, 8, 0)
     ora64 = Fp64Model(ora.cfg, ora.w)
     ora64._deq = ora._deq
     toks_64, _, logits_64 = om.generate(ora64, prompt, n, prefill_step=2048, kv_bits=8, quantized_kv_start=0,
@@ -155,4 +202,5 @@ def test_qwen3_06b_config():
     dev64 = 1 - cos(logits_f, logits_64, dim=-1).min().item()
     print(f"1-cos: oracle32 vs oracle64 {floor:.3e}, device vs oracle64 {dev64:.3e}")
     assert dev64 <= 1.5 * floor + 1e-6, (dev64, floor)
-    _check(toks_o, logits_o, free, toks_f, logits_f, n_equal=n, cos_min=0.9998, cos_median=0.9998, max_abs=0.07)
+    _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal=n, cos_min=0.9998, cos_median=0.9998,
+           max_abs=0.07)
