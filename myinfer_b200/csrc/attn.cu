@@ -371,6 +371,20 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream) {
   const int R = a.QB * rep;
   if (R > ATT_RMAX) return fail(M5_ERR_INVALID, "attention: queries-per-CTA x GQA group exceeds 16");
   int rc;
+  if (attn_pf_eligible(a)) {
+    // prefill: 128 rows per CTA; the caller's scratch holds a.nsplit partials per row
+    AttnArgs p = a;
+    const int S_max = a.d_S ? a.k.head_stride : a.S_host;
+    attn_pf_plan(a, (int)std::min<int64_t>(S_max, 1 << 30), std::max(1, a.nsplit), p.QB, p.nsplit);
+    if ((rc = attn_pf_launch(p, stream))) return rc;
+    if (p.nsplit > 1) {
+      const int rows = a.B * a.Hq * a.L;
+      attn_combine_kernel<128><<<rows, 128, 0, stream>>>(p.part_o, p.part_ml, p.nsplit, a.Hq, a.L, a.out_tokens_major,
+                                                         a.out);
+      M5_LAUNCH_CHECK("attention combine launch");
+    }
+    return M5_OK;
+  }
   if (attn_mma_eligible(a)) {
     rc = attn_mma_launch(a, stream);
   } else if (a.D == 128) {

@@ -41,4 +41,10 @@ bool attn_mma_eligible(const AttnArgs& a);
 int attn_mma_launch(const AttnArgs& a, cudaStream_t stream);
 int attn_mma_error(int reset);
 
+// Prefill tensor-core kernel (attn_pf.cu): 8/4-bit KV, D = 128, L * rep > 16.
+bool attn_pf_eligible(const AttnArgs& a);
+void attn_pf_plan(const AttnArgs& a, int S_max, int max_split, int& QB, int& nsplit);
+int attn_pf_launch(const AttnArgs& a, cudaStream_t stream);
+int attn_pf_error(int reset);
+
 }  // namespace m5

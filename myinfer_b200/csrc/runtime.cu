@@ -433,9 +433,10 @@ extern "C" int m5_device_status(int* code, int reset) {
   const int gt = gemv_tmap_error(reset);
   const int at = attn_mma_error(reset);
   const int gm = gemm_tc_error(reset);
-  if (g < 0 || gt < 0 || at < 0 || gm < 0)
+  const int ap = attn_pf_error(reset);
+  if (g < 0 || gt < 0 || at < 0 || gm < 0 || ap < 0)
     return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error words");
-  *code = g | gt | at | gm;
+  *code = g | gt | at | gm | ap;
   return M5_OK;
 }
 

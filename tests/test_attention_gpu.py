@@ -105,3 +105,22 @@ def test_additive_mask():
                                  add.cuda(), 64, 8)
     oracle = ref_blocked(torch.from_numpy(q), k, v, D ** -0.5, add, 64, 8, score_budget_bytes=1, min_block=128)
     assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("hq,hk,L,S,mask", [(64, 8, 64, 1500, "causal"), (64, 8, 33, 700, "causal"),
+                                            (32, 4, 300, 2100, "causal"), (64, 4, 17, 900, "causal"),
+                                            (16, 8, 130, 130, "causal"), (64, 8, 40, 500, None)])
+def test_prefill_tensor_core(bits, hq, hk, L, S, mask):
+    """Prefill kernel (128 rows per CTA, every GQA group size of the BASELINE
+    configs, ragged tails, split-KV on small grids) against the blocked oracle."""
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    rng = np.random.default_rng(L * 7 + S + bits)
+    D = 128
+    q = _bf16(rng.standard_normal((1, hq, L, D)))
+    k, v, _, _ = _kv(rng, 1, hk, S, D, bits)
+    out = blocked_quantized_sdpa(torch.from_numpy(q).to(torch.bfloat16).cuda(), _dev(k), _dev(v), D ** -0.5,
+                                 mask, 64, bits)
+    oracle = ref_blocked(torch.from_numpy(q), k, v, D ** -0.5, mask, 64, bits, score_budget_bytes=1,
+                         min_block=256)
+    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
