@@ -290,6 +290,8 @@ template <int D>
 __global__ void __launch_bounds__(D) attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                                          int nsplit, int Hq, int L, int tokens_major,
                                                          bf16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const size_t row = blockIdx.x;  // (b * Hq + h) * L + qi
   const int d = threadIdx.x;
   __shared__ float w_s[1024];
@@ -346,6 +348,8 @@ void attn_plan(int B, int Hq, int Hkv, int L, int S_max, int& QB, int& nsplit) {
   const long long ctas = (long long)B * Hkv * ((L + QB - 1) / QB);
   const int tiles = std::max(1, (S_max + ATT_TK - 1) / ATT_TK);
   // Enough CTAs for ~2 per SM, each with at least one key tile.
+  // ~2 CTAs per SM: measured on B200 at 32K context, 3, 4 or 6 per SM were
+  // 20-55% slower (more, shorter splits add per-CTA prologue and merge work)
   long long want = (2LL * sm_count() + ctas - 1) / ctas;
   nsplit = (int)std::max(1LL, std::min<long long>(std::min<long long>(want, tiles), 1024));
 }
@@ -379,8 +383,8 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream) {
     if ((rc = attn_pf_launch(p, stream))) return rc;
     if (p.nsplit > 1) {
       const int rows = a.B * a.Hq * a.L;
-      attn_combine_kernel<128><<<rows, 128, 0, stream>>>(p.part_o, p.part_ml, p.nsplit, a.Hq, a.L, a.out_tokens_major,
-                                                         a.out);
+      M5_CUDA(launch_pdl(attn_combine_kernel<128>, dim3(rows), dim3(128), 0, stream, p.part_o, p.part_ml, p.nsplit, a.Hq, a.L, a.out_tokens_major,
+                                                         a.out));
       M5_LAUNCH_CHECK("attention combine launch");
     }
     return M5_OK;
@@ -399,8 +403,8 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream) {
   if (rc) return rc;
   if (a.nsplit > 1) {
     const int rows = a.B * a.Hq * a.L;
-    if (a.D == 128) attn_combine_kernel<128><<<rows, 128, 0, stream>>>(a.part_o, a.part_ml, a.nsplit, a.Hq, a.L, a.out_tokens_major, a.out);
-    else attn_combine_kernel<64><<<rows, 64, 0, stream>>>(a.part_o, a.part_ml, a.nsplit, a.Hq, a.L, a.out_tokens_major, a.out);
+    if (a.D == 128) M5_CUDA(launch_pdl(attn_combine_kernel<128>, dim3(rows), dim3(128), 0, stream, a.part_o, a.part_ml, a.nsplit, a.Hq, a.L, a.out_tokens_major, a.out));
+    else M5_CUDA(launch_pdl(attn_combine_kernel<64>, dim3(rows), dim3(64), 0, stream, a.part_o, a.part_ml, a.nsplit, a.Hq, a.L, a.out_tokens_major, a.out));
     M5_LAUNCH_CHECK("attention combine launch");
   }
   return M5_OK;

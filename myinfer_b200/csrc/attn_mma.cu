@@ -103,6 +103,8 @@ __device__ __forceinline__ int qk_dim(int j, int t, int k) {
 
 template <int BITS>
 __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   using LY = AmLayout<BITS>;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + AM_STAGES * LY::STAGE);
@@ -515,13 +517,13 @@ int attn_mma_launch(const AttnArgs& a, cudaStream_t stream) {
       M5_CUDA(cudaFuncSetAttribute(attn_mma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       conf8 = true;
     }
-    attn_mma_kernel<8><<<grid, AM_THREADS, smem, stream>>>(a);
+    M5_CUDA(launch_pdl(attn_mma_kernel<8>, dim3(grid), dim3(AM_THREADS), smem, stream, a));
   } else {
     if (!conf4) {
       M5_CUDA(cudaFuncSetAttribute(attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       conf4 = true;
     }
-    attn_mma_kernel<4><<<grid, AM_THREADS, smem, stream>>>(a);
+    M5_CUDA(launch_pdl(attn_mma_kernel<4>, dim3(grid), dim3(AM_THREADS), smem, stream, a));
   }
   M5_LAUNCH_CHECK("attention (tensor core) launch");
   return M5_OK;

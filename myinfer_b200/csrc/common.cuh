@@ -6,7 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <string>
+#include <utility>
 
 #include "../../include/m5cuda.h"
 
@@ -98,5 +100,32 @@ __device__ __forceinline__ float byte32768(uint32_t w) {
 inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
 int sm_count();  // SMs of the current device (cached)
+
+// Programmatic dependent launch.  A kernel launched with launch_pdl() may start
+// while the previous kernel on the stream is still running: it must execute
+// pdl_wait() before touching anything an earlier kernel writes (or reading
+// what it reads and later kernels write), and it lets the next kernel start
+// early with pdl_launch_dependents().  Work that depends on nothing earlier
+// (streaming constant weights into shared memory) goes before the wait.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+bool pdl_enabled();  // true only when M5_PDL=1 is set in the environment
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace m5

@@ -4,7 +4,10 @@
 // couple of L2 round trips instead of one per element.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace m5 {
 
@@ -12,10 +15,15 @@ namespace m5 {
 // xg[t * NG + G] = sum of the 64 staged (bf16-rounded) values of group G.
 // Threads [0, NT) of the block participate; `bar` is the named barrier id used
 // among them (0 = __syncthreads when NT is the whole block).
-template <int MT, int NT>
+//
+// FP16: the pairs are fp16 values x * 2^e_t with one power of two per token
+// chosen so the token's largest |x| lands in [2^14, 2^15): exact for every
+// value above max|x| * 2^-29 (bf16 has 8 significant bits, fp16 11), and
+// 2^-e_t is written to xinv[t] for the caller to undo after the dot product.
+template <int MT, int NT, bool FP16 = false>
 __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t ldx, int K,
                                            const bf16* __restrict__ norm_w, float eps, uint32_t* xf, float* xg,
-                                           float* red, int bar) {
+                                           float* red, int bar, float* xinv = nullptr) {
   constexpr int CH = 8;  // 16-byte loads in flight per thread per pass
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NG = K >> 6, K8 = K >> 3;
@@ -23,6 +31,10 @@ __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t l
     if (bar == 0) __syncthreads();
     else asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(NT) : "memory");
   };
+  float amax[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) amax[t] = 0.f;
+#pragma unroll
   for (int t = 0; t < MT; ++t) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + t * ldx);
     float inv = 1.f;
@@ -81,6 +93,10 @@ __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t l
               e[2 * q + 1] = rbf(__fmul_rn(bf16_hi(n[q]), rbf(__fmul_rn(e[2 * q + 1], inv))));
             }
           }
+          if (FP16) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) amax[t] = fmaxf(amax[t], fabsf(e[q]));
+          }
           uint4 o;
           o.x = uint32_t(__bfloat16_as_ushort(f2bf(e[0]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[4]))) << 16);
           o.y = uint32_t(__bfloat16_as_ushort(f2bf(e[1]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[5]))) << 16);
@@ -108,7 +124,178 @@ __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t l
     s += __shfl_xor_sync(0xffffffffu, s, 2);
     if (q < total && (q & 3) == 0) xg[q >> 2] = s;
   }
+  if constexpr (FP16) {
+    // per-token max |x| -> power-of-two scale, then convert the pairs in place
+    float* rm = red + 32;  // [NT / 32][MT]
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const float m = warp_max(amax[t]);
+      if (lane == 0) rm[warp * MT + t] = m;
+    }
+    sync();
+    float sc[MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      float m = 0.f;
+#pragma unroll
+      for (int w = 0; w < NT / 32; ++w) m = fmaxf(m, rm[w * MT + t]);
+      // m = 1.f * 2^(E - 127): m * 2^(141 - E) lies in [2^14, 2^15)
+      const int E = int((__float_as_uint(m) >> 23) & 0xFFu);
+      const int ex = m > 0.f ? max(-126, min(126, 141 - E)) : 0;
+      sc[t] = __uint_as_float(uint32_t(ex + 127) << 23);
+      if (tid == 0 && xinv) xinv[t] = __uint_as_float(uint32_t(127 - ex) << 23);
+    }
+    const int words = MT * NG * 32;
+    for (int i = tid; i < words; i += NT) {
+      const int t = i / (NG * 32);
+      float f = 1.f;
+#pragma unroll
+      for (int tt = 0; tt < MT; ++tt)
+        if (tt == t) f = sc[tt];
+      const uint32_t w = xf[i];
+      __half2 h = __floats2half2_rn(bf16_lo(w) * f, bf16_hi(w) * f);
+      xf[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
   sync();
+}
+
+// Same result as stage_frag<MT, NT, FP16>, with the activation rows (and the
+// norm weight) brought into shared memory by one bulk copy each, so staging
+// costs a single L2 round trip whatever K is.  The raw bf16 row of token t is
+// copied to xf + t * NG * 32: the uint4 of raw 8-element block c sits exactly
+// where the pairs of block c go, so every thread converts its blocks in place.
+// Requirements: x rows and norm_w 16-byte aligned (ldx % 8 == 0), nbuf holds
+// K bf16 when norm_w is set, xbar is an unused mbarrier slot.  Returns false
+// (and records a device error) if the copy did not land in time.
+template <int MT, int NT, bool FP16>
+__device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int64_t ldx, int K,
+                                                const bf16* __restrict__ norm_w, float eps, uint32_t* xf,
+                                                uint32_t* nbuf, float* xg, float* red, int bar, float* xinv,
+                                                uint64_t* xbar, int* err) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NG = K >> 6, K8 = K >> 3;
+  auto sync = [&]() {
+    if (bar == 0) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(NT) : "memory");
+  };
+  if (tid == 0) {
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+  }
+  sync();
+  if (tid == 0) {
+    const uint32_t row = uint32_t(K) * 2u;
+    mbar_arrive_expect_tx(xbar, MT * row + (norm_w ? row : 0u));
+#pragma unroll
+    for (int t = 0; t < MT; ++t) bulk_g2s(xf + size_t(t) * NG * 32, x + size_t(t) * ldx, row, xbar);
+    if (norm_w) bulk_g2s(nbuf, norm_w, row, xbar);
+  }
+  const bool ok = mbar_wait(xbar, 0, err);
+  float amax[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    amax[t] = 0.f;
+    uint4* blk = reinterpret_cast<uint4*>(xf + size_t(t) * NG * 32);
+    const uint4* nw = reinterpret_cast<const uint4*>(nbuf);
+    float inv = 1.f;
+    if (norm_w) {
+      float ss = 0.f;
+      for (int c = tid; c < K8; c += NT) {
+        const uint4 v = blk[c];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float a = bf16_lo(w[q]), b = bf16_hi(w[q]);
+          ss = fmaf(a, a, fmaf(b, b, ss));
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+      sync();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < NT / 32; ++w) tot += red[w];
+      inv = __frsqrt_rn(__fadd_rn(tot / float(K), eps));
+      sync();
+    }
+    for (int c = tid; c < K8; c += NT) {
+      const uint4 v = blk[c];
+      float e[8];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        e[2 * q] = bf16_lo(w[q]);
+        e[2 * q + 1] = bf16_hi(w[q]);
+      }
+      if (norm_w) {
+        const uint4 nv = nw[c];
+        const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          e[2 * q] = rbf(__fmul_rn(bf16_lo(n[q]), rbf(__fmul_rn(e[2 * q], inv))));
+          e[2 * q + 1] = rbf(__fmul_rn(bf16_hi(n[q]), rbf(__fmul_rn(e[2 * q + 1], inv))));
+        }
+      }
+      if (FP16) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) amax[t] = fmaxf(amax[t], fabsf(e[q]));
+      }
+      uint4 o;
+      o.x = uint32_t(__bfloat16_as_ushort(f2bf(e[0]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[4]))) << 16);
+      o.y = uint32_t(__bfloat16_as_ushort(f2bf(e[1]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[5]))) << 16);
+      o.z = uint32_t(__bfloat16_as_ushort(f2bf(e[2]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[6]))) << 16);
+      o.w = uint32_t(__bfloat16_as_ushort(f2bf(e[3]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[7]))) << 16);
+      blk[c] = o;  // pairs of block c occupy the bytes its raw values came from
+    }
+  }
+  sync();
+  const int total = MT * NG * 4;
+  for (int q0 = tid - lane; q0 < total; q0 += NT) {
+    const int q = q0 + lane;
+    float sum = 0.f;
+    if (q < total) {
+      const uint32_t* p = xf + (q >> 2) * 32 + (q & 3) * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += bf16_lo(p[j]) + bf16_hi(p[j]);
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (q < total && (q & 3) == 0) xg[q >> 2] = sum;
+  }
+  if constexpr (FP16) {
+    float* rm = red + 32;  // [NT / 32][MT]
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const float m = warp_max(amax[t]);
+      if (lane == 0) rm[warp * MT + t] = m;
+    }
+    sync();
+    float sc[MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      float m = 0.f;
+#pragma unroll
+      for (int w = 0; w < NT / 32; ++w) m = fmaxf(m, rm[w * MT + t]);
+      const int E = int((__float_as_uint(m) >> 23) & 0xFFu);
+      const int ex = m > 0.f ? max(-126, min(126, 141 - E)) : 0;
+      sc[t] = __uint_as_float(uint32_t(ex + 127) << 23);
+      if (tid == 0 && xinv) xinv[t] = __uint_as_float(uint32_t(127 - ex) << 23);
+    }
+    const int words = MT * NG * 32;
+    for (int i = tid; i < words; i += NT) {
+      const int t = i / (NG * 32);
+      float f = 1.f;
+#pragma unroll
+      for (int tt = 0; tt < MT; ++tt)
+        if (tt == t) f = sc[tt];
+      const uint32_t w = xf[i];
+      __half2 h = __floats2half2_rn(bf16_lo(w) * f, bf16_hi(w) * f);
+      xf[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  sync();
+  return ok;
 }
 
 }  // namespace m5

@@ -111,6 +111,8 @@ __device__ __forceinline__ void consume(const Slot<GR>& sl, const float* xs, con
 // across group boundaries.
 template <int MT, int EPI>
 __global__ void __launch_bounds__(GW * 32, MT == 1 ? 2 : 1) gemv_kernel(const GemvArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float smem[];
   constexpr int GR = Rows<MT, EPI>::value;
   const int K = a.K;
@@ -287,7 +289,7 @@ static int launch_t(const GemvArgs& a_in, cudaStream_t stream) {
   a.rows_per_warp = std::max(1, ceil_div(groups, resident));
   const int warps_total = ceil_div(groups, a.rows_per_warp);
   const int blocks = ceil_div(warps_total, GW);
-  gemv_kernel<MT, EPI><<<blocks, GW * 32, smem, stream>>>(a);
+  M5_CUDA(launch_pdl(gemv_kernel<MT, EPI>, dim3(blocks), dim3(GW * 32), smem, stream, a));
   M5_LAUNCH_CHECK("gemv launch");
   return M5_OK;
 }

@@ -82,6 +82,8 @@ __device__ __forceinline__ void mma_row(const GemvArgs& a, int tile, int r16, in
 
 template <int MT, int EPI>
 __global__ void __launch_bounds__(MW * 32, 2) gemv_mma_kernel(const GemvArgs a, MmaScratch sc) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int K = a.K, NG = K >> 6;
   uint32_t* xf = reinterpret_cast<uint32_t*>(smem_raw);          // [MT][NG][4 t][8] bf16 pairs
@@ -284,7 +286,7 @@ static int mma_launch_t(const GemvArgs& a, const MmaScratch& sc, cudaStream_t st
   const long long steps = (long long)(vrows / 16) * (a.K / 64);
   const long long max_ctas = (long long)std::max(1, per_sm) * sm_count();
   const int grid = (int)std::max(1LL, std::min(max_ctas, (steps + MW - 1) / MW));
-  gemv_mma_kernel<MT, EPI><<<grid, MW * 32, smem, st>>>(a, sc);
+  M5_CUDA(launch_pdl(gemv_mma_kernel<MT, EPI>, dim3(grid), dim3(MW * 32), smem, st, a, sc));
   M5_LAUNCH_CHECK("gemv_mma launch");
   return M5_OK;
 }

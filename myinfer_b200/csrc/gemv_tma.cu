@@ -112,6 +112,8 @@ __device__ __forceinline__ bool tg_row(const GemvArgs& a, int tile, int r, int& 
 
 template <int MT, int EPI>
 __global__ void __launch_bounds__(TG_THREADS) gemv_tma_kernel(const GemvArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int VPR = (EPI == EPI_SWIGLU) ? 2 : 1;
   using LY = TgLayout<VPR>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -270,7 +272,7 @@ static int tma_launch_t(const GemvArgs& a, cudaStream_t st) {
   M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tma_kernel<MT, EPI>, TG_THREADS, smem));
   const int ntiles = (a.total_rows + TG_CW - 1) / TG_CW;
   const int grid = std::max(1, std::min(ntiles, std::max(1, per_sm) * sm_count()));
-  gemv_tma_kernel<MT, EPI><<<grid, TG_THREADS, smem, st>>>(a);
+  M5_CUDA(launch_pdl(gemv_tma_kernel<MT, EPI>, dim3(grid), dim3(TG_THREADS), smem, st, a));
   M5_LAUNCH_CHECK("gemv_tma launch");
   return M5_OK;
 }

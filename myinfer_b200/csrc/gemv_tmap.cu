@@ -38,6 +38,7 @@ constexpr int TP_STAGES = 5;
 constexpr int TP_UG = 16;                     // 64-column scale groups per unit (1024 columns)
 constexpr int TP_W_STAGE = 16 * TP_UG * 32;    // 16 rows x UG groups x 32 bytes (1 KB swizzled boxes)
 constexpr int TP_SB_STAGE = 16 * TP_UG * 2;    // 16 rows x UG bf16 (scales or biases)
+constexpr int TP_BARS = 2 * TP_STAGES + 2;      // full, empty, activation copy (+ pad to 16 bytes)
 
 struct TmapSet {
   CUtensorMap w[3], s[3], b[3];  // per segment
@@ -51,13 +52,27 @@ __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int x, 
       : "memory");
 }
 
-__device__ __forceinline__ uint32_t tp_nib_pair(uint32_t w, int i) {
-  return ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
+__device__ __forceinline__ uint32_t tp_hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// 8 codes of one word -> fp16 pairs (q0,q4) (q1,q5) (q2,q6) (q3,q7), exact.
+// A nibble at bits 0-3 of a half becomes 1024 + q under the fp16 exponent of
+// 1024 (0x6400); one at bits 4-7 becomes 1024 + 16 q.  The integer pipe does
+// four masks and one shift per word; the offsets come off on the FMA pipe.
+__device__ __forceinline__ void tp_codes_f16(uint32_t w, uint32_t (&p)[4]) {
+  const uint32_t w8 = w >> 8;
+  p[0] = tp_hfma2((w & 0x000F000Fu) | 0x64006400u, 0x3C003C00u, 0xE400E400u);   // * 1 - 1024
+  p[1] = tp_hfma2((w & 0x00F000F0u) | 0x64006400u, 0x2C002C00u, 0xD400D400u);   // / 16 - 64
+  p[2] = tp_hfma2((w8 & 0x000F000Fu) | 0x64006400u, 0x3C003C00u, 0xE400E400u);
+  p[3] = tp_hfma2((w8 & 0x00F000F0u) | 0x64006400u, 0x2C002C00u, 0xD400D400u);
 }
 
 __device__ __forceinline__ void tp_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -81,7 +96,7 @@ __device__ __forceinline__ void tp_half(const GemvArgs& a, int tile, int h, int&
 }
 
 template <int MT, int EPI>
-__global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a, const __grid_constant__ TmapSet tm,
+__global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs a, const __grid_constant__ TmapSet tm,
                                                                float* acc_buf, int* cnt_buf, int acc_rows) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 128-byte-swizzled boxes must start on 1 KB boundaries
@@ -91,8 +106,10 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
   unsigned char* sbring = wring + TP_STAGES * TP_W_STAGE;        // [STAGES][2 (s,b)][256]
   uint64_t* full = reinterpret_cast<uint64_t*>(sbring + TP_STAGES * 2 * TP_SB_STAGE);
   uint64_t* empty = full + TP_STAGES;
-  uint32_t* xf = reinterpret_cast<uint32_t*>(empty + TP_STAGES);  // [MT][NG][4][8] bf16 pairs
-  float* xg = reinterpret_cast<float*>(xf + MT * NG * 32);        // [MT][NG]
+  uint64_t* xbar = empty + TP_STAGES;                             // activation copy
+  uint32_t* xf = reinterpret_cast<uint32_t*>(full + TP_BARS);     // [MT][NG][4][8] pairs
+  uint32_t* nbuf = xf + MT * NG * 32;                             // [K] bf16 norm weight (if any)
+  float* xg = reinterpret_cast<float*>(nbuf + (a.norm_w ? K / 2 : 0));  // [MT][NG]
   float* red = xg + MT * NG;                                      // [8]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -109,15 +126,20 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();
 
   if (warp == TP_CW) {
     // -------------------------------------------------------------- producer
+    // streams constant weights: needs nothing from earlier kernels
     if (lane == 0) {
       int it = 0;
       int tile = int(u0 / NCH), ch = int(u0 % NCH);
       for (long long u = u0; u < u1; ++u, ++it) {
         const int st = it % TP_STAGES;
         const uint32_t par = (it / TP_STAGES) & 1;
+        // the ring is full: from here on the consumers gate this warp, and they
+        // start only once the previous kernel has finished
+        if (it == TP_STAGES) pdl_wait();
         if (!mbar_wait(&empty[st], par ^ 1, &g_gemv_tmap_err)) return;
         mbar_arrive_expect_tx(&full[st], TP_W_STAGE + 2 * TP_SB_STAGE);
         unsigned char* ws = wring + st * TP_W_STAGE;
@@ -142,17 +164,31 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
   }
 
   // ---------------------------------------------- consumers: stage activations
-  stage_frag<MT, TP_CW * 32>(a.x, a.ldx, K, a.norm_w, a.eps, xf, xg, red, 1);
+  float* xinv = red;  // [MT] 2^-e of the fp16 activation scale (red[0..7] is free after staging)
+  pdl_wait();         // activations, residual and split-tile scratch come from earlier kernels
+  stage_frag_bulk<MT, TP_CW * 32, true>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, red, 1, xinv, xbar,
+                                        &g_gemv_tmap_err);
 
   const int g = lane >> 2, tq = lane & 3;
   const int tok = g < MT ? g : MT - 1;
+  const int t0c = 2 * tq < MT ? 2 * tq : MT - 1, t1c = 2 * tq + 1 < MT ? 2 * tq + 1 : MT - 1;
   const uint32_t* xfl = xf + tok * NG * 32 + tq * 8;
-  const float* xg0 = xg + (2 * tq < MT ? 2 * tq : MT - 1) * NG;
-  const float* xg1 = xg + (2 * tq + 1 < MT ? 2 * tq + 1 : MT - 1) * NG;
+  const float* xg0 = xg + t0c * NG;
+  const float* xg1 = xg + t1c * NG;
+  const float xi0 = xinv[t0c], xi1 = xinv[t1c];
+  // per-thread smem offsets of this warp's four groups inside a stage (the
+  // 128-byte swizzle of the weight boxes depends only on g, tq and the group)
+  uint32_t woff[TP_UG / TP_CW];
+#pragma unroll
+  for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
+    const int c = 2 * jj + (tq >> 1);
+    woff[jj] = warp * 1024 + g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
+  }
+  const uint32_t soff = g * (TP_UG * 2) + warp * (TP_UG / TP_CW) * 2;  // 4 consecutive bf16 of row g
 
   float tot[4] = {0.f, 0.f, 0.f, 0.f};
+  float totD[4] = {0.f, 0.f, 0.f, 0.f}, totB[4] = {0.f, 0.f, 0.f, 0.f};
   int cur_tile = u0 < u1 ? int(u0 / NCH) : 0, done = 0;
-
   // Epilogue of one finished tile row r16 / token t with its complete sum v.
   auto epilogue = [&](int tile, int r16, int t, float v, float vu) {
     if constexpr (EPI == EPI_SWIGLU) {
@@ -180,6 +216,10 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
   // with a neighbouring CTA goes through the zeroed global scratch and the
   // last contributor finishes it.
   auto flush = [&](int tile) {
+    tot[0] = fmaf(totD[0], xi0, totB[0]);
+    tot[1] = fmaf(totD[1], xi1, totB[1]);
+    tot[2] = fmaf(totD[2], xi0, totB[2]);
+    tot[3] = fmaf(totD[3], xi1, totB[3]);
     const int t0 = 2 * tq, t1 = 2 * tq + 1;
     const bool whole = (long long)tile * NCH >= u0 && (long long)(tile + 1) * NCH <= u1;
     if (whole) {
@@ -244,16 +284,15 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) tot[i] = 0.f;
+    for (int i = 0; i < 4; ++i) tot[i] = totD[i] = totB[i] = 0.f;
     done = 0;
   };
 
-  int it = 0;
   bool failed = false;
   int tile = cur_tile, ch = u0 < u1 ? int(u0 % NCH) : 0;
-  for (long long u = u0; u < u1; ++u, ++it) {
-    const int st = it % TP_STAGES;
-    const uint32_t par = (it / TP_STAGES) & 1;
+  int st = 0;
+  uint32_t par = 0;
+  for (long long u = u0; u < u1; ++u) {
     if (tile != cur_tile) {
       flush(cur_tile);
       cur_tile = tile;
@@ -261,62 +300,71 @@ __global__ void __launch_bounds__(TP_THREADS) gemv_tmap_kernel(const GemvArgs a,
     // On a timed-out wait the warp stops computing but keeps walking the units
     // so that every consumer warp still reaches the tile barriers in flush().
     if (!failed && !mbar_wait(&full[st], par, &g_gemv_tmap_err)) failed = true;
-    if (failed) {
-      done += TP_UG / TP_CW;
-      if (++ch == NCH) {
-        ch = 0;
-        ++tile;
-      }
-      continue;
-    }
-    const unsigned char* ws = wring + st * TP_W_STAGE;
-    const unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
+    if (!failed) {
+      const unsigned char* ws = wring + st * TP_W_STAGE;
+      const unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
+      const int G0 = ch * TP_UG + warp * (TP_UG / TP_CW);  // first global group of this warp
+      // scales / biases of the warp's 4 groups, rows g and g + 8; group sums of x
+      const uint2 sv0 = *reinterpret_cast<const uint2*>(ss + soff);
+      const uint2 sv8 = *reinterpret_cast<const uint2*>(ss + TP_SB_STAGE / 2 + soff);
+      const uint2 bv0 = *reinterpret_cast<const uint2*>(ss + TP_SB_STAGE + soff);
+      const uint2 bv8 = *reinterpret_cast<const uint2*>(ss + TP_SB_STAGE + TP_SB_STAGE / 2 + soff);
+      const float4 X0 = *reinterpret_cast<const float4*>(xg0 + G0);
+      const float4 X1 = *reinterpret_cast<const float4*>(xg1 + G0);
+      const float X0a[4] = {X0.x, X0.y, X0.z, X0.w}, X1a[4] = {X1.x, X1.y, X1.z, X1.w};
+      const uint32_t sw0[2] = {sv0.x, sv0.y}, sw8[2] = {sv8.x, sv8.y}, bw0[2] = {bv0.x, bv0.y},
+                     bw8[2] = {bv8.x, bv8.y};
 #pragma unroll
-    for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
-      const int j = (TP_UG / TP_CW) * warp + jj;  // group within the unit
-      const int G = ch * TP_UG + j;               // global scale group
-      // swizzled 8-byte fragment of rows g (half 0) and g (half 1 = tile row g+8)
-      const int c = 2 * (j & 3) + (tq >> 1);
-      const int off = g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
-      const uint2 w0 = *reinterpret_cast<const uint2*>(ws + (0 * (TP_UG / 4) + (j >> 2)) * 1024 + off);
-      const uint2 w8 = *reinterpret_cast<const uint2*>(ws + (1 * (TP_UG / 4) + (j >> 2)) * 1024 + off);
-      const uint4 xa = *reinterpret_cast<const uint4*>(xfl + G * 32);
-      const uint4 xb = *reinterpret_cast<const uint4*>(xfl + G * 32 + 4);
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      {
-        uint32_t A[4] = {tp_nib_pair(w0.x, 0), tp_nib_pair(w8.x, 0), tp_nib_pair(w0.x, 1), tp_nib_pair(w8.x, 1)};
-        tp_mma(d, A, xa.x, xa.y);
+      for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
+        const uint2 w0 = *reinterpret_cast<const uint2*>(ws + woff[jj]);
+        const uint2 w8 = *reinterpret_cast<const uint2*>(ws + 4096 + woff[jj]);
+        const uint4 xa = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32);
+        const uint4 xb = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32 + 4);
+        uint32_t pa0[4], pa8[4], pb0[4], pb8[4];
+        tp_codes_f16(w0.x, pa0);
+        tp_codes_f16(w8.x, pa8);
+        tp_codes_f16(w0.y, pb0);
+        tp_codes_f16(w8.y, pb8);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          const uint32_t A[4] = {pa0[0], pa8[0], pa0[1], pa8[1]};
+          tp_mma(d, A, xa.x, xa.y);
+        }
+        {
+          const uint32_t A[4] = {pa0[2], pa8[2], pa0[3], pa8[3]};
+          tp_mma(d, A, xa.z, xa.w);
+        }
+        {
+          const uint32_t A[4] = {pb0[0], pb8[0], pb0[1], pb8[1]};
+          tp_mma(d, A, xb.x, xb.y);
+        }
+        {
+          const uint32_t A[4] = {pb0[2], pb8[2], pb0[3], pb8[3]};
+          tp_mma(d, A, xb.z, xb.w);
+        }
+        const uint32_t s0w = sw0[jj >> 1], s8w = sw8[jj >> 1], b0w = bw0[jj >> 1], b8w = bw8[jj >> 1];
+        const float sA = (jj & 1) ? bf16_hi(s0w) : bf16_lo(s0w), sB = (jj & 1) ? bf16_hi(s8w) : bf16_lo(s8w);
+        const float bA = (jj & 1) ? bf16_hi(b0w) : bf16_lo(b0w), bB = (jj & 1) ? bf16_hi(b8w) : bf16_lo(b8w);
+        totD[0] = fmaf(sA, d[0], totD[0]);
+        totD[1] = fmaf(sA, d[1], totD[1]);
+        totD[2] = fmaf(sB, d[2], totD[2]);
+        totD[3] = fmaf(sB, d[3], totD[3]);
+        totB[0] = fmaf(bA, X0a[jj], totB[0]);
+        totB[1] = fmaf(bA, X1a[jj], totB[1]);
+        totB[2] = fmaf(bB, X0a[jj], totB[2]);
+        totB[3] = fmaf(bB, X1a[jj], totB[3]);
       }
-      {
-        uint32_t A[4] = {tp_nib_pair(w0.x, 2), tp_nib_pair(w8.x, 2), tp_nib_pair(w0.x, 3), tp_nib_pair(w8.x, 3)};
-        tp_mma(d, A, xa.z, xa.w);
-      }
-      {
-        uint32_t A[4] = {tp_nib_pair(w0.y, 0), tp_nib_pair(w8.y, 0), tp_nib_pair(w0.y, 1), tp_nib_pair(w8.y, 1)};
-        tp_mma(d, A, xb.x, xb.y);
-      }
-      {
-        uint32_t A[4] = {tp_nib_pair(w0.y, 2), tp_nib_pair(w8.y, 2), tp_nib_pair(w0.y, 3), tp_nib_pair(w8.y, 3)};
-        tp_mma(d, A, xb.z, xb.w);
-      }
-      const bf16* s0 = reinterpret_cast<const bf16*>(ss + g * (TP_UG * 2)) + j;
-      const bf16* s8 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE / 2 + g * (TP_UG * 2)) + j;
-      const bf16* b0 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + g * (TP_UG * 2)) + j;
-      const bf16* b8 = reinterpret_cast<const bf16*>(ss + TP_SB_STAGE + TP_SB_STAGE / 2 + g * (TP_UG * 2)) + j;
-      const float sA = bf2f(*s0), bA = bf2f(*b0), sB = bf2f(*s8), bB = bf2f(*b8);
-      const float X0 = xg0[G], X1 = xg1[G];
-      const float oA = fmaf(-128.f, sA, bA), oB = fmaf(-128.f, sB, bB);
-      tot[0] = fmaf(sA, d[0], fmaf(oA, X0, tot[0]));
-      tot[1] = fmaf(sA, d[1], fmaf(oA, X1, tot[1]));
-      tot[2] = fmaf(sB, d[2], fmaf(oB, X0, tot[2]));
-      tot[3] = fmaf(sB, d[3], fmaf(oB, X1, tot[3]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
     done += TP_UG / TP_CW;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
     if (++ch == NCH) {
       ch = 0;
       ++tile;
+    }
+    if (++st == TP_STAGES) {
+      st = 0;
+      par ^= 1;
     }
   }
   if (u0 < u1) flush(cur_tile);
@@ -363,15 +411,17 @@ static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i) {
   return M5_OK;
 }
 
-static size_t tp_smem(int MT, int K) {
-  return TP_STAGES * (TP_W_STAGE + 2 * TP_SB_STAGE) + 2 * TP_STAGES * 8 + size_t(MT) * (K / 64) * 32 * 4 +
-         size_t(MT) * (K / 64) * 4 + 8 * 4 + size_t(TP_CW) * MT * 16 * 4 + 1024;
+static size_t tp_smem(int MT, int K, bool norm) {
+  return TP_STAGES * (TP_W_STAGE + 2 * TP_SB_STAGE) + TP_BARS * 8 + size_t(MT) * (K / 64) * 32 * 4 +
+         (norm ? size_t(K) * 2 : 0) + size_t(MT) * (K / 64) * 4 + 8 * 4 + size_t(TP_CW) * MT * 16 * 4 + 1024;
 }
 
 bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
   if (MT < 1 || MT > 8 || a.K % (64 * TP_UG)) return false;
-  if (tp_smem(MT, a.K) > 200 * 1024) return false;
+  if (tp_smem(MT, a.K, a.norm_w != nullptr) > 200 * 1024) return false;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  // activation rows and the norm weight arrive by bulk copy: 16-byte aligned
+  if (!al(a.x) || (a.ldx % 8) || (a.norm_w && !al(a.norm_w))) return false;
   for (int i = 0; i < a.nseg; ++i) {
     if (!al(a.seg[i].w) || !al(a.seg[i].s) || !al(a.seg[i].b)) return false;
     if (epi == EPI_SWIGLU ? (a.seg[i].rows % 8) : (a.seg[i].rows % 16)) return false;
@@ -383,7 +433,7 @@ bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
 
 template <int MT, int EPI>
 static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* acc, int* cnt, int acc_rows, cudaStream_t st) {
-  const size_t smem = tp_smem(MT, a.K);
+  const size_t smem = tp_smem(MT, a.K, a.norm_w != nullptr);
   static bool configured = false;
   if (!configured) {
     M5_CUDA(cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
@@ -395,8 +445,7 @@ static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* acc, int* cn
   const long long units = (long long)(vrows / 16) * (a.K / (64 * TP_UG));
   const long long max_ctas = (long long)std::max(1, per_sm) * sm_count();
   const int grid = (int)std::max(1LL, std::min(max_ctas, units));
-  gemv_tmap_kernel<MT, EPI><<<grid, TP_THREADS, smem, st>>>(a, ts, acc, cnt, acc_rows);
-  M5_LAUNCH_CHECK("gemv_tmap launch");
+  M5_CUDA(launch_pdl(gemv_tmap_kernel<MT, EPI>, dim3(grid), dim3(TP_THREADS), smem, st, a, ts, acc, cnt, acc_rows));
   return M5_OK;
 }
 

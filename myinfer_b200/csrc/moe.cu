@@ -22,6 +22,8 @@ namespace m5 {
 constexpr int MOE_WARPS = 4;
 
 __global__ void __launch_bounds__(MOE_WARPS * 32) moe_gate_up_kernel(const MoeArgs a, int rpw) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float smem[];
   const int slot = blockIdx.y;
   const int t = slot / a.k;
@@ -51,6 +53,8 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) moe_gate_up_kernel(const MoeAr
 }
 
 __global__ void __launch_bounds__(MOE_WARPS * 32) moe_down_kernel(const MoeArgs a, int rpw) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float smem[];
   const int t = blockIdx.y;
   const int H = a.H, I = a.I, k = a.k;
@@ -106,7 +110,7 @@ int moe_launch(const MoeArgs& a, cudaStream_t st) {
     const long long slots = (long long)a.T * a.k;
     const int rpw = std::max(1, (int)((a.I * slots + resident - 1) / resident));
     dim3 grid(ceil_div(a.I, MOE_WARPS * rpw), (unsigned)slots);
-    moe_gate_up_kernel<<<grid, MOE_WARPS * 32, smem, st>>>(a, rpw);
+    M5_CUDA(launch_pdl(moe_gate_up_kernel, dim3(grid), dim3(MOE_WARPS * 32), smem, st, a, rpw));
     M5_LAUNCH_CHECK("moe gate/up launch");
   }
   {
@@ -114,7 +118,7 @@ int moe_launch(const MoeArgs& a, cudaStream_t st) {
     if (smem > 200 * 1024) return fail(M5_ERR_UNSUPPORTED, "moe: k * moe_intermediate_size too large");
     const int rpw = std::max(1, (int)(((long long)a.H * a.T + resident - 1) / resident));
     dim3 grid(ceil_div(a.H, MOE_WARPS * rpw), (unsigned)a.T);
-    moe_down_kernel<<<grid, MOE_WARPS * 32, smem, st>>>(a, rpw);
+    M5_CUDA(launch_pdl(moe_down_kernel, dim3(grid), dim3(MOE_WARPS * 32), smem, st, a, rpw));
     M5_LAUNCH_CHECK("moe down launch");
   }
   return M5_OK;

@@ -55,6 +55,8 @@ __device__ __forceinline__ void store_kv_row(const float (&x)[4], int lane, void
 // ------------------------------------------------------- rope + kv append
 template <int BITS>
 __global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int D = 128;
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -111,9 +113,9 @@ int rope_append_launch(const RopeAppendArgs& a, cudaStream_t stream) {
   const int warps = a.L * (a.Hq + 2 * a.Hkv);
   const int blocks = ceil_div(warps, 8);
   switch (a.kv.bits) {
-    case 0: rope_append_kernel<0><<<blocks, 256, 0, stream>>>(a); break;
-    case 4: rope_append_kernel<4><<<blocks, 256, 0, stream>>>(a); break;
-    case 8: rope_append_kernel<8><<<blocks, 256, 0, stream>>>(a); break;
+    case 0: M5_CUDA(launch_pdl(rope_append_kernel<0>, dim3(blocks), dim3(256), 0, stream, a)); break;
+    case 4: M5_CUDA(launch_pdl(rope_append_kernel<4>, dim3(blocks), dim3(256), 0, stream, a)); break;
+    case 8: M5_CUDA(launch_pdl(rope_append_kernel<8>, dim3(blocks), dim3(256), 0, stream, a)); break;
     default: return fail(M5_ERR_INVALID, "kv bits must be 0, 4 or 8");
   }
   M5_LAUNCH_CHECK("rope_append launch");
@@ -157,6 +159,8 @@ int kv_quantize_layer_launch(const m5_layer_kv& src, const m5_layer_kv& dst, int
 __global__ void __launch_bounds__(256) embed_kernel(const int32_t* __restrict__ tokens, int T, const uint32_t* __restrict__ w,
                                                     const bf16* __restrict__ s, const bf16* __restrict__ b, int H, int V,
                                                     bf16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int H8 = H / 8;
   const int64_t total = int64_t(T) * H8;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
@@ -184,7 +188,7 @@ int embed_launch(const int32_t* tokens, int T, const uint32_t* w, const bf16* s,
   if (H % 64) return fail(M5_ERR_INVALID, "embedding: hidden size must be a multiple of 64");
   const int64_t total = int64_t(T) * (H / 8);
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, sm_count() * 8);
-  embed_kernel<<<blocks, 256, 0, stream>>>(tokens, T, w, s, b, H, V, out);
+  M5_CUDA(launch_pdl(embed_kernel, dim3(blocks), dim3(256), 0, stream, tokens, T, w, s, b, H, V, out));
   M5_LAUNCH_CHECK("embedding launch");
   return M5_OK;
 }
@@ -229,6 +233,8 @@ __device__ __forceinline__ void block_best(float& v, int& i) {
 
 __global__ void __launch_bounds__(1024) argmax_kernel(const bf16* __restrict__ x, int64_t n, int32_t* out,
                                                       ArgmaxScratch* sc) {
+  pdl_wait();
+  pdl_launch_dependents();
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const bf16* __restrict__ x
 int argmax_launch(const bf16* x, int64_t n, int32_t* out, void* scratch, cudaStream_t stream) {
   if (n <= 0) return fail(M5_ERR_INVALID, "argmax: empty input");
   const int blocks = (int)std::min<int64_t>(ARGMAX_BLOCKS, (n + 1023) / 1024);
-  argmax_kernel<<<blocks, 1024, 0, stream>>>(x, n, out, reinterpret_cast<ArgmaxScratch*>(scratch));
+  M5_CUDA(launch_pdl(argmax_kernel, dim3(blocks), dim3(1024), 0, stream, x, n, out, reinterpret_cast<ArgmaxScratch*>(scratch)));
   M5_LAUNCH_CHECK("argmax launch");
   return M5_OK;
 }
@@ -273,6 +279,8 @@ int argmax_launch(const bf16* x, int64_t n, int32_t* out, void* scratch, cudaStr
 // ---------------------------------------------------------------- rms norm
 __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
                                                        int dim, float eps, bf16* __restrict__ y) {
+  pdl_wait();
+  pdl_launch_dependents();
   const bf16* xr = x + size_t(blockIdx.x) * dim;
   bf16* yr = y + size_t(blockIdx.x) * dim;
   __shared__ float red[33];
@@ -297,7 +305,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16* __restrict__ 
 
 int rms_norm_launch(const bf16* x, const bf16* w, int64_t rows, int dim, float eps, bf16* y, cudaStream_t stream) {
   if (rows <= 0) return M5_OK;
-  rms_norm_kernel<<<(unsigned)rows, 256, 0, stream>>>(x, w, dim, eps, y);
+  M5_CUDA(launch_pdl(rms_norm_kernel, dim3((unsigned)rows), dim3(256), 0, stream, x, w, dim, eps, y));
   M5_LAUNCH_CHECK("rms_norm launch");
   return M5_OK;
 }
@@ -307,6 +315,8 @@ int rms_norm_launch(const bf16* x, const bf16* w, int64_t rows, int dim, float e
 __global__ void __launch_bounds__(256) moe_topk_kernel(const bf16* __restrict__ logits, int T, int E, int k,
                                                        int norm_topk, int32_t* __restrict__ ids,
                                                        bf16* __restrict__ scores) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -364,13 +374,15 @@ int moe_topk_launch(const bf16* logits, int T, int E, int k, int norm_topk, int3
                     cudaStream_t stream) {
   if (E > 256 || k > 32 || k > E || k <= 0) return fail(M5_ERR_INVALID, "moe top-k: E <= 256, 0 < k <= min(32, E)");
   if (T <= 0) return M5_OK;
-  moe_topk_kernel<<<ceil_div(T, 8), 256, 0, stream>>>(logits, T, E, k, norm_topk, ids, scores);
+  M5_CUDA(launch_pdl(moe_topk_kernel, dim3(ceil_div(T, 8)), dim3(256), 0, stream, logits, T, E, k, norm_topk, ids, scores));
   M5_LAUNCH_CHECK("moe top-k launch");
   return M5_OK;
 }
 
 // ------------------------------------------------------------ residual add
 __global__ void residual_add_f32_kernel(bf16* h, const float* r, int64_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
     h[i] = f2bf(bf2f(h[i]) + rbf(r[i]));
 }
@@ -378,7 +390,7 @@ __global__ void residual_add_f32_kernel(bf16* h, const float* r, int64_t n) {
 int residual_add_f32_launch(bf16* h, const float* r, int64_t n, cudaStream_t stream) {
   if (n <= 0) return M5_OK;
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, sm_count() * 4);
-  residual_add_f32_kernel<<<blocks, 256, 0, stream>>>(h, r, n);
+  M5_CUDA(launch_pdl(residual_add_f32_kernel, dim3(blocks), dim3(256), 0, stream, h, r, n));
   M5_LAUNCH_CHECK("residual add launch");
   return M5_OK;
 }

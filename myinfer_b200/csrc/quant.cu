@@ -24,6 +24,19 @@ int cuda_fail(cudaError_t e, const char* what) {
   return M5_ERR_CUDA;
 }
 
+// Off unless M5_PDL=1: measured on B200, letting the next GEMV's CTAs start
+// early made the decode step slower (they compete for HBM and SM slots with
+// the tail of the previous kernel and gain nothing while their activations
+// are not ready).
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("M5_PDL");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 int sm_count() {
   static int cached[64] = {0};
   int dev = 0;

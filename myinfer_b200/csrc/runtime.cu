@@ -223,7 +223,11 @@ static GemvSeg seg_of(const Linear& l, int rows, bf16* y) {
   return s;
 }
 
-__global__ void add_len_kernel(int32_t* d_len, int L) { *d_len += L; }
+__global__ void add_len_kernel(int32_t* d_len, int L) {
+  pdl_wait();
+  pdl_launch_dependents();
+  *d_len += L;
+}
 
 static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int L, void* logits,
                    int logits_mode, int32_t* d_argmax, cudaStream_t st) {
@@ -387,8 +391,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
   if (d_argmax && last_row) {
     if ((rc = argmax_launch(last_row, V, d_argmax, m->argmax_scratch, st))) return rc;
   }
-  add_len_kernel<<<1, 1, 0, st>>>(d_len, L);
-  M5_LAUNCH_CHECK("length update");
+  M5_CUDA(launch_pdl(add_len_kernel, dim3(1), dim3(1), 0, st, d_len, L));
   return M5_OK;
 }
 

@@ -98,9 +98,5 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
-// Programmatic dependent launch: wait for the upstream grid's memory, and let
-// the downstream grid start its prologue.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 }  // namespace m5
