@@ -1,18 +1,22 @@
-"""Batch-1 greedy decode throughput of the Qwen3-32B-shaped 4-bit model on B200.
+"""Batch-1 greedy decode and chunked prefill of the Qwen3-32B-shaped 4-bit model on B200.
 
-`python bench.py [--gpus N] [--steps K] [--warmup W] [--impl m5|reference]`
+`python bench.py [--gpus N] [--steps K] [--warmup W] [--impl m5|reference] [--ctx 32768]`
 
-A step is one decode token (one full forward of the 64-layer model at the
-current context, 8-bit KV, greedy argmax) replayed from a CUDA graph; weights
-(18.43 GB) and the 32K-token KV cache are resident in HBM before timing.
-Weights and KV are synthetic (seeded random, MLX 4-bit g64 / 8-bit g64
-layouts).  Inputs are larger than L2 (every step streams ~22.6 GB).
+A step is one decode token: one full forward of the 64-layer model at the
+current context with 8-bit KV and greedy argmax, replayed from a CUDA graph.
+Before the timed decode the prompt (seeded random ids, `--ctx` tokens) is
+prefilled in chunks of 2048 through the same model and cache (timed too:
+`prefill` in the JSON line).  Weights are seeded random MLX 4-bit g64
+tensors resident in HBM; every decode step streams ~22.6 GB (larger than L2).
+With N > 1 (torchrun) the dense model runs tensor parallel over the N GPUs
+(one sequence, so `value` is that sequence's tokens/s and scaling is strong).
 
-Printed JSON (rank 0): value = tokens/s of the whole job; roofline = the
-dominant kernel (w4 dequant-GEMV) timed alone with CUDA events;
-cpu_baseline = the CPU oracle on a bounded sample of the same step.
-`--impl reference` times the CPU restatement of the reference path (MLX is
-not installable here) on the same workload and prints the same line shape.
+Printed JSON (rank 0): value = decode tokens/s; hbm = algorithmic bytes per
+token against the measured copy bandwidth; roofline = the dominant kernel
+(w4 dequant-GEMV) timed alone with CUDA events; cpu_baseline = the CPU
+oracle on a bounded sample of the same step.  `--impl reference` times the
+CPU restatement of the reference path (MLX is not installable here) and
+prints the same line shape.
 """
 
 from __future__ import annotations
@@ -173,25 +177,6 @@ def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0) ->
 
 
 # ----------------------------------------------------------------- GPU leg
-def fill_kv_synthetic(cache, ctx: int, seed: int):
-    """Random N(0,1) K/V for positions [0, ctx) quantized into every layer."""
-    import torch
-
-    from myinfer_b200 import ops
-    g = torch.Generator(device=cache.d_len.device).manual_seed(seed)
-    for c in cache:
-        H, D = c.n_kv_heads, c.head_dim
-        for which in ("k", "v"):
-            x = torch.randn(H, ctx, D, generator=g, device=c.device).to(torch.bfloat16)
-            q, s, b = ops.quantize(x, 64, c.bits)
-            tq, ts, tb = (c._kq, c._ks, c._kb) if which == "k" else (c._vq, c._vs, c._vb)
-            tq[0, :, :ctx].copy_(q)
-            ts[0, :, :ctx].copy_(s)
-            tb[0, :, :ctx].copy_(b)
-        c.offset = ctx
-    cache.d_len.fill_(ctx)
-
-
 def gemv_roofline(model, cfg, peak_gbs) -> dict:
     """Dominant kernel (gate/up dequant-GEMV with SwiGLU... measured as the
     plain projection GEMVs of every layer) timed alone with CUDA events."""
@@ -235,7 +220,17 @@ def gemv_roofline(model, cfg, peak_gbs) -> dict:
             "alg_bytes_per_launch": int(alg), "avg_launch_us": round(ms * 1e3, 2)}
 
 
+def prefill(model, cache, ids, chunk: int):
+    """Chunked prefill of `ids` (device int32) into `cache`, like generate_step's prompt loop."""
+    import torch
+    for pos in range(0, ids.numel(), chunk):
+        model.forward(ids[pos:pos + chunk], cache)
+    return cache
+
+
 def run_gpu(args) -> dict:
+    import datetime
+
     import torch
 
     from myinfer_b200 import _lib
@@ -248,92 +243,135 @@ def run_gpu(args) -> dict:
     world = int(os.environ.get("WORLD_SIZE", 1))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    comm = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+
+        from myinfer_b200.distributed import Communicator
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        comm = Communicator(world, rank)
     cfg = CONFIGS[args.config]
     a = ModelArgs.from_dict(cfg)
     t0 = time.perf_counter()
     w = random_weights(a, seed=args.seed, device=dev)
-    model = Model(a, w, dev, max_tokens=8)
+    par = {}
+    if world > 1:
+        from myinfer_b200.distributed import shard_weights
+        par = dict(ep_size=world, ep_rank=rank) if a.num_experts else dict(tp_size=world, tp_rank=rank)
+        w = shard_weights(w, a, **par)
+        torch.cuda.empty_cache()
+    model = Model(a, w, dev, max_tokens=args.chunk, comm=comm, **par)
     torch.cuda.synchronize()
     load_s = time.perf_counter() - t0
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(ms: float) -> float:
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t)
+
+    def new_cache(cap):
+        return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, 8, capacity=cap)
+                            for _ in range(a.num_hidden_layers)], dev)
+
     ctx = args.ctx
+    g = torch.Generator(device=dev).manual_seed(args.seed + 7)
+    ids = torch.randint(0, a.vocab_size, (ctx,), generator=g, device=dev, dtype=torch.int32)
+    # ---- prefill: warm the prefill kernels on a short scratch run, then the timed prompt
+    prefill(model, new_cache(args.chunk), ids[:args.chunk], args.chunk)
     total = ctx + args.warmup + args.steps * 2 + 8
-    cache = PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, 8, capacity=total)
-                         for _ in range(a.num_hidden_layers)], dev)
-    fill_kv_synthetic(cache, ctx, seed=args.seed + 1)
-    # one eager step (configures kernels), then capture the decode graph
+    cache = new_cache(total)
+    torch.cuda.synchronize()
+    barrier()
+    ps, pe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ps.record()
+    prefill(model, cache, ids, args.chunk)
+    pe.record()
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(ps.elapsed_time(pe))
+
+    # ---- decode on the prefilled cache: one eager step, then the captured graph
     tok = torch.tensor([1], dtype=torch.int32, device=dev)
     model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
-    g = DecodeGraph(model, cache, with_logits=False)
-    g.tok.copy_(tok)
+    graph = DecodeGraph(model, cache, with_logits=False)
+    graph.tok.copy_(tok)
     for _ in range(args.warmup):
-        g.step()
+        graph.step()
     torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         start.record()
         for _ in range(args.steps):
-            g.step()
+            graph.step()
         end.record()
         torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t)
-    ms_step = ms / args.steps
+    ms_step = max_over_ranks(start.elapsed_time(end)) / args.steps
     mean_ctx = ctx + args.warmup + args.steps / 2
     bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_per_token(cfg, int(mean_ctx))
     peaks = measured_peaks()
-    tok_s = 1000.0 / ms_step * world
+    tok_s = 1000.0 / ms_step  # one sequence: every rank works on the same token
 
     # e2e through the public decode step: pinned host token in, token out, every step
     host = torch.empty(1, dtype=torch.int32, pin_memory=True)
     host[0] = 1
     torch.cuda.synchronize()
-    e_start = time.perf_counter()
+    barrier()
     e_steps = max(4, args.steps // 2)
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     es.record()
     for _ in range(e_steps):
-        g.tok.copy_(host, non_blocking=True)
-        g.step()
-        host.copy_(g.tok, non_blocking=True)
+        graph.tok.copy_(host, non_blocking=True)
+        graph.step()
+        host.copy_(graph.tok, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     ee.record()
     torch.cuda.synchronize()
-    e2e_ms = es.elapsed_time(ee) / e_steps
-    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"])
+    e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e_steps
+    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"]) if world == 1 else None
+    per_rank = bytes_tok / world
+    par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}" if world > 1 else "single")
+    prefill_flops = 2.0 * ctx * (weight_bytes_per_token(cfg) / 0.5625) + 4.0 * a.num_hidden_layers * \
+        a.num_attention_heads * a.head_dim * ctx * ctx / 2
     out = {
-        "metric": "batch-1 decode tok/s (Qwen3-32B-shaped, w4g64, 8-bit KV)",
+        "metric": "batch-1 decode tok/s (Qwen3-32B-shaped, w4g64, 8-bit KV) + HBM TB/s vs peak; prefill tok/s",
         "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "replicas" if world > 1 else "weak",
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "w4a16 (bf16 activations, fp32 accumulate), 8-bit KV",
-        "data": "synthetic (seeded random weights and KV)",
-        "config": {"workload": f"{args.config} decode, batch 1, context {ctx}", "model": args.config,
-                   "global_batch": world, "seq_len": ctx, "parallelism": f"replicas{world}",
-                   "kv_fill": "synthetic quantized N(0,1) K/V for the 32K prompt positions",
-                   "l2": "inputs larger than L2 (>=18 GB streamed per step)"},
+        "data": "synthetic (seeded random weights and prompt ids)",
+        "config": {"workload": f"{args.config} batch-1 decode after a {ctx}-token prefill", "model": args.config,
+                   "global_batch": 1, "seq_len": ctx, "parallelism": par_name, "prefill_chunk": args.chunk,
+                   "l2": "inputs larger than L2 (>=18 GB streamed per decode step)"},
         "hbm": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok / (ms_step * 1e-3) / 1e9, 1),
-                "peak_gbs": peaks["hbm_gbs"], "frac_of_measured": round(bytes_tok / (ms_step * 1e-3) / 1e9 /
-                                                                       peaks["hbm_gbs"], 4),
-                "frac_of_8tbs_nominal": round(bytes_tok / (ms_step * 1e-3) / 8e12, 4)},
+                "achieved_gbs_per_gpu": round(per_rank / (ms_step * 1e-3) / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
+                "frac_of_measured": round(per_rank / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                "frac_of_8tbs_nominal": round(per_rank / (ms_step * 1e-3) / 8e12, 4)},
+        "prefill": {"value": round(ctx / (prefill_ms * 1e-3), 1), "unit": "tok/s", "prompt_tokens": ctx,
+                    "ms": round(prefill_ms, 1), "flops": prefill_flops,
+                    "tflops": round(prefill_flops / (prefill_ms * 1e-3) / 1e12, 1)},
         "roofline": roof,
-        "e2e": {"value": round(1000.0 / e2e_ms * world, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+        "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": None,
         "clocks": clk.summary(),
         "load_seconds": round(load_s, 1),
     }
-    # kernels per step: 7 per layer + embed + lm_head + argmax + length update
-    out["gpu_launches"] = args.steps * (a.num_hidden_layers * 7 + 4)
+    # kernels per decode step: per layer qkv, rope/append, attention (+ combine), o, gate/up, down
+    # (+ 2 residual adds under tensor parallelism); embed, lm_head, argmax, length update
+    per_layer = 7 + (2 if world > 1 else 0)
+    out["gpu_launches"] = args.steps * (a.num_hidden_layers * per_layer + 4)
     if rank == 0 and not args.no_cpu:
         out["cpu_baseline"] = cpu_decode_sample(cfg, min(ctx, 4096), layers=1, threads=os.cpu_count() or 1)
+    del graph
     if world > 1:
+        torch.distributed.barrier()
+        del model
+        comm.close()
         torch.distributed.destroy_process_group()
     return out if rank == 0 else None
 
@@ -369,6 +407,7 @@ def main():
     ap.add_argument("--impl", default="m5", choices=["m5", "reference"])
     ap.add_argument("--config", default="qwen3-32b", choices=sorted(CONFIGS))
     ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--chunk", type=int, default=2048, help="prefill chunk (prefill_step_size)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()

@@ -212,6 +212,24 @@ M5_API int m5_moe_route(const void* x, int T, int H, const uint32_t* gate_w, con
                  const void* gate_b, int E, int k, int norm_topk_prob, int32_t* ids, void* scores,
                  void* logits_out, void* stream);
 
+/* ---------------------------------------------------------------- multi-GPU
+ * One process per GPU.  A model created with tp_size > 1 (dense: q/k/v heads,
+ * gate/up rows, o/down columns and lm_head rows split over ranks) or
+ * ep_size > 1 (MoE: experts split, attention replicated) needs a
+ * communicator before m5_model_check / m5_forward: rank 0 makes an id with
+ * m5_comm_unique_id, the caller hands the bytes to every rank (the reference
+ * has no multi-GPU path; torch.distributed is the usual carrier), each rank
+ * calls m5_comm_init.  m5_forward then all-reduces the o_proj / down (or MoE)
+ * partial sums in fp32 and all-gathers the vocabulary shards of the logits, so
+ * every rank returns the full logits and the same argmax. */
+#define M5_COMM_ID_BYTES 128
+M5_API int m5_comm_unique_id(void* out, size_t len);
+M5_API int m5_comm_init(const void* id, size_t len, int nranks, int rank, void** comm);
+M5_API int m5_comm_destroy(void* comm);
+M5_API int m5_model_set_comm(void* model, void* comm);
+/* In-place fp32 sum over the communicator's ranks (stream-ordered). */
+M5_API int m5_allreduce_f32(void* comm, float* buf, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

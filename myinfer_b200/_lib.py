@@ -75,7 +75,13 @@ _SIGS = {
     "m5_argmax_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     "m5_moe_route": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                              c_void_p, c_void_p, c_void_p, c_void_p]),
+    "m5_comm_unique_id": (c_int, [c_void_p, c_size_t]),
+    "m5_comm_init": (c_int, [c_void_p, c_size_t, c_int, c_int, POINTER(c_void_p)]),
+    "m5_comm_destroy": (c_int, [c_void_p]),
+    "m5_model_set_comm": (c_int, [c_void_p, c_void_p]),
+    "m5_allreduce_f32": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
 }
+M5_COMM_ID_BYTES = 128
 
 _lib: Optional[ctypes.CDLL] = None
 

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "attn.cuh"
+#include "comm.cuh"
 #include "gemv.cuh"
 #include "moe.cuh"
 #include "ops.cuh"
@@ -67,6 +68,12 @@ struct Model {
   bf16* xn = nullptr;        // RMSNorm(h) materialised for the prefill GEMM [T, H]
   bf16* gxs = nullptr;       // per-token group sums of the prefill GEMM input
   size_t gxs_bytes = 0;
+  // multi-GPU: communicator, fp32 partial sums [T, H], vocabulary shard logits
+  void* comm = nullptr;
+  int Vl = 0, v_rows = 0;    // this rank's vocabulary rows; head rows per gather chunk
+  float* hf = nullptr;
+  bf16* vpart = nullptr;     // [v_rows, Vl]
+  bf16* vgather = nullptr;   // [tp, v_rows, Vl]
 };
 
 // Token count from which a projection runs as the tensor-core GEMM instead of
@@ -129,7 +136,9 @@ static std::string missing(const Model* m) {
   const bool moe = m->cfg.num_experts > 0;
   if (!m->embed.ok()) return "model.embed_tokens";
   if (!m->final_norm) return "model.norm.weight";
-  if (!m->cfg.tie_word_embeddings && !m->lm_head.ok()) return "lm_head";
+  if ((!m->cfg.tie_word_embeddings || m->cfg.tp_size > 1) && !m->lm_head.ok())
+    return m->cfg.tp_size > 1 ? "lm_head (this rank's vocabulary rows; tied models bind a slice of the embedding)"
+                              : "lm_head";
   for (size_t i = 0; i < m->layers.size(); ++i) {
     const Layer& L = m->layers[i];
     std::string p = "model.layers." + std::to_string(i) + ".";
@@ -223,6 +232,65 @@ static GemvSeg seg_of(const Linear& l, int rows, bf16* y) {
   return s;
 }
 
+// vgather [tp][R][Vl] (rank-major, as the all-gather leaves it) -> out [R][tp * Vl]
+__global__ void vocab_unshard_kernel(const bf16* __restrict__ g, int tp, int R, int Vl, bf16* __restrict__ out) {
+  const int64_t n = int64_t(tp) * R * Vl;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t j = i % Vl, rr = (i / Vl) % R, k = i / (int64_t(Vl) * R);
+    out[rr * (int64_t(tp) * Vl) + k * Vl + j] = g[i];
+  }
+}
+
+// Sum the fp32 partials of every rank and add them to the residual stream.
+static int reduce_into_h(Model* m, int L, cudaStream_t st) {
+  const int64_t n = int64_t(L) * m->cfg.hidden_size;
+  int rc = comm_allreduce_f32(m->comm, m->hf, n, st);
+  if (rc) return rc;
+  return residual_add_f32_launch(m->h, m->hf, n, st);
+}
+
+// Final norm + lm_head of `rows` tokens starting at hidden row `h0`; under
+// tensor parallelism each rank computes its vocabulary rows and the shards
+// are gathered, so `out` ([rows, V]) is complete on every rank.
+static int head_rows(Model* m, const Linear& head, int h0, int rows, bf16* out, cudaStream_t st) {
+  const m5_model_cfg& c = m->cfg;
+  const int H = c.hidden_size, V = c.vocab_size, tp = c.tp_size;
+  GemvArgs hd{};
+  hd.ldx = H;
+  hd.K = H;
+  hd.nseg = 1;
+  hd.norm_w = m->final_norm;
+  hd.eps = c.rms_norm_eps;
+  attach(m, hd);
+  if (tp == 1) {
+    hd.x = m->h + size_t(h0) * H;
+    hd.ldy = V;
+    hd.total_rows = V;
+    hd.seg[0] = seg_of(head, V, out);
+    return linear_auto(m, hd, rows, EPI_STORE, st);
+  }
+  for (int r0 = 0; r0 < rows; r0 += m->v_rows) {
+    const int R = std::min(m->v_rows, rows - r0);
+    hd.x = m->h + size_t(h0 + r0) * H;
+    hd.ldy = m->Vl;
+    hd.total_rows = m->Vl;
+    hd.seg[0] = seg_of(head, m->Vl, m->vpart);
+    int rc = linear_auto(m, hd, R, EPI_STORE, st);
+    if (rc) return rc;
+    if ((rc = comm_allgather_bf16(m->comm, m->vpart, m->vgather, int64_t(R) * m->Vl, st))) return rc;
+    bf16* dst = out + size_t(r0) * V;
+    if (R == 1) {
+      M5_CUDA(cudaMemcpyAsync(dst, m->vgather, size_t(tp) * m->Vl * sizeof(bf16), cudaMemcpyDeviceToDevice, st));
+    } else {
+      const int64_t n = int64_t(tp) * R * m->Vl;
+      const int blocks = (int)std::min<int64_t>((n + 255) / 256, sm_count() * 8);
+      vocab_unshard_kernel<<<blocks, 256, 0, st>>>(m->vgather, tp, R, m->Vl, dst);
+      M5_LAUNCH_CHECK("vocabulary gather launch");
+    }
+  }
+  return M5_OK;
+}
+
 __global__ void add_len_kernel(int32_t* d_len, int L) {
   pdl_wait();
   pdl_launch_dependents();
@@ -302,7 +370,12 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     o.ldy = H;
     o.total_rows = H;
     attach(m, o);
-    if ((rc = linear_auto(m, o, L, EPI_RESIDUAL, st))) return rc;
+    if (c.tp_size > 1) {  // this rank's heads give a partial sum over o_proj's columns
+      o.seg[0].yf = m->hf;
+      if ((rc = linear_auto(m, o, L, EPI_F32, st)) || (rc = reduce_into_h(m, L, st))) return rc;
+    } else if ((rc = linear_auto(m, o, L, EPI_RESIDUAL, st))) {
+      return rc;
+    }
     if (c.num_experts == 0) {
       GemvArgs g{};
       g.x = m->h;
@@ -326,7 +399,12 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       d.ldy = H;
       d.total_rows = H;
       attach(m, d);
-      if ((rc = linear_auto(m, d, L, EPI_RESIDUAL, st))) return rc;
+      if (c.tp_size > 1) {  // this rank's intermediate columns give a partial sum
+        d.seg[0].yf = m->hf;
+        if ((rc = linear_auto(m, d, L, EPI_F32, st)) || (rc = reduce_into_h(m, L, st))) return rc;
+      } else if ((rc = linear_auto(m, d, L, EPI_RESIDUAL, st))) {
+        return rc;
+      }
     } else {
       // router logits of RMSNorm(h), top-k, then the routed experts
       GemvArgs g{};
@@ -361,32 +439,24 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       me.eps = c.rms_norm_eps;
       me.act = m->act;
       me.h = m->h;
-      if ((rc = moe_launch(me, st))) return rc;
+      if (c.ep_size > 1) {  // this rank's experts give a partial sum
+        me.partial = m->hf;
+        if ((rc = moe_launch(me, st)) || (rc = reduce_into_h(m, L, st))) return rc;
+      } else if ((rc = moe_launch(me, st))) {
+        return rc;
+      }
     }
   }
   // final norm + lm_head (+ argmax)
-  const Linear& head = c.tie_word_embeddings ? m->embed : m->lm_head;
+  const Linear& head = (c.tie_word_embeddings && c.tp_size == 1) ? m->embed : m->lm_head;
   const int V = c.vocab_size;
-  GemvArgs hd{};
-  hd.ldx = H;
-  hd.K = H;
-  hd.nseg = 1;
-  hd.ldy = V;
-  hd.total_rows = V;
-  hd.norm_w = m->final_norm;
-  hd.eps = c.rms_norm_eps;
-  attach(m, hd);
   bf16* last_row = nullptr;
   if (logits_mode == M5_LOGITS_ALL) {
-    hd.x = m->h;
-    hd.seg[0] = seg_of(head, V, (bf16*)logits);
-    if ((rc = linear_auto(m, hd, L, EPI_STORE, st))) return rc;
+    if ((rc = head_rows(m, head, 0, L, (bf16*)logits, st))) return rc;
     last_row = (bf16*)logits + size_t(L - 1) * V;
   } else if (logits_mode == M5_LOGITS_LAST || d_argmax) {
-    hd.x = m->h + size_t(L - 1) * H;
     last_row = logits_mode == M5_LOGITS_LAST ? (bf16*)logits : m->logits_last;
-    hd.seg[0] = seg_of(head, V, last_row);
-    if ((rc = linear_tokens(hd, 1, EPI_STORE, st))) return rc;
+    if ((rc = head_rows(m, head, L - 1, 1, last_row, st))) return rc;
   }
   if (d_argmax && last_row) {
     if ((rc = argmax_launch(last_row, V, d_argmax, m->argmax_scratch, st))) return rc;
@@ -615,10 +685,19 @@ extern "C" int m5_model_create(const m5_model_cfg* cfg, void** out) {
     }
     m->I = c.intermediate_size / tp;
   }
-  if (tp > 1 || ep > 1) {
+  if (c.num_experts > 0 && tp > 1) {
     delete m;
-    return fail(M5_ERR_UNSUPPORTED, "m5_model_create: multi-rank models need m5_model_set_comm (not in this build)");
+    return fail(M5_ERR_UNSUPPORTED, "m5_model_create: MoE models split experts (ep_size), not heads (tp_size)");
   }
+  if (c.num_experts == 0 && ep > 1) {
+    delete m;
+    return fail(M5_ERR_INVALID, "m5_model_create: ep_size > 1 needs a MoE model");
+  }
+  if (c.vocab_size % tp) {
+    delete m;
+    return fail(M5_ERR_INVALID, "m5_model_create: vocab_size not divisible by tp_size");
+  }
+  m->Vl = c.vocab_size / tp;
   m->layers.resize(c.num_layers);
   *out = m;
   return M5_OK;
@@ -646,6 +725,19 @@ extern "C" int m5_model_check(void* model) {
   std::string miss = missing(m);
   if (!miss.empty()) return fail(M5_ERR_STATE, "model tensor not bound: " + miss);
   if (!m->rope_set) return fail(M5_ERR_STATE, "model RoPE table not set (m5_model_set_rope)");
+  if ((m->cfg.tp_size > 1 || m->cfg.ep_size > 1) && !m->comm)
+    return fail(M5_ERR_STATE, "multi-rank model has no communicator (m5_model_set_comm)");
+  return M5_OK;
+}
+
+extern "C" int m5_model_set_comm(void* model, void* comm) {
+  M5_CHECK_ARG(model && comm, "m5_model_set_comm: null argument");
+  Model* m = (Model*)model;
+  const int world = std::max(m->cfg.tp_size, m->cfg.ep_size);
+  const int rank = m->cfg.tp_size > 1 ? m->cfg.tp_rank : m->cfg.ep_rank;
+  if (comm_size(comm) != world || comm_rank(comm) != rank)
+    return fail(M5_ERR_INVALID, "m5_model_set_comm: communicator size/rank do not match the model's shard");
+  m->comm = comm;
   return M5_OK;
 }
 
@@ -680,7 +772,10 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
                           size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,
                           part, argmax_scratch_bytes(), gemv_mma_scratch_bytes(mrows16),
-                          T >= kGemmMinTokens ? T * H * 2 : 0, gxs};
+                          T >= kGemmMinTokens ? T * H * 2 : 0, gxs,
+                          (c.tp_size > 1 || c.ep_size > 1) ? T * H * 4 : 0,
+                          c.tp_size > 1 ? std::min<size_t>(T, 16) * m->Vl * 2 : 0,
+                          c.tp_size > 1 ? size_t(c.tp_size) * std::min<size_t>(T, 16) * m->Vl * 2 : 0};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -711,6 +806,10 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->xn = sizes[12] ? (bf16*)carve(p, sizes[12]) : nullptr;
   m->gxs = sizes[13] ? (bf16*)carve(p, sizes[13]) : nullptr;
   m->gxs_bytes = sizes[13];
+  m->hf = sizes[14] ? (float*)carve(p, sizes[14]) : nullptr;
+  m->vpart = sizes[15] ? (bf16*)carve(p, sizes[15]) : nullptr;
+  m->vgather = sizes[16] ? (bf16*)carve(p, sizes[16]) : nullptr;
+  m->v_rows = (int)std::min<size_t>(T, 16);
   m->max_tokens = max_tokens;
   return M5_OK;
 }
@@ -726,6 +825,8 @@ extern "C" int m5_forward(void* model, const m5_layer_kv* kv, int32_t* d_len, co
   std::string miss = missing(m);
   if (!miss.empty()) return fail(M5_ERR_STATE, "model tensor not bound: " + miss);
   if (!m->rope_set) return fail(M5_ERR_STATE, "model RoPE table not set");
+  if ((m->cfg.tp_size > 1 || m->cfg.ep_size > 1) && !m->comm)
+    return fail(M5_ERR_STATE, "multi-rank model has no communicator (m5_model_set_comm)");
   for (int i = 0; i < m->cfg.num_layers; ++i) {
     const m5_layer_kv& l = kv[i];
     if (!l.k || !l.v || l.capacity <= 0) return fail(M5_ERR_INVALID, "m5_forward: cache layer " + std::to_string(i));

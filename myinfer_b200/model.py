@@ -167,7 +167,9 @@ def rope_inv_freq(dims: int, base: float, factor: float = 1.0, native: int = 327
 
 class Model:
     def __init__(self, args: ModelArgs, weights: Dict[str, torch.Tensor], device="cuda", max_tokens: int = 2048,
-                 tp_size: int = 1, tp_rank: int = 0, ep_size: int = 1, ep_rank: int = 0):
+                 tp_size: int = 1, tp_rank: int = 0, ep_size: int = 1, ep_rank: int = 0, comm=None):
+        """``weights``: this rank's shard (``distributed.shard_weights``) when
+        tp_size or ep_size > 1, with ``comm`` the rank's ``Communicator``."""
         if args.head_dim != 128:
             raise ValueError("head_dim must be 128")
         self.args = args
@@ -194,6 +196,11 @@ class Model:
             call("m5_model_bind", self._h, name.encode(), t.data_ptr())
         self.rope = _RoPE(args.head_dim, args.rope_theta)
         self.set_rope(1.0)
+        self.comm = comm
+        if tp_size > 1 or ep_size > 1:
+            if comm is None:
+                raise ValueError("a multi-rank model needs a Communicator")
+            call("m5_model_set_comm", self._h, comm.handle)
         self.max_tokens = 0
         self.reserve(max_tokens)
         call("m5_model_check", self._h)

@@ -1,0 +1,137 @@
+"""Multi-GPU host logic on CPU: weight shards (tensor / expert parallel) and the
+communicator id exchange over a world-size-2 gloo group."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from myinfer_b200.distributed import Communicator, shard_weights
+from myinfer_b200.model import ModelArgs
+from oracle import model as om
+from oracle.quant import affine_dequantize
+
+TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+            head_dim=128, intermediate_size=1024, vocab_size=4096, tie_word_embeddings=True,
+            max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+TINY_MOE = dict(TINY, model_type="qwen3_moe", num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256,
+                norm_topk_prob=True, intermediate_size=0, tie_word_embeddings=False)
+
+
+def _host(cfg):
+    w = om.generate_weights(om.Config.from_dict(cfg), seed=1)
+    out = {}
+    for k, v in w.items():
+        out[k] = torch.from_numpy(v.view(np.int32) if v.dtype == np.uint32 else v.view(np.int16))
+    return out
+
+
+def _deq(w, name):
+    return affine_dequantize(w[name + ".weight"].numpy().view(np.uint32), w[name + ".scales"].numpy().view(np.uint16),
+                             w[name + ".biases"].numpy().view(np.uint16), 64, 4).astype(np.float64)
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_tensor_parallel_shards_recompose(tp):
+    args = ModelArgs.from_dict(TINY)
+    full = _host(TINY)
+    shards = [shard_weights(full, args, tp_size=tp, tp_rank=r) for r in range(tp)]
+    p = "model.layers.1."
+    for name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "mlp.gate_proj", "mlp.up_proj"):
+        for suf in (".weight", ".scales", ".biases"):
+            cat = torch.cat([s[p + name + suf] for s in shards], dim=0)
+            assert torch.equal(cat, full[p + name + suf]), name
+    for name in ("self_attn.o_proj", "mlp.down_proj"):
+        for suf in (".weight", ".scales", ".biases"):
+            cat = torch.cat([s[p + name + suf] for s in shards], dim=-1)
+            assert torch.equal(cat, full[p + name + suf]), name
+    # tied embeddings: every rank binds its vocabulary rows of the embedding as lm_head
+    head = torch.cat([s["lm_head.weight"] for s in shards], dim=0)
+    assert torch.equal(head, full["model.embed_tokens.weight"])
+    assert all(torch.equal(s["model.embed_tokens.weight"], full["model.embed_tokens.weight"]) for s in shards)
+    assert all(torch.equal(s[p + "self_attn.q_norm.weight"], full[p + "self_attn.q_norm.weight"]) for s in shards)
+
+
+def test_column_shards_sum_to_the_full_product():
+    """o_proj / down split along K: the per-rank partial products add up to x @ W^T."""
+    args = ModelArgs.from_dict(TINY)
+    full = _host(TINY)
+    tp = 2
+    name = "model.layers.0.mlp.down_proj"
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((3, args.intermediate_size))
+    ref = x @ _deq(full, name).T
+    parts = 0
+    k = args.intermediate_size // tp
+    for r in range(tp):
+        s = shard_weights(full, args, tp_size=tp, tp_rank=r)
+        parts = parts + x[:, r * k:(r + 1) * k] @ _deq(s, name).T
+    np.testing.assert_allclose(parts, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_expert_parallel_shards():
+    args = ModelArgs.from_dict(TINY_MOE)
+    full = _host(TINY_MOE)
+    ep = 4
+    shards = [shard_weights(full, args, ep_size=ep, ep_rank=r) for r in range(ep)]
+    p = "model.layers.0.mlp."
+    for name in ("switch_mlp.gate_proj", "switch_mlp.up_proj", "switch_mlp.down_proj"):
+        cat = torch.cat([s[p + name + ".weight"] for s in shards], dim=0)
+        assert torch.equal(cat, full[p + name + ".weight"])
+        assert shards[1][p + name + ".scales"].shape[0] == args.num_experts // ep
+    # router and attention replicated
+    for s in shards:
+        assert torch.equal(s[p + "gate.weight"], full[p + "gate.weight"])
+        assert torch.equal(s["model.layers.0.self_attn.q_proj.weight"], full["model.layers.0.self_attn.q_proj.weight"])
+
+
+def test_shard_errors():
+    args = ModelArgs.from_dict(TINY)
+    full = _host(TINY)
+    with pytest.raises(ValueError):
+        shard_weights(full, args, tp_size=3, tp_rank=0)  # 8 heads over 3 ranks
+    with pytest.raises(ValueError):
+        shard_weights(full, args, ep_size=2, ep_rank=0)  # dense model
+    moe = ModelArgs.from_dict(TINY_MOE)
+    with pytest.raises(ValueError):
+        shard_weights(_host(TINY_MOE), moe, tp_size=2, tp_rank=0)
+
+
+def _exchange_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from myinfer_b200 import _lib
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    seen = {}
+
+    def fake_call(name, *a):
+        if name == "m5_comm_unique_id":
+            a[0].raw = bytes(range(128))
+        elif name == "m5_comm_init":
+            seen["id"] = bytes(a[0].raw[:128])
+            seen["world"], seen["rank"] = a[2], a[3]
+            a[4]._obj.value = 1234 + rank
+        return 0
+
+    _lib.call = fake_call
+    c = Communicator(world, rank)
+    q.put((rank, seen["id"] == bytes(range(128)), seen["world"], seen["rank"], c.handle.value))
+    c.handle = None
+    dist.destroy_process_group()
+
+
+def test_communicator_id_exchange_gloo():
+    """Rank 0's id reaches every rank through torch.distributed (gloo, 2 ranks)."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 200
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == [(0, True, 2, 0, 1234), (1, True, 2, 1, 1235)]

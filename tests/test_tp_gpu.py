@@ -1,0 +1,85 @@
+"""Tensor-parallel (dense) and expert-parallel (MoE) decode on 2 GPUs against
+the same model on one GPU: the ranks' fp32 partial sums are all-reduced, so
+logits agree to fp32 summation-order noise and greedy tokens are identical.
+Skipped with fewer than two GPUs."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=2,
+            head_dim=128, intermediate_size=1024, vocab_size=4096, tie_word_embeddings=True,
+            max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+TINY_MOE = dict(TINY, model_type="qwen3_moe", num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
+                norm_topk_prob=True, intermediate_size=0, tie_word_embeddings=False)
+
+
+def _run(cfg, rank, world, prompt, n, prefill_step):
+    from myinfer_b200.cache import make_prompt_cache
+    from myinfer_b200.distributed import Communicator, shard_weights
+    from myinfer_b200.generate import generate_step
+    from myinfer_b200.model import Model, ModelArgs, upload_weights
+    from oracle import model as om
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    args = ModelArgs.from_dict(cfg)
+    full = upload_weights(om.generate_weights(om.Config.from_dict(cfg), 3), dev)
+    moe = args.num_experts > 0
+    comm = None
+    if world > 1:
+        comm = Communicator(world, rank)
+        kw = dict(ep_size=world, ep_rank=rank) if moe else dict(tp_size=world, tp_rank=rank)
+        w = shard_weights(full, args, **kw)
+    else:
+        kw, w = {}, full
+    model = Model(args, w, dev, max_tokens=64, comm=comm, **kw)
+    out = list(generate_step(prompt, model, n, prompt_cache=make_prompt_cache(model), prefill_step_size=prefill_step,
+                             kv_bits=8, quantized_kv_start=0, return_logits=True))
+    toks = [t for t, _ in out]
+    logits = torch.stack([l.float().cpu() for _, l in out])
+    del model
+    if comm is not None:
+        comm.close()
+    return toks, logits
+
+
+def _worker(rank, world, port, cfg, prompt, n, step, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        q.put((rank, _run(cfg, rank, world, prompt, n, step)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("cfg", [TINY, TINY_MOE], ids=["tp2-dense", "ep2-moe"])
+@pytest.mark.parametrize("step", [8, 32], ids=["gemv-prefill", "gemm-prefill"])
+def test_two_rank_matches_one(cfg, step):
+    import torch.multiprocessing as mp
+    prompt = np.random.default_rng(4).integers(0, cfg["vocab_size"], 40).tolist()
+    n = 8
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29400 + os.getpid() % 500
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, cfg, prompt, n, step, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    ref_toks, ref_logits = _run(cfg, 0, 1, prompt, n, step)
+    for r in (0, 1):
+        toks, logits = res[r]
+        cos = torch.nn.functional.cosine_similarity(logits, ref_logits, dim=-1)
+        assert cos.min().item() > 0.9999, cos.tolist()
+        assert toks == ref_toks
