@@ -70,6 +70,8 @@ struct Seg {
 
 struct Params {
   int M, K, G, C;      // tokens, reduction length, scale groups, bias blocks (ceil(G / 32))
+  int vec_sb;          // G % 8 == 0: 16-byte scale loads and TMA bias tiles (else scalar global loads)
+  const bf16* bias[3]; // per segment, for the scalar bias path
   int nseg;
   Seg seg[3];
   int64_t ldy;
@@ -281,9 +283,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             }
           } else {
             const int c = b - p.G;
-            mbar_arrive_expect_tx(&full[s], X_BYTES + BR * 64);
+            mbar_arrive_expect_tx(&full[s], X_BYTES + (p.vec_sb ? BR * 64 : 0));
             tma_load_2d(x_dst, &maps.xs, c * 64, m0, &full[s]);
-            if (EPI == EPI_SWIGLU) {
+            if (!p.vec_sb) {
+              // biases are read by the dequant warps straight from global memory
+            } else if (EPI == EPI_SWIGLU) {
 #pragma unroll
               for (int qq = 0; qq < 4; ++qq) {
                 tma_load_2d(w_dst + (32 * qq) * 64, &maps.b[0], c * 32, row0 + 16 * qq, &full[s]);
@@ -351,8 +355,18 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
     int cur_tile = -1, si = 0, row0 = 0;
     const uint4* srow = nullptr;
+    const bf16* srow16 = nullptr;  // scalar path (G % 8 != 0)
+    const bf16* brow16 = nullptr;
     int cur_w = -2;
     uint4 s_cur = make_uint4(0, 0, 0, 0), s_nxt = s_cur;
+    // 8 scales of window w (16-byte load when rows are 16-byte aligned)
+    auto load_win = [&](int w) -> uint4 {
+      if (p.vec_sb) return srow[w];
+      uint32_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = (8 * w + j < p.G) ? __bfloat16_as_ushort(srow16[8 * w + j]) : 0u;
+      return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+    };
     for (int idx = 0; idx < my_blocks; ++idx) {
       const int tl = idx / nblk, b = idx % nblk;
       if (tl != cur_tile) {
@@ -361,15 +375,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         int sg, grow;
         row_of<EPI>(p, si, row0, r, sg, grow);
         srow = reinterpret_cast<const uint4*>(p.seg[sg].s + size_t(grow) * p.G);
+        srow16 = p.seg[sg].s + size_t(grow) * p.G;
+        brow16 = p.bias[sg] + size_t(grow) * p.G;
         cur_w = -2;
       }
       uint32_t s2 = 0;
       if (b < p.G) {
         const int w = b >> 3;
         if (w != cur_w) {
-          s_cur = (w == cur_w + 1) ? s_nxt : srow[w];
+          s_cur = (w == cur_w + 1) ? s_nxt : load_win(w);
           cur_w = w;
-          if (8 * (w + 1) < p.G) s_nxt = srow[w + 1];
+          if (8 * (w + 1) < p.G) s_nxt = load_win(w + 1);
         }
         s2 = pick_bf16_pair(s_cur, b & 7);
       }
@@ -390,15 +406,25 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         tmem_st16(lane_base + col, hi);
         tmem_st16(lane_base + col + 32u, nlo);
       } else {
-        const uint4* bsrc = reinterpret_cast<const uint4*>(w_src + r * 64);
         uint32_t v[16];
+        if (p.vec_sb) {
+          const uint4* bsrc = reinterpret_cast<const uint4*>(w_src + r * 64);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 c = bsrc[i];
-          v[4 * i + 0] = c.x;
-          v[4 * i + 1] = c.y;
-          v[4 * i + 2] = c.z;
-          v[4 * i + 3] = c.w;
+          for (int i = 0; i < 4; ++i) {
+            const uint4 c = bsrc[i];
+            v[4 * i + 0] = c.x;
+            v[4 * i + 1] = c.y;
+            v[4 * i + 2] = c.z;
+            v[4 * i + 3] = c.w;
+          }
+        } else {
+          const int g0 = 32 * (b - p.G);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t lo = (g0 + 2 * i < p.G) ? __bfloat16_as_ushort(brow16[g0 + 2 * i]) : 0u;
+            const uint32_t hi = (g0 + 2 * i + 1 < p.G) ? __bfloat16_as_ushort(brow16[g0 + 2 * i + 1]) : 0u;
+            v[i] = lo | (hi << 16);
+          }
         }
         tmem_st16(lane_base + col, v);  // A = [b | b] against B = [xs_hi | xs_lo]
       }
@@ -543,7 +569,7 @@ size_t gemm_tc_xs_bytes(int M, int K) {
 }
 
 bool gemm_tc_eligible(const GemvArgs& a, int M, int epi) {
-  if (M < 1 || a.K % 512 || a.norm_w || a.ldx % 8 || a.nseg < 1 || a.nseg > 3) return false;
+  if (M < 1 || a.K % 64 || a.norm_w || a.ldx % 8 || a.nseg < 1 || a.nseg > 3) return false;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!al(a.x)) return false;
   for (int i = 0; i < a.nseg; ++i) {
@@ -579,11 +605,13 @@ int gemm_tc_launch(const GemvArgs& a, int M, int epi, bf16* xs, size_t xs_bytes,
   p.K = a.K;
   p.G = a.K / 64;
   p.C = (p.G + 31) / 32;
+  p.vec_sb = (p.G % 8) == 0;
   p.nseg = a.nseg;
   p.ldy = a.ldy;
   int rows = 0;
   for (int i = 0; i < a.nseg; ++i) {
     p.seg[i].s = a.seg[i].s;
+    p.bias[i] = a.seg[i].b;
     p.seg[i].rows = a.seg[i].rows;
     p.seg[i].y = a.seg[i].y;
     p.seg[i].yf = a.seg[i].yf;
@@ -603,7 +631,7 @@ int gemm_tc_launch(const GemvArgs& a, int M, int epi, bf16* xs, size_t xs_bytes,
   for (int i = 0; i < a.nseg && !rc; ++i) {
     rc = gtc_map(&m.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, a.seg[i].w, a.K / 8, a.seg[i].rows, a.K / 2, 8, box_rows,
                  CU_TENSOR_MAP_SWIZZLE_NONE, "weights");
-    if (!rc)
+    if (!rc && p.vec_sb)
       rc = gtc_map(&m.b[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.seg[i].b, p.G, a.seg[i].rows, size_t(p.G) * 2, 32,
                    box_rows, CU_TENSOR_MAP_SWIZZLE_NONE, "biases");
   }

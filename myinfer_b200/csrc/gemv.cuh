@@ -67,7 +67,7 @@ int gemv_tma_launch(const GemvArgs& a, int MT, int epi, cudaStream_t stream);
 int gemv_tma_error(int reset);
 
 // Prefill tensor-core dequant-GEMM (gemm_tc.cu, tcgen05 + TMEM): any M >= 1,
-// K % 512 == 0, no fused norm, segments of 128-row multiples (SwiGLU: 64).
+// K % 64 == 0, no fused norm, segments of 128-row multiples (SwiGLU: 64).
 // `xs` is caller scratch of gemm_tc_xs_bytes(M, K) bytes (per-token group sums).
 bool gemm_tc_eligible(const GemvArgs& a, int M, int epi);
 size_t gemm_tc_xs_bytes(int M, int K);

@@ -243,10 +243,7 @@ __global__ void vocab_unshard_kernel(const bf16* __restrict__ g, int tp, int R, 
 
 // Sum the fp32 partials of every rank and add them to the residual stream.
 static int reduce_into_h(Model* m, int L, cudaStream_t st) {
-  const int64_t n = int64_t(L) * m->cfg.hidden_size;
-  int rc = comm_allreduce_f32(m->comm, m->hf, n, st);
-  if (rc) return rc;
-  return residual_add_f32_launch(m->h, m->hf, n, st);
+  return comm_allreduce_residual(m->comm, m->hf, m->h, int64_t(L) * m->cfg.hidden_size, st);
 }
 
 // Final norm + lm_head of `rows` tokens starting at hidden row `h0`; under
@@ -507,9 +504,10 @@ extern "C" int m5_device_status(int* code, int reset) {
   const int at = attn_mma_error(reset);
   const int gm = gemm_tc_error(reset);
   const int ap = attn_pf_error(reset);
-  if (g < 0 || gt < 0 || at < 0 || gm < 0 || ap < 0)
+  const int ar = comm_ar_error(reset);
+  if (g < 0 || gt < 0 || at < 0 || gm < 0 || ap < 0 || ar < 0)
     return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error words");
-  *code = g | gt | at | gm | ap;
+  *code = g | gt | at | gm | ap | ar;
   return M5_OK;
 }
 

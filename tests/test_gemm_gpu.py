@@ -29,7 +29,8 @@ def _check(y, ref):
 
 
 @pytest.mark.parametrize("M", [16, 77, 128, 300])
-@pytest.mark.parametrize("N,K", [(128, 512), (1024, 1024), (384, 5120), (256, 3072), (128, 25600)])
+@pytest.mark.parametrize("N,K", [(128, 512), (1024, 1024), (384, 5120), (256, 3072), (128, 25600),
+                                 (256, 3200), (128, 576), (384, 6400)])
 def test_gemm_matches_reference(M, N, K):
     from myinfer_b200 import ops
     (wq, s, b), wd = _weights(N, K, seed=N * 3 + K)
