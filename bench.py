@@ -177,7 +177,7 @@ def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0) ->
 
 
 # ----------------------------------------------------------------- GPU leg
-def gemv_roofline(model, cfg, peak_gbs) -> dict:
+def gemv_roofline(model, cfg, peak_gbs, peak_src="measured") -> dict:
     """Dominant kernel (gate/up dequant-GEMV with SwiGLU... measured as the
     plain projection GEMVs of every layer) timed alone with CUDA events."""
     import torch
@@ -215,8 +215,12 @@ def gemv_roofline(model, cfg, peak_gbs) -> dict:
     N, K = cfg["intermediate_size"], H
     alg = N * K * 0.5625 + K * 2 + N * 2
     ach = alg / (ms * 1e-3) / 1e9
-    return {"bound": "hbm", "kernel": "gemv_kernel<1,EPI_STORE> (up_proj 25600x5120 w4g64)", "achieved": round(ach, 1),
-            "peak": peak_gbs, "unit": "GB/s", "frac": round(ach / peak_gbs, 4), "traffic": None,
+    # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel and
+    # shape, from the ncu capture summarised in profiles/gemv_tmap_up_proj_25600x5120.md
+    traffic = 73_846_528 + 1_500_928
+    return {"bound": "hbm", "kernel": "gemv_tmap_kernel<1,EPI_STORE> (up_proj 25600x5120 w4g64, 1 token)",
+            "achieved": round(ach, 1), "peak": peak_gbs, "peak_source": peak_src,
+            "unit": "GB/s", "frac": round(ach / peak_gbs, 4), "traffic": traffic,
             "alg_bytes_per_launch": int(alg), "avg_launch_us": round(ms * 1e3, 2)}
 
 
@@ -333,7 +337,7 @@ def run_gpu(args) -> dict:
     ee.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e_steps
-    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"]) if world == 1 else None
+    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"], peaks["source"]) if world == 1 else None
     per_rank = bytes_tok / world
     par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}" if world > 1 else "single")
     prefill_flops = 2.0 * ctx * (weight_bytes_per_token(cfg) / 0.5625) + 4.0 * a.num_hidden_layers * \

@@ -3,6 +3,7 @@
     python -m myinfer_b200.microbench gemv --n 25600 --k 5120 [--m 1] [--iters 20]
     python -m myinfer_b200.microbench attention --s 32768 --l 1 --bits 8 [--hq 64 --hkv 8]
     python -m myinfer_b200.microbench gemm --m 2048 --n 8192 --k 5120
+    python -m myinfer_b200.microbench step --ctx 32768 --steps 2   # decode steps (profiler range)
 
 ``gemv`` cycles over enough distinct weight matrices that every launch reads
 from HBM (more than L2 in total); ``attention`` is the standalone
@@ -80,6 +81,50 @@ def bench_gemm(m: int, n: int, k: int, iters: int) -> dict:
     return {"kernel": "gemm", "m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(flops / us / 1e6, 1)}
 
 
+def bench_step(ctx: int, steps: int, config: str = "qwen3-32b") -> dict:
+    """Decode steps of the Qwen3-32B-shaped model over a synthetic 8-bit KV
+    cache of `ctx` positions; only the timed steps run inside a CUDA profiler
+    range (cudaProfilerStart/Stop), so `ncu --profile-from-start off` lists
+    exactly the kernels of `steps` decode steps."""
+    from myinfer_b200 import _lib, ops
+    from myinfer_b200.cache import PromptCache, QuantizedKVCache
+    from myinfer_b200.model import Model, ModelArgs, random_weights
+    presets = {"qwen3-32b": dict(model_type="qwen3", hidden_size=5120, num_hidden_layers=64,
+                                 num_attention_heads=64, num_key_value_heads=8, head_dim=128,
+                                 intermediate_size=25600, vocab_size=151936, tie_word_embeddings=False)}
+    a = ModelArgs.from_dict(presets[config])
+    dev = torch.device("cuda")
+    model = Model(a, random_weights(a, 0, dev), dev, max_tokens=8)
+    cache = PromptCache([QuantizedKVCache(a.num_key_value_heads, a.head_dim, dev, 64, 8, capacity=ctx + steps + 8)
+                         for _ in range(a.num_hidden_layers)], dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    for c in cache:  # random N(0,1) K/V at positions [0, ctx)
+        for which in ("k", "v"):
+            x = torch.randn(c.n_kv_heads, ctx, a.head_dim, generator=g, device=dev).to(torch.bfloat16)
+            q, sc, b = ops.quantize(x, 64, 8)
+            tq, ts, tb = (c._kq, c._ks, c._kb) if which == "k" else (c._vq, c._vs, c._vb)
+            tq[0, :, :ctx].copy_(q)
+            ts[0, :, :ctx].copy_(sc)
+            tb[0, :, :ctx].copy_(b)
+        c.offset = ctx
+    tok = torch.tensor([1], dtype=torch.int32, device=dev)
+    for _ in range(2):  # warm: configures every kernel, then rewinds the cache
+        model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
+        for c in cache:
+            c.offset -= 1
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()
+    start.record()
+    for _ in range(steps):
+        model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
+    end.record()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    return {"kernel": "decode_step", "config": config, "ctx": ctx, "steps": steps,
+            "ms_per_step_eager": round(start.elapsed_time(end) / steps, 3)}
+
+
 def bench_attention(s: int, l: int, bits: int, hq: int, hkv: int, iters: int) -> dict:
     from myinfer_b200 import ops
     from myinfer_b200.attention import blocked_quantized_sdpa
@@ -114,6 +159,9 @@ def main():
     g.add_argument("--k", type=int, default=5120)
     g.add_argument("--m", type=int, default=1)
     g.add_argument("--iters", type=int, default=20)
+    st = sub.add_parser("step")
+    st.add_argument("--ctx", type=int, default=32768)
+    st.add_argument("--steps", type=int, default=2)
     gm = sub.add_parser("gemm")
     gm.add_argument("--m", type=int, default=2048)
     gm.add_argument("--n", type=int, default=8192)
@@ -131,6 +179,8 @@ def main():
         r = bench_gemv(args.n, args.k, args.m, args.iters)
     elif args.cmd == "gemm":
         r = bench_gemm(args.m, args.n, args.k, args.iters)
+    elif args.cmd == "step":
+        r = bench_step(args.ctx, args.steps)
     else:
         r = bench_attention(args.s, args.l, args.bits, args.hq, args.hkv, args.iters)
     print(json.dumps(r), flush=True)
