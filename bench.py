@@ -197,7 +197,8 @@ def gemv_roofline(model, cfg, peak_gbs, peak_src="measured") -> dict:
     s = torch.cuda.Stream(device=model.device)
     s.wait_stream(torch.cuda.current_stream())
     graph = torch.cuda.CUDAGraph()
-    outs = [torch.empty(1, cfg["intermediate_size"], dtype=torch.bfloat16, device=model.device) for _ in names]
+    N = w[names[0] + ".weight"].shape[0]  # this rank's rows (intermediate_size / tp under tensor parallelism)
+    outs = [torch.empty(1, N, dtype=torch.bfloat16, device=model.device) for _ in names]
     with torch.cuda.stream(s):
         graph.capture_begin()
         for n, o in zip(names, outs):
@@ -212,13 +213,13 @@ def gemv_roofline(model, cfg, peak_gbs, peak_src="measured") -> dict:
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / len(names)
-    N, K = cfg["intermediate_size"], H
+    K = H
     alg = N * K * 0.5625 + K * 2 + N * 2
     ach = alg / (ms * 1e-3) / 1e9
     # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel and
     # shape, from the ncu capture summarised in profiles/gemv_tmap_up_proj_25600x5120.md
-    traffic = 73_846_528 + 1_500_928
-    return {"bound": "hbm", "kernel": "gemv_tmap_kernel<1,EPI_STORE> (up_proj 25600x5120 w4g64, 1 token)",
+    traffic = (73_846_528 + 1_500_928) * N // 25600 if N == cfg["intermediate_size"] else None
+    return {"bound": "hbm", "kernel": f"gemv_tmap_kernel<1,EPI_STORE> (up_proj {N}x{K} w4g64, 1 token)",
             "achieved": round(ach, 1), "peak": peak_gbs, "peak_source": peak_src,
             "unit": "GB/s", "frac": round(ach / peak_gbs, 4), "traffic": traffic,
             "alg_bytes_per_launch": int(alg), "avg_launch_us": round(ms * 1e3, 2)}
@@ -337,7 +338,7 @@ def run_gpu(args) -> dict:
     ee.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e_steps
-    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"], peaks["source"]) if world == 1 else None
+    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"], peaks["source"])
     per_rank = bytes_tok / world
     par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}" if world > 1 else "single")
     prefill_flops = 2.0 * ctx * (weight_bytes_per_token(cfg) / 0.5625) + 4.0 * a.num_hidden_layers * \
