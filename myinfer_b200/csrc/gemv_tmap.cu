@@ -11,9 +11,9 @@
 //     biases) into a 5-stage ring (~45 KB in flight per CTA, several CTAs per
 //     SM), no registers involved;
 //   * four consumer warps each take four 64-column scale groups of every unit
-//     and run the same mma.sync m16n8k16 bf16 dot products as gemv_mma.cu:
-//     codes -> (128 + q) bf16 pairs with one LOP3 per two codes, per-group
-//     fold  s * D + (b - 128 s) * sum(x);
+//     and run mma.sync m16n8k16 fp16 dot products of the exact codes q against
+//     the activations scaled by a per-token power of two, per-group fold
+//     s * D + b * sum(x);
 //   * units are dealt to CTAs as equal contiguous ranges (stream-K); partial
 //     tile sums go through fp32 atomics into a zeroed scratch and the warp that
 //     completes a tile runs the epilogue and re-zeroes the scratch.
@@ -58,16 +58,27 @@ __device__ __forceinline__ uint32_t tp_hfma2(uint32_t a, uint32_t b, uint32_t c)
   return d;
 }
 
+__device__ __forceinline__ uint32_t tp_hsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // 8 codes of one word -> fp16 pairs (q0,q4) (q1,q5) (q2,q6) (q3,q7), exact.
-// A nibble at bits 0-3 of a half becomes 1024 + q under the fp16 exponent of
-// 1024 (0x6400); one at bits 4-7 becomes 1024 + 16 q.  The integer pipe does
-// four masks and one shift per word; the offsets come off on the FMA pipe.
+// Under the fp16 exponent of 64 (0x5400) one mantissa step is 1/16, so a code
+// byte placed in a half's low mantissa bits reads 64 + lo/16 + hi, and its low
+// nibble alone reads 64 + lo/16.  The integer pipe builds those four halves
+// per pair of bytes (three masks, one byte permute: 4 operations per word);
+// the FMA pipe takes hi as their difference and lo = 16 (64 + lo/16) - 1024.
 __device__ __forceinline__ void tp_codes_f16(uint32_t w, uint32_t (&p)[4]) {
-  const uint32_t w8 = w >> 8;
-  p[0] = tp_hfma2((w & 0x000F000Fu) | 0x64006400u, 0x3C003C00u, 0xE400E400u);   // * 1 - 1024
-  p[1] = tp_hfma2((w & 0x00F000F0u) | 0x64006400u, 0x2C002C00u, 0xD400D400u);   // / 16 - 64
-  p[2] = tp_hfma2((w8 & 0x000F000Fu) | 0x64006400u, 0x3C003C00u, 0xE400E400u);
-  p[3] = tp_hfma2((w8 & 0x00F000F0u) | 0x64006400u, 0x2C002C00u, 0xD400D400u);
+  const uint32_t f02 = (w & 0x00FF00FFu) | 0x54005400u;  // bytes 0 and 2
+  const uint32_t l02 = (w & 0x000F000Fu) | 0x54005400u;
+  const uint32_t f13 = __byte_perm(w, 0x54u, 0x4341);     // bytes 1 and 3 under 0x54
+  const uint32_t l13 = f13 & 0xFF0FFF0Fu;
+  p[0] = tp_hfma2(l02, 0x4C004C00u, 0xE400E400u);  // * 16 - 1024
+  p[1] = tp_hsub2(f02, l02);
+  p[2] = tp_hfma2(l13, 0x4C004C00u, 0xE400E400u);
+  p[3] = tp_hsub2(f13, l13);
 }
 
 __device__ __forceinline__ void tp_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -126,7 +137,6 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_launch_dependents();
 
   if (warp == TP_CW) {
     // -------------------------------------------------------------- producer
@@ -139,7 +149,10 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
         const uint32_t par = (it / TP_STAGES) & 1;
         // the ring is full: from here on the consumers gate this warp, and they
         // start only once the previous kernel has finished
-        if (it == TP_STAGES) pdl_wait();
+        if (it == TP_STAGES) {
+          pdl_wait();
+          pdl_launch_dependents();
+        }
         if (!mbar_wait(&empty[st], par ^ 1, &g_gemv_tmap_err)) return;
         mbar_arrive_expect_tx(&full[st], TP_W_STAGE + 2 * TP_SB_STAGE);
         unsigned char* ws = wring + st * TP_W_STAGE;
@@ -166,6 +179,9 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
   // ---------------------------------------------- consumers: stage activations
   float* xinv = red;  // [MT] 2^-e of the fp16 activation scale (red[0..7] is free after staging)
   pdl_wait();         // activations, residual and split-tile scratch come from earlier kernels
+  // The next kernel may launch only now: launched earlier, its CTAs could take
+  // the SM slots this grid's own CTAs still wait for.
+  pdl_launch_dependents();
   stage_frag_bulk<MT, TP_CW * 32, true>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, red, 1, xinv, xbar,
                                         &g_gemv_tmap_err);
 
