@@ -160,30 +160,37 @@ __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t l
   sync();
 }
 
-// Same result as stage_frag<MT, NT, FP16>, with the activation rows (and the
-// norm weight) brought into shared memory by one bulk copy each, so staging
-// costs a single L2 round trip whatever K is.  The raw bf16 row of token t is
-// copied to xf + t * NG * 32: the uint4 of raw 8-element block c sits exactly
-// where the pairs of block c go, so every thread converts its blocks in place.
-// Requirements: x rows and norm_w 16-byte aligned (ldx % 8 == 0), nbuf holds
-// K bf16 when norm_w is set, xbar is an unused mbarrier slot.  Returns false
-// (and records a device error) if the copy did not land in time.
+// The fp16 variant of stage_frag<MT, NT, true> for the TMA-fed GEMV, with the
+// activation rows (and the norm weight) brought into shared memory by one
+// bulk copy each, in two passes over the row:
+//   1. per token, the sum of squares (RMSNorm) and a bound on the largest
+//      staged magnitude, max_i |x_i w_i| * inv (or max_i |x_i|): the power-of-
+//      two scale only has to keep the scaled maximum inside fp16 range, and the
+//      bound is within 2^-7 of the true maximum, so the scaled maximum stays
+//      below 2^15 * 1.01;
+//   2. per 8-element block: normalize and round to bf16 exactly as the model
+//      does, convert the pairs (e0,e4)(e1,e5)(e2,e6)(e3,e7) to fp16 with the
+//      scale, and sum the group (the 8 lanes 8j..8j+7 hold one 64-element
+//      group) with three shuffles.
+// The raw bf16 row of token t is copied to xf + t * NG * 32: the uint4 of raw
+// 8-element block c sits exactly where the pairs of block c go, so every
+// thread converts its blocks in place.  Requirements: x rows and norm_w
+// 16-byte aligned (ldx % 8 == 0), K % 1024 == 0, nbuf holds K bf16 when
+// norm_w is set, xbar is an initialised, unused mbarrier, red has room for
+// 8 + 16 * MT floats.  Returns false (and records a device error) if the copy
+// did not land in time.
 template <int MT, int NT, bool FP16>
 __device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int64_t ldx, int K,
                                                 const bf16* __restrict__ norm_w, float eps, uint32_t* xf,
                                                 uint32_t* nbuf, float* xg, float* red, int bar, float* xinv,
                                                 uint64_t* xbar, int* err) {
+  static_assert(FP16 && NT % 32 == 0 && NT / 32 <= 8, "fp16 staging by whole warps");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NG = K >> 6, K8 = K >> 3;
   auto sync = [&]() {
     if (bar == 0) __syncthreads();
     else asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(NT) : "memory");
   };
-  if (tid == 0) {
-    mbar_init(xbar, 1);
-    fence_mbar_init();
-  }
-  sync();
   if (tid == 0) {
     const uint32_t row = uint32_t(K) * 2u;
     mbar_arrive_expect_tx(xbar, MT * row + (norm_w ? row : 0u));
@@ -192,34 +199,63 @@ __device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int6
     if (norm_w) bulk_g2s(nbuf, norm_w, row, xbar);
   }
   const bool ok = mbar_wait(xbar, 0, err);
-  float amax[MT];
+  const uint4* nw = reinterpret_cast<const uint4*>(nbuf);
+  // ---- pass 1: sum of squares and max |x w| per token
+  // red[0..MT) receives xinv while other threads still read the partials:
+  // the partials live past it
+  float* rs = red + 8;           // [NT/32][MT] sums of squares
+  float* rm = red + 8 + 8 * MT;  // [NT/32][MT] maxima
 #pragma unroll
   for (int t = 0; t < MT; ++t) {
-    amax[t] = 0.f;
-    uint4* blk = reinterpret_cast<uint4*>(xf + size_t(t) * NG * 32);
-    const uint4* nw = reinterpret_cast<const uint4*>(nbuf);
-    float inv = 1.f;
-    if (norm_w) {
-      float ss = 0.f;
-      for (int c = tid; c < K8; c += NT) {
-        const uint4 v = blk[c];
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint4* blk = reinterpret_cast<const uint4*>(xf + size_t(t) * NG * 32);
+    float ss = 0.f, mx = 0.f;
+    for (int c = tid; c < K8; c += NT) {
+      const uint4 v = blk[c];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      if (norm_w) {
+        const uint4 nv = nw[c];
+        const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float a = bf16_lo(w[q]), b = bf16_hi(w[q]);
           ss = fmaf(a, a, fmaf(b, b, ss));
+          mx = fmaxf(mx, fmaxf(fabsf(a * bf16_lo(n[q])), fabsf(b * bf16_hi(n[q]))));
         }
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) red[warp] = ss;
-      sync();
-      float tot = 0.f;
+      } else {
 #pragma unroll
-      for (int w = 0; w < NT / 32; ++w) tot += red[w];
-      inv = __frsqrt_rn(__fadd_rn(tot / float(K), eps));
-      sync();
+        for (int q = 0; q < 4; ++q) mx = fmaxf(mx, fmaxf(fabsf(bf16_lo(w[q])), fabsf(bf16_hi(w[q]))));
+      }
     }
-    for (int c = tid; c < K8; c += NT) {
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if (lane == 0) {
+      rs[warp * MT + t] = ss;
+      rm[warp * MT + t] = mx;
+    }
+  }
+  sync();
+  float inv[MT], sc[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    float tot = 0.f, m = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) {
+      tot += rs[w * MT + t];
+      m = fmaxf(m, rm[w * MT + t]);
+    }
+    inv[t] = norm_w ? __frsqrt_rn(__fadd_rn(tot / float(K), eps)) : 1.f;
+    m *= inv[t];
+    const int E = int((__float_as_uint(m) >> 23) & 0xFFu);
+    const int ex = m > 0.f ? max(-126, min(126, 141 - E)) : 0;
+    sc[t] = __uint_as_float(uint32_t(ex + 127) << 23);
+    if (tid == 0 && xinv) xinv[t] = __uint_as_float(uint32_t(127 - ex) << 23);
+  }
+  // ---- pass 2: normalize, round, convert, group sums (warp-uniform loop)
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    uint4* blk = reinterpret_cast<uint4*>(xf + size_t(t) * NG * 32);
+    for (int c0 = tid - lane; c0 < K8; c0 += NT) {
+      const int c = c0 + lane;
       const uint4 v = blk[c];
       float e[8];
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -233,65 +269,28 @@ __device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int6
         const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          e[2 * q] = rbf(__fmul_rn(bf16_lo(n[q]), rbf(__fmul_rn(e[2 * q], inv))));
-          e[2 * q + 1] = rbf(__fmul_rn(bf16_hi(n[q]), rbf(__fmul_rn(e[2 * q + 1], inv))));
+          e[2 * q] = rbf(__fmul_rn(bf16_lo(n[q]), rbf(__fmul_rn(e[2 * q], inv[t]))));
+          e[2 * q + 1] = rbf(__fmul_rn(bf16_hi(n[q]), rbf(__fmul_rn(e[2 * q + 1], inv[t]))));
         }
       }
-      if (FP16) {
+      float gs = 0.f;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) amax[t] = fmaxf(amax[t], fabsf(e[q]));
-      }
+      for (int q = 0; q < 8; ++q) gs += e[q];
+      gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+      gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+      gs += __shfl_xor_sync(0xffffffffu, gs, 4);
+      if ((lane & 7) == 0) xg[t * NG + (c >> 3)] = gs;
+      const float f = sc[t];
       uint4 o;
-      o.x = uint32_t(__bfloat16_as_ushort(f2bf(e[0]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[4]))) << 16);
-      o.y = uint32_t(__bfloat16_as_ushort(f2bf(e[1]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[5]))) << 16);
-      o.z = uint32_t(__bfloat16_as_ushort(f2bf(e[2]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[6]))) << 16);
-      o.w = uint32_t(__bfloat16_as_ushort(f2bf(e[3]))) | (uint32_t(__bfloat16_as_ushort(f2bf(e[7]))) << 16);
+      __half2 h = __floats2half2_rn(e[0] * f, e[4] * f);
+      o.x = *reinterpret_cast<uint32_t*>(&h);
+      h = __floats2half2_rn(e[1] * f, e[5] * f);
+      o.y = *reinterpret_cast<uint32_t*>(&h);
+      h = __floats2half2_rn(e[2] * f, e[6] * f);
+      o.z = *reinterpret_cast<uint32_t*>(&h);
+      h = __floats2half2_rn(e[3] * f, e[7] * f);
+      o.w = *reinterpret_cast<uint32_t*>(&h);
       blk[c] = o;  // pairs of block c occupy the bytes its raw values came from
-    }
-  }
-  sync();
-  const int total = MT * NG * 4;
-  for (int q0 = tid - lane; q0 < total; q0 += NT) {
-    const int q = q0 + lane;
-    float sum = 0.f;
-    if (q < total) {
-      const uint32_t* p = xf + (q >> 2) * 32 + (q & 3) * 8;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sum += bf16_lo(p[j]) + bf16_hi(p[j]);
-    }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (q < total && (q & 3) == 0) xg[q >> 2] = sum;
-  }
-  if constexpr (FP16) {
-    float* rm = red + 32;  // [NT / 32][MT]
-#pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      const float m = warp_max(amax[t]);
-      if (lane == 0) rm[warp * MT + t] = m;
-    }
-    sync();
-    float sc[MT];
-#pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      float m = 0.f;
-#pragma unroll
-      for (int w = 0; w < NT / 32; ++w) m = fmaxf(m, rm[w * MT + t]);
-      const int E = int((__float_as_uint(m) >> 23) & 0xFFu);
-      const int ex = m > 0.f ? max(-126, min(126, 141 - E)) : 0;
-      sc[t] = __uint_as_float(uint32_t(ex + 127) << 23);
-      if (tid == 0 && xinv) xinv[t] = __uint_as_float(uint32_t(127 - ex) << 23);
-    }
-    const int words = MT * NG * 32;
-    for (int i = tid; i < words; i += NT) {
-      const int t = i / (NG * 32);
-      float f = 1.f;
-#pragma unroll
-      for (int tt = 0; tt < MT; ++tt)
-        if (tt == t) f = sc[tt];
-      const uint32_t w = xf[i];
-      __half2 h = __floats2half2_rn(bf16_lo(w) * f, bf16_hi(w) * f);
-      xf[i] = *reinterpret_cast<uint32_t*>(&h);
     }
   }
   sync();

@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], TP_CW);
     }
+    mbar_init(xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
