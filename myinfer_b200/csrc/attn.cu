@@ -286,53 +286,64 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(D) attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                                                         int nsplit, int Hq, int L, int tokens_major,
-                                                         bf16* __restrict__ out) {
+// Merge of the split-KV partials of one output row (b, h, qi): weights
+// exp(m_s - M) over the splits, out = sum_s w_s o_s / sum_s w_s l_s.  One CTA
+// per (row, 32 output dims): its 8 warps take every 8th split with coalesced
+// 128-byte loads of the partial rows, the split weights are computed once per
+// CTA, and the 8 warp sums are added in shared memory.
+constexpr int CMB_WARPS = 8;
+__global__ void __launch_bounds__(CMB_WARPS * 32) attn_combine_kernel(const float* __restrict__ part_o,
+                                                                       const float* __restrict__ part_ml,
+                                                                       int nsplit, int D, int Hq, int L,
+                                                                       int tokens_major, bf16* __restrict__ out) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t row = blockIdx.x;  // (b * Hq + h) * L + qi
-  const int d = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int d = blockIdx.y * 32 + lane;
   __shared__ float w_s[1024];
-  __shared__ float stat[2];
-  // split weights exp(m_s - M): one thread per split, loads issued in parallel
+  __shared__ float red[CMB_WARPS][33];
+  const float* ml = part_ml + row * nsplit * 2;
   float m = -INFINITY;
-  for (int s = d; s < nsplit; s += D) m = fmaxf(m, part_ml[(row * nsplit + s) * 2]);
+  for (int s = tid; s < nsplit; s += CMB_WARPS * 32) m = fmaxf(m, ml[2 * s]);
   m = warp_max(m);
-  __shared__ float wmax[D / 32];
-  if ((d & 31) == 0) wmax[d >> 5] = m;
+  if (lane == 0) red[warp][32] = m;
   __syncthreads();
-  if (d == 0) {
-    float M = -INFINITY;
-    for (int i = 0; i < D / 32; ++i) M = fmaxf(M, wmax[i]);
-    stat[0] = M;
-  }
-  __syncthreads();
-  const float M = stat[0];
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < CMB_WARPS; ++w) M = fmaxf(M, red[w][32]);
   float den = 0.f;
-  for (int s = d; s < nsplit; s += D) {
-    const float ms = part_ml[(row * nsplit + s) * 2];
+  for (int s = tid; s < nsplit; s += CMB_WARPS * 32) {
+    const float ms = ml[2 * s];
     const float w = (ms == -INFINITY) ? 0.f : expf(ms - M);
     w_s[s] = w;
-    den = fmaf(w, part_ml[(row * nsplit + s) * 2 + 1], den);
+    den = fmaf(w, ml[2 * s + 1], den);
   }
   den = warp_sum(den);
-  __shared__ float wden[D / 32];
-  if ((d & 31) == 0) wden[d >> 5] = den;
-  __syncthreads();
-  float dsum = 0.f;
-  for (int i = 0; i < D / 32; ++i) dsum += wden[i];
-  // numerator: independent loads over the splits (unrolled by the compiler)
+  __syncthreads();  // every warp has read red[.][32]; w_s complete
+  if (lane == 0) red[warp][32] = den;
   float num = 0.f;
-#pragma unroll 8
-  for (int s = 0; s < nsplit; ++s) num = fmaf(w_s[s], part_o[(row * nsplit + s) * D + d], num);
-  size_t od = row;
-  if (tokens_major) {
-    const size_t qi = row % L, bh = row / L, h = bh % Hq, b = bh / Hq;
-    od = (b * L + qi) * Hq + h;
+  if (d < D) {
+    const float* po = part_o + row * nsplit * D + d;
+#pragma unroll 4
+    for (int s = warp; s < nsplit; s += CMB_WARPS) num = fmaf(w_s[s], po[size_t(s) * D], num);
   }
-  out[od * D + d] = f2bf(num / fmaxf(dsum, 1e-30f));
+  red[warp][lane] = num;
+  __syncthreads();
+  if (warp == 0 && d < D) {
+    float tot = 0.f, dsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < CMB_WARPS; ++w) {
+      tot += red[w][lane];
+      dsum += red[w][32];
+    }
+    size_t od = row;
+    if (tokens_major) {
+      const size_t qi = row % L, bh = row / L, h = bh % Hq, b = bh / Hq;
+      od = (b * L + qi) * Hq + h;
+    }
+    out[od * D + d] = f2bf(tot / fmaxf(dsum, 1e-30f));
+  }
 }
 
 size_t attn_scratch_bytes(int B, int Hq, int L, int D, int nsplit) {
@@ -383,8 +394,8 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream) {
     if ((rc = attn_pf_launch(p, stream))) return rc;
     if (p.nsplit > 1) {
       const int rows = a.B * a.Hq * a.L;
-      M5_CUDA(launch_pdl(attn_combine_kernel<128>, dim3(rows), dim3(128), 0, stream, p.part_o, p.part_ml, p.nsplit, a.Hq, a.L, a.out_tokens_major,
-                                                         a.out));
+      M5_CUDA(launch_pdl(attn_combine_kernel, dim3(rows, 4), dim3(CMB_WARPS * 32), 0, stream, p.part_o, p.part_ml,
+                         p.nsplit, 128, a.Hq, a.L, a.out_tokens_major, a.out));
       M5_LAUNCH_CHECK("attention combine launch");
     }
     return M5_OK;
@@ -403,8 +414,8 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream) {
   if (rc) return rc;
   if (a.nsplit > 1) {
     const int rows = a.B * a.Hq * a.L;
-    if (a.D == 128) M5_CUDA(launch_pdl(attn_combine_kernel<128>, dim3(rows), dim3(128), 0, stream, a.part_o, a.part_ml, a.nsplit, a.Hq, a.L, a.out_tokens_major, a.out));
-    else M5_CUDA(launch_pdl(attn_combine_kernel<64>, dim3(rows), dim3(64), 0, stream, a.part_o, a.part_ml, a.nsplit, a.Hq, a.L, a.out_tokens_major, a.out));
+    M5_CUDA(launch_pdl(attn_combine_kernel, dim3(rows, (a.D + 31) / 32), dim3(CMB_WARPS * 32), 0, stream, a.part_o,
+                       a.part_ml, a.nsplit, a.D, a.Hq, a.L, a.out_tokens_major, a.out));
     M5_LAUNCH_CHECK("attention combine launch");
   }
   return M5_OK;
