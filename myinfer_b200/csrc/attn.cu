@@ -358,10 +358,12 @@ void attn_plan(int B, int Hq, int Hkv, int L, int S_max, int& QB, int& nsplit) {
   if (QB > L) QB = L;
   const long long ctas = (long long)B * Hkv * ((L + QB - 1) / QB);
   const int tiles = std::max(1, (S_max + ATT_TK - 1) / ATT_TK);
-  // Enough CTAs for ~2 per SM, each with at least one key tile.
-  // ~2 CTAs per SM: measured on B200 at 32K context, 3, 4 or 6 per SM were
-  // 20-55% slower (more, shorter splits add per-CTA prologue and merge work)
-  long long want = (2LL * sm_count() + ctas - 1) / ctas;
+  // Enough CTAs to fill the SMs once at the tensor-core kernel's occupancy
+  // (3 per SM for one 8-row query block, else 2), each with at least one key
+  // tile; more, shorter splits than resident slots only add per-CTA prologue
+  // and merge work.
+  const long long per_sm = attn_mma_ctas_per_sm(std::min(QB, L) * rep);
+  long long want = (per_sm * sm_count() + ctas - 1) / ctas;
   nsplit = (int)std::max(1LL, std::min<long long>(std::min<long long>(want, tiles), 1024));
 }
 

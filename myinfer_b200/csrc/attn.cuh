@@ -39,6 +39,8 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream);
 // rows (GQA group x queries per CTA) <= 16, no / causal mask, aligned views.
 bool attn_mma_eligible(const AttnArgs& a);
 int attn_mma_launch(const AttnArgs& a, cudaStream_t stream);
+// CTAs per SM the tensor-core decode kernel keeps resident for `rows` MMA rows
+int attn_mma_ctas_per_sm(int rows);
 int attn_mma_error(int reset);
 
 // Prefill tensor-core kernel (attn_pf.cu): 8/4-bit KV, D = 128, L * rep > 16.

@@ -3,26 +3,31 @@
 //
 // Work of one CTA: one kv head, one contiguous key range (a split).  A
 // producer warp streams 64-key tiles of K, V and their bf16 scales/biases
-// with 1-D bulk copies (each head's rows are contiguous) into a 4-stage
-// shared-memory ring guarded by mbarriers (bounded waits).  Four consumer
-// warps take 16 keys of every tile each and keep their own online-softmax
-// state; the states are merged at the end of the split.
+// with 1-D bulk copies (each head's rows are contiguous) into a shared-memory
+// ring guarded by mbarriers (bounded waits): 3 stages and 3 CTAs per SM for
+// one 8-row block of queries (decode), 4 stages and 2 CTAs for two.  Four
+// consumer warps take 16 keys of every tile each and keep their own
+// online-softmax state; the states are merged at the end of the split.
 //
-// Per 16-key step of a consumer warp (mma.sync m16n8k16, fp16 in, fp32 acc):
-//   S = Q K^T : A = q (rows = heads of the group, scaled by `scale` and rounded
-//               to bf16 like attention.py:49; exact in fp16), B = K codes.  A
-//               code becomes an fp16 operand with one PRMT per two codes
-//               (byte | 0x6400 = 1024 + code) and one HSUB2 (exact code);
-//               contraction dims are permuted so a lane reads 16 contiguous
-//               code bytes per 64-dim group, and every MMA stays inside one
-//               scale group, so  s = sum_g scale_g * (q . code_g) + bias_g * sum(q_g)
+// The MMAs run transposed, keys (and value dims) as the 16-row M side and the
+// query rows as the 8-column N side, so a GQA group of 8 heads fills an MMA
+// and nothing is padded.  Per 16-key step of a consumer warp (mma.sync
+// m16n8k16, fp16 in, fp32 acc):
+//   S^T = K Q^T : A = K codes (a code becomes an fp16 operand with one PRMT
+//               per two codes, byte | 0x6400 = 1024 + code, and one HSUB2),
+//               B = q^T (scaled by `scale` and rounded to bf16 like
+//               attention.py:49; exact in fp16).  Contraction dims are
+//               permuted so a lane reads 16 contiguous code bytes per 64-dim
+//               group, and every MMA stays inside one scale group, so
+//               s = sum_g scale_g * (q . code_g) + bias_g * sum(q_g)
 //               is the reference's dequantized dot product.
 //   scores rounded to bf16 (attention.py:66-69), fp32 online softmax; p rounded
 //   to bf16 for PV (attention.py:87-90), fp32 p in the denominator.
-//   O += P V  : the per-key value scale is folded into A = p * vscale_g * 2^6
-//               (one A per scale group; fp16), B = V codes transposed in
-//               registers with movmatrix; the per-key value bias adds
-//               p * vbias_g to an fp32 side sum.
+//   O^T += V^T P^T : A = V codes, 8 dims x 2 keys per lane built with byte
+//               permutes across two key rows; B = p * vscale_g * 2^6 (fp16, one
+//               per scale group), moved from the score layout with one
+//               movmatrix per 8 keys; the per-key value bias adds p * vbias_g
+//               to an fp32 side sum.
 #include <algorithm>
 #include <cmath>
 
@@ -34,7 +39,6 @@ namespace m5 {
 static __device__ int g_attn_mma_err = 0;
 
 constexpr int AM_TK = 64;       // keys per stage
-constexpr int AM_STAGES = 4;
 constexpr int AM_CW = 4;        // consumer warps (16 keys of each stage each)
 constexpr int AM_THREADS = (AM_CW + 1) * 32;
 constexpr float AM_PSCALE = 64.f;  // p * vscale is kept in fp16 scaled by 2^6
@@ -77,6 +81,13 @@ __device__ __forceinline__ uint32_t hsub1024(uint32_t x) {
   return r;
 }
 
+// fp16 pair x / 16 - 64: (1024 + 16 c) -> c exactly (4-bit codes in the high nibble)
+__device__ __forceinline__ uint32_t hsixteenth(uint32_t x) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(0x2C002C00u), "r"(0xD400D400u));
+  return r;
+}
+
 // fp16 pair (code_a, code_b) exactly, from 8-bit codes at bytes ia, ib of w.
 template <int SEL>
 __device__ __forceinline__ uint32_t code8_pair(uint32_t w) {
@@ -101,16 +112,25 @@ __device__ __forceinline__ int qk_dim(int j, int t, int k) {
   }
 }
 
-template <int BITS>
-__global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) {
+// Stages of the ring and CTAs per SM: one 8-row block of queries (decode)
+// keeps three CTAs of 4 + 1 warps resident per SM, two blocks two CTAs.
+template <int NB>
+struct AmCfg {
+  static constexpr int STAGES = NB == 1 ? 3 : 4;
+  static constexpr int MINB = NB == 1 ? 3 : 2;
+};
+
+template <int BITS, int NB>
+__global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(const AttnArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   using LY = AmLayout<BITS>;
+  constexpr int STAGES = AmCfg<NB>::STAGES;
   extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + AM_STAGES * LY::STAGE);
-  uint64_t* empty = full + AM_STAGES;
-  float* q_s = reinterpret_cast<float*>(empty + AM_STAGES);  // [16][128] scaled, bf16-rounded q
-  int* qpos = reinterpret_cast<int*>(q_s + 16 * 128);        // [16]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * LY::STAGE);
+  uint64_t* empty = full + STAGES;
+  float* q_s = reinterpret_cast<float*>(empty + STAGES);  // [16][128] scaled, bf16-rounded q
+  int* qpos = reinterpret_cast<int*>(q_s + 16 * 128);     // [16]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -130,7 +150,7 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) 
   const int ntiles = k_end > k_begin ? (k_end - k_begin + AM_TK - 1) / AM_TK : 0;
 
   if (tid == 0) {
-    for (int s = 0; s < AM_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], AM_CW);
     }
@@ -150,8 +170,8 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) 
       const unsigned char* vsd = reinterpret_cast<const unsigned char*>(a.v.scales);
       const unsigned char* vbd = reinterpret_cast<const unsigned char*>(a.v.biases);
       for (int it = 0; it < ntiles; ++it) {
-        const int st = it % AM_STAGES;
-        const uint32_t par = (it / AM_STAGES) & 1;
+        const int st = it % STAGES;
+        const uint32_t par = (it / STAGES) & 1;
         if (!mbar_wait(&empty[st], par ^ 1, &g_attn_mma_err)) return;
         const int key0 = k_begin + it * AM_TK;
         const int nk = (min(AM_TK, k_end - key0) + 3) & ~3;  // whole 16-byte scale rows
@@ -170,7 +190,7 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) 
   }
 
   // ----------------------------------------------------------- consumers
-  // stage scaled q (bf16-rounded) for the 16 MMA rows; padding rows are zero.
+  // stage scaled q (bf16-rounded) for the 16 MMA columns; padding rows are zero.
   // 16 rows x 16 blocks of 8 bf16 = 256 16-byte loads, two per thread, both
   // issued before use.
   {
@@ -201,18 +221,19 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) 
   if (tid < 16) qpos[tid] = S - a.L + q0 + (tid < rows ? tid / rep : 0);
   named_sync(1, AM_CW * 32);
 
-  // A fragments of q for the 8 contraction slices, and per-group sums of q
-  uint32_t qa[8][4];
+  // B fragments of q^T for the 8 contraction slices: column g of n-block nb is
+  // query row g + 8 nb (contraction dims permuted as the K codes are read)
+  uint32_t qb[NB][8][2];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float* r0 = q_s + g * 128;
-    const float* r8 = q_s + (g + 8) * 128;
     const int d0 = qk_dim<BITS>(j, t, 2 * t), d1 = qk_dim<BITS>(j, t, 2 * t + 1);
     const int d8 = qk_dim<BITS>(j, t, 2 * t + 8), d9 = qk_dim<BITS>(j, t, 2 * t + 9);
-    qa[j][0] = pack_h2(r0[d0], r0[d1]);
-    qa[j][1] = pack_h2(r8[d0], r8[d1]);
-    qa[j][2] = pack_h2(r0[d8], r0[d9]);
-    qa[j][3] = pack_h2(r8[d8], r8[d9]);
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const float* r = q_s + (g + 8 * nb) * 128;
+      qb[nb][j][0] = pack_h2(r[d0], r[d1]);
+      qb[nb][j][1] = pack_h2(r[d8], r[d9]);
+    }
   }
   // per-(row, group) sums of q: 4 threads x 16 elements per (row, group)
   float* qsum_s = reinterpret_cast<float*>(qpos + 16);  // [16][2]
@@ -230,226 +251,264 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) 
     if (part == 0) qsum_s[pair] = sum;
   }
   named_sync(1, AM_CW * 32);
-  float qsum[2][2];  // [row g / g+8][group]
+  // this lane's score columns: rows 2t + e + 8 nb
+  float qsr[NB][2][2];  // [nb][e][group]
+  int qp[NB][2];
 #pragma unroll
-  for (int hr = 0; hr < 2; ++hr)
+  for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-    for (int G = 0; G < 2; ++G) qsum[hr][G] = qsum_s[(g + 8 * hr) * 2 + G];
-  const int qp0 = qpos[g], qp8 = qpos[g + 8];
+    for (int e = 0; e < 2; ++e) {
+      const int r = 2 * t + e + 8 * nb;
+      qsr[nb][e][0] = qsum_s[r * 2];
+      qsr[nb][e][1] = qsum_s[r * 2 + 1];
+      qp[nb][e] = qpos[r];
+    }
   const bool causal = a.mask_kind == M5_MASK_CAUSAL;
 
-  float o[16][4];  // PV accumulators, dim-block db: rows g, g+8 x dims pv_dim(db, 2t / 2t+1)
+  // O^T accumulators: block (G, jj) rows g / g+8 are dims 64G + 8g + 2jj (+1),
+  // columns 2t, 2t+1 are query rows 2t + 8nb, 2t + 1 + 8nb
+  float o[NB][8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float vb_acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [row][group] sum p * vbias
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[nb][i][0] = o[nb][i][1] = o[nb][i][2] = o[nb][i][3] = 0.f;
+  float vb_acc[NB][2][2];  // [nb][e][group] sum p * vbias over this lane's keys
+  float m_run[NB][2], l_run[NB][2];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      vb_acc[nb][e][0] = vb_acc[nb][e][1] = 0.f;
+      m_run[nb][e] = -INFINITY;
+      l_run[nb][e] = 0.f;
+    }
 
   // A timed-out wait ends this warp's key loop (its state stays as is) but the
   // warp still joins the merge barriers below.
   for (int it = 0; it < ntiles; ++it) {
-    const int st = it % AM_STAGES;
-    const uint32_t par = (it / AM_STAGES) & 1;
+    const int st = it % STAGES;
+    const uint32_t par = (it / STAGES) & 1;
     if (!mbar_wait(&full[st], par, &g_attn_mma_err)) break;
     const unsigned char* sb = smem + st * LY::STAGE;
     const int kw0 = warp * 16;  // this warp's first key within the tile
     const int key_base = k_begin + it * AM_TK + kw0;
 
-    // ---------------- S = Q K^T for two blocks of 8 keys
-    float sc[2][4];
+    // ---------------- S^T = K Q^T: A rows g / g+8 are keys kw0 + g / kw0 + 8 + g
+    float dG[NB][2][4];
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
-      const int kl = kw0 + 8 * kb + g;  // key row this lane feeds as B column g
-      float dG[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-      for (int G = 0; G < 2; ++G) {
-        if constexpr (BITS == 8) {
-          const uint4 c = *reinterpret_cast<const uint4*>(sb + LY::K_OFF + kl * 128 + 64 * G + 16 * t);
-          const uint32_t w4[4] = {c.x, c.y, c.z, c.w};
+      for (int G = 0; G < 2; ++G) dG[nb][G][0] = dG[nb][G][1] = dG[nb][G][2] = dG[nb][G][3] = 0.f;
 #pragma unroll
-          for (int sub = 0; sub < 4; ++sub)
-            mma_f16(dG[G], qa[4 * G + sub], code8_pair<0x4140>(w4[sub]), code8_pair<0x4342>(w4[sub]));
-        } else {
-          const uint2 c = *reinterpret_cast<const uint2*>(sb + LY::K_OFF + kl * 64 + 32 * G + 8 * t);
-          const uint32_t w2[2] = {c.x, c.y};
+    for (int G = 0; G < 2; ++G) {
+      if constexpr (BITS == 8) {
+        const uint4 c0 = *reinterpret_cast<const uint4*>(sb + LY::K_OFF + (kw0 + g) * 128 + 64 * G + 16 * t);
+        const uint4 c1 = *reinterpret_cast<const uint4*>(sb + LY::K_OFF + (kw0 + 8 + g) * 128 + 64 * G + 16 * t);
+        const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w}, w1[4] = {c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-          for (int sub = 0; sub < 4; ++sub) {
-            const uint32_t w = w2[sub >> 1];
-            const int i0 = 2 * (sub & 1);
-            mma_f16(dG[G], qa[4 * G + sub], code4_pair(w, i0), code4_pair(w, i0 + 1));
-          }
+        for (int sub = 0; sub < 4; ++sub) {
+          const uint32_t A[4] = {code8_pair<0x4140>(w0[sub]), code8_pair<0x4140>(w1[sub]),
+                                 code8_pair<0x4342>(w0[sub]), code8_pair<0x4342>(w1[sub])};
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) mma_f16(dG[nb][G], A, qb[nb][4 * G + sub][0], qb[nb][4 * G + sub][1]);
+        }
+      } else {
+        const uint2 c0 = *reinterpret_cast<const uint2*>(sb + LY::K_OFF + (kw0 + g) * 64 + 32 * G + 8 * t);
+        const uint2 c1 = *reinterpret_cast<const uint2*>(sb + LY::K_OFF + (kw0 + 8 + g) * 64 + 32 * G + 8 * t);
+        const uint32_t w0[2] = {c0.x, c0.y}, w1[2] = {c1.x, c1.y};
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {
+          const int i0 = 2 * (sub & 1);
+          const uint32_t A[4] = {code4_pair(w0[sub >> 1], i0), code4_pair(w1[sub >> 1], i0),
+                                 code4_pair(w0[sub >> 1], i0 + 1), code4_pair(w1[sub >> 1], i0 + 1)};
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) mma_f16(dG[nb][G], A, qb[nb][4 * G + sub][0], qb[nb][4 * G + sub][1]);
         }
       }
-      // scale/bias per (key, group): keys 2t, 2t+1 of this block
-      const int kk = kw0 + 8 * kb + 2 * t;
-      const uint2 ks2 = *reinterpret_cast<const uint2*>(sb + LY::KS_OFF + kk * 4);  // [k][g0,g1],[k+1][g0,g1]
-      const uint2 kb2 = *reinterpret_cast<const uint2*>(sb + LY::KB_OFF + kk * 4);
-      const float s00 = bf16_lo(ks2.x), s01 = bf16_hi(ks2.x), s10 = bf16_lo(ks2.y), s11 = bf16_hi(ks2.y);
-      const float b00 = bf16_lo(kb2.x), b01 = bf16_hi(kb2.x), b10 = bf16_lo(kb2.y), b11 = bf16_hi(kb2.y);
-      // d[0]: (row g, key 2t) d[1]: (row g, key 2t+1) d[2]: (row g+8, 2t) d[3]: (row g+8, 2t+1)
-      float s[4];
-      s[0] = fmaf(s00, dG[0][0], b00 * qsum[0][0]) + fmaf(s01, dG[1][0], b01 * qsum[0][1]);
-      s[1] = fmaf(s10, dG[0][1], b10 * qsum[0][0]) + fmaf(s11, dG[1][1], b11 * qsum[0][1]);
-      s[2] = fmaf(s00, dG[0][2], b00 * qsum[1][0]) + fmaf(s01, dG[1][2], b01 * qsum[1][1]);
-      s[3] = fmaf(s10, dG[0][3], b10 * qsum[1][0]) + fmaf(s11, dG[1][3], b11 * qsum[1][1]);
-      const int key0 = key_base + 8 * kb + 2 * t;
+    }
+    // key scale/bias of keys g (fragments 0,1) and 8 + g (fragments 2,3), both groups
+    const uint32_t ksA = *reinterpret_cast<const uint32_t*>(sb + LY::KS_OFF + (kw0 + g) * 4);
+    const uint32_t ksB = *reinterpret_cast<const uint32_t*>(sb + LY::KS_OFF + (kw0 + 8 + g) * 4);
+    const uint32_t kbA = *reinterpret_cast<const uint32_t*>(sb + LY::KB_OFF + (kw0 + g) * 4);
+    const uint32_t kbB = *reinterpret_cast<const uint32_t*>(sb + LY::KB_OFF + (kw0 + 8 + g) * 4);
+    const float sk[2][2] = {{bf16_lo(ksA), bf16_hi(ksA)}, {bf16_lo(ksB), bf16_hi(ksB)}};
+    const float bk[2][2] = {{bf16_lo(kbA), bf16_hi(kbA)}, {bf16_lo(kbB), bf16_hi(kbB)}};
+    const int keyA = key_base + g, keyB = key_base + 8 + g;
+    float sc[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int key = key0 + (i & 1);
-        const int qp = (i < 2) ? qp0 : qp8;
-        const bool valid = key < k_end && (!causal || key <= qp);
-        sc[kb][i] = valid ? rbf(s[i]) : -INFINITY;
+        const int kk = i >> 1, e = i & 1;
+        const float s = fmaf(sk[kk][0], dG[nb][0][i], bk[kk][0] * qsr[nb][e][0]) +
+                        fmaf(sk[kk][1], dG[nb][1][i], bk[kk][1] * qsr[nb][e][1]);
+        const int key = kk ? keyB : keyA;
+        const bool valid = key < k_end && (!causal || key <= qp[nb][e]);
+        sc[nb][i] = valid ? rbf(s) : -INFINITY;
       }
-    }
 
-    // ---------------- online softmax (rows g and g+8; quads share a row)
-    float pm[2];
-    pm[0] = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-    pm[1] = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      pm[hr] = fmaxf(pm[hr], __shfl_xor_sync(0xffffffffu, pm[hr], 1));
-      pm[hr] = fmaxf(pm[hr], __shfl_xor_sync(0xffffffffu, pm[hr], 2));
-    }
-    float corr[2];
+    // ---------------- online softmax: column (row) maxima over the 8 key lanes
+    float p[NB][4];
     bool changed = false;
+    float corr[NB][2];
 #pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      const float mn = fmaxf(m_run[hr], pm[hr]);
-      corr[hr] = (m_run[hr] == mn) ? 1.f : (m_run[hr] == -INFINITY ? 0.f : expf(m_run[hr] - mn));
-      changed |= corr[hr] != 1.f;
-      m_run[hr] = mn;
-    }
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float pm = fmaxf(sc[nb][e], sc[nb][2 + e]);
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
+        const float mn = fmaxf(m_run[nb][e], pm);
+        corr[nb][e] = (m_run[nb][e] == mn) ? 1.f : (m_run[nb][e] == -INFINITY ? 0.f : expf(m_run[nb][e] - mn));
+        changed |= corr[nb][e] != 1.f;
+        m_run[nb][e] = mn;
+      }
     if (__any_sync(0xffffffffu, changed)) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        o[i][0] *= corr[0];
-        o[i][1] *= corr[0];
-        o[i][2] *= corr[1];
-        o[i][3] *= corr[1];
-      }
+      for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
-      for (int G = 0; G < 2; ++G) {
-        vb_acc[0][G] *= corr[0];
-        vb_acc[1][G] *= corr[1];
+        for (int i = 0; i < 8; ++i) {
+          o[nb][i][0] *= corr[nb][0];
+          o[nb][i][1] *= corr[nb][1];
+          o[nb][i][2] *= corr[nb][0];
+          o[nb][i][3] *= corr[nb][1];
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          vb_acc[nb][e][0] *= corr[nb][e];
+          vb_acc[nb][e][1] *= corr[nb][e];
+          l_run[nb][e] *= corr[nb][e];
+        }
       }
-      l_run[0] *= corr[0];
-      l_run[1] *= corr[1];
     }
-    float p[2][4];  // fp32 p, same layout as sc
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb)
+    for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float mm = m_run[i >> 1];
-        p[kb][i] = (sc[kb][i] == -INFINITY) ? 0.f : expf(sc[kb][i] - mm);
-        l_run[i >> 1] += p[kb][i];
+        p[nb][i] = (sc[nb][i] == -INFINITY) ? 0.f : expf(sc[nb][i] - m_run[nb][i & 1]);
+        l_run[nb][i & 1] += p[nb][i];
       }
 
-    // ---------------- O += P V
-    // value scale / bias of keys 2t, 2t+1 (block 0) and 8+2t, 8+2t+1 (block 1)
-    const int vk0 = kw0 + 2 * t, vk1 = kw0 + 8 + 2 * t;
-    const uint2 vs0 = *reinterpret_cast<const uint2*>(sb + LY::VS_OFF + vk0 * 4);
-    const uint2 vs1 = *reinterpret_cast<const uint2*>(sb + LY::VS_OFF + vk1 * 4);
-    const uint2 vb0 = *reinterpret_cast<const uint2*>(sb + LY::VB_OFF + vk0 * 4);
-    const uint2 vb1 = *reinterpret_cast<const uint2*>(sb + LY::VB_OFF + vk1 * 4);
-    uint32_t pa[2][4];  // A fragments per value group
+    // ---------------- O^T += V^T P^T
+    const uint32_t vsA = *reinterpret_cast<const uint32_t*>(sb + LY::VS_OFF + (kw0 + g) * 4);
+    const uint32_t vsB = *reinterpret_cast<const uint32_t*>(sb + LY::VS_OFF + (kw0 + 8 + g) * 4);
+    const uint32_t vbA = *reinterpret_cast<const uint32_t*>(sb + LY::VB_OFF + (kw0 + g) * 4);
+    const uint32_t vbB = *reinterpret_cast<const uint32_t*>(sb + LY::VB_OFF + (kw0 + 8 + g) * 4);
+    // masked keys have p == 0; their stage bytes may be stale, so never multiply them
+    auto mul = [](float r, float x) { return r == 0.f ? 0.f : r * x; };
+    // B fragments per value group: p * vscale * 2^6 of this lane's keys, moved
+    // to the (keys 2t, 2t+1 ; row g) layout with one transpose per 8 keys
+    uint32_t pb[NB][2][2];  // [nb][group][b0 / b1]
 #pragma unroll
-    for (int G = 0; G < 2; ++G) {
-      // scales of keys (2t, 2t+1) for block 0 and block 1 in group G
-      const float sA0 = G ? bf16_hi(vs0.x) : bf16_lo(vs0.x), sA1 = G ? bf16_hi(vs0.y) : bf16_lo(vs0.y);
-      const float sB0 = G ? bf16_hi(vs1.x) : bf16_lo(vs1.x), sB1 = G ? bf16_hi(vs1.y) : bf16_lo(vs1.y);
-      const float bA0 = G ? bf16_hi(vb0.x) : bf16_lo(vb0.x), bA1 = G ? bf16_hi(vb0.y) : bf16_lo(vb0.y);
-      const float bB0 = G ? bf16_hi(vb1.x) : bf16_lo(vb1.x), bB1 = G ? bf16_hi(vb1.y) : bf16_lo(vb1.y);
-      const float r00 = rbf(p[0][0]), r01 = rbf(p[0][1]), r02 = rbf(p[0][2]), r03 = rbf(p[0][3]);
-      const float r10 = rbf(p[1][0]), r11 = rbf(p[1][1]), r12 = rbf(p[1][2]), r13 = rbf(p[1][3]);
-      // masked keys have p == 0; their stage bytes may be stale, so never multiply them
-      auto mul = [](float r, float x) { return r == 0.f ? 0.f : r * x; };
-      pa[G][0] = pack_h2(mul(r00, sA0 * AM_PSCALE), mul(r01, sA1 * AM_PSCALE));  // row g, keys 2t, 2t+1
-      pa[G][1] = pack_h2(mul(r02, sA0 * AM_PSCALE), mul(r03, sA1 * AM_PSCALE));  // row g+8
-      pa[G][2] = pack_h2(mul(r10, sB0 * AM_PSCALE), mul(r11, sB1 * AM_PSCALE));  // row g, keys 8+2t, 8+2t+1
-      pa[G][3] = pack_h2(mul(r12, sB0 * AM_PSCALE), mul(r13, sB1 * AM_PSCALE));  // row g+8
-      vb_acc[0][G] += mul(r00, bA0) + mul(r01, bA1) + mul(r10, bB0) + mul(r11, bB1);
-      vb_acc[1][G] += mul(r02, bA0) + mul(r03, bA1) + mul(r12, bB0) + mul(r13, bB1);
-    }
-    // V rows this lane feeds to movmatrix: key g of block 0 and of block 1,
-    // 16 (8-bit) / 8 (4-bit) bytes per value group at offset 16t (8t).
+    for (int nb = 0; nb < NB; ++nb) {
+      const float r0 = rbf(p[nb][0]), r1 = rbf(p[nb][1]), r2 = rbf(p[nb][2]), r3 = rbf(p[nb][3]);
 #pragma unroll
-    for (int G = 0; G < 2; ++G) {
-      uint32_t vw[2][4];
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
-        const int kl = kw0 + 8 * kb + g;
-        if constexpr (BITS == 8) {
-          const uint4 c = *reinterpret_cast<const uint4*>(sb + LY::V_OFF + kl * 128 + 64 * G + 16 * t);
-          vw[kb][0] = c.x; vw[kb][1] = c.y; vw[kb][2] = c.z; vw[kb][3] = c.w;
-        } else {
-          const uint2 c = *reinterpret_cast<const uint2*>(sb + LY::V_OFF + kl * 64 + 32 * G + 8 * t);
-          vw[kb][0] = c.x; vw[kb][1] = c.y; vw[kb][2] = 0; vw[kb][3] = 0;
-        }
+      for (int G = 0; G < 2; ++G) {
+        const float sA = (G ? bf16_hi(vsA) : bf16_lo(vsA)) * AM_PSCALE;
+        const float sB = (G ? bf16_hi(vsB) : bf16_lo(vsB)) * AM_PSCALE;
+        const float bA = G ? bf16_hi(vbA) : bf16_lo(vbA), bB = G ? bf16_hi(vbB) : bf16_lo(vbB);
+        pb[nb][G][0] = movmatrix_t(pack_h2(mul(r0, sA), mul(r1, sA)));
+        pb[nb][G][1] = movmatrix_t(pack_h2(mul(r2, sB), mul(r3, sB)));
+        vb_acc[nb][0][G] += mul(r0, bA) + mul(r2, bB);
+        vb_acc[nb][1][G] += mul(r1, bA) + mul(r3, bB);
       }
+    }
+    // V codes of keys 2t, 2t+1, 8+2t, 8+2t+1 at dims 64G + 8g .. +7
+    const int kv0 = kw0 + 2 * t, kv8 = kw0 + 8 + 2 * t;
 #pragma unroll
-      for (int dbl = 0; dbl < 8; ++dbl) {  // dim-block within the group
-        uint32_t bb[2];
+    for (int G = 0; G < 2; ++G) {
+      if constexpr (BITS == 8) {
+        const unsigned char* vrow = sb + LY::V_OFF + 64 * G + 8 * g;
+        const uint2 v0 = *reinterpret_cast<const uint2*>(vrow + kv0 * 128);
+        const uint2 v1 = *reinterpret_cast<const uint2*>(vrow + (kv0 + 1) * 128);
+        const uint2 v8 = *reinterpret_cast<const uint2*>(vrow + kv8 * 128);
+        const uint2 v9 = *reinterpret_cast<const uint2*>(vrow + (kv8 + 1) * 128);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-          uint32_t pr;  // fp16 pair: this key, dims pv_dim(db, 2t), pv_dim(db, 2t+1)
-          if constexpr (BITS == 8) {
-            const uint32_t w = vw[kb][dbl >> 1];
-            pr = (dbl & 1) ? code8_pair<0x4342>(w) : code8_pair<0x4140>(w);
-          } else {
-            // 4-bit: dims 16t + 2*dbl + {0,1} -> word dbl >> 2, nibbles (2*dbl) & 7, +1
-            const uint32_t w = vw[kb][dbl >> 2];
-            const int n0 = (2 * dbl) & 7;
-            const uint32_t lo = (w >> (4 * n0)) & 0xFu, hi = (w >> (4 * n0 + 4)) & 0xFu;
-            pr = hsub1024(0x64006400u | lo | (hi << 16));
-          }
-          bb[kb] = movmatrix_t(pr);
+        for (int jj = 0; jj < 4; ++jj) {
+          // bytes 2jj, 2jj+1 of the 8 (dims 2jj, 2jj+1): [key a, key b] x 2 dims
+          const int wd = jj >> 1;
+          const uint32_t sel = (jj & 1) ? 0x7362u : 0x5140u;  // [a.b, b.b, a.b+1, b.b+1]
+          const uint32_t x01 = __byte_perm(wd ? v0.y : v0.x, wd ? v1.y : v1.x, sel);
+          const uint32_t x89 = __byte_perm(wd ? v8.y : v8.x, wd ? v9.y : v9.x, sel);
+          const uint32_t A[4] = {code8_pair<0x4140>(x01), code8_pair<0x4342>(x01), code8_pair<0x4140>(x89),
+                                 code8_pair<0x4342>(x89)};
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) mma_f16(o[nb][4 * G + jj], A, pb[nb][G][0], pb[nb][G][1]);
         }
-        mma_f16(o[8 * G + dbl], pa[G], bb[0], bb[1]);
+      } else {
+        const unsigned char* vrow = sb + LY::V_OFF + 32 * G + 4 * g;
+        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vrow + kv0 * 64);
+        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vrow + (kv0 + 1) * 64);
+        const uint32_t v8 = *reinterpret_cast<const uint32_t*>(vrow + kv8 * 64);
+        const uint32_t v9 = *reinterpret_cast<const uint32_t*>(vrow + (kv8 + 1) * 64);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          // byte jj holds dims 2jj (low nibble) and 2jj+1 (high nibble)
+          const uint32_t sel = uint32_t(jj) | (uint32_t(4 + jj) << 8);  // [a.jj, -, b.jj, -]
+          const uint32_t y01 = __byte_perm(v0, v1, sel), y89 = __byte_perm(v8, v9, sel);
+          const uint32_t A[4] = {hsub1024((y01 & 0x000F000Fu) | 0x64006400u),
+                                 hsixteenth((y01 & 0x00F000F0u) | 0x64006400u),
+                                 hsub1024((y89 & 0x000F000Fu) | 0x64006400u),
+                                 hsixteenth((y89 & 0x00F000F0u) | 0x64006400u)};
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) mma_f16(o[nb][4 * G + jj], A, pb[nb][G][0], pb[nb][G][1]);
+        }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
   }
 
-  // ---------------- reduce quad partials, merge the four warps
+  // ---------------- reduce over the 8 key lanes, merge the four warps
 #pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
-    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
-    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
+  for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-    for (int G = 0; G < 2; ++G) {
-      vb_acc[hr][G] += __shfl_xor_sync(0xffffffffu, vb_acc[hr][G], 1);
-      vb_acc[hr][G] += __shfl_xor_sync(0xffffffffu, vb_acc[hr][G], 2);
+    for (int e = 0; e < 2; ++e) {
+#pragma unroll
+      for (int o_ = 4; o_ <= 16; o_ <<= 1) {
+        l_run[nb][e] += __shfl_xor_sync(0xffffffffu, l_run[nb][e], o_);
+        vb_acc[nb][e][0] += __shfl_xor_sync(0xffffffffu, vb_acc[nb][e][0], o_);
+        vb_acc[nb][e][1] += __shfl_xor_sync(0xffffffffu, vb_acc[nb][e][1], o_);
+      }
     }
-  }
   named_sync(1, AM_CW * 32);  // all consumers are done with the stages: reuse them
   float* wm = reinterpret_cast<float*>(smem);       // [CW][16]
   float* wl = wm + AM_CW * 16;                      // [CW][16]
   float* wo = wl + AM_CW * 16;                      // [CW][16][128]
-  if (t == 0) {
-    wm[warp * 16 + g] = m_run[0];
-    wm[warp * 16 + g + 8] = m_run[1];
-    wl[warp * 16 + g] = l_run[0];
-    wl[warp * 16 + g + 8] = l_run[1];
+  float* wvb = wo + AM_CW * 16 * 128;               // [CW][16][2]
+  if (g == 0) {
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int r = 2 * t + e + 8 * nb;
+        wm[warp * 16 + r] = m_run[nb][e];
+        wl[warp * 16 + r] = l_run[nb][e];
+        wvb[(warp * 16 + r) * 2 + 0] = vb_acc[nb][e][0];
+        wvb[(warp * 16 + r) * 2 + 1] = vb_acc[nb][e][1];
+      }
+  }
+  if (NB == 1) {  // rows 8..15 are unused: mark them empty
+    if (lane < 8) {
+      wm[warp * 16 + 8 + lane] = -INFINITY;
+      wl[warp * 16 + 8 + lane] = 0.f;
+    }
   }
 #pragma unroll
-  for (int db = 0; db < 16; ++db) {
-    const int G = db >> 3, dbl = db & 7;
-    // dims of columns 2t, 2t+1 of dim-block db (value permutation: 16t + 2 dbl + e within the group)
-    const int d0 = 64 * G + 16 * t + 2 * dbl;
-    wo[(warp * 16 + g) * 128 + d0] = o[db][0] / AM_PSCALE;
-    wo[(warp * 16 + g) * 128 + d0 + 1] = o[db][1] / AM_PSCALE;
-    wo[(warp * 16 + g + 8) * 128 + d0] = o[db][2] / AM_PSCALE;
-    wo[(warp * 16 + g + 8) * 128 + d0 + 1] = o[db][3] / AM_PSCALE;
-  }
-  float* wvb = wo + AM_CW * 16 * 128;               // [CW][16][2]
-  if (t == 0) {
-    wvb[(warp * 16 + g) * 2 + 0] = vb_acc[0][0];
-    wvb[(warp * 16 + g) * 2 + 1] = vb_acc[0][1];
-    wvb[(warp * 16 + g + 8) * 2 + 0] = vb_acc[1][0];
-    wvb[(warp * 16 + g + 8) * 2 + 1] = vb_acc[1][1];
-  }
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int G = 0; G < 2; ++G)
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int d = 64 * G + 8 * g + 2 * jj;
+        const int r0 = 2 * t + 8 * nb;
+        const float* ob = o[nb][4 * G + jj];
+        wo[(warp * 16 + r0) * 128 + d] = ob[0] / AM_PSCALE;
+        wo[(warp * 16 + r0 + 1) * 128 + d] = ob[1] / AM_PSCALE;
+        wo[(warp * 16 + r0) * 128 + d + 1] = ob[2] / AM_PSCALE;
+        wo[(warp * 16 + r0 + 1) * 128 + d + 1] = ob[3] / AM_PSCALE;
+      }
   named_sync(1, AM_CW * 32);
   for (int i = tid; i < rows * 128; i += AM_CW * 32) {
     const int r = i >> 7, d = i & 127;
@@ -480,12 +539,16 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const AttnArgs a) 
   }
 }
 
-static size_t am_smem(int bits) {
+static size_t am_smem(int bits, int nb) {
   const size_t stage = bits == 8 ? AmLayout<8>::STAGE : AmLayout<4>::STAGE;
-  const size_t main = AM_STAGES * stage;
+  const int stages = nb == 1 ? AmCfg<1>::STAGES : AmCfg<2>::STAGES;
+  const size_t main = stages * stage;
   const size_t merge = size_t(AM_CW) * 16 * (2 + 128 + 2) * 4;
-  return std::max(main, merge) + 2 * AM_STAGES * 8 + 16 * 128 * 4 + 16 * 4 + 32 * 4;
+  return std::max(main, merge) + 2 * stages * 8 + 16 * 128 * 4 + 16 * 4 + 32 * 4;
 }
+
+int attn_mma_rows(const AttnArgs& a) { return std::min(a.QB, a.L) * (a.Hq / a.Hkv); }
+int attn_mma_ctas_per_sm(int rows) { return rows <= 8 ? AmCfg<1>::MINB : AmCfg<2>::MINB; }
 
 bool attn_mma_eligible(const AttnArgs& a) {
   if (a.D != 128 || (a.bits != 8 && a.bits != 4)) return false;
@@ -508,23 +571,25 @@ bool attn_mma_eligible(const AttnArgs& a) {
   return true;
 }
 
-int attn_mma_launch(const AttnArgs& a, cudaStream_t stream) {
-  const size_t smem = am_smem(a.bits);
-  static bool conf8 = false, conf4 = false;
-  dim3 grid(a.nsplit, (a.L + a.QB - 1) / a.QB, a.B * a.Hkv);
-  if (a.bits == 8) {
-    if (!conf8) {
-      M5_CUDA(cudaFuncSetAttribute(attn_mma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      conf8 = true;
-    }
-    M5_CUDA(launch_pdl(attn_mma_kernel<8>, dim3(grid), dim3(AM_THREADS), smem, stream, a));
-  } else {
-    if (!conf4) {
-      M5_CUDA(cudaFuncSetAttribute(attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      conf4 = true;
-    }
-    M5_CUDA(launch_pdl(attn_mma_kernel<4>, dim3(grid), dim3(AM_THREADS), smem, stream, a));
+template <int BITS, int NB>
+static int am_launch_t(const AttnArgs& a, cudaStream_t stream) {
+  const size_t smem = am_smem(BITS, NB);
+  static bool conf = false;
+  if (!conf) {
+    M5_CUDA(cudaFuncSetAttribute(attn_mma_kernel<BITS, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    conf = true;
   }
+  dim3 grid(a.nsplit, (a.L + a.QB - 1) / a.QB, a.B * a.Hkv);
+  M5_CUDA(launch_pdl(attn_mma_kernel<BITS, NB>, dim3(grid), dim3(AM_THREADS), smem, stream, a));
+  return M5_OK;
+}
+
+int attn_mma_launch(const AttnArgs& a, cudaStream_t stream) {
+  const bool one = attn_mma_rows(a) <= 8;
+  int rc;
+  if (a.bits == 8) rc = one ? am_launch_t<8, 1>(a, stream) : am_launch_t<8, 2>(a, stream);
+  else rc = one ? am_launch_t<4, 1>(a, stream) : am_launch_t<4, 2>(a, stream);
+  if (rc) return rc;
   M5_LAUNCH_CHECK("attention (tensor core) launch");
   return M5_OK;
 }
