@@ -1,15 +1,19 @@
-"""Batch-1 greedy decode and chunked prefill of the Qwen3-32B-shaped 4-bit model on B200.
+"""Batch-1 greedy decode and chunked prefill of a Qwen3-family 4-bit model on B200.
 
-`python bench.py [--gpus N] [--steps K] [--warmup W] [--impl m5|reference] [--ctx 32768]`
+`python bench.py [--gpus N] [--steps K] [--warmup W] [--impl m5|reference]
+                 [--config qwen3-32b|qwen3-30b-a3b|qwen3-235b-a22b|qwen3-0.6b] [--ctx T] [--kv-bits 8|4]`
 
-A step is one decode token: one full forward of the 64-layer model at the
-current context with 8-bit KV and greedy argmax, replayed from a CUDA graph.
-Before the timed decode the prompt (seeded random ids, `--ctx` tokens) is
-prefilled in chunks of 2048 through the same model and cache (timed too:
-`prefill` in the JSON line).  Weights are seeded random MLX 4-bit g64
-tensors resident in HBM; every decode step streams ~22.6 GB (larger than L2).
-With N > 1 (torchrun) the dense model runs tensor parallel over the N GPUs
-(one sequence, so `value` is that sequence's tokens/s and scaling is strong).
+The default is the headline workload, Qwen3-32B shape with a 32K-token prompt
+and 8-bit KV; the MoE configs default to their BASELINE prompts and KV bits
+(30B-A3B: 4K, 8-bit; 235B-A22B: 8K, 4-bit).  A step is one decode token: one
+full forward of the model at the current context with greedy argmax, replayed
+from a CUDA graph.  Before the timed decode the prompt (seeded random ids,
+`--ctx` tokens) is prefilled in chunks of 2048 through the same model and
+cache (timed too: `prefill` in the JSON line).  Weights are seeded random MLX
+4-bit g64 tensors resident in HBM; every decode step streams more than L2
+(~22.6 GB for the 32B shape).  With N > 1 (torchrun) a dense model runs tensor
+parallel and a MoE model expert parallel over the N GPUs (one sequence, so
+`value` is that sequence's tokens/s and scaling is strong).
 
 Printed JSON (rank 0): value = decode tokens/s; hbm = algorithmic bytes per
 token against the measured copy bandwidth; roofline = the dominant kernel
@@ -40,14 +44,33 @@ CONFIGS = {
     "qwen3-0.6b": dict(model_type="qwen3", hidden_size=1024, num_hidden_layers=28, num_attention_heads=16,
                        num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=151936,
                        tie_word_embeddings=True, max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6),
+    "qwen3-30b-a3b": dict(model_type="qwen3_moe", hidden_size=2048, num_hidden_layers=48, num_attention_heads=32,
+                          num_key_value_heads=4, head_dim=128, intermediate_size=6144, moe_intermediate_size=768,
+                          num_experts=128, num_experts_per_tok=8, norm_topk_prob=True, vocab_size=151936,
+                          tie_word_embeddings=False, max_position_embeddings=40960, rms_norm_eps=1e-6,
+                          rope_theta=1e6),
+    "qwen3-235b-a22b": dict(model_type="qwen3_moe", hidden_size=4096, num_hidden_layers=94, num_attention_heads=64,
+                            num_key_value_heads=4, head_dim=128, intermediate_size=12288, moe_intermediate_size=1536,
+                            num_experts=128, num_experts_per_tok=8, norm_topk_prob=True, vocab_size=151936,
+                            tie_word_embeddings=False, max_position_embeddings=40960, rms_norm_eps=1e-6,
+                            rope_theta=1e6),
 }
+# prompt length and KV bits each config is quoted with
+DEFAULTS = {"qwen3-32b": (32768, 8), "qwen3-0.6b": (512, 8), "qwen3-30b-a3b": (4096, 8), "qwen3-235b-a22b": (8192, 4)}
+NAMES = {"qwen3-32b": "Qwen3-32B", "qwen3-0.6b": "Qwen3-0.6B", "qwen3-30b-a3b": "Qwen3-30B-A3B",
+         "qwen3-235b-a22b": "Qwen3-235B-A22B"}
 
 
 def weight_bytes_per_token(cfg: dict) -> int:
-    """Packed weight bytes one decode token streams (0.5625 B per weight + norms)."""
+    """Packed weight bytes one decode token streams (0.5625 B per weight + norms);
+    for MoE the router and the k routed experts of every layer."""
     H, L, D = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["head_dim"]
     Hq, Hkv, I, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["intermediate_size"], cfg["vocab_size"]
-    per_layer = (Hq * D * H + 2 * Hkv * D * H + H * Hq * D + 3 * I * H) * 0.5625 + (2 * H + 2 * D) * 2
+    if cfg.get("num_experts", 0):
+        mlp = cfg["num_experts"] * H + cfg["num_experts_per_tok"] * 3 * cfg["moe_intermediate_size"] * H
+    else:
+        mlp = 3 * I * H
+    per_layer = (Hq * D * H + 2 * Hkv * D * H + H * Hq * D + mlp) * 0.5625 + (2 * H + 2 * D) * 2
     head = V * H * 0.5625
     return int(L * per_layer + head + H * 2)
 
@@ -115,7 +138,7 @@ def measured_peaks() -> dict:
 
 
 # ----------------------------------------------------------------- CPU legs
-def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0) -> dict:
+def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0, kv_bits: int = 8) -> dict:
     """Time the CPU oracle's decode step on `layers` decoder layers (+ a vocab
     slice of the lm_head) and scale to one full token.  Returns tok/s."""
     import numpy as np
@@ -139,11 +162,11 @@ def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0) ->
     rng = np.random.default_rng(1)
     cache = []
     for _ in range(layers):
-        qc = om.QuantizedKVCache(64, 8)
+        qc = om.QuantizedKVCache(64, kv_bits)
         k = rng.standard_normal((c.num_key_value_heads, ctx, c.head_dim)).astype(np.float32)
         v = rng.standard_normal((c.num_key_value_heads, ctx, c.head_dim)).astype(np.float32)
-        qc.k_parts.append(affine_quantize(k, 64, 8))
-        qc.v_parts.append(affine_quantize(v, 64, 8))
+        qc.k_parts.append(affine_quantize(k, 64, kv_bits))
+        qc.v_parts.append(affine_quantize(v, 64, kv_bits))
         qc.offset = ctx
         cache.append(qc)
     x = om.rb(torch.randn(1, cfg["hidden_size"], generator=g))
@@ -171,22 +194,22 @@ def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0) ->
     head_s = (time.perf_counter() - t1) * cfg["vocab_size"] / rows
     tok_s = cfg["num_hidden_layers"] * layer_s + head_s
     return {"value": 1.0 / tok_s, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{layers} of {cfg['num_hidden_layers']} decoder layers at ctx {ctx} (8-bit KV) + "
+            "sample": f"{layers} of {cfg['num_hidden_layers']} decoder layers at ctx {ctx} ({kv_bits}-bit KV) + "
                       f"{rows}/{cfg['vocab_size']} lm_head rows, scaled to one token; oracle weights "
                       f"pre-dequantized to fp32"}
 
 
 # ----------------------------------------------------------------- GPU leg
-def gemv_roofline(model, cfg, peak_gbs, peak_src="measured") -> dict:
-    """Dominant kernel (gate/up dequant-GEMV with SwiGLU... measured as the
-    plain projection GEMVs of every layer) timed alone with CUDA events."""
+def gemv_roofline(model, cfg, peak_gbs, peak_src="measured", proj="mlp.up_proj") -> dict:
+    """Dominant kernel: the decode dequant-GEMV, timed alone with CUDA events on
+    one projection of every layer (dense: up_proj; MoE: q_proj)."""
     import torch
 
     from myinfer_b200 import ops
     H = cfg["hidden_size"]
     L = cfg["num_hidden_layers"]
     x = torch.randn(1, H, device=model.device).to(torch.bfloat16)
-    names = [f"model.layers.{i}.mlp.up_proj" for i in range(L)]
+    names = [f"model.layers.{i}.{proj}" for i in range(L)]
     w = model.weights
     for _ in range(2):
         for n in names[:4]:
@@ -218,8 +241,9 @@ def gemv_roofline(model, cfg, peak_gbs, peak_src="measured") -> dict:
     ach = alg / (ms * 1e-3) / 1e9
     # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel and
     # shape, from the ncu capture summarised in profiles/gemv_tmap_up_proj_25600x5120.md
-    traffic = (73_846_528 + 1_500_928) * N // 25600 if N == cfg["intermediate_size"] else None
-    return {"bound": "hbm", "kernel": f"gemv_tmap_kernel<1,EPI_STORE> (up_proj {N}x{K} w4g64, 1 token)",
+    traffic = (73_846_528 + 1_500_928) * N // 25600 if proj == "mlp.up_proj" and N == cfg["intermediate_size"] \
+        else None
+    return {"bound": "hbm", "kernel": f"gemv_tmap_kernel<1,EPI_STORE> ({proj.split('.')[-1]} {N}x{K} w4g64, 1 token)",
             "achieved": round(ach, 1), "peak": peak_gbs, "peak_source": peak_src,
             "unit": "GB/s", "frac": round(ach / peak_gbs, 4), "traffic": traffic,
             "alg_bytes_per_launch": int(alg), "avg_launch_us": round(ms * 1e3, 2)}
@@ -281,7 +305,7 @@ def run_gpu(args) -> dict:
         return float(t)
 
     def new_cache(cap):
-        return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, 8, capacity=cap)
+        return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, args.kv_bits, capacity=cap)
                             for _ in range(a.num_hidden_layers)], dev)
 
     ctx = args.ctx
@@ -318,7 +342,7 @@ def run_gpu(args) -> dict:
         torch.cuda.synchronize()
     ms_step = max_over_ranks(start.elapsed_time(end)) / args.steps
     mean_ctx = ctx + args.warmup + args.steps / 2
-    bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_per_token(cfg, int(mean_ctx))
+    bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_per_token(cfg, int(mean_ctx), args.kv_bits)
     peaks = measured_peaks()
     tok_s = 1000.0 / ms_step  # one sequence: every rank works on the same token
 
@@ -338,20 +362,23 @@ def run_gpu(args) -> dict:
     ee.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e_steps
-    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"], peaks["source"])
+    roof = gemv_roofline(model, cfg, peaks["hbm_gbs"], peaks["source"],
+                         "mlp.up_proj" if not a.num_experts else "self_attn.q_proj")
     per_rank = bytes_tok / world
     par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}" if world > 1 else "single")
     prefill_flops = 2.0 * ctx * (weight_bytes_per_token(cfg) / 0.5625) + 4.0 * a.num_hidden_layers * \
         a.num_attention_heads * a.head_dim * ctx * ctx / 2
     out = {
-        "metric": "batch-1 decode tok/s (Qwen3-32B-shaped, w4g64, 8-bit KV) + HBM TB/s vs peak; prefill tok/s",
+        "metric": f"batch-1 decode tok/s ({NAMES[args.config]}-shaped, w4g64, {args.kv_bits}-bit KV) + HBM TB/s vs "
+                  "peak; prefill tok/s",
         "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
-        "vs_baseline": None, "dtype": "w4a16 (bf16 activations, fp32 accumulate), 8-bit KV",
+        "vs_baseline": None, "dtype": f"w4a16 (bf16 activations, fp32 accumulate), {args.kv_bits}-bit KV",
         "data": "synthetic (seeded random weights and prompt ids)",
         "config": {"workload": f"{args.config} batch-1 decode after a {ctx}-token prefill", "model": args.config,
                    "global_batch": 1, "seq_len": ctx, "parallelism": par_name, "prefill_chunk": args.chunk,
-                   "l2": "inputs larger than L2 (>=18 GB streamed per decode step)"},
+                   "kv_bits": args.kv_bits,
+                   "l2": f"inputs larger than L2 ({bytes_tok / 1e9:.1f} GB streamed per decode step)"},
         "hbm": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok / (ms_step * 1e-3) / 1e9, 1),
                 "achieved_gbs_per_gpu": round(per_rank / (ms_step * 1e-3) / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
                 "frac_of_measured": round(per_rank / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
@@ -368,10 +395,12 @@ def run_gpu(args) -> dict:
     }
     # kernels per decode step: per layer qkv, rope/append, attention (+ combine), o, gate/up, down
     # (+ 2 residual adds under tensor parallelism); embed, lm_head, argmax, length update
-    per_layer = 7 + (2 if world > 1 else 0)
+    # MoE: q|k|v, rope/append, attention, combine, o, router, top-k, expert gate/up, expert down
+    per_layer = (9 + (1 if world > 1 else 0)) if a.num_experts else (7 + (2 if world > 1 else 0))
     out["gpu_launches"] = args.steps * (a.num_hidden_layers * per_layer + 4)
     if rank == 0 and not args.no_cpu:
-        out["cpu_baseline"] = cpu_decode_sample(cfg, min(ctx, 4096), layers=1, threads=os.cpu_count() or 1)
+        out["cpu_baseline"] = cpu_decode_sample(cfg, min(ctx, 4096), layers=1, threads=os.cpu_count() or 1,
+                                                kv_bits=args.kv_bits)
     del graph
     if world > 1:
         torch.distributed.barrier()
@@ -389,10 +418,13 @@ def run_reference(args) -> dict:
     vals = []
     base = None
     for _ in range(max(1, args.steps // 8) if args.steps else 1):
-        base = cpu_decode_sample(cfg, min(args.ctx, 4096), layers=1, threads=os.cpu_count() or 1)
+        base = cpu_decode_sample(cfg, min(args.ctx, 4096), layers=1, threads=os.cpu_count() or 1,
+                                 kv_bits=args.kv_bits)
         vals.append(base["value"])
     v = statistics.mean(vals)
-    return {"impl": "reference", "metric": "batch-1 decode tok/s (Qwen3-32B-shaped, w4g64, 8-bit KV)",
+    return {"impl": "reference",
+            "metric": f"batch-1 decode tok/s ({NAMES[args.config]}-shaped, w4g64, {args.kv_bits}-bit KV) + HBM TB/s "
+                      "vs peak; prefill tok/s",
             "value": round(v, 5), "unit": "tok/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / v, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (CPU oracle)",
@@ -411,11 +443,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="m5", choices=["m5", "reference"])
     ap.add_argument("--config", default="qwen3-32b", choices=sorted(CONFIGS))
-    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--ctx", type=int, default=None, help="prompt tokens (default: the config's)")
+    ap.add_argument("--kv-bits", type=int, default=None, choices=[4, 8], help="KV cache bits (default: the config's)")
     ap.add_argument("--chunk", type=int, default=2048, help="prefill chunk (prefill_step_size)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
+    if args.ctx is None:
+        args.ctx = DEFAULTS[args.config][0]
+    if args.kv_bits is None:
+        args.kv_bits = DEFAULTS[args.config][1]
     if args.warmup < 3:
         args.warmup = 3
     out = run_reference(args) if args.impl == "reference" else run_gpu(args)
