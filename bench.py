@@ -257,6 +257,40 @@ def prefill(model, cache, ids, chunk: int):
     return cache
 
 
+class BatchDecodeGraph:
+    """One captured batched decode step: tokens [B] in, greedy tokens into the
+    same buffer (logits [B, V] kept on the device)."""
+
+    def __init__(self, model, cache):
+        import torch
+        self.model, self.cache = model, cache
+        B = cache.batch
+        dev = model.device
+        self.tok = torch.ones(B, dtype=torch.int32, device=dev)
+        self.logits = torch.empty(B, model.args.vocab_size, dtype=torch.bfloat16, device=dev)
+        cache.d_len.fill_(cache.offset)
+        model.forward_batch(self.tok, cache, logits=self.logits, argmax_out=self.tok, sync_len=False)  # eager warm
+        torch.cuda.synchronize()
+        offsets = [c.offset for c in cache]
+        self.graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            self.graph.capture_begin()
+            try:
+                model.forward_batch(self.tok, cache, logits=self.logits, argmax_out=self.tok, sync_len=False)
+            finally:
+                self.graph.capture_end()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for c, o in zip(cache, offsets):  # capture ran nothing
+            c.offset = o
+
+    def step(self) -> None:
+        self.graph.replay()
+        for c in self.cache:
+            c.offset += 1
+
+
 def run_gpu(args) -> dict:
     import datetime
 
@@ -304,9 +338,11 @@ def run_gpu(args) -> dict:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t)
 
-    def new_cache(cap):
-        return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, args.kv_bits, capacity=cap)
-                            for _ in range(a.num_hidden_layers)], dev)
+    B = args.batch
+
+    def new_cache(cap, batch=1):
+        return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, args.kv_bits, capacity=cap,
+                                             batch=batch) for _ in range(a.num_hidden_layers)], dev)
 
     ctx = args.ctx
     g = torch.Generator(device=dev).manual_seed(args.seed + 7)
@@ -314,21 +350,32 @@ def run_gpu(args) -> dict:
     # ---- prefill: warm the prefill kernels on a short scratch run, then the timed prompt
     prefill(model, new_cache(args.chunk), ids[:args.chunk], args.chunk)
     total = ctx + args.warmup + args.steps * 2 + 8
-    cache = new_cache(total)
+    cache = new_cache(total, B)
     torch.cuda.synchronize()
     barrier()
     ps, pe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ps.record()
-    prefill(model, cache, ids, args.chunk)
+    if B == 1:
+        prefill(model, cache, ids, args.chunk)
+    else:  # the timed prompt fills sequence 0; the other sequences get copies of its KV
+        model.prefill_sequence(ids, cache, 0, args.chunk)
     pe.record()
     torch.cuda.synchronize()
     prefill_ms = max_over_ranks(ps.elapsed_time(pe))
+    if B > 1:
+        for c in cache:
+            for t in c._tensors():
+                t[1:].copy_(t[:1].expand_as(t[1:]))
+            c.offset = ctx
 
     # ---- decode on the prefilled cache: one eager step, then the captured graph
-    tok = torch.tensor([1], dtype=torch.int32, device=dev)
-    model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
-    graph = DecodeGraph(model, cache, with_logits=False)
-    graph.tok.copy_(tok)
+    if B == 1:
+        tok = torch.tensor([1], dtype=torch.int32, device=dev)
+        model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
+        graph = DecodeGraph(model, cache, with_logits=False)
+        graph.tok.copy_(tok)
+    else:
+        graph = BatchDecodeGraph(model, cache)
     for _ in range(args.warmup):
         graph.step()
     torch.cuda.synchronize()
@@ -342,13 +389,14 @@ def run_gpu(args) -> dict:
         torch.cuda.synchronize()
     ms_step = max_over_ranks(start.elapsed_time(end)) / args.steps
     mean_ctx = ctx + args.warmup + args.steps / 2
-    bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_per_token(cfg, int(mean_ctx), args.kv_bits)
+    # bytes one step streams: the weights once, the KV of every sequence
+    bytes_step = weight_bytes_per_token(cfg) + B * kv_bytes_per_token(cfg, int(mean_ctx), args.kv_bits)
+    bytes_tok = bytes_step / B
     peaks = measured_peaks()
-    tok_s = 1000.0 / ms_step  # one sequence: every rank works on the same token
+    tok_s = B * 1000.0 / ms_step  # every rank works on the same B tokens
 
-    # e2e through the public decode step: pinned host token in, token out, every step
-    host = torch.empty(1, dtype=torch.int32, pin_memory=True)
-    host[0] = 1
+    # e2e through the public decode step: pinned host tokens in, tokens out, every step
+    host = torch.ones(B, dtype=torch.int32, pin_memory=True)
     torch.cuda.synchronize()
     barrier()
     e_steps = max(4, args.steps // 2)
@@ -364,22 +412,24 @@ def run_gpu(args) -> dict:
     e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e_steps
     roof = gemv_roofline(model, cfg, peaks["hbm_gbs"], peaks["source"],
                          "mlp.up_proj" if not a.num_experts else "self_attn.q_proj")
-    per_rank = bytes_tok / world
+    per_rank = bytes_step / world
     par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}" if world > 1 else "single")
     prefill_flops = 2.0 * ctx * (weight_bytes_per_token(cfg) / 0.5625) + 4.0 * a.num_hidden_layers * \
         a.num_attention_heads * a.head_dim * ctx * ctx / 2
     out = {
-        "metric": f"batch-1 decode tok/s ({NAMES[args.config]}-shaped, w4g64, {args.kv_bits}-bit KV) + HBM TB/s vs "
-                  "peak; prefill tok/s",
+        "metric": f"batch-{B} decode tok/s ({NAMES[args.config]}-shaped, w4g64, {args.kv_bits}-bit KV) + HBM TB/s "
+                  "vs peak; prefill tok/s",
         "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": f"w4a16 (bf16 activations, fp32 accumulate), {args.kv_bits}-bit KV",
         "data": "synthetic (seeded random weights and prompt ids)",
-        "config": {"workload": f"{args.config} batch-1 decode after a {ctx}-token prefill", "model": args.config,
-                   "global_batch": 1, "seq_len": ctx, "parallelism": par_name, "prefill_chunk": args.chunk,
+        "config": {"workload": f"{args.config} batch-{B} decode after a {ctx}-token prefill"
+                               + (" (one prompt prefilled, its KV copied to every sequence)" if B > 1 else ""),
+                   "model": args.config, "global_batch": B, "seq_len": ctx, "parallelism": par_name, "prefill_chunk": args.chunk,
                    "kv_bits": args.kv_bits,
-                   "l2": f"inputs larger than L2 ({bytes_tok / 1e9:.1f} GB streamed per decode step)"},
-        "hbm": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok / (ms_step * 1e-3) / 1e9, 1),
+                   "l2": f"inputs larger than L2 ({bytes_step / 1e9:.1f} GB streamed per decode step)"},
+        "hbm": {"bytes_per_step": bytes_step, "bytes_per_token": round(bytes_tok),
+                "achieved_gbs": round(bytes_step / (ms_step * 1e-3) / 1e9, 1),
                 "achieved_gbs_per_gpu": round(per_rank / (ms_step * 1e-3) / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
                 "frac_of_measured": round(per_rank / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                 "frac_of_8tbs_nominal": round(per_rank / (ms_step * 1e-3) / 8e12, 4)},
@@ -387,8 +437,8 @@ def run_gpu(args) -> dict:
                     "ms": round(prefill_ms, 1), "flops": prefill_flops,
                     "tflops": round(prefill_flops / (prefill_ms * 1e-3) / 1e12, 1)},
         "roofline": roof,
-        "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
-                "d2h_bytes_per_step": 4},
+        "e2e": {"value": round(B * 1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B},
         "gpu_launches": None,
         "clocks": clk.summary(),
         "load_seconds": round(load_s, 1),
@@ -445,6 +495,7 @@ def main():
     ap.add_argument("--config", default="qwen3-32b", choices=sorted(CONFIGS))
     ap.add_argument("--ctx", type=int, default=None, help="prompt tokens (default: the config's)")
     ap.add_argument("--kv-bits", type=int, default=None, choices=[4, 8], help="KV cache bits (default: the config's)")
+    ap.add_argument("--batch", type=int, default=1, help="sequences decoded together (m5_forward_batch when > 1)")
     ap.add_argument("--chunk", type=int, default=2048, help="prefill chunk (prefill_step_size)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")

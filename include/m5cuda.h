@@ -196,6 +196,17 @@ M5_API int m5_model_reserve(void* model, int max_tokens);
 M5_API int m5_forward(void* model, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int L,
                void* logits, int logits_mode, int32_t* d_argmax, void* stream);
 
+/* Batched decode: one new token for each of B independent sequences, all at
+ * position *d_len (so *d_len += 1 after the call), over caches whose layers
+ * hold the B sequences back to back: k/v [B, Hkv_local, capacity, ...], batch
+ * stride Hkv_local * capacity rows.  logits [B, V] bf16 (LAST and ALL both
+ * give the B rows), d_argmax [B] (needs logits).  The batched model call of
+ * mlx-lm (model(tokens[B, 1], cache) -> logits[B, 1, V], the contract used at
+ * m5engine/context.py:53) at the batch sizes of the benchmark configs
+ * (16/32/64); projections take the tensor-core GEMM from 16 rows on. */
+M5_API int m5_forward_batch(void* model, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int B,
+                            void* logits, int logits_mode, int32_t* d_argmax, void* stream);
+
 /* Convert rows [0, len) of a bf16 cache layer into a packed one (the
  * reference's KVCache.to_quantized at m5engine/attention.py:111-112). */
 M5_API int m5_kv_quantize_layer(const m5_layer_kv* src, const m5_layer_kv* dst, int num_kv_heads, int head_dim,

@@ -71,6 +71,8 @@ _SIGS = {
     "m5_model_reserve": (c_int, [c_void_p, c_int]),
     "m5_forward": (c_int, [c_void_p, POINTER(M5LayerKv), c_void_p, c_void_p, c_int, c_void_p, c_int,
                            c_void_p, c_void_p]),
+    "m5_forward_batch": (c_int, [c_void_p, POINTER(M5LayerKv), c_void_p, c_void_p, c_int, c_void_p, c_int,
+                                 c_void_p, c_void_p]),
     "m5_kv_quantize_layer": (c_int, [POINTER(M5LayerKv), POINTER(M5LayerKv), c_int, c_int, c_int, c_void_p]),
     "m5_argmax_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     "m5_moe_route": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

@@ -7,9 +7,10 @@ array or an MLX tuple whose sequence axis is -2 (context.py:41-47), ``state``
 ``trim_prompt_cache`` (prefix_cache.py:14, 90, 97-99).  Quantization switches a
 ``KVCache`` to a ``QuantizedKVCache`` (attention.py:106-112).
 
-Layout in HBM (batch 1): bf16 K/V ``[1, Hkv, capacity, D]``; packed K/V
-``[1, Hkv, capacity, D*bits/32]`` int32 words + bf16 scales/biases
-``[1, Hkv, capacity, D/64]``.  Capacity grows in steps of 256 positions like
+Layout in HBM: bf16 K/V ``[B, Hkv, capacity, D]``; packed K/V
+``[B, Hkv, capacity, D*bits/32]`` int32 words + bf16 scales/biases
+``[B, Hkv, capacity, D/64]`` (B = 1 except for batched decode, where the B
+sequences share one length).  Capacity grows in steps of 256 positions like
 mlx-lm, and may be reserved ahead of time so a captured decode graph never
 sees a reallocation.  Trimming only moves ``offset`` back (move-not-copy).
 """
@@ -34,9 +35,10 @@ class _Base:
     bits = 0
     group_size = 64
 
-    def __init__(self, n_kv_heads: int, head_dim: int, device, capacity: int = 0):
+    def __init__(self, n_kv_heads: int, head_dim: int, device, capacity: int = 0, batch: int = 1):
         self.n_kv_heads = n_kv_heads
         self.head_dim = head_dim
+        self.batch = batch
         self.device = torch.device(device)
         self.offset = 0
         self.capacity = 0
@@ -75,8 +77,12 @@ class _Base:
         self.capacity = capacity
         self.generation += 1
 
-    def layer_struct(self) -> M5LayerKv:
+    def layer_struct(self, seq: Optional[int] = None) -> M5LayerKv:
+        """The C-ABI view of this layer: all sequences, or (seq given) sequence
+        `seq` alone as a batch-1 layer (per-sequence prefill)."""
         t = self._tensors()
+        if seq is not None:
+            t = [x[seq] for x in t]
         if len(t) == 2:
             return M5LayerKv(t[0].data_ptr(), None, None, t[1].data_ptr(), None, None, self.capacity, 0,
                              self.group_size)
@@ -91,7 +97,7 @@ class KVCache(_Base):
     """Unquantized bf16 cache (mlx-lm ``KVCache``)."""
 
     def _alloc(self, cap):
-        shape = (1, self.n_kv_heads, cap, self.head_dim)
+        shape = (self.batch, self.n_kv_heads, cap, self.head_dim)
         return [torch.zeros(shape, dtype=torch.bfloat16, device=self.device) for _ in range(2)]
 
     def _set(self, t):
@@ -131,20 +137,20 @@ class QuantizedKVCache(_Base):
     """Packed 8/4-bit cache (mlx-lm ``QuantizedKVCache``)."""
 
     def __init__(self, n_kv_heads: int, head_dim: int, device, group_size: int = 64, bits: int = 8,
-                 capacity: int = 0):
+                 capacity: int = 0, batch: int = 1):
         if bits not in (4, 8) or group_size != 64:
             raise ValueError("quantized KV cache supports bits 4/8 with group_size 64")
         self.bits = bits
         self.group_size = group_size
-        super().__init__(n_kv_heads, head_dim, device, capacity)
+        super().__init__(n_kv_heads, head_dim, device, capacity, batch)
 
     def _alloc(self, cap):
-        H, D = self.n_kv_heads, self.head_dim
+        B, H, D = self.batch, self.n_kv_heads, self.head_dim
         out = []
         for _ in range(2):
-            out.append(torch.zeros((1, H, cap, D * self.bits // 32), dtype=torch.int32, device=self.device))
-            out.append(torch.zeros((1, H, cap, D // self.group_size), dtype=torch.bfloat16, device=self.device))
-            out.append(torch.zeros((1, H, cap, D // self.group_size), dtype=torch.bfloat16, device=self.device))
+            out.append(torch.zeros((B, H, cap, D * self.bits // 32), dtype=torch.int32, device=self.device))
+            out.append(torch.zeros((B, H, cap, D // self.group_size), dtype=torch.bfloat16, device=self.device))
+            out.append(torch.zeros((B, H, cap, D // self.group_size), dtype=torch.bfloat16, device=self.device))
         return out
 
     def _set(self, t):
@@ -183,8 +189,13 @@ class PromptCache(list):
         for c in self:
             c.reserve(capacity)
 
-    def structs(self):
-        arr = (M5LayerKv * len(self))(*[c.layer_struct() for c in self])
+    @property
+    def batch(self) -> int:
+        return self[0].batch if len(self) else 1
+
+    def structs(self, seq: Optional[int] = None):
+        """C-ABI layer views: the whole batch, or one sequence of it."""
+        arr = (M5LayerKv * len(self))(*[c.layer_struct(seq) for c in self])
         return arr
 
     def signature(self):

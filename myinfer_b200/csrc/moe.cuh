@@ -24,8 +24,17 @@ struct MoeArgs {
   bf16* act;            // scratch [T * k, I]
   bf16* h;              // [T, H], h += sum_j bf16(y_j * score_j)
   float* partial;       // when non-null: write fp32 sums here instead of h (expert parallel)
+  // zeroed scratch of the tensor-core decode path (moe_mma.cu), left zeroed
+  float* acc;           // >= max(2 k I, k H) floats
+  int* cnt;             // >= acc_rows / 16 counters
+  int acc_rows;
+  float* ybuf;          // [k, H] per-slot score-weighted rows
+  int* ncnt;            // [H / 16] slot counters
 };
 
 int moe_launch(const MoeArgs& a, cudaStream_t stream);
+// One decode token (T == 1, k == 8) on the tensor cores; moe_launch otherwise.
+bool moe_mma_eligible(const MoeArgs& a);
+int moe_mma_launch(const MoeArgs& a, cudaStream_t stream);
 
 }  // namespace m5

@@ -1,0 +1,326 @@
+// Routed experts of one decode token on the tensor cores (kernel K6, T = 1).
+//
+// The CUDA-core expert GEMVs (moe.cu) spend ~2.5 issue slots per 4-bit
+// weight and stay near 0.5 TB/s whatever their grid; here the expert
+// projections run the register-prefetch MMA scheme of gemv_mma.cu
+// (mma.sync m16n8k16 bf16, codes as exact (128 + q) pairs, per-group fold
+// s*D + (b - 128 s)*sum(x), fine-grained (tile, group) steps dealt to every
+// warp, split tiles through the zeroed fp32 scratch with a last-arriver
+// epilogue), over the rows of the routed experts only:
+//   gate/up - tile = 8 gate rows + the 8 matching up rows of one routed
+//             expert; input RMSNorm(h) staged once per CTA; the tile's last
+//             arriver writes bf16(bf16(g * bf16(sigmoid g)) * u) (mlx-lm
+//             SwiGLU) into act[slot][I];
+//   down    - the k SwiGLU rows are staged as the k B-columns of the MMA, so
+//             a tile (16 rows of one routed expert) computes every slot's
+//             column and keeps its own; its last arriver writes the row's
+//             bf16(bf16(y) * score) into ybuf[slot][H], and the last slot to
+//             finish a 16-row block adds the slots in slot order,
+//             h += bf16(sum_j bf16(bf16(y_j) * score_j)) (mlx-lm
+//             Qwen3MoeSparseMoeBlock), or writes the fp32 sum as this rank's
+//             partial under expert parallelism.
+// Only experts in [e_first, e_first + e_local) are streamed; each CTA lists
+// the token's local slots from the router ids, so no host sync is needed.
+#include <algorithm>
+
+#include "frag_stage.cuh"
+#include "gemv.cuh"
+#include "mma_dq.cuh"
+#include "moe.cuh"
+
+namespace m5 {
+
+constexpr int MX_W = 8;     // warps per CTA
+constexpr int MX_PIPE = 12;  // steps prefetched per warp
+constexpr int MX_KMAX = 8;   // routed experts per token this path supports
+
+// local slots of the token: ls -> (slot, local expert index); returns their
+// count.  Lanes 0..k-1 of warp 0 read the k ids in one load and compact the
+// local ones with a ballot, in slot order.
+__device__ __forceinline__ int mx_local_slots(const MoeArgs& a, int* s_slot, int* s_eid, int* s_n) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int e = lane < a.k ? a.ids[lane] - a.e_first : -1;
+    const bool local = lane < a.k && e >= 0 && e < a.e_local;
+    const unsigned m = __ballot_sync(0xffffffffu, local);
+    if (local) {
+      const int pos = __popc(m & ((1u << lane) - 1u));
+      s_slot[pos] = lane;
+      s_eid[pos] = e;
+    }
+    if (lane == 0) *s_n = __popc(m);
+  }
+  __syncthreads();
+  return *s_n;
+}
+
+// One warp's walk over steps [s_begin, s_end) of (tile, 64-column group):
+// row_of(tile, r16) gives the weight row (and its matrix) of tile row r16,
+// flush(tile, tot, done) receives the warp's partial sums of a tile.
+template <int MT, class RowOf, class Flush>
+__device__ __forceinline__ void mx_walk(long long s_begin, long long s_end, int K, const uint32_t* xf,
+                                        const float* xg, RowOf row_of, Flush flush) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int NG = K >> 6;
+  const size_t K8 = K >> 3, K64 = K >> 6;
+  const int tok = g < MT ? g : MT - 1;  // B column n = g reads this token (slot)
+  const uint32_t* xfl = xf + tok * NG * 32 + tq * 8;
+
+  long long is = s_begin;
+  int it_tile = int(is / NG), it_G = int(is % NG);
+  const uint32_t *w_g = nullptr, *w_g8 = nullptr;
+  const bf16 *s_g = nullptr, *b_g = nullptr, *s_g8 = nullptr, *b_g8 = nullptr;
+  auto set_tile = [&](int tile) {
+    QW m;
+    size_t rr;
+    row_of(tile, g, m, rr);
+    w_g = m.w + rr * K8 + 2 * tq;
+    s_g = m.s + rr * K64;
+    b_g = m.b + rr * K64;
+    row_of(tile, g + 8, m, rr);
+    w_g8 = m.w + rr * K8 + 2 * tq;
+    s_g8 = m.s + rr * K64;
+    b_g8 = m.b + rr * K64;
+  };
+  set_tile(it_tile);
+  uint2 rw[MX_PIPE], rw8[MX_PIPE];
+  uint32_t rsb[MX_PIPE], rsb8[MX_PIPE];
+  auto issue = [&](int slot) {
+    if (is < s_end) {
+      rw[slot] = ldg_nc_u2(w_g + it_G * 8);
+      rw8[slot] = ldg_nc_u2(w_g8 + it_G * 8);
+      rsb[slot] = uint32_t(ldg_nc_u16(s_g + it_G)) | (uint32_t(ldg_nc_u16(b_g + it_G)) << 16);
+      rsb8[slot] = uint32_t(ldg_nc_u16(s_g8 + it_G)) | (uint32_t(ldg_nc_u16(b_g8 + it_G)) << 16);
+      ++is;
+      if (++it_G == NG) {
+        it_G = 0;
+        if (is < s_end) set_tile(++it_tile);
+      }
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < MX_PIPE; ++s) issue(s);
+
+  int c_tile = int(s_begin / NG), c_G = int(s_begin % NG), c_done = 0;
+  float tot[4] = {0.f, 0.f, 0.f, 0.f};  // (g, 2t) (g, 2t+1) (g8, 2t) (g8, 2t+1)
+  const float* xgl0 = xg + (2 * tq < MT ? 2 * tq : MT - 1) * NG;
+  const float* xgl1 = xg + (2 * tq + 1 < MT ? 2 * tq + 1 : MT - 1) * NG;
+  for (long long s0 = s_begin; s0 < s_end; s0 += MX_PIPE) {
+#pragma unroll
+    for (int slot = 0; slot < MX_PIPE; ++slot) {
+      if (s0 + slot < s_end) {
+        const uint4 xa = *reinterpret_cast<const uint4*>(xfl + c_G * 32);
+        const uint4 xb = *reinterpret_cast<const uint4*>(xfl + c_G * 32 + 4);
+        const uint32_t wg[2] = {rw[slot].x, rw[slot].y}, wg8[2] = {rw8[slot].x, rw8[slot].y};
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          uint32_t A[4] = {nib_pair(wg[0], 0), nib_pair(wg8[0], 0), nib_pair(wg[0], 1), nib_pair(wg8[0], 1)};
+          mma_bf16(d, A, xa.x, xa.y);
+        }
+        {
+          uint32_t A[4] = {nib_pair(wg[0], 2), nib_pair(wg8[0], 2), nib_pair(wg[0], 3), nib_pair(wg8[0], 3)};
+          mma_bf16(d, A, xa.z, xa.w);
+        }
+        {
+          uint32_t A[4] = {nib_pair(wg[1], 0), nib_pair(wg8[1], 0), nib_pair(wg[1], 1), nib_pair(wg8[1], 1)};
+          mma_bf16(d, A, xb.x, xb.y);
+        }
+        {
+          uint32_t A[4] = {nib_pair(wg[1], 2), nib_pair(wg8[1], 2), nib_pair(wg[1], 3), nib_pair(wg8[1], 3)};
+          mma_bf16(d, A, xb.z, xb.w);
+        }
+        const float sA = bf16_lo(rsb[slot]), bA = bf16_hi(rsb[slot]);
+        const float sB = bf16_lo(rsb8[slot]), bB = bf16_hi(rsb8[slot]);
+        const float X0 = xgl0[c_G], X1 = xgl1[c_G];
+        const float oA = fmaf(-128.f, sA, bA), oB = fmaf(-128.f, sB, bB);
+        tot[0] = fmaf(sA, d[0], fmaf(oA, X0, tot[0]));
+        tot[1] = fmaf(sA, d[1], fmaf(oA, X1, tot[1]));
+        tot[2] = fmaf(sB, d[2], fmaf(oB, X0, tot[2]));
+        tot[3] = fmaf(sB, d[3], fmaf(oB, X1, tot[3]));
+        issue(slot);
+        ++c_done;
+        if (++c_G == NG) {
+          flush(c_tile, tot, c_done);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) tot[i] = 0.f;
+          c_done = 0;
+          c_G = 0;
+          ++c_tile;
+        }
+      }
+    }
+  }
+  if (c_done) flush(c_tile, tot, c_done);
+}
+
+// warp's range of `steps` steps over the grid's warps
+__device__ __forceinline__ void mx_range(long long steps, long long& b, long long& e) {
+  const long long nw = (long long)gridDim.x * MX_W, wid = (long long)blockIdx.x * MX_W + (threadIdx.x >> 5);
+  b = steps * wid / nw;
+  e = steps * (wid + 1) / nw;
+}
+
+__global__ void __launch_bounds__(MX_W * 32, 2) moe_gu_mma_kernel(const MoeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
+  const int H = a.H, I = a.I, NG = H >> 6;
+  uint32_t* xf = reinterpret_cast<uint32_t*>(smem_raw);  // [NG][4][8] bf16 pairs
+  float* xg = reinterpret_cast<float*>(xf + NG * 32);    // [NG]
+  float* red = xg + NG;                                  // [33]
+  const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
+  if (nl == 0) return;
+  stage_frag<1, MX_W * 32>(a.x, H, H, a.norm_w, a.eps, xf, xg, red, 0);
+  const int tpe = I / 8;  // tiles per expert
+  long long sb, se;
+  mx_range((long long)nl * tpe * NG, sb, se);
+  if (sb >= se) return;
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  auto row_of = [&](int tile, int r16, QW& m, size_t& rr) {
+    const int ls = tile / tpe, rt = tile % tpe;
+    m = r16 < 8 ? a.gate : a.up;
+    rr = size_t(s_eid[ls]) * I + rt * 8 + (r16 & 7);
+  };
+  auto flush = [&](int tile, const float (&tot)[4], int done) {
+    float* acc = a.acc;
+    const int base = tile * 16;
+    if (tq == 0) {  // token column 0
+      atomicAdd(&acc[base + g], tot[0]);
+      atomicAdd(&acc[base + g + 8], tot[2]);
+    }
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = (atomicAdd(&a.cnt[tile], done) + done == NG);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence();
+      if (lane < 8) {
+        float* p = &acc[base + lane];
+        const float v = __ldcg(p), u = __ldcg(p + 8);
+        p[0] = 0.f;
+        p[8] = 0.f;
+        const float gv = rbf(v), uv = rbf(u);
+        const float sg = rbf(1.f / (1.f + expf(-gv)));
+        const int ls = tile / tpe, rt = tile % tpe;
+        a.act[size_t(s_slot[ls]) * I + rt * 8 + lane] = f2bf(rbf(gv * sg) * uv);
+      }
+      __syncwarp();
+      if (lane == 0) a.cnt[tile] = 0;
+    }
+  };
+  mx_walk<1>(sb, se, H, xf, xg, row_of, flush);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(MX_W * 32, 2) moe_down_mma_kernel(const MoeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
+  const int H = a.H, I = a.I, NG = I >> 6;
+  const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
+  if (nl == 0) {  // no expert of this token is local: this rank's share is zero
+    if (a.partial)
+      for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < H; n += gridDim.x * blockDim.x) a.partial[n] = 0.f;
+    return;
+  }
+  uint32_t* xf = reinterpret_cast<uint32_t*>(smem_raw);  // [MT][NG][4][8]
+  float* xg = reinterpret_cast<float*>(xf + MT * NG * 32);  // [MT][NG]
+  float* red = xg + MT * NG;
+  stage_frag<MT, MX_W * 32>(a.act, I, I, nullptr, 0.f, xf, xg, red, 0);
+  const int tpe = H / 16;
+  long long sb, se;
+  mx_range((long long)nl * tpe * NG, sb, se);
+  if (sb >= se) return;
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  auto row_of = [&](int tile, int r16, QW& m, size_t& rr) {
+    const int ls = tile / tpe, nb = tile % tpe;
+    m = a.down;
+    rr = size_t(s_eid[ls]) * H + nb * 16 + r16;
+  };
+  auto flush = [&](int tile, const float (&tot)[4], int done) {
+    float* acc = a.acc;
+    const int base = tile * 16;
+    const int ls = tile / tpe, nb = tile % tpe;
+    const int j = s_slot[ls];  // this tile's own B column
+    if ((j >> 1) == tq) {
+      atomicAdd(&acc[base + g], tot[j & 1]);
+      atomicAdd(&acc[base + g + 8], tot[2 + (j & 1)]);
+    }
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = (atomicAdd(&a.cnt[tile], done) + done == NG);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    const float sj = bf2f(a.scores[j]);
+    if (lane < 16) {
+      float* p = &acc[base + lane];
+      const float y = rbf(__ldcg(p));
+      *p = 0.f;
+      a.ybuf[size_t(j) * H + nb * 16 + lane] = rbf(y * sj);
+    }
+    __threadfence();
+    __syncwarp();
+    int blk_last = 0;
+    if (lane == 0) {
+      a.cnt[tile] = 0;
+      blk_last = (atomicAdd(&a.ncnt[nb], 1) + 1 == nl);
+    }
+    blk_last = __shfl_sync(0xffffffffu, blk_last, 0);
+    if (!blk_last) return;
+    __threadfence();
+    if (lane < 16) {
+      const int n = nb * 16 + lane;
+      float sum = 0.f;
+      for (int q = 0; q < nl; ++q) sum += __ldcg(&a.ybuf[size_t(s_slot[q]) * H + n]);
+      if (a.partial) {
+        a.partial[n] = sum;
+      } else {
+        bf16* o = a.h + n;
+        *o = f2bf(bf2f(*o) + rbf(sum));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) a.ncnt[nb] = 0;
+  };
+  mx_walk<MT>(sb, se, I, xf, xg, row_of, flush);
+}
+
+static size_t mx_smem(int MT, int K) { return size_t(MT) * (K / 64) * 32 * 4 + size_t(MT) * (K / 64) * 4 + 33 * 4; }
+
+bool moe_mma_eligible(const MoeArgs& a) {
+  return a.T == 1 && a.k == MX_KMAX && a.acc && a.cnt && a.ybuf && a.ncnt && a.H % 64 == 0 && a.I % 64 == 0 &&
+         a.I % 8 == 0 && a.H % 16 == 0 && size_t(a.k) * a.I * 2 <= size_t(a.acc_rows) &&
+         size_t(a.k) * a.H <= size_t(a.acc_rows) && mx_smem(MX_KMAX, a.I) <= 200 * 1024 &&
+         mx_smem(1, a.H) <= 200 * 1024;
+}
+
+int moe_mma_launch(const MoeArgs& a, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    M5_CUDA(cudaFuncSetAttribute(moe_gu_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    M5_CUDA(cudaFuncSetAttribute(moe_down_mma_kernel<MX_KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024));
+    configured = true;
+  }
+  const int max_ctas = 2 * sm_count();
+  {
+    const long long steps = (long long)a.k * (a.I / 8) * (a.H / 64);
+    const int grid = (int)std::max(1LL, std::min<long long>(max_ctas, (steps + MX_W * 4 - 1) / (MX_W * 4)));
+    M5_CUDA(launch_pdl(moe_gu_mma_kernel, dim3(grid), dim3(MX_W * 32), mx_smem(1, a.H), st, a));
+    M5_LAUNCH_CHECK("moe gate/up (tensor core) launch");
+  }
+  {
+    const long long steps = (long long)a.k * (a.H / 16) * (a.I / 64);
+    const int grid = (int)std::max(1LL, std::min<long long>(max_ctas, (steps + MX_W * 4 - 1) / (MX_W * 4)));
+    M5_CUDA(launch_pdl(moe_down_mma_kernel<MX_KMAX>, dim3(grid), dim3(MX_W * 32), mx_smem(MX_KMAX, a.I), st, a));
+    M5_LAUNCH_CHECK("moe down (tensor core) launch");
+  }
+  return M5_OK;
+}
+
+}  // namespace m5

@@ -63,7 +63,8 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendArgs a
   const int H3 = a.Hq + 2 * a.Hkv;
   if (gw >= a.L * H3) return;
   const int t = gw / H3, h = gw - t * H3;
-  const int pos = *a.d_len + t;
+  const bool batched = a.batch > 1;
+  const int pos = *a.d_len + (batched ? 0 : t);
   const uint2 raw = *reinterpret_cast<const uint2*>(a.qkv + (size_t(t) * H3 + h) * D + 4 * lane);
   float x[4] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y)};
   const bool is_q = h < a.Hq;
@@ -99,12 +100,13 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendArgs a
     uint2 v;
     v.x = uint32_t(__bfloat16_as_ushort(f2bf(x[0]))) | (uint32_t(__bfloat16_as_ushort(f2bf(x[1]))) << 16);
     v.y = uint32_t(__bfloat16_as_ushort(f2bf(x[2]))) | (uint32_t(__bfloat16_as_ushort(f2bf(x[3]))) << 16);
-    reinterpret_cast<uint2*>(a.q_out + (size_t(h) * a.L + t) * D)[lane] = v;
+    const size_t qrow = batched ? size_t(t) * a.Hq + h : size_t(h) * a.L + t;
+    reinterpret_cast<uint2*>(a.q_out + qrow * D)[lane] = v;
     return;
   }
   if (pos >= a.kv.capacity) return;  // the host checks capacity; never write past it
   const int kh = is_k ? h - a.Hq : h - a.Hq - a.Hkv;
-  const size_t row = size_t(kh) * a.kv.capacity + pos;
+  const size_t row = (size_t(batched ? t : 0) * a.Hkv + kh) * a.kv.capacity + pos;
   if (is_k) store_kv_row<BITS>(x, lane, a.kv.k, (bf16*)a.kv.k_scales, (bf16*)a.kv.k_biases, row);
   else store_kv_row<BITS>(x, lane, a.kv.v, (bf16*)a.kv.v_scales, (bf16*)a.kv.v_biases, row);
 }
@@ -266,6 +268,27 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const bf16* __restrict__ x
     *out = bi;
     sc->counter = 0;  // ready for the next launch (also inside graph replays)
   }
+}
+
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const bf16* __restrict__ x, int64_t n, int32_t* out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const bf16* xr = x + size_t(blockIdx.x) * n;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = bf2f(xr[i]);
+    if (better(v, int(i), bv, bi)) { bv = v; bi = int(i); }
+  }
+  block_best(bv, bi);
+  if (threadIdx.x == 0) out[blockIdx.x] = bi;
+}
+
+int argmax_rows_launch(const bf16* x, int rows, int64_t n, int32_t* out, cudaStream_t stream) {
+  if (n <= 0 || rows <= 0) return fail(M5_ERR_INVALID, "argmax: empty input");
+  M5_CUDA(launch_pdl(argmax_rows_kernel, dim3(rows), dim3(1024), 0, stream, x, n, out));
+  M5_LAUNCH_CHECK("argmax rows launch");
+  return M5_OK;
 }
 
 int argmax_launch(const bf16* x, int64_t n, int32_t* out, void* scratch, cudaStream_t stream) {

@@ -19,8 +19,10 @@ struct RopeAppendArgs {
   const float* inv_freq;  // device [D/2]
   float mscale;
   const int32_t* d_len;   // position of token 0
-  bf16* q_out;            // [Hq, L, D]
+  bf16* q_out;            // [Hq, L, D]; batch > 1: [batch, Hq, D]
   m5_layer_kv kv;
+  int batch;              // > 1: token t is sequence t (L == batch), all at position *d_len;
+                          // kv holds [batch, Hkv, capacity, ...]
 };
 int rope_append_launch(const RopeAppendArgs& a, cudaStream_t stream);
 
@@ -32,6 +34,8 @@ int embed_launch(const int32_t* tokens, int T, const uint32_t* w, const bf16* s,
 // Uses `scratch` (argmax_scratch_bytes) and leaves it ready for the next call.
 size_t argmax_scratch_bytes();
 int argmax_launch(const bf16* x, int64_t n, int32_t* out, void* scratch, cudaStream_t stream);
+// out[r] = argmax over row r of x[rows, n] (one CTA per row, same tie rule).
+int argmax_rows_launch(const bf16* x, int rows, int64_t n, int32_t* out, cudaStream_t stream);
 
 // rms norm rows.
 int rms_norm_launch(const bf16* x, const bf16* w, int64_t rows, int dim, float eps, bf16* y, cudaStream_t stream);

@@ -65,6 +65,8 @@ struct Model {
   float* mma_acc = nullptr;  // zeroed split-tile scratch of the tensor-core GEMV
   int* mma_cnt = nullptr;
   int mma_rows = 0;
+  float* moe_ybuf = nullptr;  // zeroed [k, H] and [H/16] scratch of the tensor-core expert path
+  int* moe_ncnt = nullptr;
   bf16* xn = nullptr;        // RMSNorm(h) materialised for the prefill GEMM [T, H]
   bf16* gxs = nullptr;       // per-token group sums of the prefill GEMM input
   size_t gxs_bytes = 0;
@@ -294,13 +296,17 @@ __global__ void add_len_kernel(int32_t* d_len, int L) {
   *d_len += L;
 }
 
+// One model call: L tokens of one sequence at positions *d_len.., or (B > 1,
+// L == 1) one token of each of B sequences, all at position *d_len, over a
+// cache of [B, Hkv, capacity, ...] layers.  T = L * B activation rows.
 static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int L, void* logits,
-                   int logits_mode, int32_t* d_argmax, cudaStream_t st) {
+                   int logits_mode, int32_t* d_argmax, cudaStream_t st, int B = 1) {
+  const int T = L * B;
   const m5_model_cfg& c = m->cfg;
   const int H = c.hidden_size, D = c.head_dim;
   const int Hq = m->Hq, Hkv = m->Hkv;
   const int QKV = (Hq + 2 * Hkv) * D;
-  int rc = embed_launch(d_tokens, L, m->embed.w, m->embed.s, m->embed.b, H, c.vocab_size, m->h, st);
+  int rc = embed_launch(d_tokens, T, m->embed.w, m->embed.s, m->embed.b, H, c.vocab_size, m->h, st);
   if (rc) return rc;
   for (int li = 0; li < c.num_layers; ++li) {
     const Layer& ly = m->layers[li];
@@ -319,11 +325,12 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     a.norm_w = ly.in_norm;
     a.eps = c.rms_norm_eps;
     attach(m, a);
-    if ((rc = linear_auto(m, a, L, EPI_STORE, st))) return rc;
+    if ((rc = linear_auto(m, a, T, EPI_STORE, st))) return rc;
     // QK-norm + RoPE + KV append
     RopeAppendArgs r{};
     r.qkv = m->qkv;
-    r.L = L;
+    r.L = T;
+    r.batch = B;
     r.Hq = Hq;
     r.Hkv = Hkv;
     r.q_norm = ly.q_norm;
@@ -338,22 +345,22 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     // attention over the cache (S = *d_len + L keys after the append)
     AttnArgs at{};
     at.q = m->q;
-    at.B = 1;
+    at.B = B;
     at.Hq = Hq;
     at.L = L;
     at.D = D;
-    at.k = m5_kv_view{lk.k, lk.k_scales, lk.k_biases, 0, lk.capacity};
-    at.v = m5_kv_view{lk.v, lk.v_scales, lk.v_biases, 0, lk.capacity};
+    at.k = m5_kv_view{lk.k, lk.k_scales, lk.k_biases, int64_t(Hkv) * lk.capacity, lk.capacity};
+    at.v = m5_kv_view{lk.v, lk.v_scales, lk.v_biases, int64_t(Hkv) * lk.capacity, lk.capacity};
     at.bits = lk.bits;
     at.Hkv = Hkv;
     at.d_S = d_len;
     at.S_add = L;
     at.scale = 1.f / sqrtf(float(D));
     at.mask_kind = L > 1 ? M5_MASK_CAUSAL : M5_MASK_NONE;
-    attn_plan(1, Hq, Hkv, L, (int)lk.capacity, at.QB, at.nsplit);
-    if (attn_scratch_bytes(1, Hq, L, D, at.nsplit) > m->attn_part_bytes) at.nsplit = 1;
+    attn_plan(B, Hq, Hkv, L, (int)lk.capacity, at.QB, at.nsplit);
+    if (attn_scratch_bytes(B, Hq, L, D, at.nsplit) > m->attn_part_bytes) at.nsplit = 1;
     at.part_o = m->attn_part;
-    at.part_ml = m->attn_part + size_t(Hq) * L * at.nsplit * D;
+    at.part_ml = m->attn_part + size_t(B) * Hq * L * at.nsplit * D;
     at.out = m->attn;
     at.out_tokens_major = 1;
     if ((rc = attn_launch(at, st))) return rc;
@@ -369,8 +376,8 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     attach(m, o);
     if (c.tp_size > 1) {  // this rank's heads give a partial sum over o_proj's columns
       o.seg[0].yf = m->hf;
-      if ((rc = linear_auto(m, o, L, EPI_F32, st)) || (rc = reduce_into_h(m, L, st))) return rc;
-    } else if ((rc = linear_auto(m, o, L, EPI_RESIDUAL, st))) {
+      if ((rc = linear_auto(m, o, T, EPI_F32, st)) || (rc = reduce_into_h(m, T, st))) return rc;
+    } else if ((rc = linear_auto(m, o, T, EPI_RESIDUAL, st))) {
       return rc;
     }
     if (c.num_experts == 0) {
@@ -386,7 +393,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       g.norm_w = ly.post_norm;
       g.eps = c.rms_norm_eps;
       attach(m, g);
-      if ((rc = linear_auto(m, g, L, EPI_SWIGLU, st))) return rc;
+      if ((rc = linear_auto(m, g, T, EPI_SWIGLU, st))) return rc;
       GemvArgs d{};
       d.x = m->act;
       d.ldx = m->I;
@@ -398,8 +405,8 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       attach(m, d);
       if (c.tp_size > 1) {  // this rank's intermediate columns give a partial sum
         d.seg[0].yf = m->hf;
-        if ((rc = linear_auto(m, d, L, EPI_F32, st)) || (rc = reduce_into_h(m, L, st))) return rc;
-      } else if ((rc = linear_auto(m, d, L, EPI_RESIDUAL, st))) {
+        if ((rc = linear_auto(m, d, T, EPI_F32, st)) || (rc = reduce_into_h(m, T, st))) return rc;
+      } else if ((rc = linear_auto(m, d, T, EPI_RESIDUAL, st))) {
         return rc;
       }
     } else {
@@ -415,13 +422,13 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       g.norm_w = ly.post_norm;
       g.eps = c.rms_norm_eps;
       attach(m, g);
-      if ((rc = linear_auto(m, g, L, EPI_STORE, st))) return rc;
-      if ((rc = moe_topk_launch(m->rlogits, L, c.num_experts, c.experts_per_tok, c.norm_topk_prob, m->rids,
+      if ((rc = linear_auto(m, g, T, EPI_STORE, st))) return rc;
+      if ((rc = moe_topk_launch(m->rlogits, T, c.num_experts, c.experts_per_tok, c.norm_topk_prob, m->rids,
                                 m->rscores, st)))
         return rc;
       MoeArgs me{};
       me.x = m->h;
-      me.T = L;
+      me.T = T;
       me.H = H;
       me.I = c.moe_intermediate_size;
       me.k = c.experts_per_tok;
@@ -436,19 +443,28 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       me.eps = c.rms_norm_eps;
       me.act = m->act;
       me.h = m->h;
-      if (c.ep_size > 1) {  // this rank's experts give a partial sum
-        me.partial = m->hf;
-        if ((rc = moe_launch(me, st)) || (rc = reduce_into_h(m, L, st))) return rc;
-      } else if ((rc = moe_launch(me, st))) {
-        return rc;
-      }
+      me.acc = m->mma_acc;
+      me.cnt = m->mma_cnt;
+      me.acc_rows = m->mma_rows;
+      me.ybuf = m->moe_ybuf;
+      me.ncnt = m->moe_ncnt;
+      if (c.ep_size > 1) me.partial = m->hf;  // this rank's experts give a partial sum
+      rc = moe_mma_eligible(me) ? moe_mma_launch(me, st) : moe_launch(me, st);
+      if (rc || (c.ep_size > 1 && (rc = reduce_into_h(m, T, st)))) return rc;
     }
   }
   // final norm + lm_head (+ argmax)
   const Linear& head = (c.tie_word_embeddings && c.tp_size == 1) ? m->embed : m->lm_head;
   const int V = c.vocab_size;
   bf16* last_row = nullptr;
-  if (logits_mode == M5_LOGITS_ALL) {
+  if (B > 1) {  // every row is the last (only) token of its sequence: logits [B, V]
+    bf16* out = logits_mode == M5_LOGITS_NONE ? nullptr : (bf16*)logits;
+    if (out || d_argmax) {
+      if (!out) return fail(M5_ERR_INVALID, "batched forward: argmax needs a logits buffer");
+      if ((rc = head_rows(m, head, 0, B, out, st))) return rc;
+      if (d_argmax && (rc = argmax_rows_launch(out, B, V, d_argmax, st))) return rc;
+    }
+  } else if (logits_mode == M5_LOGITS_ALL) {
     if ((rc = head_rows(m, head, 0, L, (bf16*)logits, st))) return rc;
     last_row = (bf16*)logits + size_t(L - 1) * V;
   } else if (logits_mode == M5_LOGITS_LAST || d_argmax) {
@@ -759,8 +775,9 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   const size_t QKV = size_t(m->Hq + 2 * m->Hkv) * D;
   const size_t k = std::max(1, c.experts_per_tok);
   const size_t act = c.num_experts ? T * k * m->I : T * m->I;
-  // Attention partials for decode-sized calls (L <= 16): nsplit <= 2 * SMs.
-  const size_t part = attn_scratch_bytes(1, m->Hq, (int)std::min<size_t>(T, 4), (int)D, 2 * sm_count());
+  // Attention partials for decode-sized calls (L <= 16): nsplit <= 3 * SMs
+  // (attn_plan fills the SMs once at up to 3 CTAs each).
+  const size_t part = attn_scratch_bytes(1, m->Hq, (int)std::min<size_t>(T, 4), (int)D, 3 * sm_count());
   size_t total = 0;
   const int mrows = (int)std::max<size_t>({QKV, H, size_t(2) * m->I, size_t(c.vocab_size),
                                             size_t(std::max(1, c.num_experts)), size_t(16)});
@@ -773,7 +790,9 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
                           T >= kGemmMinTokens ? T * H * 2 : 0, gxs,
                           (c.tp_size > 1 || c.ep_size > 1) ? T * H * 4 : 0,
                           c.tp_size > 1 ? std::min<size_t>(T, 16) * m->Vl * 2 : 0,
-                          c.tp_size > 1 ? size_t(c.tp_size) * std::min<size_t>(T, 16) * m->Vl * 2 : 0};
+                          c.tp_size > 1 ? size_t(c.tp_size) * std::min<size_t>(T, 16) * m->Vl * 2 : 0,
+                          c.num_experts ? k * H * sizeof(float) : 0,
+                          c.num_experts ? (H / 16 + 1) * sizeof(int) : 0};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -808,18 +827,18 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->vpart = sizes[15] ? (bf16*)carve(p, sizes[15]) : nullptr;
   m->vgather = sizes[16] ? (bf16*)carve(p, sizes[16]) : nullptr;
   m->v_rows = (int)std::min<size_t>(T, 16);
+  m->moe_ybuf = sizes[17] ? (float*)carve(p, sizes[17]) : nullptr;
+  m->moe_ncnt = sizes[18] ? (int*)carve(p, sizes[18]) : nullptr;
   m->max_tokens = max_tokens;
   return M5_OK;
 }
 
-extern "C" int m5_forward(void* model, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int L,
-                          void* logits, int logits_mode, int32_t* d_argmax, void* stream) {
-  M5_CHECK_ARG(model && kv && d_len && d_tokens, "m5_forward: null argument");
-  Model* m = (Model*)model;
-  M5_CHECK_ARG(L > 0, "m5_forward: L must be positive");
-  M5_CHECK_ARG(logits_mode >= M5_LOGITS_NONE && logits_mode <= M5_LOGITS_ALL, "m5_forward: logits_mode");
-  M5_CHECK_ARG(logits_mode == M5_LOGITS_NONE || logits, "m5_forward: logits buffer required");
-  if (L > m->max_tokens) return fail(M5_ERR_STATE, "m5_forward: L exceeds m5_model_reserve size");
+static int check_forward(Model* m, const m5_layer_kv* kv, int rows, int logits_mode, void* logits,
+                         const char* who) {
+  const std::string w(who);
+  M5_CHECK_ARG(logits_mode >= M5_LOGITS_NONE && logits_mode <= M5_LOGITS_ALL, w + ": logits_mode");
+  M5_CHECK_ARG(logits_mode == M5_LOGITS_NONE || logits, w + ": logits buffer required");
+  if (rows > m->max_tokens) return fail(M5_ERR_STATE, w + ": tokens exceed the m5_model_reserve size");
   std::string miss = missing(m);
   if (!miss.empty()) return fail(M5_ERR_STATE, "model tensor not bound: " + miss);
   if (!m->rope_set) return fail(M5_ERR_STATE, "model RoPE table not set");
@@ -827,10 +846,29 @@ extern "C" int m5_forward(void* model, const m5_layer_kv* kv, int32_t* d_len, co
     return fail(M5_ERR_STATE, "multi-rank model has no communicator (m5_model_set_comm)");
   for (int i = 0; i < m->cfg.num_layers; ++i) {
     const m5_layer_kv& l = kv[i];
-    if (!l.k || !l.v || l.capacity <= 0) return fail(M5_ERR_INVALID, "m5_forward: cache layer " + std::to_string(i));
-    if (l.bits != 0 && l.bits != 4 && l.bits != 8) return fail(M5_ERR_INVALID, "m5_forward: cache bits");
+    if (!l.k || !l.v || l.capacity <= 0) return fail(M5_ERR_INVALID, w + ": cache layer " + std::to_string(i));
+    if (l.bits != 0 && l.bits != 4 && l.bits != 8) return fail(M5_ERR_INVALID, w + ": cache bits");
     if (l.bits && (!l.k_scales || !l.k_biases || !l.v_scales || !l.v_biases || l.group_size != 64))
-      return fail(M5_ERR_INVALID, "m5_forward: packed cache needs scales/biases and group 64");
+      return fail(M5_ERR_INVALID, w + ": packed cache needs scales/biases and group 64");
   }
+  return M5_OK;
+}
+
+extern "C" int m5_forward(void* model, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int L,
+                          void* logits, int logits_mode, int32_t* d_argmax, void* stream) {
+  M5_CHECK_ARG(model && kv && d_len && d_tokens, "m5_forward: null argument");
+  M5_CHECK_ARG(L > 0, "m5_forward: L must be positive");
+  Model* m = (Model*)model;
+  if (int rc = check_forward(m, kv, L, logits_mode, logits, "m5_forward")) return rc;
   return forward(m, kv, d_len, d_tokens, L, logits, logits_mode, d_argmax, (cudaStream_t)stream);
+}
+
+extern "C" int m5_forward_batch(void* model, const m5_layer_kv* kv, int32_t* d_len, const int32_t* d_tokens, int B,
+                                void* logits, int logits_mode, int32_t* d_argmax, void* stream) {
+  M5_CHECK_ARG(model && kv && d_len && d_tokens, "m5_forward_batch: null argument");
+  M5_CHECK_ARG(B > 0, "m5_forward_batch: B must be positive");
+  M5_CHECK_ARG(!d_argmax || logits_mode != M5_LOGITS_NONE, "m5_forward_batch: argmax needs logits");
+  Model* m = (Model*)model;
+  if (int rc = check_forward(m, kv, B, logits_mode, logits, "m5_forward_batch")) return rc;
+  return forward(m, kv, d_len, d_tokens, 1, logits, logits_mode, d_argmax, (cudaStream_t)stream, B);
 }

@@ -3,7 +3,7 @@
     python -m myinfer_b200.microbench gemv --n 25600 --k 5120 [--m 1] [--iters 20]
     python -m myinfer_b200.microbench attention --s 32768 --l 1 --bits 8 [--hq 64 --hkv 8]
     python -m myinfer_b200.microbench gemm --m 2048 --n 8192 --k 5120
-    python -m myinfer_b200.microbench step --ctx 32768 --steps 2   # decode steps (profiler range)
+    python -m myinfer_b200.microbench step --ctx 32768 --steps 2 [--config qwen3-30b-a3b]   # decode steps
 
 ``gemv`` cycles over enough distinct weight matrices that every launch reads
 from HBM (more than L2 in total); ``attention`` is the standalone
@@ -82,7 +82,7 @@ def bench_gemm(m: int, n: int, k: int, iters: int) -> dict:
 
 
 def bench_step(ctx: int, steps: int, config: str = "qwen3-32b") -> dict:
-    """Decode steps of the Qwen3-32B-shaped model over a synthetic 8-bit KV
+    """Decode steps of a Qwen3-32B- or Qwen3-30B-A3B-shaped model over a synthetic 8-bit KV
     cache of `ctx` positions; only the timed steps run inside a CUDA profiler
     range (cudaProfilerStart/Stop), so `ncu --profile-from-start off` lists
     exactly the kernels of `steps` decode steps."""
@@ -91,7 +91,12 @@ def bench_step(ctx: int, steps: int, config: str = "qwen3-32b") -> dict:
     from myinfer_b200.model import Model, ModelArgs, random_weights
     presets = {"qwen3-32b": dict(model_type="qwen3", hidden_size=5120, num_hidden_layers=64,
                                  num_attention_heads=64, num_key_value_heads=8, head_dim=128,
-                                 intermediate_size=25600, vocab_size=151936, tie_word_embeddings=False)}
+                                 intermediate_size=25600, vocab_size=151936, tie_word_embeddings=False),
+               "qwen3-30b-a3b": dict(model_type="qwen3_moe", hidden_size=2048, num_hidden_layers=48,
+                                     num_attention_heads=32, num_key_value_heads=4, head_dim=128,
+                                     intermediate_size=6144, moe_intermediate_size=768, num_experts=128,
+                                     num_experts_per_tok=8, norm_topk_prob=True, vocab_size=151936,
+                                     tie_word_embeddings=False)}
     a = ModelArgs.from_dict(presets[config])
     dev = torch.device("cuda")
     model = Model(a, random_weights(a, 0, dev), dev, max_tokens=8)
@@ -162,6 +167,7 @@ def main():
     st = sub.add_parser("step")
     st.add_argument("--ctx", type=int, default=32768)
     st.add_argument("--steps", type=int, default=2)
+    st.add_argument("--config", default="qwen3-32b", choices=["qwen3-32b", "qwen3-30b-a3b"])
     gm = sub.add_parser("gemm")
     gm.add_argument("--m", type=int, default=2048)
     gm.add_argument("--n", type=int, default=8192)
@@ -180,7 +186,7 @@ def main():
     elif args.cmd == "gemm":
         r = bench_gemm(args.m, args.n, args.k, args.iters)
     elif args.cmd == "step":
-        r = bench_step(args.ctx, args.steps)
+        r = bench_step(args.ctx, args.steps, args.config)
     else:
         r = bench_attention(args.s, args.l, args.bits, args.hq, args.hkv, args.iters)
     print(json.dumps(r), flush=True)

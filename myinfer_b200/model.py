@@ -249,6 +249,48 @@ class Model:
         for c in cache:
             c.offset += L
 
+    def prefill_sequence(self, tokens: torch.Tensor, cache: PromptCache, seq: int, chunk: int = 2048) -> None:
+        """Prefill sequence `seq` of a batched cache with `tokens` (int32 CUDA
+        [L]) from position 0, in chunks; the cache's shared offset is left to
+        the caller (every sequence of a batch is prefilled to the same length)."""
+        L = int(tokens.numel())
+        for c in cache:
+            if c.capacity < L:
+                c.reserve(L)
+        structs = cache.structs(seq)
+        d_len = torch.zeros(1, dtype=torch.int32, device=self.device)
+        for p0 in range(0, L, chunk):
+            n = min(chunk, L - p0)
+            if n > self.max_tokens:
+                self.reserve(n)
+            call("m5_forward", self._h, structs, d_len.data_ptr(), tokens[p0:p0 + n].data_ptr(), n, None,
+                 _lib.M5_LOGITS_NONE, None, _stream())
+
+    def forward_batch(self, tokens: torch.Tensor, cache: PromptCache, logits: Optional[torch.Tensor] = None,
+                      argmax_out: Optional[torch.Tensor] = None, sync_len: bool = True) -> None:
+        """One decode token for each of the cache's B sequences (int32 CUDA
+        tokens [B], all at position cache.offset): logits [B, V] and / or the
+        greedy tokens [B]; advances the shared offset by one."""
+        B = int(tokens.numel())
+        if B != cache.batch:
+            raise ValueError(f"forward_batch: {B} tokens for a cache of {cache.batch} sequences")
+        if B > self.max_tokens:
+            self.reserve(B)
+        need = cache.offset + 1
+        for c in cache:
+            if c.capacity < need:
+                c.reserve(need)
+        if argmax_out is not None and logits is None:
+            logits = torch.empty(B, self.args.vocab_size, dtype=torch.bfloat16, device=self.device)
+        if sync_len:
+            cache.d_len.fill_(cache.offset)
+        call("m5_forward_batch", self._h, cache.structs(), cache.d_len.data_ptr(), tokens.data_ptr(), B,
+             None if logits is None else logits.data_ptr(),
+             _lib.M5_LOGITS_NONE if logits is None else _lib.M5_LOGITS_ALL,
+             None if argmax_out is None else argmax_out.data_ptr(), _stream())
+        for c in cache:
+            c.offset += 1
+
     def __call__(self, tokens, cache: Optional[PromptCache] = None) -> torch.Tensor:
         """``model(tokens[1, L], cache) -> logits[1, L, V]`` (bf16)."""
         if cache is None:

@@ -1,0 +1,86 @@
+"""Batched decode (m5_forward_batch): B sequences, one token each per call, all
+at the same position, against the same sequences decoded one at a time.
+
+Both runs are teacher-forced on the single-sequence greedy tokens, so every
+step compares logits of identical inputs.  The batched projections run as
+one GEMV over B rows (B <= 15) or the tensor-core GEMM (B >= 16) instead of
+B single-row GEMVs, so fp32 sums differ in order: logits cosine > 0.9999 and
+max-abs <= 0.05, greedy tokens equal except at top-2 gaps below 0.02."""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=2,
+            head_dim=128, intermediate_size=1024, vocab_size=4096, tie_word_embeddings=False,
+            max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+TINY_MOE = dict(TINY, model_type="qwen3_moe", num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
+                norm_topk_prob=True, intermediate_size=0)
+
+
+def _model(cfg, seed):
+    from myinfer_b200.model import Model, ModelArgs, upload_weights
+    from oracle import model as om
+    host = om.generate_weights(om.Config.from_dict(cfg), seed)
+    return Model(ModelArgs.from_dict(cfg), upload_weights(host, "cuda"), "cuda", max_tokens=64)
+
+
+def _cache(model, bits, batch, cap):
+    from myinfer_b200.cache import PromptCache, QuantizedKVCache
+    a = model.args
+    return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, "cuda", 64, bits, capacity=cap,
+                                         batch=batch) for _ in range(a.num_hidden_layers)], "cuda")
+
+
+def _single(model, prompt, n, bits):
+    """Greedy tokens and per-step logits of one sequence decoded alone."""
+    from myinfer_b200 import _lib
+    cache = _cache(model, bits, 1, len(prompt) + n + 8)
+    ids = torch.tensor(prompt, dtype=torch.int32, device="cuda")
+    model.forward(ids[:-1], cache)
+    tok = ids[-1:].clone()
+    toks, logits = [], []
+    for _ in range(n):
+        lg = torch.empty(model.args.vocab_size, dtype=torch.bfloat16, device="cuda")
+        model.forward(tok, cache, _lib.M5_LOGITS_LAST, lg)
+        logits.append(lg.float().cpu())
+        nxt = int(lg.float().argmax())
+        toks.append(nxt)
+        tok = torch.tensor([nxt], dtype=torch.int32, device="cuda")
+    return toks, torch.stack(logits)
+
+
+@pytest.mark.parametrize("cfg", [TINY, TINY_MOE], ids=["dense", "moe"])
+@pytest.mark.parametrize("B", [4, 20], ids=["gemv", "gemm"])
+def test_batched_decode_matches_single(cfg, B):
+    model = _model(cfg, seed=21)
+    bits, L, n = 8, 24, 6
+    rng = np.random.default_rng(B)
+    prompts = [rng.integers(0, cfg["vocab_size"], L).tolist() for _ in range(B)]
+    singles = [_single(model, p, n, bits) for p in prompts]
+
+    cache = _cache(model, bits, B, L + n + 8)
+    for b, p in enumerate(prompts):
+        model.prefill_sequence(torch.tensor(p[:-1], dtype=torch.int32, device="cuda"), cache, b)
+    for c in cache:
+        c.offset = L - 1
+    tok = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device="cuda")
+    out = torch.empty(B, dtype=torch.int32, device="cuda")
+    for step in range(n):
+        lg = torch.empty(B, cfg["vocab_size"], dtype=torch.bfloat16, device="cuda")
+        model.forward_batch(tok, cache, logits=lg, argmax_out=out)
+        got = lg.float().cpu()
+        assert torch.equal(out.cpu().long(), got.argmax(-1)), "device argmax vs its own logits"
+        for b in range(B):
+            ref = singles[b][1][step]
+            cos = torch.nn.functional.cosine_similarity(got[b], ref, dim=0).item()
+            assert cos > 0.9999, (b, step, cos)
+            assert (got[b] - ref).abs().max().item() <= 0.05, (b, step)
+            top2 = ref.topk(2).values
+            if (top2[0] - top2[1]).item() > 0.02:
+                assert int(got[b].argmax()) == singles[b][0][step], (b, step)
+        # teacher-force every sequence on its single-run greedy token
+        tok = torch.tensor([s[0][step] for s in singles], dtype=torch.int32, device="cuda")
+    assert cache.offset == L - 1 + n

@@ -18,6 +18,8 @@ TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attent
             max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
 TINY_MOE = dict(TINY, model_type="qwen3_moe", num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
                 norm_topk_prob=True, intermediate_size=0)
+# top-8 routing (as Qwen3-30B-A3B / 235B-A22B): decode tokens take the tensor-core expert path
+TINY_MOE8 = dict(TINY_MOE, num_experts=32, num_experts_per_tok=8, moe_intermediate_size=192)
 QWEN3_06B = dict(model_type="qwen3", hidden_size=1024, num_hidden_layers=28, num_attention_heads=16,
                  num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=151936,
                  tie_word_embeddings=True, max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
@@ -132,6 +134,15 @@ def test_tiny_moe():
     rng = np.random.default_rng(9)
     prompt = rng.integers(0, TINY_MOE["vocab_size"], 20).tolist()
     _check(*_run(dev_model, ora, prompt, 6, 8, 8, 0), n_equal=6)
+
+
+def test_tiny_moe_top8_decode():
+    """k = 8 experts per token: decode steps run the tensor-core expert GEMVs
+    (moe_mma.cu), prefill the CUDA-core ones; both against the oracle."""
+    dev_model, ora = _build(TINY_MOE8, seed=12)
+    rng = np.random.default_rng(13)
+    prompt = rng.integers(0, TINY_MOE8["vocab_size"], 24).tolist()
+    _check(*_run(dev_model, ora, prompt, 10, 8, 8, 0), n_equal=10)
 
 
 def test_tiny_moe_prefill_gemm():

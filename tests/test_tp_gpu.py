@@ -16,6 +16,8 @@ TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attent
             max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
 TINY_MOE = dict(TINY, model_type="qwen3_moe", num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
                 norm_topk_prob=True, intermediate_size=0, tie_word_embeddings=False)
+# top-8: decode tokens take the tensor-core expert path, whose ranks write fp32 partials
+TINY_MOE8 = dict(TINY_MOE, num_experts=32, num_experts_per_tok=8, moe_intermediate_size=192)
 
 
 def _run(cfg, rank, world, prompt, n, prefill_step):
@@ -62,7 +64,7 @@ def _worker(rank, world, port, cfg, prompt, n, step, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("cfg", [TINY, TINY_MOE], ids=["tp2-dense", "ep2-moe"])
+@pytest.mark.parametrize("cfg", [TINY, TINY_MOE, TINY_MOE8], ids=["tp2-dense", "ep2-moe", "ep2-moe-top8"])
 @pytest.mark.parametrize("step", [8, 32], ids=["gemv-prefill", "gemm-prefill"])
 def test_two_rank_matches_one(cfg, step):
     import torch.multiprocessing as mp
