@@ -124,4 +124,96 @@ int moe_launch(const MoeArgs& a, cudaStream_t st) {
   return M5_OK;
 }
 
+// ------------------------------------------------ prefill: grouped by expert
+// (token, slot) pairs sorted by local expert with a single-CTA counting sort:
+// counts, exclusive offsets, and each pair's row in the expert-ordered
+// buffers (rows of one expert in any order: a GEMM row does not depend on the
+// others).  Pairs of experts on other ranks get -1.
+__global__ void __launch_bounds__(1024) moe_sort_kernel(const int32_t* __restrict__ ids, int pairs, int e_first,
+                                                        int e_local, int32_t* __restrict__ counts,
+                                                        int32_t* __restrict__ offsets, int32_t* __restrict__ pos) {
+  extern __shared__ int sh[];  // [e_local] counts, [e_local] fill cursors
+  int* cnt = sh;
+  int* cur = sh + e_local;
+  for (int e = threadIdx.x; e < e_local; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+    const int e = ids[i] - e_first;
+    if (e >= 0 && e < e_local) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < e_local; ++e) {
+      cur[e] = run;
+      offsets[e] = run;
+      counts[e] = cnt[e];
+      run += cnt[e];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+    const int e = ids[i] - e_first;
+    pos[i] = (e >= 0 && e < e_local) ? atomicAdd(&cur[e], 1) : -1;
+  }
+}
+
+// rows_out[pos[t * k + j]] = x[t] (16-byte copies), for pairs with a row
+__global__ void __launch_bounds__(256) moe_gather_kernel(const bf16* __restrict__ x, int H, int pairs, int k,
+                                                         const int32_t* __restrict__ pos, bf16* __restrict__ out) {
+  const int H8 = H >> 3;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < int64_t(pairs) * H8;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int pr = int(i / H8), c = int(i % H8);
+    const int r = pos[pr];
+    if (r < 0) continue;
+    reinterpret_cast<uint4*>(out + size_t(r) * H)[c] = reinterpret_cast<const uint4*>(x + size_t(pr / k) * H)[c];
+  }
+}
+
+// h[t] += bf16(sum_j bf16(y[pos[t, j]] * score[t, j])) in slot order (mlx-lm
+// Qwen3MoeSparseMoeBlock), or partial[t] = the fp32 sum (expert parallel).
+__global__ void __launch_bounds__(256) moe_combine_kernel(const bf16* __restrict__ y, int T, int H, int k,
+                                                          const int32_t* __restrict__ pos,
+                                                          const bf16* __restrict__ scores, bf16* __restrict__ h,
+                                                          float* __restrict__ partial) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < int64_t(T) * H;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int t = int(i / H), n = int(i % H);
+    float sum = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int r = pos[t * k + j];
+      if (r < 0) continue;
+      sum += rbf(bf2f(y[size_t(r) * H + n]) * bf2f(scores[t * k + j]));
+    }
+    if (partial) partial[i] = sum;
+    else h[i] = f2bf(bf2f(h[i]) + rbf(sum));
+  }
+}
+
+int moe_sort_launch(const int32_t* ids, int pairs, int e_first, int e_local, int32_t* counts, int32_t* offsets,
+                    int32_t* pos, cudaStream_t st) {
+  moe_sort_kernel<<<1, 1024, size_t(2) * e_local * sizeof(int), st>>>(ids, pairs, e_first, e_local, counts, offsets,
+                                                                      pos);
+  M5_LAUNCH_CHECK("moe sort launch");
+  return M5_OK;
+}
+
+int moe_gather_launch(const bf16* x, int H, int pairs, int k, const int32_t* pos, bf16* out, cudaStream_t st) {
+  const int64_t n = int64_t(pairs) * (H / 8);
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, sm_count() * 8);
+  moe_gather_kernel<<<blocks, 256, 0, st>>>(x, H, pairs, k, pos, out);
+  M5_LAUNCH_CHECK("moe gather launch");
+  return M5_OK;
+}
+
+int moe_combine_launch(const bf16* y, int T, int H, int k, const int32_t* pos, const bf16* scores, bf16* h,
+                       float* partial, cudaStream_t st) {
+  const int64_t n = int64_t(T) * H;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, sm_count() * 8);
+  moe_combine_kernel<<<blocks, 256, 0, st>>>(y, T, H, k, pos, scores, h, partial);
+  M5_LAUNCH_CHECK("moe combine launch");
+  return M5_OK;
+}
+
 }  // namespace m5

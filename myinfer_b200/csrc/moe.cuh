@@ -33,6 +33,14 @@ struct MoeArgs {
 };
 
 int moe_launch(const MoeArgs& a, cudaStream_t stream);
+// Prefill grouped by expert: sort (token, slot) pairs by local expert, gather
+// the normalised rows into expert order, and after the per-expert GEMMs add the
+// slots back per token (moe.cu; the runtime drives the GEMMs).
+int moe_sort_launch(const int32_t* ids, int pairs, int e_first, int e_local, int32_t* counts, int32_t* offsets,
+                    int32_t* pos, cudaStream_t stream);
+int moe_gather_launch(const bf16* x, int H, int pairs, int k, const int32_t* pos, bf16* out, cudaStream_t stream);
+int moe_combine_launch(const bf16* y, int T, int H, int k, const int32_t* pos, const bf16* scores, bf16* h,
+                       float* partial, cudaStream_t stream);
 // One decode token (T == 1, k == 8) on the tensor cores; moe_launch otherwise.
 bool moe_mma_eligible(const MoeArgs& a);
 int moe_mma_launch(const MoeArgs& a, cudaStream_t stream);

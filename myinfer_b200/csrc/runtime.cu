@@ -67,6 +67,18 @@ struct Model {
   int mma_rows = 0;
   float* moe_ybuf = nullptr;  // zeroed [k, H] and [H/16] scratch of the tensor-core expert path
   int* moe_ncnt = nullptr;
+  // MoE prefill grouped by expert (T >= kGemmMinTokens): expert-ordered rows and
+  // the per-expert GEMMs' side streams
+  bf16* moe_x = nullptr;       // [T k, H]
+  bf16* moe_act = nullptr;     // [T k, I]
+  bf16* moe_y = nullptr;       // [T k, H]
+  bf16* moe_xs = nullptr;      // [T k, 64 (C_H + C_I)] group sums of the GEMM inputs
+  int32_t* moe_pos = nullptr;  // [T k]
+  int32_t* moe_cnt = nullptr;  // [E_local] counts, [E_local] offsets
+  int32_t* h_moe_cnt = nullptr;  // pinned copy of the counts
+  static constexpr int kMoeStreams = 4;
+  cudaStream_t moe_st[kMoeStreams] = {};
+  cudaEvent_t moe_fork = nullptr, moe_join[kMoeStreams] = {};
   bf16* xn = nullptr;        // RMSNorm(h) materialised for the prefill GEMM [T, H]
   bf16* gxs = nullptr;       // per-token group sums of the prefill GEMM input
   size_t gxs_bytes = 0;
@@ -296,6 +308,70 @@ __global__ void add_len_kernel(int32_t* d_len, int L) {
   *d_len += L;
 }
 
+// Routed experts of T >= kGemmMinTokens tokens grouped by expert: counting
+// sort of the (token, slot) pairs, the normalised rows gathered into expert
+// order, one host sync for the per-expert counts, then per local expert a
+// gate/up (SwiGLU) and a down tensor-core GEMM over just its rows, spread over
+// side streams, and a per-token combine in slot order.  Each expert's weights
+// stream once per chunk instead of once per routed token.
+static int moe_prefill_grouped(Model* m, const Layer& ly, int T, cudaStream_t st) {
+  const m5_model_cfg& c = m->cfg;
+  const int H = c.hidden_size, I = m->I, k = c.experts_per_tok, El = m->E_local, pairs = T * k;
+  int rc = rms_norm_launch(m->h, ly.post_norm, T, H, c.rms_norm_eps, m->xn, st);
+  if (!rc) rc = moe_sort_launch(m->rids, pairs, m->e_first, El, m->moe_cnt, m->moe_cnt + El, m->moe_pos, st);
+  if (!rc) rc = moe_gather_launch(m->xn, H, pairs, k, m->moe_pos, m->moe_x, st);
+  if (rc) return rc;
+  M5_CUDA(cudaMemcpyAsync(m->h_moe_cnt, m->moe_cnt, size_t(El) * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  M5_CUDA(cudaStreamSynchronize(st));
+  M5_CUDA(cudaEventRecord(m->moe_fork, st));
+  for (int i = 0; i < Model::kMoeStreams; ++i) M5_CUDA(cudaStreamWaitEvent(m->moe_st[i], m->moe_fork, 0));
+  const size_t xs_h = size_t(64) * ((H / 64 + 31) / 32), xs_i = size_t(64) * ((I / 64 + 31) / 32);
+  bf16* xs_gu = m->moe_xs;
+  bf16* xs_dn = m->moe_xs + size_t(pairs) * xs_h;
+  const size_t H8 = H / 8, H64 = H / 64, I8 = I / 8, I64 = I / 64;
+  int off = 0, used = 0;
+  for (int e = 0; e < El && !rc; ++e) {
+    const int n = m->h_moe_cnt[e];
+    if (n <= 0) continue;
+    cudaStream_t ss = m->moe_st[used++ % Model::kMoeStreams];
+    GemvArgs g{};
+    g.x = m->moe_x + size_t(off) * H;
+    g.ldx = H;
+    g.K = H;
+    g.nseg = 2;
+    g.seg[0] = GemvSeg{ly.e_gate.w + size_t(e) * I * H8, ly.e_gate.s + size_t(e) * I * H64,
+                       ly.e_gate.b + size_t(e) * I * H64, I, m->moe_act + size_t(off) * I, nullptr};
+    g.seg[1] = GemvSeg{ly.e_up.w + size_t(e) * I * H8, ly.e_up.s + size_t(e) * I * H64,
+                       ly.e_up.b + size_t(e) * I * H64, I, nullptr, nullptr};
+    g.ldy = I;
+    g.total_rows = I;
+    rc = gemm_tc_launch(g, n, EPI_SWIGLU, xs_gu + size_t(off) * xs_h, size_t(n) * xs_h * 2, ss);
+    if (rc) break;
+    GemvArgs d{};
+    d.x = m->moe_act + size_t(off) * I;
+    d.ldx = I;
+    d.K = I;
+    d.nseg = 1;
+    d.seg[0] = GemvSeg{ly.e_down.w + size_t(e) * H * I8, ly.e_down.s + size_t(e) * H * I64,
+                       ly.e_down.b + size_t(e) * H * I64, H, m->moe_y + size_t(off) * H, nullptr};
+    d.ldy = H;
+    d.total_rows = H;
+    rc = gemm_tc_launch(d, n, EPI_STORE, xs_dn + size_t(off) * xs_i, size_t(n) * xs_i * 2, ss);
+    off += n;
+  }
+  for (int i = 0; i < Model::kMoeStreams; ++i) {  // join even after an error: no stream is left behind
+    M5_CUDA(cudaEventRecord(m->moe_join[i], m->moe_st[i]));
+    M5_CUDA(cudaStreamWaitEvent(st, m->moe_join[i], 0));
+  }
+  if (rc) return rc;
+  return moe_combine_launch(m->moe_y, T, H, k, m->moe_pos, m->rscores, m->h, c.ep_size > 1 ? m->hf : nullptr, st);
+}
+
+static bool stream_capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  return cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+}
+
 // One model call: L tokens of one sequence at positions *d_len.., or (B > 1,
 // L == 1) one token of each of B sequences, all at position *d_len, over a
 // cache of [B, Hkv, capacity, ...] layers.  T = L * B activation rows.
@@ -449,7 +525,10 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       me.ybuf = m->moe_ybuf;
       me.ncnt = m->moe_ncnt;
       if (c.ep_size > 1) me.partial = m->hf;  // this rank's experts give a partial sum
-      rc = moe_mma_eligible(me) ? moe_mma_launch(me, st) : moe_launch(me, st);
+      if (T >= kGemmMinTokens && m->moe_x && T <= m->max_tokens && !stream_capturing(st))
+        rc = moe_prefill_grouped(m, ly, T, st);
+      else
+        rc = moe_mma_eligible(me) ? moe_mma_launch(me, st) : moe_launch(me, st);
       if (rc || (c.ep_size > 1 && (rc = reduce_into_h(m, T, st)))) return rc;
     }
   }
@@ -722,6 +801,12 @@ extern "C" int m5_model_destroy(void* model) {
   if (!m) return M5_OK;
   if (m->arena) cudaFree(m->arena);
   if (m->d_inv_freq) cudaFree(m->d_inv_freq);
+  if (m->h_moe_cnt) cudaFreeHost(m->h_moe_cnt);
+  for (int i = 0; i < Model::kMoeStreams; ++i) {
+    if (m->moe_st[i]) cudaStreamDestroy(m->moe_st[i]);
+    if (m->moe_join[i]) cudaEventDestroy(m->moe_join[i]);
+  }
+  if (m->moe_fork) cudaEventDestroy(m->moe_fork);
   delete m;
   return M5_OK;
 }
@@ -784,6 +869,8 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   const int mrows16 = (mrows + 15) / 16 * 16;
   const int maxK = (int)std::max<size_t>({H, size_t(m->Hq) * D, size_t(m->I)});
   const size_t gxs = T >= kGemmMinTokens ? gemm_tc_xs_bytes((int)T, maxK) : 0;
+  const bool moe_pre = c.num_experts > 0 && T >= kGemmMinTokens;  // prefill grouped by expert
+  auto gxs_c = [](size_t K) { return (K / 64 + 31) / 32; };         // bias blocks of a GEMM input
   const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
                           size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,
                           part, argmax_scratch_bytes(), gemv_mma_scratch_bytes(mrows16),
@@ -792,7 +879,13 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
                           c.tp_size > 1 ? std::min<size_t>(T, 16) * m->Vl * 2 : 0,
                           c.tp_size > 1 ? size_t(c.tp_size) * std::min<size_t>(T, 16) * m->Vl * 2 : 0,
                           c.num_experts ? k * H * sizeof(float) : 0,
-                          c.num_experts ? (H / 16 + 1) * sizeof(int) : 0};
+                          c.num_experts ? (H / 16 + 1) * sizeof(int) : 0,
+                          moe_pre ? T * k * H * 2 : 0,
+                          moe_pre ? T * k * m->I * 2 : 0,
+                          moe_pre ? T * k * H * 2 : 0,
+                          moe_pre ? T * k * 64 * (gxs_c(H) + gxs_c(m->I)) * 2 : 0,
+                          moe_pre ? T * k * 4 : 0,
+                          moe_pre ? size_t(2) * m->E_local * 4 : 0};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -829,6 +922,20 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->v_rows = (int)std::min<size_t>(T, 16);
   m->moe_ybuf = sizes[17] ? (float*)carve(p, sizes[17]) : nullptr;
   m->moe_ncnt = sizes[18] ? (int*)carve(p, sizes[18]) : nullptr;
+  m->moe_x = sizes[19] ? (bf16*)carve(p, sizes[19]) : nullptr;
+  m->moe_act = sizes[20] ? (bf16*)carve(p, sizes[20]) : nullptr;
+  m->moe_y = sizes[21] ? (bf16*)carve(p, sizes[21]) : nullptr;
+  m->moe_xs = sizes[22] ? (bf16*)carve(p, sizes[22]) : nullptr;
+  m->moe_pos = sizes[23] ? (int32_t*)carve(p, sizes[23]) : nullptr;
+  m->moe_cnt = sizes[24] ? (int32_t*)carve(p, sizes[24]) : nullptr;
+  if (moe_pre && !m->h_moe_cnt) {
+    M5_CUDA(cudaMallocHost(&m->h_moe_cnt, size_t(m->E_local) * sizeof(int32_t)));
+    M5_CUDA(cudaEventCreateWithFlags(&m->moe_fork, cudaEventDisableTiming));
+    for (int i = 0; i < Model::kMoeStreams; ++i) {
+      M5_CUDA(cudaStreamCreateWithFlags(&m->moe_st[i], cudaStreamNonBlocking));
+      M5_CUDA(cudaEventCreateWithFlags(&m->moe_join[i], cudaEventDisableTiming));
+    }
+  }
   m->max_tokens = max_tokens;
   return M5_OK;
 }

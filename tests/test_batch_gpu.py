@@ -5,7 +5,10 @@ Both runs are teacher-forced on the single-sequence greedy tokens, so every
 step compares logits of identical inputs.  The batched projections run as
 one GEMV over B rows (B <= 15) or the tensor-core GEMM (B >= 16) instead of
 B single-row GEMVs, so fp32 sums differ in order: logits cosine > 0.9999 and
-max-abs <= 0.05, greedy tokens equal except at top-2 gaps below 0.02."""
+max-abs <= 0.05, greedy tokens equal except at top-2 gaps below 0.02.  MoE
+rows may route differently at router near-ties (the router logits come from
+a different kernel), as the model parity tests allow: for MoE at least 95 %
+of the rows meet the bar and all have cosine > 0.999."""
 
 import numpy as np
 import pytest
@@ -68,6 +71,8 @@ def test_batched_decode_matches_single(cfg, B):
         c.offset = L - 1
     tok = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device="cuda")
     out = torch.empty(B, dtype=torch.int32, device="cuda")
+    moe = "num_experts" in cfg
+    off_bar = []
     for step in range(n):
         lg = torch.empty(B, cfg["vocab_size"], dtype=torch.bfloat16, device="cuda")
         model.forward_batch(tok, cache, logits=lg, argmax_out=out)
@@ -76,11 +81,15 @@ def test_batched_decode_matches_single(cfg, B):
         for b in range(B):
             ref = singles[b][1][step]
             cos = torch.nn.functional.cosine_similarity(got[b], ref, dim=0).item()
-            assert cos > 0.9999, (b, step, cos)
-            assert (got[b] - ref).abs().max().item() <= 0.05, (b, step)
+            close = cos > 0.9999 and (got[b] - ref).abs().max().item() <= 0.05
+            if not close:
+                assert moe and cos > 0.999, (b, step, cos)
+                off_bar.append((b, step, cos))
+                continue
             top2 = ref.topk(2).values
             if (top2[0] - top2[1]).item() > 0.02:
                 assert int(got[b].argmax()) == singles[b][0][step], (b, step)
         # teacher-force every sequence on its single-run greedy token
         tok = torch.tensor([s[0][step] for s in singles], dtype=torch.int32, device="cuda")
+    assert len(off_bar) <= 0.05 * B * n, off_bar
     assert cache.offset == L - 1 + n
