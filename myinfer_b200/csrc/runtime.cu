@@ -67,7 +67,7 @@ struct Model {
   int mma_rows = 0;
   float* moe_ybuf = nullptr;  // zeroed [k, H] and [H/16] scratch of the tensor-core expert path
   int* moe_ncnt = nullptr;
-  // MoE prefill grouped by expert (T >= kGemmMinTokens): expert-ordered rows and
+  // MoE prefill grouped by expert (T >= kMoeGroupedMinTokens): expert-ordered rows and
   // the per-expert GEMMs' side streams
   bf16* moe_x = nullptr;       // [T k, H]
   bf16* moe_act = nullptr;     // [T k, I]
@@ -93,6 +93,13 @@ struct Model {
 // Token count from which a projection runs as the tensor-core GEMM instead of
 // chunks of the streaming GEMV (the GEMV re-reads the weights every 8 tokens).
 constexpr int kGemmMinTokens = 16;
+// Projections take the tensor-core GEMM from this many rows on: its dequant
+// work per weight does not shrink with the row count, so below ~40 rows
+// (batched decode) passes of the 8-row GEMV stream the weights faster.
+constexpr int kGemmMinRows = 40;
+// Routed experts of a call go through the per-expert GEMMs from this many
+// tokens on (below, the per-token expert GEMVs: too few rows per expert).
+constexpr int kMoeGroupedMinTokens = 64;
 
 static bool parse_layer(const char* name, int& idx, const char*& rest) {
   const char* p = "model.layers.";
@@ -217,7 +224,7 @@ static void attach(const Model* m, GemvArgs& a) {
 // One projection of T tokens: the tensor-core GEMM for prefill-sized T (with
 // the fused RMSNorm materialised first), the streaming GEMV otherwise.
 static int linear_auto(const Model* m, const GemvArgs& proto, int T, int epi, cudaStream_t st) {
-  if (T >= kGemmMinTokens && m->gxs && gemm_tc_xs_bytes(T, proto.K) <= m->gxs_bytes) {
+  if (T >= kGemmMinRows && m->gxs && gemm_tc_xs_bytes(T, proto.K) <= m->gxs_bytes) {
     GemvArgs a = proto;
     if (proto.norm_w) {
       a.norm_w = nullptr;
@@ -308,7 +315,7 @@ __global__ void add_len_kernel(int32_t* d_len, int L) {
   *d_len += L;
 }
 
-// Routed experts of T >= kGemmMinTokens tokens grouped by expert: counting
+// Routed experts of T >= kMoeGroupedMinTokens tokens grouped by expert: counting
 // sort of the (token, slot) pairs, the normalised rows gathered into expert
 // order, one host sync for the per-expert counts, then per local expert a
 // gate/up (SwiGLU) and a down tensor-core GEMM over just its rows, spread over
@@ -525,7 +532,7 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       me.ybuf = m->moe_ybuf;
       me.ncnt = m->moe_ncnt;
       if (c.ep_size > 1) me.partial = m->hf;  // this rank's experts give a partial sum
-      if (T >= kGemmMinTokens && m->moe_x && T <= m->max_tokens && !stream_capturing(st))
+      if (T >= kMoeGroupedMinTokens && m->moe_x && T <= m->max_tokens && !stream_capturing(st))
         rc = moe_prefill_grouped(m, ly, T, st);
       else
         rc = moe_mma_eligible(me) ? moe_mma_launch(me, st) : moe_launch(me, st);
@@ -869,7 +876,7 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   const int mrows16 = (mrows + 15) / 16 * 16;
   const int maxK = (int)std::max<size_t>({H, size_t(m->Hq) * D, size_t(m->I)});
   const size_t gxs = T >= kGemmMinTokens ? gemm_tc_xs_bytes((int)T, maxK) : 0;
-  const bool moe_pre = c.num_experts > 0 && T >= kGemmMinTokens;  // prefill grouped by expert
+  const bool moe_pre = c.num_experts > 0 && T >= kMoeGroupedMinTokens;  // prefill grouped by expert
   auto gxs_c = [](size_t K) { return (K / 64 + 31) / 32; };         // bias blocks of a GEMM input
   const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
                           size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,

@@ -146,11 +146,12 @@ def test_tiny_moe_top8_decode():
 
 
 def test_tiny_moe_prefill_gemm():
-    """32-token prefill chunks: attention projections on the tensor-core GEMM."""
+    """64-token prefill chunks: projections on the tensor-core GEMM, routed
+    experts grouped by expert (per-expert GEMMs)."""
     dev_model, ora = _build(TINY_MOE, seed=8)
     rng = np.random.default_rng(10)
     prompt = rng.integers(0, TINY_MOE["vocab_size"], 70).tolist()
-    _check(*_run(dev_model, ora, prompt, 6, 32, 8, 0), n_equal=6)
+    _check(*_run(dev_model, ora, prompt, 6, 64, 8, 0), n_equal=6)
 
 
 def test_tiny_dense_long_prefill():

@@ -38,7 +38,7 @@ def _run(cfg, rank, world, prompt, n, prefill_step):
         w = shard_weights(full, args, **kw)
     else:
         kw, w = {}, full
-    model = Model(args, w, dev, max_tokens=64, comm=comm, **kw)
+    model = Model(args, w, dev, max_tokens=128, comm=comm, **kw)
     out = list(generate_step(prompt, model, n, prompt_cache=make_prompt_cache(model), prefill_step_size=prefill_step,
                              kv_bits=8, quantized_kv_start=0, return_logits=True))
     toks = [t for t, _ in out]
@@ -65,10 +65,10 @@ def _worker(rank, world, port, cfg, prompt, n, step, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("cfg", [TINY, TINY_MOE, TINY_MOE8], ids=["tp2-dense", "ep2-moe", "ep2-moe-top8"])
-@pytest.mark.parametrize("step", [8, 32], ids=["gemv-prefill", "gemm-prefill"])
+@pytest.mark.parametrize("step", [8, 64], ids=["gemv-prefill", "gemm-prefill"])
 def test_two_rank_matches_one(cfg, step):
     import torch.multiprocessing as mp
-    prompt = np.random.default_rng(4).integers(0, cfg["vocab_size"], 40).tolist()
+    prompt = np.random.default_rng(4).integers(0, cfg["vocab_size"], 80).tolist()
     n = 8
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
