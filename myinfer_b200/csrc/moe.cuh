@@ -41,6 +41,21 @@ int moe_sort_launch(const int32_t* ids, int pairs, int e_first, int e_local, int
 int moe_gather_launch(const bf16* x, int H, int pairs, int k, const int32_t* pos, bf16* out, cudaStream_t stream);
 int moe_combine_launch(const bf16* y, int T, int H, int k, const int32_t* pos, const bf16* scores, bf16* h,
                        float* partial, cudaStream_t stream);
+// Router logits + top-k of one decode token in one launch (moe_mma.cu).
+struct MoeRouterArgs {
+  const bf16* x;          // [H] residual stream, RMS-normalised inside with norm_w
+  const bf16* norm_w;
+  float eps;
+  const uint32_t* w;      // router [E, H/8] w4g64
+  const bf16* s;
+  const bf16* b;
+  int H, E, k, norm_topk;
+  bf16* logits;           // [E] scratch
+  int32_t* ids;           // [k]
+  bf16* scores;           // [k]
+  int* counter;           // zeroed, left zeroed
+};
+int moe_router_topk_launch(const MoeRouterArgs& a, cudaStream_t stream);
 // One decode token (T == 1, k == 8) on the tensor cores; moe_launch otherwise.
 bool moe_mma_eligible(const MoeArgs& a);
 int moe_mma_launch(const MoeArgs& a, cudaStream_t stream);

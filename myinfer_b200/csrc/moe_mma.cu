@@ -25,6 +25,7 @@
 
 #include "frag_stage.cuh"
 #include "gemv.cuh"
+#include "gemv_impl.cuh"
 #include "mma_dq.cuh"
 #include "moe.cuh"
 
@@ -288,6 +289,111 @@ __global__ void __launch_bounds__(MX_W * 32, 2) moe_down_mma_kernel(const MoeArg
     if (lane == 0) a.ncnt[nb] = 0;
   };
   mx_walk<MT>(sb, se, I, xf, xg, row_of, flush);
+}
+
+// Router + top-k of one decode token in one launch: each warp takes one of
+// the E router rows (RMSNorm(h) staged once per CTA, CUDA-core dot product as
+// moe.cu), rounds the logit to bf16 like the router projection's output, and
+// the last CTA to finish (a zeroed counter it leaves zeroed) runs the top-k:
+// softmax in fp32 rounded to bf16, the k largest probabilities (ties -> lower
+// expert id) in order, renormalised when norm_topk (same rules as
+// moe_topk_kernel for one token).
+constexpr int RT_W = 8;
+__global__ void __launch_bounds__(RT_W * 32) moe_router_topk_kernel(const MoeRouterArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) float rsm[];
+  const int H = a.H, E = a.E;
+  float* xs = rsm;
+  float* xsum = xs + H;
+  float* red = xsum + (H >> 5);
+  stage_rows<1>(a.x, H, H, a.norm_w, a.eps, xs, xsum, red);
+  const int lane = threadIdx.x & 31, row = blockIdx.x * RT_W + (threadIdx.x >> 5);
+  if (row < E) {
+    float acc[1] = {0.f};
+    const size_t H8 = H >> 3, H64 = H >> 6;
+    row_dot<1, 4>(a.w + row * H8, a.s + row * H64, a.b + row * H64, H, xs, xsum, acc);
+    const float v = rbf(warp_sum(acc[0]));
+    if (lane == 0) a.logits[row] = f2bf(v);
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) last = atomicAdd(a.counter, 1) == int(gridDim.x) - 1;
+  __syncthreads();
+  if (!last || threadIdx.x >= 32) return;
+  __threadfence();
+  constexpr int PER = 8;  // E <= 256
+  float v[PER];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? bf2f(__ldcg(a.logits + e)) : -INFINITY;
+    mx = fmaxf(mx, v[j]);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    v[j] = (lane + 32 * j < E) ? expf(v[j] - mx) : 0.f;
+    sum += v[j];
+  }
+  sum = warp_sum(sum);
+#pragma unroll
+  for (int j = 0; j < PER; ++j) v[j] = (lane + 32 * j < E) ? rbf(__fdiv_rn(v[j], sum)) : -INFINITY;
+  float chosen = 0.f, my_score = 0.f;
+  int my_id = -1;
+  for (int r = 0; r < a.k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && (v[j] > bv || (v[j] == bv && e < bi))) {
+        bv = v[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (lane + 32 * j == bi) v[j] = -INFINITY;
+    chosen += bv;
+    if (lane == r) {
+      my_score = bv;
+      my_id = bi;
+    }
+  }
+  if (lane < a.k) {
+    float sc = my_score;
+    if (a.norm_topk) sc = rbf(__fdiv_rn(sc, rbf(chosen)));
+    a.ids[lane] = my_id;
+    a.scores[lane] = f2bf(sc);
+  }
+  if (lane == 0) *a.counter = 0;
+}
+
+int moe_router_topk_launch(const MoeRouterArgs& a, cudaStream_t st) {
+  if (a.E > 256 || a.k <= 0 || a.k > 32 || a.k > a.E || a.H % 256) return fail(M5_ERR_INVALID, "moe router: shape");
+  const size_t smem = size_t(a.H) * 4 + size_t(a.H / 32) * 4 + 33 * 4;
+  static bool configured = false;
+  if (!configured) {
+    M5_CUDA(cudaFuncSetAttribute(moe_router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    configured = true;
+  }
+  if (smem > 100 * 1024) return fail(M5_ERR_INVALID, "moe router: hidden size too large");
+  M5_CUDA(launch_pdl(moe_router_topk_kernel, dim3(ceil_div(a.E, RT_W)), dim3(RT_W * 32), smem, st, a));
+  M5_LAUNCH_CHECK("moe router/top-k launch");
+  return M5_OK;
 }
 
 static size_t mx_smem(int MT, int K) { return size_t(MT) * (K / 64) * 32 * 4 + size_t(MT) * (K / 64) * 4 + 33 * 4; }
