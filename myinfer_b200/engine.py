@@ -20,14 +20,14 @@ import json
 import logging
 import threading
 import time
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass, field, replace
 from pathlib import Path
 from typing import Any, Dict, Iterator, List, Optional
 
 import torch
 
 from . import attention
-from .cache import make_prompt_cache
+from .cache import PromptCache, make_prompt_cache
 from .context import (GB, MAX_YARN_FACTOR, ContextPlan, KVFootprint, apply_yarn, kv_estimate_per_token,
                       measure_kv_footprint, native_context, plan_context, reserve_bytes, yarn_capable,
                       yarn_factor_for)
@@ -281,12 +281,16 @@ class Engine:
         t0 = time.perf_counter()
         if opts.kv_bits not in (0, 4, 8):
             raise EngineError("kv_bits must be 0 (bf16), 4 or 8")
-        if opts.draft_model:
-            raise EngineError("draft models are not supported by this build")
         model, tokenizer, config = _load_model(opts)
+        draft, draft_yarn = None, False
+        if opts.draft_model:  # engine.py:223-228: a second, smaller model for speculative decoding
+            draft, _, dconfig = _load_model(replace(opts, model=opts.draft_model))
+            if draft.args.vocab_size != model.args.vocab_size:
+                raise EngineError("draft model vocabulary differs from the main model's")
+            draft_yarn = yarn_capable(dconfig)
         budget = self.budget_bytes(opts)
         native, plain_limit = native_context(config)
-        resident = model.nbytes
+        resident = model.nbytes + (draft.nbytes if draft is not None else 0)
         hidden = int(config.get("hidden_size") or 4096)
         if resident + reserve_bytes(budget, hidden, opts.prefill_step) > budget:
             raise EngineError(f"Model needs {resident / GB:.1f} GB but the GPU budget is {budget / GB:.1f} GB.")
@@ -295,6 +299,9 @@ class Engine:
             dense_fp = measure_kv_footprint(model, 0)
             extra = max(0.0, dense_fp.bytes_per_token - fp.bytes_per_token) * opts.quantized_kv_start
             fp = KVFootprint(fp.bytes_per_token, int(fp.fixed_bytes + extra), fp.kv_bits)
+        if draft is not None:  # the draft's cache grows with the same tokens (engine.py:276-277)
+            dfp = measure_kv_footprint(draft, opts.kv_bits, opts.kv_group_size)
+            fp = KVFootprint(fp.bytes_per_token + dfp.bytes_per_token, fp.fixed_bytes + dfp.fixed_bytes, fp.kv_bits)
         plan = plan_context(config=config, footprint=fp, budget_bytes=budget, resident_weight_bytes=resident,
                             expert_cache_bytes=0, prefill_step=opts.prefill_step, rope_scaling=opts.rope_scaling,
                             requested_context=opts.max_context)
@@ -302,6 +309,7 @@ class Engine:
             raise EngineError(f"Only {plan.max_context} tokens of KV cache fit in memory; "
                               "use kv_bits=4 or a smaller model.")
         self.model, self.tokenizer = model, tokenizer
+        self.draft_model, self._draft_yarn = draft, draft_yarn
         self.config, self.options = config, opts
         self.plan, self.footprint = plan, fp
         self.resident_bytes = resident
@@ -319,6 +327,8 @@ class Engine:
         if factor == self._yarn_now:
             return
         apply_yarn(self.model, factor, self._native)
+        if self.draft_model is not None and self._draft_yarn:
+            apply_yarn(self.draft_model, factor, self._native)
         self._yarn_now = factor
 
     def _yarn_for_request(self, tokens: int) -> float:
@@ -372,19 +382,32 @@ class Engine:
             self._set_yarn(factor)
             key = f"yarn={factor}"
             use_prefix = opts.prefix_cache and params.use_prefix_cache
+            draft = self.draft_model if params.use_draft else None
+            # with a draft model the cached context covers both models' layers
+            # (engine.py:373-377); a request without it keeps the main layers only
+            # and does not return them to the prefix cache (engine.py:393-395, 459)
+            if self.draft_model is not None and draft is None:
+                use_prefix = False
             cache, hit = (self.prefix.take(key, tokens) if use_prefix else (None, 0))
             if cache is None:
                 cache = make_prompt_cache(self.model)
+                if draft is not None:
+                    cache = PromptCache(list(cache) + list(make_prompt_cache(draft)), self.model.device)
                 hit = 0
+            n_main = self.model.args.num_hidden_layers
+            main_cache = cache if draft is None else PromptCache(list(cache)[:n_main], self.model.device)
             need = self.footprint.bytes_for(len(tokens) + max_tokens)
             self.prefix.evict_to(self.plan.kv_budget_bytes - need)
             if params.seed is not None:
                 torch.manual_seed(params.seed)
             sampler = _make_sampler(params.temperature, params.top_p if params.top_p < 1 else 0.0, params.min_p,
                                     params.top_k)
-            kwargs = dict(sampler=sampler, prompt_cache=cache, prefill_step_size=opts.prefill_step,
+            kwargs = dict(sampler=sampler, prompt_cache=main_cache, prefill_step_size=opts.prefill_step,
                           kv_bits=opts.kv_bits or None, kv_group_size=opts.kv_group_size,
                           quantized_kv_start=opts.quantized_kv_start)
+            if draft is not None:
+                kwargs.update(draft_model=draft, num_draft_tokens=opts.num_draft_tokens,
+                              draft_cache=PromptCache(list(cache)[n_main:], self.model.device))
             m = RequestMetrics(prompt_tokens=len(tokens), cached_tokens=hit, yarn_factor=factor)
             torch.cuda.reset_peak_memory_stats(self.model.device)
             generated: List[int] = []
@@ -435,6 +458,8 @@ class Engine:
                 self.totals["completion_tokens"] += m.completion_tokens
                 self.totals["cached_tokens"] += m.cached_tokens
                 if use_prefix:
+                    if draft is not None:  # the sub-lists may have swapped layers when quantizing
+                        cache = PromptCache(list(main_cache) + list(kwargs["draft_cache"]), self.model.device)
                     self.prefix.put(key, tokens + generated, cache)
             yield Chunk("", finish, m)
 
@@ -455,7 +480,9 @@ class Engine:
         return {"time": time.time(), "model": self.options.model, "prompt_tokens": m.prompt_tokens,
                 "completion_tokens": m.completion_tokens, "ttft_ms": round(m.ttft_ms, 1),
                 "prompt_tps": round(m.prompt_tps, 1), "decode_tps": round(m.decode_tps, 2),
-                "peak_memory_gb": m.peak_memory_gb, "draft_model": None, "draft_accepted": 0,
+                "peak_memory_gb": m.peak_memory_gb,
+                "draft_model": self.options.draft_model if use_draft and self.draft_model is not None else None,
+                "draft_accepted": m.draft_accepted,
                 "kv_bits": self.options.kv_bits, "max_context": self.plan.max_context,
                 "expert_streaming": False, "expert_hit_rate": None, "device": torch.cuda.get_device_name(),
                 "chip": torch.cuda.get_device_name()}

@@ -24,7 +24,7 @@ import torch
 
 from . import _lib
 from .attention import safe_maybe_quantize_kv_cache
-from .cache import PromptCache, make_prompt_cache
+from .cache import PromptCache, make_prompt_cache, trim_prompt_cache
 
 
 @dataclass
@@ -165,11 +165,112 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
         stats["decode_time"] = time.perf_counter() - t1
 
 
+def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_tokens: int = 2,
+                              max_tokens: int = 256, sampler: Optional[Callable] = None,
+                              prompt_cache: Optional[PromptCache] = None, draft_cache: Optional[PromptCache] = None,
+                              prefill_step_size: int = 2048, kv_bits: Optional[int] = None,
+                              kv_group_size: int = 64, quantized_kv_start: int = 0,
+                              stats: Optional[dict] = None) -> Iterator[tuple]:
+    """Speculative decoding with a draft model (the algorithm of mlx-lm's
+    ``speculative_generate_step``, which the reference reaches through
+    ``stream_generate(..., draft_model=...)`` at m5engine/engine.py:420-423):
+    each round the draft model proposes up to ``num_draft_tokens`` tokens one at
+    a time, the main model scores the pending token plus all proposals in one
+    call, the longest prefix of proposals equal to the main model's own choices
+    is accepted, and the main model's choice after it is emitted too.  Yields
+    (token, from_draft).  Both caches are trimmed back to the accepted context
+    (move-not-copy); when every proposal was accepted, the last one is fed to the
+    draft model at the start of the next round.  With a greedy sampler the
+    tokens equal the main model's greedy decode."""
+    if not prompt:
+        raise ValueError("empty prompt")
+    if draft_model.args.vocab_size != model.args.vocab_size:
+        raise ValueError("draft model vocabulary differs from the main model's")
+    dev = model.device
+    mcache = prompt_cache if prompt_cache is not None else make_prompt_cache(model)
+    dcache = draft_cache if draft_cache is not None else make_prompt_cache(draft_model)
+    prompt_t = torch.as_tensor(prompt, dtype=torch.int32).to(dev, non_blocking=True)
+    greedy = sampler is None
+    k_max = max(1, num_draft_tokens)
+    total = max(mcache.offset, dcache.offset) + len(prompt) + max_tokens + k_max + 1
+    model.reserve(max(k_max + 1, min(prefill_step_size, max(1, len(prompt) - 1))))
+    draft_model.reserve(min(prefill_step_size, max(1, len(prompt) - 1)))
+
+    def maybe_quantize(cache):
+        safe_maybe_quantize_kv_cache(cache, quantized_kv_start, kv_group_size, kv_bits)
+        for c in cache:
+            if c.capacity < total:
+                c.reserve(total)
+
+    def prefill(m, cache, ids):
+        for p0 in range(0, ids.numel(), prefill_step_size):
+            m.forward(ids[p0:p0 + prefill_step_size], cache)
+            maybe_quantize(cache)
+
+    def pick(logits):  # [L, V] -> int32 [L] on the device
+        if greedy:
+            return logits.float().argmax(dim=-1).to(torch.int32)
+        return sampler(logits.float()).to(torch.int32).reshape(-1)
+
+    t0 = time.perf_counter()
+    prefill(model, mcache, prompt_t[:-1])
+    prefill(draft_model, dcache, prompt_t[:-1])
+    if stats is not None:
+        stats["prompt_time"] = time.perf_counter() - t0
+        stats["prompt_tokens"] = len(prompt)
+    V = model.args.vocab_size
+    y = prompt_t[-1:].clone()          # pending token: in neither cache yet
+    backlog = None                     # draft token the draft cache still lacks
+    ntoks = 0
+    t1 = time.perf_counter()
+    while ntoks < max_tokens:
+        nd = min(max_tokens - ntoks, k_max)
+        if backlog is not None:
+            draft_model.forward(backlog, dcache)
+            maybe_quantize(dcache)
+            backlog = None
+        drafts = []
+        t = y
+        for _ in range(nd):
+            lg = torch.empty(1, V, dtype=torch.bfloat16, device=dev)
+            draft_model.forward(t, dcache, _lib.M5_LOGITS_LAST, lg)
+            maybe_quantize(dcache)
+            t = pick(lg)
+            drafts.append(t)
+        d = torch.cat(drafts)
+        vlog = torch.empty(nd + 1, V, dtype=torch.bfloat16, device=dev)
+        model.forward(torch.cat([y, d]), mcache, _lib.M5_LOGITS_ALL, vlog)
+        maybe_quantize(mcache)
+        v = pick(vlog)
+        dh, vh = d.tolist(), v.tolist()  # one host sync per round
+        n = 0
+        while n < nd and vh[n] == dh[n]:
+            n += 1
+        for i in range(n):
+            ntoks += 1
+            yield dh[i], True
+            if ntoks == max_tokens:
+                break
+        if ntoks == max_tokens:
+            break
+        ntoks += 1
+        yield vh[n], False
+        # keep y + the n accepted proposals in both caches
+        trim_prompt_cache(mcache, nd - n)
+        if n < nd:
+            trim_prompt_cache(dcache, nd - n - 1)
+        else:
+            backlog = d[nd - 1:nd]
+        y = v[n:n + 1].clone()
+    if stats is not None:
+        stats["decode_time"] = time.perf_counter() - t1
+
+
 def stream_generate(model, tokenizer, prompt, max_tokens: int = 256, draft_model=None,
                     **kwargs) -> Iterator[GenerationResponse]:
-    """mlx-lm ``stream_generate`` surface used by the engine (greedy or sampler)."""
-    if draft_model is not None:
-        raise NotImplementedError("speculative decoding with a draft model is not implemented")
+    """mlx-lm ``stream_generate`` surface used by the engine (greedy or sampler;
+    speculative decoding when ``draft_model`` is given: ``num_draft_tokens`` and
+    ``draft_cache`` are then read from the keyword arguments)."""
     if isinstance(prompt, str):
         prompt = tokenizer.encode(prompt)
     prompt = [int(t) for t in (prompt.tolist() if hasattr(prompt, "tolist") else prompt)]
@@ -178,7 +279,14 @@ def stream_generate(model, tokenizer, prompt, max_tokens: int = 256, draft_model
     stats: dict = {}
     t_start = time.perf_counter()
     n = 0
-    for token, _ in generate_step(prompt, model, max_tokens, stats=stats, **kwargs):
+    if draft_model is not None:
+        kwargs.pop("use_graph", None)
+        steps = speculative_generate_step(prompt, model, draft_model, max_tokens=max_tokens, stats=stats, **kwargs)
+    else:
+        kwargs.pop("num_draft_tokens", None)
+        kwargs.pop("draft_cache", None)
+        steps = ((t, False) for t, _ in generate_step(prompt, model, max_tokens, stats=stats, **kwargs))
+    for token, from_draft in steps:
         n += 1
         prompt_tps = stats.get("prompt_tokens", len(prompt)) / max(stats.get("prompt_time", 1e-9), 1e-9)
         gen_time = time.perf_counter() - t_start - stats.get("prompt_time", 0.0)
@@ -189,7 +297,7 @@ def stream_generate(model, tokenizer, prompt, max_tokens: int = 256, draft_model
             finish = "length"
         yield GenerationResponse(
             text="" if finish == "stop" else tokenizer.decode([token]), token=token, logprobs=None,
-            from_draft=False, prompt_tokens=len(prompt), prompt_tps=prompt_tps, generation_tokens=n,
+            from_draft=from_draft, prompt_tokens=len(prompt), prompt_tps=prompt_tps, generation_tokens=n,
             generation_tps=n / max(gen_time, 1e-9),
             peak_memory=torch.cuda.max_memory_allocated(model.device) / 1e9, finish_reason=finish)
         if finish:
