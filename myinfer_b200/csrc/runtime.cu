@@ -93,10 +93,11 @@ struct Model {
 // Token count from which a projection runs as the tensor-core GEMM instead of
 // chunks of the streaming GEMV (the GEMV re-reads the weights every 8 tokens).
 constexpr int kGemmMinTokens = 16;
-// Projections take the tensor-core GEMM from this many rows on: its dequant
-// work per weight does not shrink with the row count, so below ~40 rows
-// (batched decode) passes of the 8-row GEMV stream the weights faster.
-constexpr int kGemmMinRows = 40;
+// Projections take the tensor-core GEMM from this many rows on.  Its dequant
+// work per weight does not shrink with the row count, but neither do GEMV
+// passes of 8 rows (2 rows for K = 25600) win below it: Qwen3-32B batch 16 at
+// 32K measured 224.9 tok/s with the GEMM and 216.7 with GEMV passes.
+constexpr int kGemmMinRows = 16;
 // Routed experts of a call go through the per-expert GEMMs from this many
 // tokens on (below, the per-token expert GEMVs: too few rows per expert).
 constexpr int kMoeGroupedMinTokens = 64;

@@ -3,7 +3,7 @@ at the same position, against the same sequences decoded one at a time.
 
 Both runs are teacher-forced on the single-sequence greedy tokens, so every
 step compares logits of identical inputs.  The batched projections run as
-8-row GEMV passes (B < 40) or the tensor-core GEMM (B >= 40) instead of
+one GEMV over B rows (B < 16) or the tensor-core GEMM (B >= 16) instead of
 B single-row GEMVs, so fp32 sums differ in order: logits cosine > 0.9999 and
 max-abs <= 0.05, greedy tokens equal except at top-2 gaps below 0.02.  MoE
 rows may route differently at router near-ties (the router logits come from
@@ -56,7 +56,7 @@ def _single(model, prompt, n, bits):
 
 
 @pytest.mark.parametrize("cfg", [TINY, TINY_MOE], ids=["dense", "moe"])
-@pytest.mark.parametrize("B", [4, 48], ids=["gemv", "gemm"])
+@pytest.mark.parametrize("B", [4, 20], ids=["gemv", "gemm"])
 def test_batched_decode_matches_single(cfg, B):
     model = _model(cfg, seed=21)
     bits, L, n = 8, 24, 6
