@@ -458,9 +458,17 @@ class Engine:
                 self.totals["completion_tokens"] += m.completion_tokens
                 self.totals["cached_tokens"] += m.cached_tokens
                 if use_prefix:
+                    context = tokens + generated
                     if draft is not None:  # the sub-lists may have swapped layers when quantizing
                         cache = PromptCache(list(main_cache) + list(kwargs["draft_cache"]), self.model.device)
-                    self.prefix.put(key, tokens + generated, cache)
+                        # The draft cache lags one position after a fully accepted round and the main
+                        # cache may hold verified positions past the last yielded token: cut every layer
+                        # to the context both models hold, so the entry is reusable.
+                        common = min([c.offset for c in cache] + [len(context)])
+                        for c in cache:
+                            if c.offset > common:
+                                c.trim(c.offset - common)
+                    self.prefix.put(key, context, cache)
             yield Chunk("", finish, m)
 
     # ------------------------------------------------------------ benchmark
