@@ -215,6 +215,41 @@ M5_API int m5_kv_quantize_layer(const m5_layer_kv* src, const m5_layer_kv* dst, 
 /* Greedy sampler: out[0] = argmax(x[n]) over bf16 logits, first index wins. */
 M5_API int m5_argmax_bf16(const void* x, int64_t n, int32_t* out, void* stream);
 
+/* Sampling parameters: the sampler and logits processors the reference builds
+ * per request (m5engine/engine.py:384-392: mlx-lm 0.31.3 make_sampler(temp,
+ * top_p, min_p, top_k) and make_logits_processors(repetition_penalty,
+ * presence_penalty, frequency_penalty)).  A filter is off at its neutral
+ * value: top_p outside (0, 1), min_p <= 0, top_k <= 0 or >= vocab,
+ * repetition_penalty 1 (or 0), presence/frequency 0.  Row r draws the
+ * uniform number with counter offset (+ state[0]) + r of the SplitMix64
+ * stream of seed. */
+typedef struct m5_sample_params {
+  float temperature;  /* <= 0: greedy (first index of the max after penalties) */
+  float top_p;
+  float min_p;
+  int top_k;
+  float repetition_penalty;
+  float presence_penalty;
+  float frequency_penalty;
+  int flags;          /* M5_SAMPLE_APPEND_HISTORY */
+  uint64_t seed;
+  uint64_t offset;
+} m5_sample_params;
+
+#define M5_SAMPLE_APPEND_HISTORY 1
+
+/* One token per row of bf16 logits [rows, vocab] (row stride ld).  history:
+ * int32 [rows, hist_ld], the first hist_len entries per row are the penalty
+ * window, oldest first (negative entries are empty); with
+ * M5_SAMPLE_APPEND_HISTORY each window rolls left by one and ends with the
+ * drawn token.  Penalised logits are written back in place (mlx-lm returns
+ * the processed logits).  state: NULL, or two zero-initialised uint64 on the
+ * device holding the draw counter, which the call advances by rows (so a
+ * captured graph draws new numbers on every replay).  out: int32 [rows].
+ * vocab <= 524288, hist_len <= 1024.  Logits must be free of NaN. */
+M5_API int m5_sample_bf16(void* logits, int rows, int64_t vocab, int64_t ld, int32_t* history, int hist_len,
+                          int64_t hist_ld, const m5_sample_params* p, uint64_t* state, int32_t* out, void* stream);
+
 /* Qwen3-MoE router for T tokens: logits = x @ gate^T (w4g64), probabilities =
  * softmax (fp32 math, bf16 result), top-k by probability (ties -> lower
  * expert id), renormalised when norm_topk_prob.  ids int32 [T, k], scores

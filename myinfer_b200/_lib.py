@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import re
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 from typing import List, Optional
 
@@ -20,6 +20,7 @@ M5_OK, M5_ERR_INVALID, M5_ERR_CUDA, M5_ERR_UNSUPPORTED, M5_ERR_TIMEOUT, M5_ERR_C
 M5_DTYPE_BF16, M5_DTYPE_F32 = 0, 1
 M5_MASK_NONE, M5_MASK_CAUSAL, M5_MASK_BOOL, M5_MASK_ADDITIVE = range(4)
 M5_LOGITS_NONE, M5_LOGITS_LAST, M5_LOGITS_ALL = range(3)
+M5_SAMPLE_APPEND_HISTORY = 1
 
 
 class M5CudaError(RuntimeError):
@@ -37,6 +38,12 @@ class M5LayerKv(ctypes.Structure):
     _fields_ = [("k", c_void_p), ("k_scales", c_void_p), ("k_biases", c_void_p),
                 ("v", c_void_p), ("v_scales", c_void_p), ("v_biases", c_void_p),
                 ("capacity", c_int64), ("bits", c_int), ("group_size", c_int)]
+
+
+class M5SampleParams(ctypes.Structure):
+    _fields_ = [("temperature", c_float), ("top_p", c_float), ("min_p", c_float), ("top_k", c_int),
+                ("repetition_penalty", c_float), ("presence_penalty", c_float), ("frequency_penalty", c_float),
+                ("flags", c_int), ("seed", c_uint64), ("offset", c_uint64)]
 
 
 class M5ModelCfg(ctypes.Structure):
@@ -75,6 +82,8 @@ _SIGS = {
                                  c_void_p, c_void_p]),
     "m5_kv_quantize_layer": (c_int, [POINTER(M5LayerKv), POINTER(M5LayerKv), c_int, c_int, c_int, c_void_p]),
     "m5_argmax_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
+    "m5_sample_bf16": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_int, c_int64,
+                               POINTER(M5SampleParams), c_void_p, c_void_p, c_void_p]),
     "m5_moe_route": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                              c_void_p, c_void_p, c_void_p, c_void_p]),
     "m5_comm_unique_id": (c_int, [c_void_p, c_size_t]),

@@ -26,7 +26,7 @@ from typing import Any, Dict, Iterator, List, Optional
 
 import torch
 
-from . import attention
+from . import attention, sample
 from .cache import PromptCache, make_prompt_cache
 from .context import (GB, MAX_YARN_FACTOR, ContextPlan, KVFootprint, apply_yarn, kv_estimate_per_token,
                       measure_kv_footprint, native_context, plan_context, reserve_bytes, yarn_capable,
@@ -187,29 +187,6 @@ def _load_model(opts: LoadOptions):
     except Exception:
         tok = ByteTokenizer(args.vocab_size)
     return model, tok, config
-
-
-def _make_sampler(temp: float, top_p: float, min_p: float, top_k: int):
-    """None for greedy (the device argmax); otherwise a torch sampler over logits."""
-    if temp <= 0:
-        return None
-
-    def sample(logits: torch.Tensor) -> torch.Tensor:
-        x = logits / temp
-        if top_k and top_k > 0:
-            kth = torch.topk(x, min(top_k, x.shape[-1]), dim=-1).values[..., -1:]
-            x = torch.where(x < kth, torch.full_like(x, -float("inf")), x)
-        probs = torch.softmax(x, dim=-1)
-        if min_p and min_p > 0:
-            probs = torch.where(probs < min_p * probs.max(dim=-1, keepdim=True).values, torch.zeros_like(probs),
-                                probs)
-        if top_p and 0 < top_p < 1:
-            sp, si = torch.sort(probs, descending=True, dim=-1)
-            keep = torch.cumsum(sp, dim=-1) - sp < top_p
-            sp = sp * keep
-            probs = torch.zeros_like(probs).scatter(-1, si, sp)
-        return torch.multinomial(probs / probs.sum(dim=-1, keepdim=True), 1).reshape(-1)
-    return sample
 
 
 class Engine:
@@ -399,10 +376,14 @@ class Engine:
             need = self.footprint.bytes_for(len(tokens) + max_tokens)
             self.prefix.evict_to(self.plan.kv_budget_bytes - need)
             if params.seed is not None:
-                torch.manual_seed(params.seed)
-            sampler = _make_sampler(params.temperature, params.top_p if params.top_p < 1 else 0.0, params.min_p,
-                                    params.top_k)
-            kwargs = dict(sampler=sampler, prompt_cache=main_cache, prefill_step_size=opts.prefill_step,
+                sample.seed(params.seed)
+            sampler = sample.make_sampler(temp=params.temperature, top_p=params.top_p if params.top_p < 1 else 0.0,
+                                          min_p=params.min_p, top_k=params.top_k)
+            processors = sample.make_logits_processors(repetition_penalty=params.repetition_penalty,
+                                                       presence_penalty=params.presence_penalty,
+                                                       frequency_penalty=params.frequency_penalty)
+            kwargs = dict(sampler=sampler, logits_processors=processors, prompt_cache=main_cache,
+                          prefill_step_size=opts.prefill_step,
                           kv_bits=opts.kv_bits or None, kv_group_size=opts.kv_group_size,
                           quantized_kv_start=opts.quantized_kv_start)
             if draft is not None:

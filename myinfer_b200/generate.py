@@ -9,9 +9,11 @@ feeds the previous token.  Like ``generate_step`` the next step is computed
 before the current token is yielded, so the cache ends holding prompt +
 max_tokens positions.
 
-Greedy decode steps run as one replayed CUDA graph per cache layout: the graph
+Decode steps run as one replayed CUDA graph per cache layout: the graph
 reads the previous token and the cache length from device memory and writes
-the argmax back, so the host only copies 4 bytes per token out.
+the next token back (the argmax, or the device sampler's draw, which also
+applies the logits processors and rolls their token window on the device), so
+the host only copies 4 bytes per token out.
 """
 
 from __future__ import annotations
@@ -25,6 +27,7 @@ import torch
 from . import _lib
 from .attention import safe_maybe_quantize_kv_cache
 from .cache import PromptCache, make_prompt_cache, trim_prompt_cache
+from .sample import DeviceSampler, with_processors
 
 
 @dataclass
@@ -43,13 +46,18 @@ class GenerationResponse:
 
 
 class DecodeGraph:
-    """One captured L=1 forward: token buffer in, argmax into the same buffer."""
+    """One captured L=1 forward: token buffer in, next token (argmax, or the
+    device sampler's draw with its penalty window rolled) into the same buffer."""
 
-    def __init__(self, model, cache: PromptCache, with_logits: bool):
+    def __init__(self, model, cache: PromptCache, with_logits: bool, sampler: Optional[DeviceSampler] = None,
+                 history: Optional[torch.Tensor] = None):
         self.model, self.cache = model, cache
         dev = model.device
         self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        with_logits = with_logits or sampler is not None
         self.logits = torch.empty(model.args.vocab_size, dtype=torch.bfloat16, device=dev) if with_logits else None
+        if sampler is not None:
+            sampler.state(dev)  # the draw counter must exist before the capture
         self.sig = cache.signature()
         self.graph = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(device=dev)
@@ -59,7 +67,9 @@ class DecodeGraph:
             self.graph.capture_begin()
             try:
                 model.forward(self.tok, cache, _lib.M5_LOGITS_LAST if with_logits else _lib.M5_LOGITS_NONE,
-                              self.logits, self.tok, sync_len=False)
+                              self.logits, None if sampler is not None else self.tok, sync_len=False)
+                if sampler is not None:
+                    sampler(self.logits, history=history, out=self.tok, append=history is not None)
             finally:
                 self.graph.capture_end()
         torch.cuda.current_stream(dev).wait_stream(s)
@@ -83,14 +93,19 @@ def _step_eager(model, cache: PromptCache, tokens: torch.Tensor, want_logits: bo
 
 
 def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Optional[Callable] = None,
+                  logits_processors: Optional[list] = None,
                   prompt_cache: Optional[PromptCache] = None, prefill_step_size: int = 2048,
                   kv_bits: Optional[int] = None, kv_group_size: int = 64, quantized_kv_start: int = 0,
                   use_graph: bool = True, return_logits: bool = False,
                   stats: Optional[dict] = None, feed: Optional[List[int]] = None) -> Iterator[tuple]:
-    """Yields (token, logits-or-None) pairs; ``sampler`` None means greedy on the device.
+    """Yields (token, logits-or-None) pairs; ``sampler`` None means greedy on the
+    device, a ``DeviceSampler`` (``sample.make_sampler``) samples on the device
+    inside the decode graph, any other callable gets fp32 logits [1, V] eagerly.
+    ``logits_processors`` (``sample.make_logits_processors``) fold into the
+    device sampler.  Yielded logits are the processed ones.
 
-    ``feed`` (testing) replaces the token fed at decode step i with feed[i] while
-    the yielded tokens stay the device's own argmax (teacher forcing)."""
+    ``feed`` (testing, greedy) replaces the token fed at decode step i with
+    feed[i] while the yielded tokens stay the device's own choice."""
     if not prompt:
         raise ValueError("empty prompt")
     V = model.args.vocab_size
@@ -116,10 +131,16 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
         model.forward(prompt_t[pos:pos + m], cache)
         maybe_quantize()
         pos += m
+    sampler = with_processors(sampler, logits_processors)
     greedy = sampler is None
+    dev_sampler = isinstance(sampler, DeviceSampler)
+    # penalty window: the tokens that pass through the sampling step (mlx-lm generate_step)
+    hist = sampler.history(prompt[-1:], dev) if dev_sampler else None
     tok, logits = _step_eager(model, cache, prompt_t[pos:], return_logits or not greedy)
     maybe_quantize()
-    if not greedy:
+    if dev_sampler:
+        tok = sampler(logits, history=hist, out=tok, append=hist is not None)
+    elif not greedy:
         tok = sampler(logits.float()[None]).to(torch.int32).reshape(1)
     host = torch.empty(2, dtype=torch.int32, pin_memory=True)
     host[0:1].copy_(tok, non_blocking=True)
@@ -141,9 +162,9 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
             y_in = int(feed[i])
         else:
             y_in = y
-        if greedy and use_graph:
+        if (greedy or dev_sampler) and use_graph:
             if graph is None or not graph.valid_for(cache):
-                graph = DecodeGraph(model, cache, return_logits)
+                graph = DecodeGraph(model, cache, return_logits, sampler if dev_sampler else None, hist)
             if tok is not graph.tok:
                 graph.tok.copy_(tok)
             graph.step()
@@ -152,7 +173,9 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
         else:
             tok_in = torch.tensor([y_in], dtype=torch.int32, device=dev)
             tok, nxt_logits = _step_eager(model, cache, tok_in, return_logits or not greedy)
-            if not greedy:
+            if dev_sampler:
+                tok = sampler(nxt_logits, history=hist, out=tok, append=hist is not None)
+            elif not greedy:
                 tok = sampler(nxt_logits.float()[None]).to(torch.int32).reshape(1)
             maybe_quantize()
         slot = (i + 1) & 1
@@ -167,6 +190,7 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
 
 def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_tokens: int = 2,
                               max_tokens: int = 256, sampler: Optional[Callable] = None,
+                              logits_processors: Optional[list] = None,
                               prompt_cache: Optional[PromptCache] = None, draft_cache: Optional[PromptCache] = None,
                               prefill_step_size: int = 2048, kv_bits: Optional[int] = None,
                               kv_group_size: int = 64, quantized_kv_start: int = 0,
@@ -190,7 +214,9 @@ def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_t
     mcache = prompt_cache if prompt_cache is not None else make_prompt_cache(model)
     dcache = draft_cache if draft_cache is not None else make_prompt_cache(draft_model)
     prompt_t = torch.as_tensor(prompt, dtype=torch.int32).to(dev, non_blocking=True)
+    sampler = with_processors(sampler, logits_processors)
     greedy = sampler is None
+    dev_sampler = isinstance(sampler, DeviceSampler)
     k_max = max(1, num_draft_tokens)
     total = max(mcache.offset, dcache.offset) + len(prompt) + max_tokens + k_max + 1
     model.reserve(max(k_max + 1, min(prefill_step_size, max(1, len(prompt) - 1))))
@@ -207,9 +233,22 @@ def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_t
             m.forward(ids[p0:p0 + prefill_step_size], cache)
             maybe_quantize(cache)
 
-    def pick(logits):  # [L, V] -> int32 [L] on the device
+    ctx: List[int] = []  # sampled-through tokens before the pending one (the penalty window)
+
+    def windows(fed: torch.Tensor) -> Optional[torch.Tensor]:
+        """Penalty window of each row whose logits follow the tokens ``fed``."""
+        if not dev_sampler or sampler.window == 0:
+            return None
+        W = sampler.window
+        seq = torch.cat([sampler.history(ctx, dev)[0], fed.to(torch.int32)])
+        return seq.unfold(0, W, 1)[1:1 + fed.numel()].contiguous()
+
+    def pick(logits, fed):  # logits [L, V] after the last L tokens of ``fed`` -> int32 [L] on the device
         if greedy:
             return logits.float().argmax(dim=-1).to(torch.int32)
+        if dev_sampler:
+            w = windows(fed)
+            return sampler(logits, history=None if w is None else w[-logits.shape[0]:].contiguous())
         return sampler(logits.float()).to(torch.int32).reshape(-1)
 
     t0 = time.perf_counter()
@@ -220,6 +259,7 @@ def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_t
         stats["prompt_tokens"] = len(prompt)
     V = model.args.vocab_size
     y = prompt_t[-1:].clone()          # pending token: in neither cache yet
+    y_host = int(prompt[-1])
     backlog = None                     # draft token the draft cache still lacks
     ntoks = 0
     t1 = time.perf_counter()
@@ -235,13 +275,13 @@ def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_t
             lg = torch.empty(1, V, dtype=torch.bfloat16, device=dev)
             draft_model.forward(t, dcache, _lib.M5_LOGITS_LAST, lg)
             maybe_quantize(dcache)
-            t = pick(lg)
+            t = pick(lg, torch.cat([y] + drafts))
             drafts.append(t)
         d = torch.cat(drafts)
         vlog = torch.empty(nd + 1, V, dtype=torch.bfloat16, device=dev)
         model.forward(torch.cat([y, d]), mcache, _lib.M5_LOGITS_ALL, vlog)
         maybe_quantize(mcache)
-        v = pick(vlog)
+        v = pick(vlog, torch.cat([y, d]))
         dh, vh = d.tolist(), v.tolist()  # one host sync per round
         n = 0
         while n < nd and vh[n] == dh[n]:
@@ -261,7 +301,9 @@ def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_t
             trim_prompt_cache(dcache, nd - n - 1)
         else:
             backlog = d[nd - 1:nd]
+        ctx.extend([y_host] + dh[:n])
         y = v[n:n + 1].clone()
+        y_host = vh[n]
     if stats is not None:
         stats["decode_time"] = time.perf_counter() - t1
 
@@ -274,7 +316,6 @@ def stream_generate(model, tokenizer, prompt, max_tokens: int = 256, draft_model
     if isinstance(prompt, str):
         prompt = tokenizer.encode(prompt)
     prompt = [int(t) for t in (prompt.tolist() if hasattr(prompt, "tolist") else prompt)]
-    kwargs.pop("logits_processors", None)
     eos = set(getattr(tokenizer, "eos_token_ids", []) or [])
     stats: dict = {}
     t_start = time.perf_counter()

@@ -1,0 +1,239 @@
+"""Device sampler (m5_sample_bf16) against the oracle's restatement of mlx-lm's
+sampler and logits processors (m5engine/engine.py:384-392).
+
+Given the same seed and counter both sides draw the same uniform number, so
+tokens are compared one for one.  The kernel sums in fp32 (and the top-p mass
+in 2^-40 fixed point) where the oracle sums in fp64, so a draw that lands
+within 1e-5 of the total mass from a boundary of the inverse CDF (or a top-p
+cut within 1e-4 of a boundary) may pick the neighbour: such rows must still be
+consistent with the oracle at that tolerance, and at least 90 % of all rows
+must match exactly.  Penalised logits are compared bit for bit."""
+
+import numpy as np
+import pytest
+import torch
+
+from myinfer_b200.sample import DeviceSampler, LogitsPenalty
+from oracle import sample as osmp
+
+pytestmark = pytest.mark.gpu
+
+V_FULL = 151936
+
+
+def _logits(R, V, seed, scales=None):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(R, V, generator=g)
+    if scales is not None:
+        x = x * torch.tensor(scales, dtype=torch.float32)[:, None]
+    return x.to(torch.bfloat16)
+
+
+def _consistent(v, g, temp, top_p, min_p, top_k, u):
+    """g is a draw the oracle accepts at a 1e-4 top-p / 1e-5 CDF tolerance."""
+    for tp in ([top_p] if not (0 < top_p < 1) else [top_p, min(top_p * (1 + 1e-4), 0.999999),
+                                                   top_p * (1 - 1e-4)]):
+        keep = osmp.kept_mask(v, tp, min_p, top_k)
+        if not keep[g]:
+            continue
+        vv = v.astype(np.float64)
+        w = np.where(keep, np.exp((vv - vv[keep].max()) / temp), 0.0)
+        cdf = np.cumsum(w)
+        total = cdf[-1]
+        before = cdf[g - 1] if g > 0 else 0.0
+        tol = 1e-5 * total
+        if before - tol <= u * total <= cdf[g] + tol:
+            return True
+    return False
+
+
+def _check(got, logits_f32, temp, top_p=0.0, min_p=0.0, top_k=0, seed=0, offset=0, windows=None, pen=None):
+    pen = pen or {}
+    want, pen_rows = osmp.sample_rows(logits_f32, temp, top_p, min_p, top_k, windows=windows, seed=seed,
+                                      offset=offset, **pen)
+    exact = 0
+    for r, g in enumerate(got):
+        if g == want[r]:
+            exact += 1
+            continue
+        assert temp > 0, (r, g, want[r])
+        assert _consistent(pen_rows[r], g, temp, top_p, min_p, top_k, osmp.uniform(seed, offset + r)), \
+            (r, int(g), int(want[r]))
+    return exact
+
+
+CASES = [dict(temp=1.0), dict(temp=0.7, top_p=0.9), dict(temp=1.0, top_k=50), dict(temp=0.8, min_p=0.05),
+         dict(temp=1.2, top_p=0.8, min_p=0.02, top_k=40), dict(temp=0.5, top_p=0.95, top_k=1000),
+         dict(temp=1.0, top_p=0.3), dict(temp=2.0, top_k=1)]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[str(i) for i in range(len(CASES))])
+def test_matches_oracle_full_vocab(case):
+    R = 12
+    x = _logits(R, V_FULL, 3, scales=[0.5, 1, 2, 3, 4, 6, 8, 1.5, 2.5, 5, 0.25, 10])
+    s = DeviceSampler(case["temp"], case.get("top_p", 0.0), case.get("min_p", 0.0), case.get("top_k", 0), seed=99)
+    got = s(x.cuda()).cpu().numpy()
+    exact = _check(got, x.float().numpy(), seed=99, **case)
+    assert exact >= 0.9 * R, exact
+
+
+def test_penalties_bit_exact_and_greedy():
+    R, W = 4, 24
+    x = _logits(R, V_FULL, 5, scales=[3, 3, 3, 3])
+    top = x.float().topk(6, dim=-1).indices.numpy()
+    rng = np.random.default_rng(1)
+    windows = []
+    for r in range(R):  # the rows' best tokens, repeated, plus noise and empty slots
+        w = list(top[r][:3]) * 3 + list(rng.integers(0, V_FULL, W - 11)) + [-1, -1]
+        windows.append([int(t) for t in w])
+    hist = torch.tensor(windows, dtype=torch.int32, device="cuda")
+    pen = dict(repetition=1.3, presence=0.4, frequency=0.2)
+    procs = [LogitsPenalty("repetition", 1.3, W), LogitsPenalty("presence", 0.4, W),
+             LogitsPenalty("frequency", 0.2, W)]
+    xg = x.cuda()
+    got = DeviceSampler(0.0, processors=procs)(xg, history=hist).cpu().numpy()
+    want, pen_rows = osmp.sample_rows(x.float().numpy(), 0.0, windows=windows, **pen)
+    assert np.array_equal(xg.float().cpu().numpy(), pen_rows), "penalised logits differ"
+    assert got.tolist() == want.tolist()
+    assert any(int(want[r]) != int(top[r][0]) for r in range(R)), "penalties changed no argmax"
+    # sampled, with penalties
+    xg = x.cuda()
+    got = DeviceSampler(0.9, top_p=0.95, processors=procs, seed=4)(xg, history=hist).cpu().numpy()
+    assert _check(got, x.float().numpy(), 0.9, top_p=0.95, seed=4, windows=windows, pen=pen) >= R - 1
+
+
+def test_distribution_small_vocab_scalar_path():
+    """V = 37 (scalar loads, a partial tile); 20000 rows of the same logits: every
+    row matches the oracle's draw and the frequencies match the kept softmax."""
+    V, R = 37, 20000
+    base = torch.linspace(-3, 3, V)[torch.randperm(V, generator=torch.Generator().manual_seed(0))]
+    x = base.to(torch.bfloat16).repeat(R, 1)
+    s = DeviceSampler(0.9, top_p=0.9, seed=2024)
+    got = s(x.cuda()).cpu().numpy()
+    v = x[0].float().numpy()
+    keep = osmp.kept_mask(v, 0.9)
+    prob = np.where(keep, np.exp((v.astype(np.float64) - v.max()) / 0.9), 0)
+    prob /= prob.sum()
+    mism = 0
+    for r in range(R):
+        if got[r] != osmp.draw(v, keep, 0.9, osmp.uniform(2024, r))[0]:
+            mism += 1
+            assert _consistent(v, int(got[r]), 0.9, 0.9, 0.0, 0, osmp.uniform(2024, r))
+    assert mism <= R // 1000
+    freq = np.bincount(got, minlength=V) / R
+    assert 0.5 * np.abs(freq - prob).sum() < 0.02
+    assert set(np.nonzero(freq)[0]) <= set(np.nonzero(keep)[0])
+
+
+def test_strided_unaligned_rows():
+    R, V = 6, 1001
+    buf = _logits(R, V + 5, 8, scales=[2] * R)
+    xg = buf.cuda()[:, 1:1 + V]          # row stride V + 5, base 2 bytes off: scalar loads
+    got = DeviceSampler(0.8, top_k=20, seed=6)(xg).cpu().numpy()
+    assert _check(got, buf[:, 1:1 + V].float().numpy(), 0.8, top_k=20, seed=6) >= R - 1
+
+
+def test_counter_advances_and_window_rolls():
+    R, V, W = 5, 4096, 8
+    x = _logits(R, V, 9, scales=[1] * R)
+    procs = [LogitsPenalty("repetition", 1.1, W)]
+    s = DeviceSampler(1.0, processors=procs, seed=77)
+    rows = [[int(t) for t in np.random.default_rng(r).integers(0, V, W)] for r in range(R)]
+    hist = torch.tensor(rows, dtype=torch.int32, device="cuda")
+    xg = x.cuda()
+    t1 = s(xg, history=hist, append=True).cpu().numpy()
+    assert s.state("cuda")[0].item() == R and s.state("cuda")[1].item() == 0
+    assert _check(t1, x.float().numpy(), 1.0, seed=77, windows=rows, pen=dict(repetition=1.1)) >= R - 1
+    rolled = [rows[r][1:] + [int(t1[r])] for r in range(R)]
+    assert hist.cpu().tolist() == rolled
+    x2 = _logits(R, V, 10, scales=[1] * R)
+    t2 = s(x2.cuda(), history=hist, append=True).cpu().numpy()
+    assert s.state("cuda")[0].item() == 2 * R
+    assert _check(t2, x2.float().numpy(), 1.0, seed=77, offset=R, windows=rolled,
+                  pen=dict(repetition=1.1)) >= R - 1
+
+
+def test_graph_replay_draws_fresh_numbers():
+    R, V = 4, 8192
+    x = _logits(R, V, 11, scales=[1.5] * R)
+    xg = x.cuda()
+    out = torch.empty(R, dtype=torch.int32, device="cuda")
+    s = DeviceSampler(1.0, min_p=0.01, seed=13)
+    s.state("cuda")
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        g.capture_begin()
+        s(xg, out=out)
+        g.capture_end()
+    torch.cuda.current_stream().wait_stream(st)
+    seen = []
+    for k in range(3):
+        g.replay()
+        got = out.cpu().numpy()
+        assert _check(got, x.float().numpy(), 1.0, min_p=0.01, seed=13, offset=k * R) >= R - 1
+        seen.append(got.tolist())
+    assert s.state("cuda")[0].item() == 3 * R
+    assert len({tuple(t) for t in seen}) > 1
+    del g
+
+
+def test_edge_rows():
+    s = DeviceSampler(1.0, seed=1)
+    one = torch.tensor([[0.5]], dtype=torch.bfloat16, device="cuda")
+    assert s(one).item() == 0
+    ninf = torch.full((1, 300), float("-inf"), dtype=torch.bfloat16, device="cuda")
+    assert s(ninf).item() == 0
+    x = _logits(3, 5000, 12, scales=[3, 3, 3])
+    am = x.float().argmax(-1).tolist()
+    assert DeviceSampler(1.0, top_k=1, seed=3)(x.cuda()).cpu().tolist() == am
+    assert DeviceSampler(1e-4, seed=3)(x.cuda()).cpu().tolist() == am
+    assert DeviceSampler(1.0, min_p=1.0, seed=3)(x.cuda()).cpu().tolist() == am
+    assert DeviceSampler(0.0)(x.cuda()).cpu().tolist() == am
+
+
+TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+            head_dim=128, intermediate_size=1024, vocab_size=4096, tie_word_embeddings=False,
+            max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+
+
+def _tiny_model():
+    from myinfer_b200.model import Model, ModelArgs, upload_weights
+    from oracle import model as om
+    host = om.generate_weights(om.Config.from_dict(TINY), 17)
+    return Model(ModelArgs.from_dict(TINY), upload_weights(host, "cuda"), "cuda", max_tokens=64)
+
+
+def test_token_loop_graph_equals_eager():
+    """Sampled decode with penalties: the captured-graph loop (sampler and window
+    roll inside the graph) draws the same tokens as the eager loop."""
+    from myinfer_b200.generate import generate_step
+    from myinfer_b200.sample import make_logits_processors
+    model = _tiny_model()
+    prompt = list(np.random.default_rng(3).integers(0, 4096, 40))
+    runs = []
+    for use_graph in (True, False):
+        s = DeviceSampler(0.8, top_p=0.95, seed=21)
+        procs = make_logits_processors(repetition_penalty=1.2, frequency_penalty=0.1)
+        runs.append([t for t, _ in generate_step(prompt, model, 24, sampler=s, logits_processors=procs,
+                                                 use_graph=use_graph)])
+    assert runs[0] == runs[1]
+    assert all(0 <= t < 4096 for t in runs[0])
+    # greedy with a strong repetition penalty: no token repeats inside the window
+    procs = make_logits_processors(repetition_penalty=50.0)
+    toks = [t for t, _ in generate_step(prompt, model, 30, logits_processors=procs)]
+    window = [prompt[-1]] + toks
+    for i in range(1, len(window)):
+        assert window[i] not in window[max(0, i - 20):i], (i, window[max(0, i - 20):i + 1])
+
+
+def test_speculative_with_sampler():
+    from myinfer_b200.generate import speculative_generate_step
+    from myinfer_b200.sample import make_logits_processors
+    model = _tiny_model()
+    prompt = list(np.random.default_rng(4).integers(0, 4096, 30))
+    s = DeviceSampler(0.7, top_k=30, seed=8)
+    out = list(speculative_generate_step(prompt, model, model, num_draft_tokens=3, max_tokens=20, sampler=s,
+                                         logits_processors=make_logits_processors(presence_penalty=0.5)))
+    assert len(out) == 20 and all(0 <= t < 4096 for t, _ in out)
