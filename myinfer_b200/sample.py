@@ -95,6 +95,8 @@ class DeviceSampler:
     def state(self, device) -> torch.Tensor:
         """The device draw counter {count, CTAs done} (create it before a graph capture)."""
         dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         if dev not in self._state:
             self._state[dev] = torch.zeros(2, dtype=torch.int64, device=dev)
         return self._state[dev]
