@@ -4,6 +4,7 @@
     python -m myinfer_b200.microbench attention --s 32768 --l 1 --bits 8 [--hq 64 --hkv 8]
     python -m myinfer_b200.microbench gemm --m 2048 --n 8192 --k 5120
     python -m myinfer_b200.microbench step --ctx 32768 --steps 2 [--config qwen3-30b-a3b]   # decode steps
+    python -m myinfer_b200.microbench sample [--rows 1] [--vocab 151936]   # device sampler vs torch ops
 
 ``gemv`` cycles over enough distinct weight matrices that every launch reads
 from HBM (more than L2 in total); ``attention`` is the standalone
@@ -156,6 +157,46 @@ def bench_attention(s: int, l: int, bits: int, hq: int, hkv: int, iters: int) ->
             "alg_bytes": int(alg), "gbs": round(alg / us / 1e3, 1), "tflops": round(flops / us / 1e6, 2)}
 
 
+def bench_sample(rows: int, vocab: int, iters: int) -> dict:
+    """The device sampler (temperature 0.7, top-p 0.9, top-k 50, repetition
+    penalty 1.1 over a 20-token window) on bf16 logits [rows, vocab], graph
+    replayed; beside it the same filters as a chain of torch ops on the GPU
+    (topk, softmax, sort, cumsum, scatter, multinomial), timed eagerly with
+    CUDA events because multinomial does not capture."""
+    from myinfer_b200.sample import DeviceSampler, make_logits_processors
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = (2 * torch.randn(rows, vocab, generator=g, device="cuda")).to(torch.bfloat16)
+    hist = torch.randint(0, vocab, (rows, 20), generator=g, device="cuda", dtype=torch.int32)
+    s = DeviceSampler(0.7, top_p=0.9, top_k=50, processors=make_logits_processors(repetition_penalty=1.1), seed=1)
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    us = _timed(lambda i: s(x, history=hist, out=out), iters)
+    gs = DeviceSampler(0.0)
+    gs.state("cuda")
+    us_greedy = _timed(lambda i: gs(x, out=out), iters)
+
+    def torch_chain(lg):
+        z = lg.float() / 0.7
+        kth = torch.topk(z, 50, dim=-1).values[..., -1:]
+        z = torch.where(z < kth, torch.full_like(z, -float("inf")), z)
+        probs = torch.softmax(z, dim=-1)
+        sp, si = torch.sort(probs, descending=True, dim=-1)
+        keep = torch.cumsum(sp, dim=-1) - sp < 0.9
+        probs = torch.zeros_like(probs).scatter(-1, si, sp * keep)
+        return torch.multinomial(probs / probs.sum(dim=-1, keepdim=True), 1)
+
+    for _ in range(3):
+        torch_chain(x)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(iters):
+        torch_chain(x)
+    t1.record()
+    torch.cuda.synchronize()
+    return {"kernel": "sample", "rows": rows, "vocab": vocab, "us": round(us, 2), "us_greedy": round(us_greedy, 2),
+            "torch_ops_us": round(t0.elapsed_time(t1) * 1e3 / iters, 2)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -180,11 +221,17 @@ def main():
     a.add_argument("--hq", type=int, default=64)
     a.add_argument("--hkv", type=int, default=8)
     a.add_argument("--iters", type=int, default=20)
+    sm = sub.add_parser("sample")
+    sm.add_argument("--rows", type=int, default=1)
+    sm.add_argument("--vocab", type=int, default=151936)
+    sm.add_argument("--iters", type=int, default=50)
     args = ap.parse_args()
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.m, args.iters)
     elif args.cmd == "gemm":
         r = bench_gemm(args.m, args.n, args.k, args.iters)
+    elif args.cmd == "sample":
+        r = bench_sample(args.rows, args.vocab, args.iters)
     elif args.cmd == "step":
         r = bench_step(args.ctx, args.steps, args.config)
     else:
