@@ -130,14 +130,15 @@ class DeviceSampler:
             h = history if history.dim() == 2 else history.reshape(1, -1)
             if h.dtype != torch.int32 or not h.is_cuda or h.shape[0] != R or h.stride(-1) != 1:
                 raise ValueError("history must be int32 CUDA [rows, window] with contiguous rows")
-            hist_ptr, hist_len, hist_ld = h.data_ptr(), h.shape[1], h.stride(0)
+            # a single row's stride is meaningless (torch keeps any stride on a size-1 dimension)
+            hist_ptr, hist_len, hist_ld = h.data_ptr(), h.shape[1], h.stride(0) if R > 1 else h.shape[1]
         elif append:
             raise ValueError("append needs a history window")
         p = M5SampleParams(temperature=self.temp, top_p=self.top_p, min_p=self.min_p, top_k=self.top_k,
                            repetition_penalty=self.repetition, presence_penalty=self.presence,
                            frequency_penalty=self.frequency,
                            flags=_lib.M5_SAMPLE_APPEND_HISTORY if append else 0, seed=self.seed, offset=0)
-        call("m5_sample_bf16", lg.data_ptr(), R, V, lg.stride(0), hist_ptr, hist_len, hist_ld, p,
+        call("m5_sample_bf16", lg.data_ptr(), R, V, lg.stride(0) if R > 1 else V, hist_ptr, hist_len, hist_ld, p,
              self.state(lg.device).data_ptr(), out.data_ptr(), torch.cuda.current_stream(lg.device).cuda_stream)
         return out
 
