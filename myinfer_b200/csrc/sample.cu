@@ -20,13 +20,18 @@
 //     order-preserving key of the bf16 value (high byte, then low byte) with
 //     per-warp histograms in shared memory: counts, and probability mass
 //     exp(v - max) in 2^-40 fixed point, so every sum is exact and independent
-//     of the order the atomics land in.
+//     of the order the atomics land in.  One atomic-free pass first counts the
+//     entries and mass within 1, 2, 4, 8 and 16 of the max; when the narrowest
+//     band that contains both crossings holds at most 8192 entries (a peaked
+//     row) those are compacted into shared memory and the select runs there,
+//     otherwise (a flat row) it runs over the whole row.
 //  3. An inverse-CDF draw at the temperature: u = SplitMix64(seed, counter)
 //     in [0, 1), target u * sum over the kept set of exp((v - max) / T),
 //     found in index order tile by tile (one pass for the tile sums, then one
 //     tile re-read and scanned).
 // Temperature <= 0 is greedy: the first index of the largest (penalised)
-// value.  The row is read from L2 once per pass (a 151936-entry row is 297 KB).
+// value.  The row is read from L2 once per pass (a 151936-entry row is 297 KB),
+// each thread keeping four 16-byte loads in flight.
 //
 // Row r uses counter offset + state[0] + r.  With a device state the last CTA
 // to finish adds the row count to state[0] (CTAs count themselves in
@@ -47,7 +52,13 @@ constexpr int kSmpTile = kSmpThreads * kSmpPer;    // 8192 entries
 constexpr int kSmpMaxTiles = 64;
 constexpr int kSmpMaxHist = 1024;
 constexpr float kSmpMassScale = 1099511627776.f;   // 2^40
-constexpr size_t kSmpSmem = size_t(kSmpWarps) * 256 * (sizeof(uint32_t) + sizeof(unsigned long long));
+constexpr int kSmpAhead = 4;                       // tiles whose loads a thread keeps in flight
+constexpr int kSmpCap = 8192;                      // candidate entries compacted into shared memory
+constexpr int kSmpLevels = 5;                      // candidate bands: within 1, 2, 4, 8, 16 of the max
+constexpr size_t kSmpSmem = size_t(kSmpWarps) * 256 * (sizeof(uint32_t) + sizeof(unsigned long long)) +
+                            size_t(kSmpCap) * sizeof(unsigned short);
+
+__device__ __forceinline__ float smp_band(int i) { return (float)(1 << i); }
 
 struct SampleArgs {
   bf16* logits;
@@ -81,24 +92,46 @@ __device__ __forceinline__ float smp_uniform(unsigned long long seed, unsigned l
   return (float)(z >> 40) * (1.f / 16777216.f);
 }
 
-// The raw bf16 bits of one thread's 8 entries of a tile; returns how many lie
-// inside the row.  Plain loads: the penalties may have just rewritten them.
-__device__ __forceinline__ int smp_load8(const bf16* row, int vocab, int i0, int vec, uint32_t (&b)[kSmpPer]) {
+// One thread's 8 consecutive entries of a tile as raw bf16 bits (entry j in
+// half j & 1 of word j >> 1); returns how many lie inside the row.  Plain
+// loads: the penalties may have just rewritten them.
+__device__ __forceinline__ int smp_load(const bf16* row, int vocab, int i0, int vec, uint4& u) {
+  u = make_uint4(0u, 0u, 0u, 0u);
   if (i0 >= vocab) return 0;
   if (vec && i0 + kSmpPer <= vocab) {
-    const uint4 u = *reinterpret_cast<const uint4*>(row + i0);
-    b[0] = u.x & 0xFFFFu; b[1] = u.x >> 16; b[2] = u.y & 0xFFFFu; b[3] = u.y >> 16;
-    b[4] = u.z & 0xFFFFu; b[5] = u.z >> 16; b[6] = u.w & 0xFFFFu; b[7] = u.w >> 16;
+    u = *reinterpret_cast<const uint4*>(row + i0);
     return kSmpPer;
   }
   const unsigned short* r = reinterpret_cast<const unsigned short*>(row);
   const int n = min(kSmpPer, vocab - i0);
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-  for (int j = 0; j < kSmpPer; ++j) b[j] = j < n ? (uint32_t)r[i0 + j] : 0u;
+  for (int j = 0; j < kSmpPer; ++j)
+    if (j < n) w[j >> 1] |= (uint32_t)r[i0 + j] << (16 * (j & 1));
+  u = make_uint4(w[0], w[1], w[2], w[3]);
   return n;
 }
+__device__ __forceinline__ uint32_t smp_bits(const uint4& u, int j) {
+  const uint32_t w = j < 2 ? u.x : j < 4 ? u.y : j < 6 ? u.z : u.w;
+  return (j & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
 
-// Block-wide max / sum / min with a fixed combination order (every thread gets
+// Calls f(i0, n, u) for this thread's slot of every tile, with the loads of
+// kSmpAhead tiles issued before the first of them is used.
+template <class F>
+__device__ __forceinline__ void smp_tiles(const bf16* row, int vocab, int vec, int ntile, F&& f) {
+  const int off = threadIdx.x * kSmpPer;
+  for (int t0 = 0; t0 < ntile; t0 += kSmpAhead) {
+    uint4 u[kSmpAhead];
+    int n[kSmpAhead];
+#pragma unroll
+    for (int q = 0; q < kSmpAhead; ++q) n[q] = smp_load(row, vocab, (t0 + q) * kSmpTile + off, vec, u[q]);
+#pragma unroll
+    for (int q = 0; q < kSmpAhead; ++q) f(t0 + q, (t0 + q) * kSmpTile + off, n[q], u[q]);
+  }
+}
+
+// Block-wide max / min with a fixed combination order (every thread gets
 // the same bits back).
 __device__ float smp_block_max(float v, float* red) {
   v = warp_max(v);
@@ -107,15 +140,6 @@ __device__ float smp_block_max(float v, float* red) {
   __syncthreads();
   float r = red[0];
   for (int w = 1; w < kSmpWarps; ++w) r = fmaxf(r, red[w]);
-  return r;
-}
-__device__ float smp_block_sum(float v, float* red) {
-  v = warp_sum(v);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float r = 0.f;
-  for (int w = 0; w < kSmpWarps; ++w) r += red[w];
   return r;
 }
 __device__ int smp_block_min(int v, int* red) {
@@ -177,18 +201,135 @@ __device__ __forceinline__ unsigned long long smp_fixed_mass(float v, float vmax
   return __float2ull_rn(expf(v - vmax) * kSmpMassScale);
 }
 
+// Shared scratch of one row's selection.
+struct SmpShared {
+  uint32_t* wcnt;              // [warps][256] per-warp counts
+  unsigned long long* wmass;   // [warps][256] per-warp fixed-point mass
+  uint32_t* cnt1;              // [256] merged counts
+  unsigned long long* mass1;   // [256] merged mass
+  int* s_int;
+  unsigned long long* s_u;
+};
+
+// Exact 16-bit key thresholds of top-k (k entries) and top-p (fixed-point
+// mass P) over the entries visit() yields to each thread: a round of per-warp
+// 256-bin histograms over the high key byte, the crossing bins, then a round
+// over the low byte of the entries inside them.  Returns the larger key (0
+// when the filters keep everything).  Counts and masses are integers, so the
+// result does not depend on the order the atomics land in.
+template <class Visit>
+__device__ uint32_t smp_select(Visit&& visit, bool do_k, bool do_p, unsigned long long k, unsigned long long P,
+                               float vmax, const SmpShared& sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint32_t* my_cnt = sh.wcnt + warp * 256;
+  unsigned long long* my_mass = sh.wmass + warp * 256;
+  for (int i = tid; i < kSmpWarps * 256; i += kSmpThreads) {
+    sh.wcnt[i] = 0u;
+    sh.wmass[i] = 0ull;
+  }
+  __syncthreads();
+  {  // round 1: high byte, equal consecutive bins of a thread merged before the atomic
+    uint32_t ccur = 0xFFFFFFFFu, crun = 0, mcur = 0xFFFFFFFFu;
+    unsigned long long mrun = 0;
+    visit([&](uint32_t bits) {
+      const uint32_t bin = smp_key(bits) >> 8;
+      if (do_k) {
+        if (bin != ccur) {
+          if (crun) atomicAdd(my_cnt + ccur, crun);
+          ccur = bin;
+          crun = 0;
+        }
+        ++crun;
+      }
+      if (do_p) {
+        if (bin != mcur) {
+          if (mrun) atomicAdd(my_mass + mcur, mrun);
+          mcur = bin;
+          mrun = 0;
+        }
+        mrun += smp_fixed_mass(smp_val(bits), vmax);
+      }
+    });
+    if (crun) atomicAdd(my_cnt + ccur, crun);
+    if (mrun) atomicAdd(my_mass + mcur, mrun);
+  }
+  __syncthreads();
+  if (tid < 256) {
+    uint32_t c = 0;
+    unsigned long long m = 0;
+    for (int w = 0; w < kSmpWarps; ++w) {
+      c += sh.wcnt[w * 256 + tid];
+      m += sh.wmass[w * 256 + tid];
+    }
+    sh.cnt1[tid] = c;
+    sh.mass1[tid] = m;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    unsigned long long bk_bef = 0, bp_bef = 0;
+    const int bk = do_k ? smp_cross(sh.cnt1, k, &bk_bef) : -1;
+    const int bp = do_p ? smp_cross(sh.mass1, P, &bp_bef) : -1;
+    if (lane == 0) {
+      sh.s_int[0] = bk;
+      sh.s_int[1] = bp;
+      sh.s_u[0] = bk_bef;
+      sh.s_u[1] = bp_bef;
+    }
+  }
+  __syncthreads();
+  const int bk = sh.s_int[0], bp = sh.s_int[1];
+  const unsigned long long bk_bef = sh.s_u[0], bp_bef = sh.s_u[1];
+  if (bk < 0 && bp < 0) return 0u;
+  for (int i = tid; i < kSmpWarps * 256; i += kSmpThreads) {
+    sh.wcnt[i] = 0u;
+    sh.wmass[i] = 0ull;
+  }
+  __syncthreads();
+  visit([&](uint32_t bits) {  // round 2: low byte inside the crossing bins
+    const uint32_t key = smp_key(bits);
+    const int hb = (int)(key >> 8);
+    if (hb == bk) atomicAdd(my_cnt + (key & 255u), 1u);
+    if (hb == bp) atomicAdd(my_mass + (key & 255u), smp_fixed_mass(smp_val(bits), vmax));
+  });
+  __syncthreads();
+  if (tid < 256) {
+    uint32_t c = 0;
+    unsigned long long m = 0;
+    for (int w = 0; w < kSmpWarps; ++w) {
+      c += sh.wcnt[w * 256 + tid];
+      m += sh.wmass[w * 256 + tid];
+    }
+    sh.cnt1[tid] = c;
+    sh.mass1[tid] = m;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t kk = 0, kp = 0;
+    unsigned long long unused;
+    if (bk >= 0) kk = ((uint32_t)bk << 8) | (uint32_t)max(smp_cross(sh.cnt1, k - bk_bef, &unused), 0);
+    if (bp >= 0) kp = ((uint32_t)bp << 8) | (uint32_t)max(smp_cross(sh.mass1, P - bp_bef, &unused), 0);
+    if (lane == 0) sh.s_int[2] = (int)max(kk, kp);
+  }
+  __syncthreads();
+  return (uint32_t)sh.s_int[2];
+}
+
 // Draws the token of one row into *pick_out (left untouched when nothing has weight).
 __device__ __forceinline__ void sample_row(const SampleArgs& a, int row, unsigned long long base, int* pick_out) {
   extern __shared__ __align__(16) unsigned char smp_smem[];
   uint32_t* wcnt = reinterpret_cast<uint32_t*>(smp_smem);  // [warps][256] counts
   unsigned long long* wmass =
       reinterpret_cast<unsigned long long*>(smp_smem + size_t(kSmpWarps) * 256 * sizeof(uint32_t));  // [warps][256]
+  unsigned short* cand = reinterpret_cast<unsigned short*>(wmass + kSmpWarps * 256);  // [kSmpCap] raw bits
   __shared__ float red[kSmpWarps];
+  __shared__ float red4[kSmpAhead][kSmpWarps];
   __shared__ int red_i[kSmpWarps];
   __shared__ uint32_t cnt1[256];
   __shared__ unsigned long long mass1[256];
+  __shared__ unsigned long long lvl_part[kSmpWarps][2 * kSmpLevels + 1];
+  __shared__ unsigned long long lvl[2 * kSmpLevels + 1];
   __shared__ float tile_sum[kSmpMaxTiles];
-  __shared__ int s_int[4];
+  __shared__ int s_int[5];
   __shared__ unsigned long long s_u[4];
   __shared__ float s_f[1];
 
@@ -229,49 +370,22 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, int row, unsigne
   const bool do_k = !greedy && a.top_k > 0 && a.top_k < V;
   const bool do_p = !greedy && a.top_p > 0.f && a.top_p < 1.f;
 
-  // ---- 2a. max (+ level-1 counts for top-k)
-  if (do_k) {
-    for (int i = tid; i < kSmpWarps * 256; i += kSmpThreads) wcnt[i] = 0u;
-    __syncthreads();
-  }
-  uint32_t* my_cnt = wcnt + warp * 256;
-  unsigned long long* my_mass = wmass + warp * 256;
+  // ---- 2a. max
   float vmax = -INFINITY;
-  for (int t = 0; t < ntile; ++t) {
-    uint32_t b[kSmpPer];
-    const int i0 = t * kSmpTile + tid * kSmpPer;
-    const int n = smp_load8(lg, V, i0, a.vec, b);
-    uint32_t cur = 0xFFFFFFFFu, run = 0;
+  smp_tiles(lg, V, a.vec, ntile, [&](int, int, int n, const uint4& u) {
 #pragma unroll
-    for (int j = 0; j < kSmpPer; ++j) {
-      if (j < n) {
-        vmax = fmaxf(vmax, smp_val(b[j]));
-        if (do_k) {
-          const uint32_t bin = smp_key(b[j]) >> 8;
-          if (bin != cur) {
-            if (run) atomicAdd(my_cnt + cur, run);
-            cur = bin;
-            run = 0;
-          }
-          ++run;
-        }
-      }
-    }
-    if (do_k && run) atomicAdd(my_cnt + cur, run);
-  }
+    for (int j = 0; j < kSmpPer; ++j)
+      if (j < n) vmax = fmaxf(vmax, smp_val(smp_bits(u, j)));
+  });
   vmax = smp_block_max(vmax, red);
 
   if (greedy) {  // first index of the max
     int best = INT_MAX;
-    for (int t = 0; t < ntile; ++t) {
-      uint32_t b[kSmpPer];
-      const int i0 = t * kSmpTile + tid * kSmpPer;
-      const int n = smp_load8(lg, V, i0, a.vec, b);
+    smp_tiles(lg, V, a.vec, ntile, [&](int, int i0, int n, const uint4& u) {
 #pragma unroll
-      for (int j = kSmpPer - 1; j >= 0; --j)
-        if (j < n && smp_val(b[j]) == vmax) best = i0 + j;
-      if (best != INT_MAX) break;
-    }
+      for (int j = 0; j < kSmpPer; ++j)  // tiles and entries in index order: the first hit is the lowest
+        if (j < n && best == INT_MAX && smp_val(smp_bits(u, j)) == vmax) best = i0 + j;
+    });
     best = smp_block_min(best, red_i);
     if (tid == 0 && best != INT_MAX) *pick_out = best;
     return;
@@ -279,150 +393,132 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, int row, unsigne
   // reference point of the exponentials (a row of -inf keeps every weight 0 and draws index 0)
   if (vmax == -INFINITY) vmax = 0.f;
 
-  // ---- 2b. level-1 crossing for top-k
-  int bk = -1, bp = -1;
-  unsigned long long bef_k = 0, bef_p = 0, ptarget = 0;
-  if (do_k) {
-    if (tid < 256) {
-      uint32_t s = 0;
-      for (int w = 0; w < kSmpWarps; ++w) s += wcnt[w * 256 + tid];
-      cnt1[tid] = s;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      unsigned long long bef;
-      const int bin = smp_cross(cnt1, (unsigned long long)a.top_k, &bef);
-      if (lane == 0) {
-        s_int[0] = bin;
-        s_u[0] = bef;
-      }
-    }
-    __syncthreads();
-    bk = s_int[0];
-    bef_k = s_u[0];
-  }
-
-  // ---- 2c. level-1 mass and crossing for top-p
-  if (do_p) {
-    for (int i = tid; i < kSmpWarps * 256; i += kSmpThreads) wmass[i] = 0ull;
-    __syncthreads();
-    for (int t = 0; t < ntile; ++t) {
-      uint32_t b[kSmpPer];
-      const int i0 = t * kSmpTile + tid * kSmpPer;
-      const int n = smp_load8(lg, V, i0, a.vec, b);
-      uint32_t cur = 0xFFFFFFFFu;
-      unsigned long long run = 0;
-#pragma unroll
-      for (int j = 0; j < kSmpPer; ++j) {
-        if (j < n) {
-          const uint32_t bin = smp_key(b[j]) >> 8;
-          if (bin != cur) {
-            if (run) atomicAdd(my_mass + cur, run);
-            cur = bin;
-            run = 0;
-          }
-          run += smp_fixed_mass(smp_val(b[j]), vmax);
-        }
-      }
-      if (run) atomicAdd(my_mass + cur, run);
-    }
-    __syncthreads();
-    if (tid < 256) {
-      unsigned long long s = 0;
-      for (int w = 0; w < kSmpWarps; ++w) s += wmass[w * 256 + tid];
-      mass1[tid] = s;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      unsigned long long tot = 0;
-      for (int j = lane; j < 256; j += 32) tot += mass1[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-      // keep a value while the mass strictly above it is below top_p * total
-      unsigned long long P = (unsigned long long)ceil((double)a.top_p * (double)tot);
-      if (P < 1ull) P = 1ull;
-      unsigned long long bef;
-      const int bin = smp_cross(mass1, P, &bef);
-      if (lane == 0) {
-        s_int[1] = bin;
-        s_u[1] = bef;
-        s_u[2] = P;
-      }
-    }
-    __syncthreads();
-    bp = s_int[1];
-    bef_p = s_u[1];
-    ptarget = s_u[2];
-  }
-
-  // ---- 2d. level 2 inside the crossing bins: exact 16-bit keys
+  // ---- 2b. thresholds of top-k / top-p
   uint32_t key_th = 0;
-  if (bk >= 0 || bp >= 0) {
-    for (int i = tid; i < kSmpWarps * 256; i += kSmpThreads) {
-      wcnt[i] = 0u;
-      wmass[i] = 0ull;
+  if (do_k || do_p) {
+    // Bands [max - 2^i, max]: entries and fixed-point mass in each, and the
+    // row's total mass, in one pass without atomics.
+    uint32_t lc[kSmpLevels];
+    unsigned long long lm[kSmpLevels], ztot = 0;
+#pragma unroll
+    for (int i = 0; i < kSmpLevels; ++i) {
+      lc[i] = 0u;
+      lm[i] = 0ull;
     }
-    __syncthreads();
-    for (int t = 0; t < ntile; ++t) {
-      uint32_t b[kSmpPer];
-      const int i0 = t * kSmpTile + tid * kSmpPer;
-      const int n = smp_load8(lg, V, i0, a.vec, b);
+    smp_tiles(lg, V, a.vec, ntile, [&](int, int, int n, const uint4& u) {
 #pragma unroll
       for (int j = 0; j < kSmpPer; ++j) {
         if (j < n) {
-          const uint32_t key = smp_key(b[j]);
-          const int hb = (int)(key >> 8);
-          if (hb == bk) atomicAdd(my_cnt + (key & 255u), 1u);
-          if (hb == bp) atomicAdd(my_mass + (key & 255u), smp_fixed_mass(smp_val(b[j]), vmax));
+          const float v = smp_val(smp_bits(u, j));
+          const unsigned long long w = smp_fixed_mass(v, vmax);
+          ztot += w;
+#pragma unroll
+          for (int i = 0; i < kSmpLevels; ++i)
+            if (v >= vmax - smp_band(i)) {
+              ++lc[i];
+              lm[i] += w;
+            }
         }
       }
+    });
+#pragma unroll
+    for (int i = 0; i < 2 * kSmpLevels + 1; ++i) {
+      unsigned long long x = i < kSmpLevels ? (unsigned long long)lc[i] : i < 2 * kSmpLevels ? lm[i - kSmpLevels] : ztot;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (lane == 0) lvl_part[warp][i] = x;
     }
     __syncthreads();
-    if (tid < 256) {
-      uint32_t c = 0;
-      unsigned long long m = 0;
-      for (int w = 0; w < kSmpWarps; ++w) {
-        c += wcnt[w * 256 + tid];
-        m += wmass[w * 256 + tid];
-      }
-      cnt1[tid] = c;
-      mass1[tid] = m;
+    if (tid < 2 * kSmpLevels + 1) {
+      unsigned long long x = 0;
+      for (int w = 0; w < kSmpWarps; ++w) x += lvl_part[w][tid];
+      lvl[tid] = x;
     }
     __syncthreads();
-    if (warp == 0) {
-      uint32_t kk = 0, kp = 0;
-      unsigned long long unused;
-      if (bk >= 0) {
-        const int low = smp_cross(cnt1, (unsigned long long)a.top_k - bef_k, &unused);
-        kk = ((uint32_t)bk << 8) | (uint32_t)max(low, 0);
-      }
-      if (bp >= 0) {
-        const int low = smp_cross(mass1, ptarget - bef_p, &unused);
-        kp = ((uint32_t)bp << 8) | (uint32_t)max(low, 0);
-      }
-      if (lane == 0) s_int[2] = (int)max(kk, kp);
+    // keep a value while the mass strictly above it is below top_p * total
+    unsigned long long P = 0;
+    if (do_p) {
+      P = (unsigned long long)ceil((double)a.top_p * (double)lvl[2 * kSmpLevels]);
+      if (P < 1ull) P = 1ull;
     }
-    __syncthreads();
-    key_th = (uint32_t)s_int[2];
+    const unsigned long long K = do_k ? (unsigned long long)a.top_k : 0ull;
+    // the narrowest band that holds both crossings, if it fits the candidate store
+    int band = -1;
+    for (int i = 0; i < kSmpLevels; ++i) {
+      if ((!do_k || lvl[i] >= K) && (!do_p || lvl[kSmpLevels + i] >= P)) {
+        band = i;
+        break;
+      }
+    }
+    if (band >= 0 && lvl[band] > (unsigned long long)kSmpCap) band = -1;
+    SmpShared sh{wcnt, wmass, cnt1, mass1, s_int, s_u};
+    if (band >= 0) {
+      if (tid == 0) s_int[4] = 0;
+      __syncthreads();
+      const float thr = vmax - smp_band(band);
+      smp_tiles(lg, V, a.vec, ntile, [&](int, int, int n, const uint4& u) {
+#pragma unroll
+        for (int j = 0; j < kSmpPer; ++j) {
+          const uint32_t bits = smp_bits(u, j);
+          const bool take = j < n && smp_val(bits) >= thr;
+          const unsigned m = __ballot_sync(0xffffffffu, take);
+          if (m) {
+            const int leader = __ffs(m) - 1;
+            int pos = 0;
+            if (lane == leader) pos = atomicAdd(&s_int[4], __popc(m));
+            pos = __shfl_sync(0xffffffffu, pos, leader) + __popc(m & ((1u << lane) - 1u));
+            if (take && pos < kSmpCap) cand[pos] = (unsigned short)bits;
+          }
+        }
+      });
+      __syncthreads();
+      const int ncand = min(s_int[4], kSmpCap);
+      key_th = smp_select(
+          [&](auto&& g) {
+            for (int i = tid; i < ncand; i += kSmpThreads) g((uint32_t)cand[i]);
+          },
+          do_k, do_p, K, P, vmax, sh);
+    } else {  // flat rows: the crossing lies deep in the bulk, select over the whole row
+      key_th = smp_select(
+          [&](auto&& g) {
+            smp_tiles(lg, V, a.vec, ntile, [&](int, int, int n, const uint4& u) {
+#pragma unroll
+              for (int j = 0; j < kSmpPer; ++j)
+                if (j < n) g(smp_bits(u, j));
+            });
+          },
+          do_k, do_p, K, P, vmax, sh);
+    }
   }
   const float thr_m = a.min_p > 0.f ? vmax + logf(a.min_p) : -INFINITY;
   const float inv_t = 1.f / a.temp;
 
   // ---- 3. inverse-CDF draw over the kept set at the temperature
-  for (int t = 0; t < ntile; ++t) {
-    uint32_t b[kSmpPer];
-    const int i0 = t * kSmpTile + tid * kSmpPer;
-    const int n = smp_load8(lg, V, i0, a.vec, b);
-    float s = 0.f;
+  for (int t0 = 0; t0 < ntile; t0 += kSmpAhead) {
+    uint4 u[kSmpAhead];
+    int n[kSmpAhead];
 #pragma unroll
-    for (int j = 0; j < kSmpPer; ++j) {
-      const float v = smp_val(b[j]);
-      if (j < n && smp_key(b[j]) >= key_th && v >= thr_m) s += expf((v - vmax) * inv_t);
+    for (int q = 0; q < kSmpAhead; ++q) n[q] = smp_load(lg, V, (t0 + q) * kSmpTile + tid * kSmpPer, a.vec, u[q]);
+#pragma unroll
+    for (int q = 0; q < kSmpAhead; ++q) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kSmpPer; ++j) {
+        const uint32_t bits = smp_bits(u[q], j);
+        const float v = smp_val(bits);
+        if (j < n[q] && smp_key(bits) >= key_th && v >= thr_m) s += expf((v - vmax) * inv_t);
+      }
+      s = warp_sum(s);
+      if (lane == 0) red4[q][warp] = s;
     }
-    s = smp_block_sum(s, red);
-    if (tid == 0) tile_sum[t] = s;
+    __syncthreads();
+    if (tid < kSmpAhead && t0 + tid < ntile) {
+      float s = 0.f;
+      for (int w = 0; w < kSmpWarps; ++w) s += red4[tid][w];
+      tile_sum[t0 + tid] = s;
+    }
+    __syncthreads();
   }
-  __syncthreads();
   if (tid == 0) {
     float z = 0.f;
     for (int t = 0; t < ntile; ++t) z += tile_sum[t];
@@ -452,15 +548,16 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, int row, unsigne
   __syncthreads();
   const int ti = s_int[3];
   float rem = s_f[0];
-  uint32_t b[kSmpPer];
+  uint4 u;
   const int i0 = ti * kSmpTile + tid * kSmpPer;
-  const int n = smp_load8(lg, V, i0, a.vec, b);
+  const int n = smp_load(lg, V, i0, a.vec, u);
   float w[kSmpPer];
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < kSmpPer; ++j) {
-    const float v = smp_val(b[j]);
-    w[j] = (j < n && smp_key(b[j]) >= key_th && v >= thr_m) ? expf((v - vmax) * inv_t) : 0.f;
+    const uint32_t bits = smp_bits(u, j);
+    const float v = smp_val(bits);
+    w[j] = (j < n && smp_key(bits) >= key_th && v >= thr_m) ? expf((v - vmax) * inv_t) : 0.f;
     s += w[j];
   }
   // block-wide scan: the exclusive prefix of thread i is bit-identical to the

@@ -158,21 +158,36 @@ def bench_attention(s: int, l: int, bits: int, hq: int, hkv: int, iters: int) ->
 
 
 def bench_sample(rows: int, vocab: int, iters: int) -> dict:
-    """The device sampler (temperature 0.7, top-p 0.9, top-k 50, repetition
-    penalty 1.1 over a 20-token window) on bf16 logits [rows, vocab], graph
-    replayed; beside it the same filters as a chain of torch ops on the GPU
-    (topk, softmax, sort, cumsum, scatter, multinomial), timed eagerly with
-    CUDA events because multinomial does not capture."""
+    """The device sampler on bf16 logits [rows, vocab], graph replayed, on a
+    flat row (N(0, 2): top-p's cut lies in the bulk, so the threshold search
+    runs over the whole row) and a peaked one (the same plus 64 tokens lifted
+    by 12..20, as a language model's next-token row usually is: the cut lies
+    in a narrow band under the max).  Settings: "full" = temperature 0.7,
+    top-p 0.9, top-k 50, repetition penalty 1.1 over 20 tokens; "top_p" =
+    temperature 0.7, top-p 0.9; "temp" = temperature only; "greedy".  Beside
+    them the same filters as a chain of torch ops on the GPU (topk, softmax,
+    sort, cumsum, scatter, multinomial), timed eagerly with CUDA events
+    because multinomial does not capture."""
     from myinfer_b200.sample import DeviceSampler, make_logits_processors
     g = torch.Generator(device="cuda").manual_seed(0)
-    x = (2 * torch.randn(rows, vocab, generator=g, device="cuda")).to(torch.bfloat16)
+    flat = (2 * torch.randn(rows, vocab, generator=g, device="cuda")).to(torch.bfloat16)
+    peaked = flat.float()
+    idx = torch.randint(0, vocab, (rows, 64), generator=g, device="cuda")
+    peaked.scatter_add_(1, idx, 12 + 8 * torch.rand(rows, 64, generator=g, device="cuda"))
+    peaked = peaked.to(torch.bfloat16)
     hist = torch.randint(0, vocab, (rows, 20), generator=g, device="cuda", dtype=torch.int32)
-    s = DeviceSampler(0.7, top_p=0.9, top_k=50, processors=make_logits_processors(repetition_penalty=1.1), seed=1)
     out = torch.empty(rows, dtype=torch.int32, device="cuda")
-    us = _timed(lambda i: s(x, history=hist, out=out), iters)
-    gs = DeviceSampler(0.0)
-    gs.state("cuda")
-    us_greedy = _timed(lambda i: gs(x, out=out), iters)
+    pen = make_logits_processors(repetition_penalty=1.1)
+    settings = {"full": (DeviceSampler(0.7, top_p=0.9, top_k=50, processors=pen, seed=1), hist),
+                "top_p": (DeviceSampler(0.7, top_p=0.9, seed=1), None),
+                "temp": (DeviceSampler(0.7, seed=1), None),
+                "greedy": (DeviceSampler(0.0), None)}
+    res = {"kernel": "sample", "rows": rows, "vocab": vocab}
+    for name, x in (("flat", flat), ("peaked", peaked)):
+        for key, (smp, h) in settings.items():
+            smp.state("cuda")
+            xs = x.clone()
+            res[f"{name}_{key}_us"] = round(_timed(lambda i: smp(xs, history=h, out=out), iters), 2)
 
     def torch_chain(lg):
         z = lg.float() / 0.7
@@ -185,16 +200,16 @@ def bench_sample(rows: int, vocab: int, iters: int) -> dict:
         return torch.multinomial(probs / probs.sum(dim=-1, keepdim=True), 1)
 
     for _ in range(3):
-        torch_chain(x)
+        torch_chain(flat)
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(iters):
-        torch_chain(x)
+        torch_chain(flat)
     t1.record()
     torch.cuda.synchronize()
-    return {"kernel": "sample", "rows": rows, "vocab": vocab, "us": round(us, 2), "us_greedy": round(us_greedy, 2),
-            "torch_ops_us": round(t0.elapsed_time(t1) * 1e3 / iters, 2)}
+    res["torch_ops_us"] = round(t0.elapsed_time(t1) * 1e3 / iters, 2)
+    return res
 
 
 def main():
