@@ -77,6 +77,26 @@ def test_matches_oracle_full_vocab(case):
     assert exact >= 0.9 * R, exact
 
 
+@pytest.mark.parametrize("case", [dict(temp=0.7, top_p=0.9), dict(temp=1.0, top_k=50), dict(temp=0.9, top_p=0.5, top_k=3),
+                                  dict(temp=1.3, top_p=0.99, min_p=0.001), dict(temp=1.0, top_k=5000)],
+                         ids=["p", "k", "pk", "pm", "bigk"])
+def test_matches_oracle_peaked_rows(case):
+    """Rows with a few lifted tokens (the shape of a language model's
+    next-token row): the cuts fall in a narrow band under the max, so the
+    threshold search runs over candidates compacted into shared memory (top-k
+    5000 needs more than the narrowest bands hold)."""
+    R, V = 8, V_FULL
+    x = _logits(R, V, 21, scales=[2] * R).float()
+    g = torch.Generator().manual_seed(22)
+    for r in range(R):
+        idx = torch.randint(0, V, (16 * (r + 1),), generator=g)
+        x[r, idx] += 10 + 10 * torch.rand(idx.numel(), generator=g)
+    x = x.to(torch.bfloat16)
+    s = DeviceSampler(case["temp"], case.get("top_p", 0.0), case.get("min_p", 0.0), case.get("top_k", 0), seed=5)
+    got = s(x.cuda()).cpu().numpy()
+    assert _check(got, x.float().numpy(), seed=5, **case) >= R - 1
+
+
 def test_penalties_bit_exact_and_greedy():
     R, W = 4, 24
     x = _logits(R, V_FULL, 5, scales=[3, 3, 3, 3])
