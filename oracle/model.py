@@ -234,6 +234,7 @@ class Model:
         self.cfg = cfg
         self.w = weights
         self._deq: Dict[str, torch.Tensor] = {}
+        self.route_log: Optional[list] = None  # set to a list to record router margins
         self.set_rope(yarn_factor, native_ctx)
 
     def set_rope(self, factor: float, native: int = 32768):
@@ -300,6 +301,10 @@ class Model:
         k = cfg.num_experts_per_tok
         # Highest probability first; equal probabilities -> lower expert id first.
         order = torch.sort(probs, dim=-1, descending=True, stable=True).indices[:, :k]
+        if self.route_log is not None:  # (rows, smallest k-th minus (k+1)-th probability) per call
+            sp = torch.sort(probs, dim=-1, descending=True).values
+            margin = (sp[:, k - 1] - sp[:, k]).min().item() if k < probs.shape[-1] else float("inf")
+            self.route_log.append((x.shape[0], margin))
         scores = torch.gather(probs, 1, order)
         if cfg.norm_topk_prob:
             scores = rb(scores / rb(scores.sum(dim=-1, keepdim=True)))

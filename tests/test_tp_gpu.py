@@ -1,7 +1,10 @@
 """Tensor-parallel (dense) and expert-parallel (MoE) decode on 2 GPUs against
 the same model on one GPU: the ranks' fp32 partial sums are all-reduced, so
 logits agree to fp32 summation-order noise and greedy tokens are identical.
-Skipped with fewer than two GPUs."""
+For MoE that noise can flip a router tie (the router's probabilities are bf16,
+so the k-th and (k+1)-th expert often tie exactly): the runs may part from the
+first step whose routing the oracle finds within 1e-3 of a tie, the allowance
+the single-GPU model tests make too.  Skipped with fewer than two GPUs."""
 
 import os
 
@@ -63,6 +66,19 @@ def _worker(rank, world, port, cfg, prompt, n, step, q):
         dist.destroy_process_group()
 
 
+def _router_tie_rows(cfg, prompt, n, step):
+    """Decode rows whose producing model call routes some token within 1e-3 of
+    a tie in the oracle (same weights, prompt and prefill chunking)."""
+    from oracle import model as om
+    c = om.Config.from_dict(cfg)
+    m = om.Model(c, om.generate_weights(c, 3))
+    m.route_log = []
+    om.generate(m, prompt, n, prefill_step=step, kv_bits=8, quantized_kv_start=0)
+    L = c.num_hidden_layers
+    single = [margin for rows, margin in m.route_log if rows == 1][-(n + 1) * L:]  # last prompt token + decode
+    return {r for r in range(n) if min(single[r * L:(r + 1) * L]) < 1e-3}
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("cfg", [TINY, TINY_MOE, TINY_MOE8], ids=["tp2-dense", "ep2-moe", "ep2-moe-top8"])
 @pytest.mark.parametrize("step", [8, 64], ids=["gemv-prefill", "gemm-prefill"])
@@ -80,8 +96,15 @@ def test_two_rank_matches_one(cfg, step):
     for p in procs:
         p.join(timeout=60)
     ref_toks, ref_logits = _run(cfg, 0, 1, prompt, n, step)
+    ties = None
     for r in (0, 1):
         toks, logits = res[r]
         cos = torch.nn.functional.cosine_similarity(logits, ref_logits, dim=-1)
-        assert cos.min().item() > 0.9999, cos.tolist()
-        assert toks == ref_toks
+        bad = [i for i in range(n) if not cos[i].item() > 0.9999]
+        if bad and "num_experts" in cfg:
+            ties = _router_tie_rows(cfg, prompt, n, step) if ties is None else ties
+            assert bad[0] in ties, (bad[0], sorted(ties), cos.tolist())
+            assert toks[:bad[0]] == ref_toks[:bad[0]]
+        else:
+            assert not bad, cos.tolist()
+            assert toks == ref_toks
