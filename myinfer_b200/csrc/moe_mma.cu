@@ -355,8 +355,7 @@ __device__ __forceinline__ void router_topk_warp(const MoeRouterArgs& a, Logit l
   }
 }
 
-// Router + top-k of one decode token in one launch (routers larger than
-// 128 x 2048; smaller ones take moe_router_topk1_kernel): each warp takes one of
+// Router + top-k of one decode token in one launch: each warp takes one of
 // the E router rows (RMSNorm(h) staged once per CTA, CUDA-core dot product as
 // moe.cu), rounds the logit to bf16 like the router projection's output, and
 // the last CTA to finish (a zeroed counter it leaves zeroed) runs the top-k:
@@ -392,83 +391,8 @@ __global__ void __launch_bounds__(RT_W * 32) moe_router_topk_kernel(const MoeRou
   if (lane == 0) *a.counter = 0;
 }
 
-// The same router + top-k in one 1024-thread CTA, for routers of at most
-// 32 * RPW rows and 1024 * CPL columns (Qwen3-30B-A3B: 128 x 2048): every warp
-// issues the loads of all its rows (row = warp + 32 r, chunks lane + 32 c of
-// 32 columns) before RMSNorm(h) is staged, so the weight fetch overlaps the
-// staging, and the top-k follows a CTA barrier instead of a fenced counter and
-// a re-read by the last CTA.  Each row's chunks accumulate in the order
-// row_dot uses, so the logits are bit-identical to moe_router_topk_kernel's.
-template <int RPW, int CPL>
-__global__ void __launch_bounds__(1024, 1) moe_router_topk1_kernel(const MoeRouterArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  extern __shared__ __align__(16) float rsm[];
-  const int H = a.H, E = a.E, K32 = H >> 5;
-  float* xs = rsm;
-  float* xsum = xs + H;
-  float* red = xsum + K32;
-  float* lg = red + 33;  // [E] bf16-rounded logits
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint4* wr = reinterpret_cast<const uint4*>(a.w);
-  const int H64 = H >> 6;
-  uint4 wv[RPW][CPL];
-  uint32_t sb[RPW][CPL];  // bf16 scale (low half) and bias (high half)
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    const int row = warp + 32 * r;
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-      const int i = lane + 32 * c;
-      if (row < E && i < K32) {
-        wv[r][c] = ldg_stream(wr + size_t(row) * K32 + i);
-        sb[r][c] = uint32_t(ldg_nc_u16(a.s + size_t(row) * H64 + (i >> 1))) |
-                   (uint32_t(ldg_nc_u16(a.b + size_t(row) * H64 + (i >> 1))) << 16);
-      }
-    }
-  }
-  stage_rows<1>(a.x, H, H, a.norm_w, a.eps, xs, xsum, red);
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    const int row = warp + 32 * r;
-    if (row >= E) break;  // warp-uniform
-    float acc = 0.f;
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-      const int i = lane + 32 * c;
-      if (i < K32) {
-        const float sv = bf16_lo(sb[r][c]), bv = bf16_hi(sb[r][c]);
-        const float off = fmaf(-128.f, sv, bv);
-        const float A = dot32(wv[r][c], xs, i);
-        acc = fmaf(sv, A, fmaf(off, xsum[i], acc));
-      }
-    }
-    const float v = rbf(warp_sum(acc));
-    if (lane == 0) {
-      lg[row] = v;
-      a.logits[row] = f2bf(v);
-    }
-  }
-  __syncthreads();
-  if (warp == 0) router_topk_warp(a, [&](int e) { return lg[e]; });
-}
-
-template <int RPW, int CPL>
-static int router1_launch(const MoeRouterArgs& a, cudaStream_t st) {
-  const size_t smem = size_t(a.H) * 4 + size_t(a.H / 32) * 4 + 33 * 4 + size_t(a.E) * 4;
-  M5_CUDA(launch_pdl(moe_router_topk1_kernel<RPW, CPL>, dim3(1), dim3(1024), smem, st, a));
-  M5_LAUNCH_CHECK("moe router/top-k (one CTA) launch");
-  return M5_OK;
-}
-
 int moe_router_topk_launch(const MoeRouterArgs& a, cudaStream_t st) {
   if (a.E > 256 || a.k <= 0 || a.k > 32 || a.k > a.E || a.H % 256) return fail(M5_ERR_INVALID, "moe router: shape");
-  if (a.E <= 128 && a.H <= 2048) {  // smem <= 8 KB + 1 KB: no opt-in needed
-    const bool c1 = a.H <= 1024;
-    if (a.E <= 32) return c1 ? router1_launch<1, 1>(a, st) : router1_launch<1, 2>(a, st);
-    if (a.E <= 64) return c1 ? router1_launch<2, 1>(a, st) : router1_launch<2, 2>(a, st);
-    return c1 ? router1_launch<4, 1>(a, st) : router1_launch<4, 2>(a, st);
-  }
   const size_t smem = size_t(a.H) * 4 + size_t(a.H / 32) * 4 + 33 * 4;
   static bool configured = false;
   if (!configured) {
