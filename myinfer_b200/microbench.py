@@ -3,7 +3,7 @@
     python -m myinfer_b200.microbench gemv --n 25600 --k 5120 [--m 1] [--iters 20]
     python -m myinfer_b200.microbench attention --s 32768 --l 1 --bits 8 [--hq 64 --hkv 8]
     python -m myinfer_b200.microbench gemm --m 2048 --n 8192 --k 5120
-    python -m myinfer_b200.microbench step --ctx 32768 --steps 2 [--config qwen3-30b-a3b]   # decode steps
+    python -m myinfer_b200.microbench step --ctx 32768 --steps 2 [--config qwen3-30b-a3b] [--batch 16]   # decode steps
     python -m myinfer_b200.microbench sample [--rows 1] [--vocab 151936]   # device sampler vs torch ops
 
 ``gemv`` cycles over enough distinct weight matrices that every launch reads
@@ -82,11 +82,12 @@ def bench_gemm(m: int, n: int, k: int, iters: int) -> dict:
     return {"kernel": "gemm", "m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(flops / us / 1e6, 1)}
 
 
-def bench_step(ctx: int, steps: int, config: str = "qwen3-32b") -> dict:
+def bench_step(ctx: int, steps: int, config: str = "qwen3-32b", batch: int = 1) -> dict:
     """Decode steps of a Qwen3-32B- or Qwen3-30B-A3B-shaped model over a synthetic 8-bit KV
-    cache of `ctx` positions; only the timed steps run inside a CUDA profiler
-    range (cudaProfilerStart/Stop), so `ncu --profile-from-start off` lists
-    exactly the kernels of `steps` decode steps."""
+    cache of `ctx` positions (`batch` > 1: that many sequences per step through
+    m5_forward_batch); only the timed steps run inside a CUDA profiler range
+    (cudaProfilerStart/Stop), so `ncu --profile-from-start off` lists exactly
+    the kernels of `steps` decode steps."""
     from myinfer_b200 import _lib, ops
     from myinfer_b200.cache import PromptCache, QuantizedKVCache
     from myinfer_b200.model import Model, ModelArgs, random_weights
@@ -101,21 +102,30 @@ def bench_step(ctx: int, steps: int, config: str = "qwen3-32b") -> dict:
     a = ModelArgs.from_dict(presets[config])
     dev = torch.device("cuda")
     model = Model(a, random_weights(a, 0, dev), dev, max_tokens=8)
-    cache = PromptCache([QuantizedKVCache(a.num_key_value_heads, a.head_dim, dev, 64, 8, capacity=ctx + steps + 8)
-                         for _ in range(a.num_hidden_layers)], dev)
+    cache = PromptCache([QuantizedKVCache(a.num_key_value_heads, a.head_dim, dev, 64, 8, capacity=ctx + steps + 8,
+                                          batch=batch) for _ in range(a.num_hidden_layers)], dev)
     g = torch.Generator(device=dev).manual_seed(1)
-    for c in cache:  # random N(0,1) K/V at positions [0, ctx)
+    for c in cache:  # random N(0,1) K/V at positions [0, ctx) of every sequence
         for which in ("k", "v"):
-            x = torch.randn(c.n_kv_heads, ctx, a.head_dim, generator=g, device=dev).to(torch.bfloat16)
-            q, sc, b = ops.quantize(x, 64, 8)
             tq, ts, tb = (c._kq, c._ks, c._kb) if which == "k" else (c._vq, c._vs, c._vb)
-            tq[0, :, :ctx].copy_(q)
-            ts[0, :, :ctx].copy_(sc)
-            tb[0, :, :ctx].copy_(b)
+            for bi in range(batch):
+                x = torch.randn(c.n_kv_heads, ctx, a.head_dim, generator=g, device=dev).to(torch.bfloat16)
+                q, sc, b = ops.quantize(x, 64, 8)
+                tq[bi, :, :ctx].copy_(q)
+                ts[bi, :, :ctx].copy_(sc)
+                tb[bi, :, :ctx].copy_(b)
         c.offset = ctx
-    tok = torch.tensor([1], dtype=torch.int32, device=dev)
+    tok = torch.ones(batch, dtype=torch.int32, device=dev)
+    logits = torch.empty(batch, a.vocab_size, dtype=torch.bfloat16, device=dev) if batch > 1 else None
+
+    def step():
+        if batch > 1:
+            model.forward_batch(tok, cache, logits=logits, argmax_out=tok)
+        else:
+            model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
+
     for _ in range(2):  # warm: configures every kernel, then rewinds the cache
-        model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
+        step()
         for c in cache:
             c.offset -= 1
     torch.cuda.synchronize()
@@ -123,12 +133,13 @@ def bench_step(ctx: int, steps: int, config: str = "qwen3-32b") -> dict:
     torch.cuda.profiler.start()
     start.record()
     for _ in range(steps):
-        model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
+        step()
     end.record()
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
-    return {"kernel": "decode_step", "config": config, "ctx": ctx, "steps": steps,
-            "ms_per_step_eager": round(start.elapsed_time(end) / steps, 3)}
+    ms = start.elapsed_time(end) / steps
+    return {"kernel": "decode_step", "config": config, "ctx": ctx, "batch": batch, "steps": steps,
+            "ms_per_step_eager": round(ms, 3), "tok_s_eager": round(batch * 1e3 / ms, 1)}
 
 
 def bench_attention(s: int, l: int, bits: int, hq: int, hkv: int, iters: int) -> dict:
@@ -224,6 +235,7 @@ def main():
     st.add_argument("--ctx", type=int, default=32768)
     st.add_argument("--steps", type=int, default=2)
     st.add_argument("--config", default="qwen3-32b", choices=["qwen3-32b", "qwen3-30b-a3b"])
+    st.add_argument("--batch", type=int, default=1)
     gm = sub.add_parser("gemm")
     gm.add_argument("--m", type=int, default=2048)
     gm.add_argument("--n", type=int, default=8192)
@@ -248,7 +260,7 @@ def main():
     elif args.cmd == "sample":
         r = bench_sample(args.rows, args.vocab, args.iters)
     elif args.cmd == "step":
-        r = bench_step(args.ctx, args.steps, args.config)
+        r = bench_step(args.ctx, args.steps, args.config, args.batch)
     else:
         r = bench_attention(args.s, args.l, args.bits, args.hq, args.hkv, args.iters)
     print(json.dumps(r), flush=True)
