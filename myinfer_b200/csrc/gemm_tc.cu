@@ -70,6 +70,7 @@ struct Seg {
 
 struct Params {
   int M, K, G, C;      // tokens, reduction length, scale groups, bias blocks (ceil(G / 32))
+  int gld;             // scale / bias row stride in groups (G, or more for a K slice)
   int vec_sb;          // G % 8 == 0: 16-byte scale loads and TMA bias tiles (else scalar global loads)
   const bf16* bias[3]; // per segment, for the scalar bias path
   int nseg;
@@ -374,9 +375,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         tile_rows(p, EPI, (blockIdx.x + tl * gridDim.x) / p.m_tiles, si, row0);
         int sg, grow;
         row_of<EPI>(p, si, row0, r, sg, grow);
-        srow = reinterpret_cast<const uint4*>(p.seg[sg].s + size_t(grow) * p.G);
-        srow16 = p.seg[sg].s + size_t(grow) * p.G;
-        brow16 = p.bias[sg] + size_t(grow) * p.G;
+        srow = reinterpret_cast<const uint4*>(p.seg[sg].s + size_t(grow) * p.gld);
+        srow16 = p.seg[sg].s + size_t(grow) * p.gld;
+        brow16 = p.bias[sg] + size_t(grow) * p.gld;
         cur_w = -2;
       }
       uint32_t s2 = 0;
@@ -570,6 +571,7 @@ size_t gemm_tc_xs_bytes(int M, int K) {
 
 bool gemm_tc_eligible(const GemvArgs& a, int M, int epi) {
   if (M < 1 || a.K % 64 || a.norm_w || a.ldx % 8 || a.nseg < 1 || a.nseg > 3) return false;
+  if (a.ldk && (a.ldk % 512 || a.ldk < a.K)) return false;  // slice rows stay 16-byte aligned
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!al(a.x)) return false;
   for (int i = 0; i < a.nseg; ++i) {
@@ -605,6 +607,8 @@ int gemm_tc_launch(const GemvArgs& a, int M, int epi, bf16* xs, size_t xs_bytes,
   p.K = a.K;
   p.G = a.K / 64;
   p.C = (p.G + 31) / 32;
+  const int64_t kst = a.ldk ? a.ldk : a.K;  // full row length of the weights (K slices)
+  p.gld = (int)(kst / 64);
   p.vec_sb = (p.G % 8) == 0;
   p.nseg = a.nseg;
   p.ldy = a.ldy;
@@ -629,10 +633,10 @@ int gemm_tc_launch(const GemvArgs& a, int M, int epi, bf16* xs, size_t xs_bytes,
                  CU_TENSOR_MAP_SWIZZLE_128B, "xs");
   const uint32_t box_rows = epi == EPI_SWIGLU ? 16 : gtc::BR;
   for (int i = 0; i < a.nseg && !rc; ++i) {
-    rc = gtc_map(&m.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, a.seg[i].w, a.K / 8, a.seg[i].rows, a.K / 2, 8, box_rows,
-                 CU_TENSOR_MAP_SWIZZLE_NONE, "weights");
+    rc = gtc_map(&m.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, a.seg[i].w, a.K / 8, a.seg[i].rows, size_t(kst) / 2, 8,
+                 box_rows, CU_TENSOR_MAP_SWIZZLE_NONE, "weights");
     if (!rc && p.vec_sb)
-      rc = gtc_map(&m.b[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.seg[i].b, p.G, a.seg[i].rows, size_t(p.G) * 2, 32,
+      rc = gtc_map(&m.b[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.seg[i].b, p.G, a.seg[i].rows, size_t(p.gld) * 2, 32,
                    box_rows, CU_TENSOR_MAP_SWIZZLE_NONE, "biases");
   }
   if (rc) return rc;
@@ -650,6 +654,35 @@ int gemm_tc_launch(const GemvArgs& a, int M, int epi, bf16* xs, size_t xs_bytes,
     case EPI_F32: return gtc_launch_t<EPI_F32>(p, m, st);
   }
   return fail(M5_ERR_INVALID, "gemm_tc: bad epilogue");
+}
+
+// y[m, n] = epi(sum over the S slices of part[s][m][n]), slices added in
+// order: EPI_RESIDUAL adds bf16(sum) into bf16 y (the GEMM's own residual
+// epilogue), EPI_F32 stores the fp32 sum.
+__global__ void gemm_splitk_reduce_kernel(const float* __restrict__ part, int S, int M, int N, int epi, bf16* y,
+                                          float* yf, int64_t ldy) {
+  const int64_t total = int64_t(M) * N;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    float v = 0.f;
+    for (int s = 0; s < S; ++s) v += part[size_t(s) * total + i];
+    const int64_t m = i / N, n = i % N;
+    if (epi == EPI_RESIDUAL) {
+      bf16* o = y + m * ldy + n;
+      *o = f2bf(bf2f(*o) + rbf(v));
+    } else {
+      yf[m * ldy + n] = v;
+    }
+  }
+}
+
+int gemm_splitk_reduce_launch(const float* part, int S, int M, int N, int epi, bf16* y, float* yf, int64_t ldy,
+                              cudaStream_t st) {
+  if (epi != EPI_RESIDUAL && epi != EPI_F32) return fail(M5_ERR_INVALID, "split-K reduce: epilogue");
+  const int64_t total = int64_t(M) * N;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
+  gemm_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, S, M, N, epi, y, yf, ldy);
+  M5_LAUNCH_CHECK("split-K reduce launch");
+  return M5_OK;
 }
 
 int gemm_tc_error(int reset) {

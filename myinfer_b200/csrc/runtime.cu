@@ -88,6 +88,15 @@ struct Model {
   float* hf = nullptr;
   bf16* vpart = nullptr;     // [v_rows, Vl]
   bf16* vgather = nullptr;   // [tp, v_rows, Vl]
+  // GEMMs of few rows split over K (batched decode): fp32 slice products, the
+  // slices' group-sum scratch and the side streams they run on
+  static constexpr int kSplitK = 4;
+  static constexpr int kSplitKMaxRows = 64;
+  float* sk_f = nullptr;     // [kSplitK][rows <= kSplitKMaxRows][N <= hidden]
+  char* sk_xs = nullptr;     // kSplitK regions of sk_xs_stride bytes
+  size_t sk_xs_stride = 0;
+  cudaStream_t sk_st[kSplitK] = {};
+  cudaEvent_t sk_fork = nullptr, sk_join[kSplitK] = {};
 };
 
 // Token count from which a projection runs as the tensor-core GEMM instead of
@@ -224,6 +233,42 @@ static void attach(const Model* m, GemvArgs& a) {
 
 // One projection of T tokens: the tensor-core GEMM for prefill-sized T (with
 // the fused RMSNorm materialised first), the streaming GEMV otherwise.
+// A projection of few rows with few output tiles (batched decode's o_proj and
+// down: N / 128 tiles on a 148-SM GPU) leaves most SMs idle as one GEMM.  Its
+// K range is cut into slices of whole 8-group blocks that run as concurrent
+// GEMMs on side streams, each writing fp32 products, and one kernel adds the
+// slices in order and applies the epilogue.
+static int gemm_splitk(const Model* m, const GemvArgs& a, int T, int epi, cudaStream_t st) {
+  const int N = a.seg[0].rows, G = a.K / 64;
+  const int tiles = (N / 128) * ((T + 127) / 128);
+  const int S = std::min({Model::kSplitK, sm_count() / std::max(1, tiles), G / 8});
+  if (S < 2 || N > m->cfg.hidden_size || a.ldk || a.K % 512)
+    return gemm_tc_launch(a, T, epi, m->gxs, m->gxs_bytes, st);
+  M5_CUDA(cudaEventRecord(m->sk_fork, st));
+  const int G8 = G / 8;
+  const size_t slice = size_t(T) * N;
+  for (int sl = 0; sl < S; ++sl) {
+    const int g0 = 8 * (G8 * sl / S), g1 = 8 * (G8 * (sl + 1) / S);
+    GemvArgs b = a;
+    b.K = (g1 - g0) * 64;
+    b.ldk = a.K;
+    b.x = a.x + size_t(g0) * 64;
+    b.seg[0].w = a.seg[0].w + size_t(g0) * 8;  // 8 words of codes per group
+    b.seg[0].s = a.seg[0].s + g0;
+    b.seg[0].b = a.seg[0].b + g0;
+    b.seg[0].y = nullptr;
+    b.seg[0].yf = m->sk_f + sl * slice;
+    b.ldy = N;
+    M5_CUDA(cudaStreamWaitEvent(m->sk_st[sl], m->sk_fork, 0));
+    const int rc = gemm_tc_launch(b, T, EPI_F32, reinterpret_cast<bf16*>(m->sk_xs + sl * m->sk_xs_stride),
+                                  m->sk_xs_stride, m->sk_st[sl]);
+    M5_CUDA(cudaEventRecord(m->sk_join[sl], m->sk_st[sl]));
+    M5_CUDA(cudaStreamWaitEvent(st, m->sk_join[sl], 0));
+    if (rc) return rc;
+  }
+  return gemm_splitk_reduce_launch(m->sk_f, S, T, N, epi, a.seg[0].y, a.seg[0].yf, a.ldy, st);
+}
+
 static int linear_auto(const Model* m, const GemvArgs& proto, int T, int epi, cudaStream_t st) {
   if (T >= kGemmMinRows && m->gxs && gemm_tc_xs_bytes(T, proto.K) <= m->gxs_bytes) {
     GemvArgs a = proto;
@@ -238,6 +283,8 @@ static int linear_auto(const Model* m, const GemvArgs& proto, int T, int epi, cu
         int rc = rms_norm_launch(proto.x, proto.norm_w, T, a.K, proto.eps, m->xn, st);
         if (rc) return rc;
       }
+      if (T <= Model::kSplitKMaxRows && m->sk_f && a.nseg == 1 && (epi == EPI_RESIDUAL || epi == EPI_F32))
+        return gemm_splitk(m, a, T, epi, st);
       return gemm_tc_launch(a, T, epi, m->gxs, m->gxs_bytes, st);
     }
   }
@@ -823,6 +870,11 @@ extern "C" int m5_model_destroy(void* model) {
     if (m->moe_join[i]) cudaEventDestroy(m->moe_join[i]);
   }
   if (m->moe_fork) cudaEventDestroy(m->moe_fork);
+  for (int i = 0; i < Model::kSplitK; ++i) {
+    if (m->sk_st[i]) cudaStreamDestroy(m->sk_st[i]);
+    if (m->sk_join[i]) cudaEventDestroy(m->sk_join[i]);
+  }
+  if (m->sk_fork) cudaEventDestroy(m->sk_fork);
   delete m;
   return M5_OK;
 }
@@ -887,6 +939,8 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   const size_t gxs = T >= kGemmMinTokens ? gemm_tc_xs_bytes((int)T, maxK) : 0;
   const bool moe_pre = c.num_experts > 0 && T >= kMoeGroupedMinTokens;  // prefill grouped by expert
   auto gxs_c = [](size_t K) { return (K / 64 + 31) / 32; };         // bias blocks of a GEMM input
+  const size_t sk_rows = std::min<size_t>(T, Model::kSplitKMaxRows);
+  const size_t sk_xs = (gemm_tc_xs_bytes((int)sk_rows, maxK) + 255) & ~size_t(255);  // per slice
   const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
                           size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,
                           part, argmax_scratch_bytes(), gemv_mma_scratch_bytes(mrows16),
@@ -901,7 +955,9 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
                           moe_pre ? T * k * H * 2 : 0,
                           moe_pre ? T * k * 64 * (gxs_c(H) + gxs_c(m->I)) * 2 : 0,
                           moe_pre ? T * k * 4 : 0,
-                          moe_pre ? size_t(2) * m->E_local * 4 : 0};
+                          moe_pre ? size_t(2) * m->E_local * 4 : 0,
+                          T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_rows * H * 4 : 0,
+                          T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_xs : 0};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -944,6 +1000,16 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->moe_xs = sizes[22] ? (bf16*)carve(p, sizes[22]) : nullptr;
   m->moe_pos = sizes[23] ? (int32_t*)carve(p, sizes[23]) : nullptr;
   m->moe_cnt = sizes[24] ? (int32_t*)carve(p, sizes[24]) : nullptr;
+  m->sk_f = sizes[25] ? (float*)carve(p, sizes[25]) : nullptr;
+  m->sk_xs = sizes[26] ? carve(p, sizes[26]) : nullptr;
+  m->sk_xs_stride = sizes[26] ? sk_xs : 0;
+  if (m->sk_f && !m->sk_fork) {
+    M5_CUDA(cudaEventCreateWithFlags(&m->sk_fork, cudaEventDisableTiming));
+    for (int i = 0; i < Model::kSplitK; ++i) {
+      M5_CUDA(cudaStreamCreateWithFlags(&m->sk_st[i], cudaStreamNonBlocking));
+      M5_CUDA(cudaEventCreateWithFlags(&m->sk_join[i], cudaEventDisableTiming));
+    }
+  }
   if (moe_pre && !m->h_moe_cnt) {
     M5_CUDA(cudaMallocHost(&m->h_moe_cnt, size_t(m->E_local) * sizeof(int32_t)));
     M5_CUDA(cudaEventCreateWithFlags(&m->moe_fork, cudaEventDisableTiming));
