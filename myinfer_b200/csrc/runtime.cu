@@ -102,7 +102,8 @@ struct Model {
 // Token count from which a projection runs as the tensor-core GEMM instead of
 // chunks of the streaming GEMV (the GEMV re-reads the weights every 8 tokens).
 constexpr int kGemmMinTokens = 16;
-// Projections take the tensor-core GEMM from this many rows on.  Its dequant
+// Projections take the tensor-core GEMM from this many rows on (split over K
+// when few output tiles would leave SMs idle).  Its dequant
 // work per weight does not shrink with the row count, but neither do GEMV
 // passes of 8 rows (2 rows for K = 25600) win below it: Qwen3-32B batch 16 at
 // 32K measured 224.9 tok/s with the GEMM and 216.7 with GEMV passes.
