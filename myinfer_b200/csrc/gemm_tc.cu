@@ -657,8 +657,8 @@ int gemm_tc_launch(const GemvArgs& a, int M, int epi, bf16* xs, size_t xs_bytes,
 }
 
 // y[m, n] = epi(sum over the S slices of part[s][m][n]), slices added in
-// order: EPI_RESIDUAL adds bf16(sum) into bf16 y (the GEMM's own residual
-// epilogue), EPI_F32 stores the fp32 sum.
+// order, with the GEMM's own epilogues: EPI_STORE y = bf16(sum), EPI_RESIDUAL
+// y += bf16(sum), EPI_F32 yf = sum.
 __global__ void gemm_splitk_reduce_kernel(const float* __restrict__ part, int S, int M, int N, int epi, bf16* y,
                                           float* yf, int64_t ldy) {
   const int64_t total = int64_t(M) * N;
@@ -669,6 +669,8 @@ __global__ void gemm_splitk_reduce_kernel(const float* __restrict__ part, int S,
     if (epi == EPI_RESIDUAL) {
       bf16* o = y + m * ldy + n;
       *o = f2bf(bf2f(*o) + rbf(v));
+    } else if (epi == EPI_STORE) {
+      y[m * ldy + n] = f2bf(v);
     } else {
       yf[m * ldy + n] = v;
     }
@@ -677,7 +679,7 @@ __global__ void gemm_splitk_reduce_kernel(const float* __restrict__ part, int S,
 
 int gemm_splitk_reduce_launch(const float* part, int S, int M, int N, int epi, bf16* y, float* yf, int64_t ldy,
                               cudaStream_t st) {
-  if (epi != EPI_RESIDUAL && epi != EPI_F32) return fail(M5_ERR_INVALID, "split-K reduce: epilogue");
+  if (epi != EPI_RESIDUAL && epi != EPI_F32 && epi != EPI_STORE) return fail(M5_ERR_INVALID, "split-K reduce: epilogue");
   const int64_t total = int64_t(M) * N;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
   gemm_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, S, M, N, epi, y, yf, ldy);

@@ -76,7 +76,8 @@ bool gemm_tc_eligible(const GemvArgs& a, int M, int epi);
 size_t gemm_tc_xs_bytes(int M, int K);
 int gemm_tc_launch(const GemvArgs& a, int M, int epi, bf16* xs, size_t xs_bytes, cudaStream_t stream);
 // Adds the fp32 partial products of S K slices (part [S][M][N], in slice order)
-// and applies EPI_RESIDUAL (y += bf16(sum)) or EPI_F32 (yf = sum).
+// and applies EPI_STORE (y = bf16(sum)), EPI_RESIDUAL (y += bf16(sum)) or
+// EPI_F32 (yf = sum).
 int gemm_splitk_reduce_launch(const float* part, int S, int M, int N, int epi, bf16* y, float* yf, int64_t ldy,
                               cudaStream_t stream);
 int gemm_tc_error(int reset);

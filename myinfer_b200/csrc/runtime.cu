@@ -92,7 +92,8 @@ struct Model {
   // slices' group-sum scratch and the side streams they run on
   static constexpr int kSplitK = 4;
   static constexpr int kSplitKMaxRows = 64;
-  float* sk_f = nullptr;     // [kSplitK][rows <= kSplitKMaxRows][N <= hidden]
+  float* sk_f = nullptr;     // [kSplitK][rows <= kSplitKMaxRows][N <= sk_n]
+  int sk_n = 0;              // widest projection the slice products hold
   char* sk_xs = nullptr;     // kSplitK regions of sk_xs_stride bytes
   size_t sk_xs_stride = 0;
   cudaStream_t sk_st[kSplitK] = {};
@@ -235,7 +236,8 @@ static void attach(const Model* m, GemvArgs& a) {
 // One projection of T tokens: the tensor-core GEMM for prefill-sized T (with
 // the fused RMSNorm materialised first), the streaming GEMV otherwise.
 // A projection of few rows with few output tiles (batched decode's o_proj and
-// down: N / 128 tiles on a 148-SM GPU) leaves most SMs idle as one GEMM.  Its
+// down: N / 128 = 40 tiles on a 148-SM GPU; MoE shapes' q|k|v and router)
+// leaves most SMs idle as one GEMM.  Its
 // K range is cut into slices of whole 8-group blocks that run as concurrent
 // GEMMs on side streams, each writing fp32 products, and one kernel adds the
 // slices in order and applies the epilogue.
@@ -243,7 +245,7 @@ static int gemm_splitk(const Model* m, const GemvArgs& a, int T, int epi, cudaSt
   const int N = a.seg[0].rows, G = a.K / 64;
   const int tiles = (N / 128) * ((T + 127) / 128);
   const int S = std::min({Model::kSplitK, sm_count() / std::max(1, tiles), G / 8});
-  if (S < 2 || N > m->cfg.hidden_size || a.ldk || a.K % 512)
+  if (S < 2 || N > m->sk_n || a.ldk || a.K % 512)
     return gemm_tc_launch(a, T, epi, m->gxs, m->gxs_bytes, st);
   M5_CUDA(cudaEventRecord(m->sk_fork, st));
   const int G8 = G / 8;
@@ -284,7 +286,7 @@ static int linear_auto(const Model* m, const GemvArgs& proto, int T, int epi, cu
         int rc = rms_norm_launch(proto.x, proto.norm_w, T, a.K, proto.eps, m->xn, st);
         if (rc) return rc;
       }
-      if (T <= Model::kSplitKMaxRows && m->sk_f && a.nseg == 1 && (epi == EPI_RESIDUAL || epi == EPI_F32))
+      if (T <= Model::kSplitKMaxRows && m->sk_f && a.nseg == 1 && epi != EPI_SWIGLU)
         return gemm_splitk(m, a, T, epi, st);
       return gemm_tc_launch(a, T, epi, m->gxs, m->gxs_bytes, st);
     }
@@ -941,6 +943,7 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   const bool moe_pre = c.num_experts > 0 && T >= kMoeGroupedMinTokens;  // prefill grouped by expert
   auto gxs_c = [](size_t K) { return (K / 64 + 31) / 32; };         // bias blocks of a GEMM input
   const size_t sk_rows = std::min<size_t>(T, Model::kSplitKMaxRows);
+  const size_t sk_n = std::max<size_t>({H, QKV, size_t(std::max(1, c.num_experts))});
   const size_t sk_xs = (gemm_tc_xs_bytes((int)sk_rows, maxK) + 255) & ~size_t(255);  // per slice
   const size_t sizes[] = {T * H * 2, T * QKV * 2, T * m->Hq * D * 2, T * m->Hq * D * 2, act * 2,
                           size_t(c.vocab_size) * 2, T * std::max(1, c.num_experts) * 2, T * k * 2, T * k * 4,
@@ -957,7 +960,7 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
                           moe_pre ? T * k * 64 * (gxs_c(H) + gxs_c(m->I)) * 2 : 0,
                           moe_pre ? T * k * 4 : 0,
                           moe_pre ? size_t(2) * m->E_local * 4 : 0,
-                          T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_rows * H * 4 : 0,
+                          T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_rows * sk_n * 4 : 0,
                           T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_xs : 0};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
@@ -1002,6 +1005,7 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->moe_pos = sizes[23] ? (int32_t*)carve(p, sizes[23]) : nullptr;
   m->moe_cnt = sizes[24] ? (int32_t*)carve(p, sizes[24]) : nullptr;
   m->sk_f = sizes[25] ? (float*)carve(p, sizes[25]) : nullptr;
+  m->sk_n = sizes[25] ? (int)sk_n : 0;
   m->sk_xs = sizes[26] ? carve(p, sizes[26]) : nullptr;
   m->sk_xs_stride = sizes[26] ? sk_xs : 0;
   if (m->sk_f && !m->sk_fork) {
