@@ -326,9 +326,79 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16* __restrict__ 
     yr[i] = f2bf(__fmul_rn(bf2f(w[i]), rbf(__fmul_rn(bf2f(xr[i]), inv))));
 }
 
+// The same with 16-byte loads and stores: each thread holds up to VPT chunks
+// of 8 values of its row in registers between the sum of squares and the
+// scaling, so the row is read once and every load is issued up front (the
+// strided scalar loop above waits on dim / 256 dependent loads per pass).
+template <int VPT>
+__global__ void __launch_bounds__(256) rms_norm_vec_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                           int dim, float eps, bf16* __restrict__ y) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int nv = dim >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + size_t(blockIdx.x) * dim);
+  uint4* yr = reinterpret_cast<uint4*>(y + size_t(blockIdx.x) * dim);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  __shared__ float red[33];
+  uint4 xv[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    const int i = threadIdx.x + 256 * q;
+    xv[q] = i < nv ? xr[i] : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    const uint32_t u[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = bf16_lo(u[j]), hi = bf16_hi(u[j]);
+      ss += lo * lo;
+      ss += hi * hi;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[32] = v;
+  }
+  __syncthreads();
+  const float inv = __frsqrt_rn(__fadd_rn(red[32] / float(dim), eps));
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    const int i = threadIdx.x + 256 * q;
+    if (i < nv) {
+      const uint4 wv = wr[i];
+      const uint32_t xu[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w}, wu[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a0 = __fmul_rn(bf16_lo(wu[j]), rbf(__fmul_rn(bf16_lo(xu[j]), inv)));
+        const float a1 = __fmul_rn(bf16_hi(wu[j]), rbf(__fmul_rn(bf16_hi(xu[j]), inv)));
+        o[j] = uint32_t(__bfloat16_as_ushort(f2bf(a0))) | (uint32_t(__bfloat16_as_ushort(f2bf(a1))) << 16);
+      }
+      yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 int rms_norm_launch(const bf16* x, const bf16* w, int64_t rows, int dim, float eps, bf16* y, cudaStream_t stream) {
   if (rows <= 0) return M5_OK;
-  M5_CUDA(launch_pdl(rms_norm_kernel, dim3((unsigned)rows), dim3(256), 0, stream, x, w, dim, eps, y));
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const int vpt = (dim / 8 + 255) / 256;
+  if (dim % 8 == 0 && al(x) && al(w) && al(y) && vpt >= 1 && vpt <= 4) {
+    switch (vpt) {
+      case 1: M5_CUDA(launch_pdl(rms_norm_vec_kernel<1>, dim3((unsigned)rows), dim3(256), 0, stream, x, w, dim, eps, y)); break;
+      case 2: M5_CUDA(launch_pdl(rms_norm_vec_kernel<2>, dim3((unsigned)rows), dim3(256), 0, stream, x, w, dim, eps, y)); break;
+      case 3: M5_CUDA(launch_pdl(rms_norm_vec_kernel<3>, dim3((unsigned)rows), dim3(256), 0, stream, x, w, dim, eps, y)); break;
+      default: M5_CUDA(launch_pdl(rms_norm_vec_kernel<4>, dim3((unsigned)rows), dim3(256), 0, stream, x, w, dim, eps, y)); break;
+    }
+  } else {
+    M5_CUDA(launch_pdl(rms_norm_kernel, dim3((unsigned)rows), dim3(256), 0, stream, x, w, dim, eps, y));
+  }
   M5_LAUNCH_CHECK("rms_norm launch");
   return M5_OK;
 }
