@@ -188,6 +188,15 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
         stats["decode_time"] = time.perf_counter() - t1
 
 
+def penalty_windows(prefix: torch.Tensor, fed: torch.Tensor) -> torch.Tensor:
+    """[L, W] int32 penalty windows for L logits rows that follow the tokens
+    ``fed`` [L]: row i holds the last W of ``prefix`` [W] (the window before
+    fed[0], -1 where empty) + fed[:i + 1]."""
+    W = prefix.numel()
+    seq = torch.cat([prefix.to(torch.int32), fed.to(torch.int32)])
+    return seq.unfold(0, W, 1)[1:1 + fed.numel()].contiguous()
+
+
 def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_tokens: int = 2,
                               max_tokens: int = 256, sampler: Optional[Callable] = None,
                               logits_processors: Optional[list] = None,
@@ -239,9 +248,7 @@ def speculative_generate_step(prompt: List[int], model, draft_model, num_draft_t
         """Penalty window of each row whose logits follow the tokens ``fed``."""
         if not dev_sampler or sampler.window == 0:
             return None
-        W = sampler.window
-        seq = torch.cat([sampler.history(ctx, dev)[0], fed.to(torch.int32)])
-        return seq.unfold(0, W, 1)[1:1 + fed.numel()].contiguous()
+        return penalty_windows(sampler.history(ctx, dev)[0], fed)
 
     def pick(logits, fed):  # logits [L, V] after the last L tokens of ``fed`` -> int32 [L] on the device
         if greedy:

@@ -127,3 +127,19 @@ def test_sample_argument_checks():
     p.flags = 0
     p.min_p = 2.0
     assert L.m5_sample_bf16(dummy, 1, 100, 100, None, 0, 0, p, None, dummy, None) == _lib.M5_ERR_INVALID
+
+
+def test_penalty_windows_of_verify_rows():
+    """The speculative loop's per-row windows: row i = last W of the context
+    before the pending token + the pending token and the first i proposals."""
+    from myinfer_b200.generate import penalty_windows
+    W = 5
+    for ctx in ([], [7], [1, 2, 3, 4, 5, 6, 7, 8]):
+        s = DeviceSampler(0.0, processors=[LogitsPenalty("repetition", 1.2, W)])
+        prefix = s.history(ctx, "cpu")[0]
+        fed = torch.tensor([40, 41, 42, 43], dtype=torch.int32)
+        rows = penalty_windows(prefix, fed)
+        assert rows.shape == (4, W) and rows.dtype == torch.int32 and rows.is_contiguous()
+        for i in range(4):
+            full = [-1] * W + list(ctx) + fed[:i + 1].tolist()
+            assert rows[i].tolist() == full[-W:], (ctx, i)
