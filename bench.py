@@ -138,65 +138,71 @@ def measured_peaks() -> dict:
 
 
 # ----------------------------------------------------------------- CPU legs
-def cpu_decode_sample(cfg: dict, ctx: int, layers: int = 1, threads: int = 0, kv_bits: int = 8) -> dict:
-    """Time the CPU oracle's decode step on `layers` decoder layers (+ a vocab
-    slice of the lm_head) and scale to one full token.  Returns tok/s."""
+def cpu_decode_sample(cfg: dict, ctx: int, kv_bits: int = 8, threads: int = 0, budget_s: float = 20.0) -> dict:
+    """The CPU oracle's decode step at the stated context, on a bounded sample.
+
+    Times whole decoder layers of the config (attention over `ctx` cached
+    positions in the packed KV layout, the MLP or the routed experts) with the
+    oracle's real per-call work: every call dequantizes the packed weights it
+    multiplies by (as a quantized matmul does) and the KV it attends over, then
+    multiplies in fp32.  Packed codes, scales and biases are random (their
+    values do not change the work).  Layers repeat until `budget_s` is spent
+    (at least one); the lm_head (vocab x hidden, dequantized per call) is
+    timed on a slice of its rows.  One token = layers x the mean layer time +
+    the full lm_head."""
     import numpy as np
     import torch
 
     from oracle import model as om
-    from oracle.quant import affine_quantize
 
     if threads:
         torch.set_num_threads(threads)
-    c = om.Config.from_dict(dict(cfg, num_hidden_layers=layers))
-    # The oracle multiplies by dequantized fp32 weights; for timing, those are
-    # drawn directly (their values do not change the work), norms are ones.
-    m = om.Model(c, {})
-    g = torch.Generator().manual_seed(7)
+    c = om.Config.from_dict(dict(cfg, num_hidden_layers=1, vocab_size=16384))
+    rng = np.random.default_rng(1)
+    w = {}
     for name, shape, kind in om.weight_specs(c):
         if kind == "norm":
-            m.w[name + ".weight"] = np.full(shape, 0x3F80, dtype=np.uint16)
-        elif name.startswith("model.layers."):
-            m._deq[name] = 0.02 * torch.randn(shape, generator=g)
-    rng = np.random.default_rng(1)
-    cache = []
-    for _ in range(layers):
-        qc = om.QuantizedKVCache(64, kv_bits)
-        k = rng.standard_normal((c.num_key_value_heads, ctx, c.head_dim)).astype(np.float32)
-        v = rng.standard_normal((c.num_key_value_heads, ctx, c.head_dim)).astype(np.float32)
-        qc.k_parts.append(affine_quantize(k, 64, kv_bits))
-        qc.v_parts.append(affine_quantize(v, 64, kv_bits))
-        qc.offset = ctx
-        cache.append(qc)
-    x = om.rb(torch.randn(1, cfg["hidden_size"], generator=g))
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
-        h = x
-        for i in range(layers):
-            p = f"model.layers.{i}."
-            r = m.attention(i, om.rms_norm(h, m.norm_w(p + "input_layernorm"), c.rms_norm_eps), cache[i])
-            h = om.rb(h + r)
-            r = m.mlp(i, om.rms_norm(h, m.norm_w(p + "post_attention_layernorm"), c.rms_norm_eps))
-            h = om.rb(h + r)
-            qc = cache[i]  # drop the appended position so every repetition sees ctx keys
-            qc.k_parts, qc.v_parts, qc.offset = qc.k_parts[:1], qc.v_parts[:1], ctx
-        reps += 1
-        if time.perf_counter() - t0 > 5.0 or reps >= 3:
-            break
-    layer_s = (time.perf_counter() - t0) / reps / layers
-    # lm_head: a 16384-row slice of the vocab, scaled
+            w[name + ".weight"] = np.full(shape, 0x3F80, dtype=np.uint16)
+            continue
+        K = shape[-1]
+        w[name + ".weight"] = rng.integers(0, 2 ** 32, shape[:-1] + (K // 8,), dtype=np.uint32)
+        for suf in (".scales", ".biases"):
+            w[name + suf] = om.f32_to_bf16_bits((0.01 * rng.standard_normal(shape[:-1] + (K // 64,))).astype(np.float32))
+    m = om.Model(c, w)
+    words = c.head_dim * kv_bits // 32
+
+    def kv_part():
+        return (rng.integers(0, 2 ** 32, (c.num_key_value_heads, ctx, words), dtype=np.uint32),
+                om.f32_to_bf16_bits((0.05 * rng.standard_normal((c.num_key_value_heads, ctx, 2))).astype(np.float32)),
+                om.f32_to_bf16_bits((0.05 * rng.standard_normal((c.num_key_value_heads, ctx, 2))).astype(np.float32)))
+    qc = om.QuantizedKVCache(64, kv_bits)
+    qc.k_parts.append(kv_part())
+    qc.v_parts.append(kv_part())
+    qc.offset = ctx
+    x = om.rb(torch.randn(1, cfg["hidden_size"]))
+    p = "model.layers.0."
+    times = []
+    t_start = time.perf_counter()
+    while not times or (time.perf_counter() - t_start < budget_s and len(times) < cfg["num_hidden_layers"]):
+        m._deq.clear()  # a quantized matmul dequantizes on every call
+        t0 = time.perf_counter()
+        r = m.attention(0, om.rms_norm(x, m.norm_w(p + "input_layernorm"), c.rms_norm_eps), qc)
+        h = om.rb(x + r)
+        r = m.mlp(0, om.rms_norm(h, m.norm_w(p + "post_attention_layernorm"), c.rms_norm_eps))
+        h = om.rb(h + r)
+        times.append(time.perf_counter() - t0)
+        qc.k_parts, qc.v_parts, qc.offset = qc.k_parts[:1], qc.v_parts[:1], ctx  # every layer sees ctx keys
+    layer_s = sum(times) / len(times)
     rows = 16384
-    head = torch.randn(rows, cfg["hidden_size"])
+    m._deq.clear()
     t1 = time.perf_counter()
-    _ = om.rb(h @ head.T)
+    _ = m.lm_head(m.final_hidden(h))
     head_s = (time.perf_counter() - t1) * cfg["vocab_size"] / rows
     tok_s = cfg["num_hidden_layers"] * layer_s + head_s
-    return {"value": 1.0 / tok_s, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{layers} of {cfg['num_hidden_layers']} decoder layers at ctx {ctx} ({kv_bits}-bit KV) + "
-                      f"{rows}/{cfg['vocab_size']} lm_head rows, scaled to one token; oracle weights "
-                      f"pre-dequantized to fp32"}
+    return {"value": round(1.0 / tok_s, 6), "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(times)} decoder-layer call(s) of the {cfg['num_hidden_layers']}-layer model at context "
+                      f"{ctx} ({kv_bits}-bit KV), weights and KV dequantized on every call, timed and scaled by the "
+                      f"layer count; lm_head timed on {rows} of {cfg['vocab_size']} rows and scaled to all rows"}
 
 
 # ----------------------------------------------------------------- GPU leg
@@ -215,7 +221,7 @@ def gemv_roofline(model, cfg, peak_gbs, peak_src="measured", proj="mlp.up_proj")
         for n in names[:4]:
             ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"])
     torch.cuda.synchronize()
-    # all layers' up_proj back to back (distinct weights, no L2 reuse),
+    # all layers' projections back to back (distinct weights, no L2 reuse),
     # captured in one CUDA graph so host launch overhead is not timed
     s = torch.cuda.Stream(device=model.device)
     s.wait_stream(torch.cuda.current_stream())
@@ -225,7 +231,7 @@ def gemv_roofline(model, cfg, peak_gbs, peak_src="measured", proj="mlp.up_proj")
     with torch.cuda.stream(s):
         graph.capture_begin()
         for n, o in zip(names, outs):
-            o.copy_(ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"]))
+            ops.quantized_matmul(x, w[n + ".weight"], w[n + ".scales"], w[n + ".biases"], out=o)
         graph.capture_end()
     torch.cuda.current_stream().wait_stream(s)
     graph.replay()
@@ -239,19 +245,16 @@ def gemv_roofline(model, cfg, peak_gbs, peak_src="measured", proj="mlp.up_proj")
     K = H
     alg = N * K * 0.5625 + K * 2 + N * 2
     ach = alg / (ms * 1e-3) / 1e9
-    # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel and
-    # shape, from the ncu capture summarised in profiles/gemv_tmap_up_proj_25600x5120.md
-    traffic = (73_846_528 + 1_500_928) * N // 25600 if proj == "mlp.up_proj" and N == cfg["intermediate_size"] \
-        else None
+    # `traffic` (DRAM bytes per launch) comes from an ncu capture, which this
+    # run does not make: null here, the captured figure is in the profiles
     return {"bound": "hbm", "kernel": f"gemv_tmap_kernel<1,EPI_STORE> ({proj.split('.')[-1]} {N}x{K} w4g64, 1 token)",
             "achieved": round(ach, 1), "peak": peak_gbs, "peak_source": peak_src,
-            "unit": "GB/s", "frac": round(ach / peak_gbs, 4), "traffic": traffic,
+            "unit": "GB/s", "frac": round(ach / peak_gbs, 4), "traffic": None,
             "alg_bytes_per_launch": int(alg), "avg_launch_us": round(ms * 1e3, 2)}
 
 
 def prefill(model, cache, ids, chunk: int):
     """Chunked prefill of `ids` (device int32) into `cache`, like generate_step's prompt loop."""
-    import torch
     for pos in range(0, ids.numel(), chunk):
         model.forward(ids[pos:pos + chunk], cache)
     return cache
@@ -291,131 +294,242 @@ class BatchDecodeGraph:
             c.offset += 1
 
 
-def run_gpu(args) -> dict:
-    import datetime
+class Ctx:
+    """Rank, device and communicator of this process (torchrun env)."""
 
-    import torch
+    def __init__(self):
+        import datetime
 
-    from myinfer_b200 import _lib
-    from myinfer_b200.cache import QuantizedKVCache, PromptCache
-    from myinfer_b200.generate import DecodeGraph
-    from myinfer_b200.model import Model, ModelArgs, random_weights
+        import torch
+        self.rank = int(os.environ.get("RANK", 0))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.comm = None
+        if self.world > 1:
+            import torch.distributed as dist
 
-    rank = int(os.environ.get("RANK", 0))
-    local = int(os.environ.get("LOCAL_RANK", 0))
-    world = int(os.environ.get("WORLD_SIZE", 1))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    comm = None
-    if world > 1:
-        import torch.distributed as dist
+            from myinfer_b200.distributed import Communicator
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
+            self.comm = Communicator(self.world, self.rank)
 
-        from myinfer_b200.distributed import Communicator
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-        comm = Communicator(world, rank)
-    cfg = CONFIGS[args.config]
-    a = ModelArgs.from_dict(cfg)
-    t0 = time.perf_counter()
-    w = random_weights(a, seed=args.seed, device=dev)
-    par = {}
-    if world > 1:
-        from myinfer_b200.distributed import shard_weights
-        par = dict(ep_size=world, ep_rank=rank) if a.num_experts else dict(tp_size=world, tp_rank=rank)
-        w = shard_weights(w, a, **par)
-        torch.cuda.empty_cache()
-    model = Model(a, w, dev, max_tokens=args.chunk, comm=comm, **par)
-    torch.cuda.synchronize()
-    load_s = time.perf_counter() - t0
-
-    def barrier():
-        if world > 1:
+    def barrier(self):
+        import torch
+        if self.world > 1:
             torch.distributed.barrier()
 
-    def max_over_ranks(ms: float) -> float:
-        if world == 1:
-            return ms
-        t = torch.tensor([ms], device=dev)
+    def max_over_ranks(self, v: float) -> float:
+        import torch
+        if self.world == 1:
+            return v
+        t = torch.tensor([v], device=self.dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t)
 
-    B = args.batch
 
-    def new_cache(cap, batch=1):
-        return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, dev, 64, args.kv_bits, capacity=cap,
-                                             batch=batch) for _ in range(a.num_hidden_layers)], dev)
+def build_model(cx: Ctx, cfg: dict, seed: int, chunk: int, sharded: bool = True):
+    """This rank's shard of the seeded random model (dense: tensor parallel,
+    MoE: expert parallel over all ranks), or the whole model on this GPU."""
+    import torch
 
-    ctx = args.ctx
-    g = torch.Generator(device=dev).manual_seed(args.seed + 7)
-    ids = torch.randint(0, a.vocab_size, (ctx,), generator=g, device=dev, dtype=torch.int32)
-    # ---- prefill: warm the prefill kernels on a short scratch run, then the timed prompt
-    prefill(model, new_cache(args.chunk), ids[:args.chunk], args.chunk)
-    total = ctx + args.warmup + args.steps * 2 + 8
-    cache = new_cache(total, B)
+    from myinfer_b200.model import Model, ModelArgs, random_weights
+    a = ModelArgs.from_dict(cfg)
+    world = cx.world if sharded else 1
+    par = {}
+    if world > 1 and a.num_experts:
+        El = a.num_experts // world
+        w = random_weights(a, seed=seed, device=cx.dev, experts=(cx.rank * El, El))  # this rank's experts only
+        par = dict(ep_size=world, ep_rank=cx.rank)
+    else:
+        w = random_weights(a, seed=seed, device=cx.dev)
+        if world > 1:
+            from myinfer_b200.distributed import shard_weights
+            par = dict(tp_size=world, tp_rank=cx.rank)
+            w = shard_weights(w, a, **par)
+            torch.cuda.empty_cache()
+    model = Model(a, w, cx.dev, max_tokens=chunk, comm=cx.comm if world > 1 else None, **par)
     torch.cuda.synchronize()
-    barrier()
+    return model
+
+
+def new_cache(model, cap: int, kv_bits: int, batch: int = 1):
+    from myinfer_b200.cache import PromptCache, QuantizedKVCache
+    a = model.args
+    return PromptCache([QuantizedKVCache(model.n_kv_heads_local, a.head_dim, model.device, 64, kv_bits, capacity=cap,
+                                         batch=batch) for _ in range(a.num_hidden_layers)], model.device)
+
+
+def greedy_tokens(model, ids, n: int, kv_bits: int, chunk: int):
+    """Eager greedy decode: prefill ids[:-1], then n tokens (host list)."""
+    import torch
+
+    from myinfer_b200 import _lib
+    cache = new_cache(model, ids.numel() + n + 8, kv_bits)
+    prefill(model, cache, ids[:-1], chunk)
+    tok = ids[-1:].clone()
+    out, margins = [], []
+    lg = torch.empty(model.args.vocab_size, dtype=torch.bfloat16, device=model.device)
+    for _ in range(n):
+        model.forward(tok, cache, _lib.M5_LOGITS_LAST, lg, tok)
+        top = lg.float().topk(2).values
+        margins.append(float(top[0] - top[1]))
+        out.append(int(tok.item()))
+    return out, margins
+
+
+def n1_token_check(cx: Ctx, model, cfg: dict, seed: int, kv_bits: int, chunk: int, n: int = 16) -> dict:
+    """Greedy tokens of the N-GPU model against the same seeded model on one GPU
+    (rank 0), at a 64-token prompt.  Tokens may part only where the 1-GPU run's
+    top-2 logits are within 0.02 (the ranks add their fp32 partial sums in
+    another order than one GPU)."""
+    import torch
+    g = torch.Generator(device=cx.dev).manual_seed(seed + 11)
+    ids = torch.randint(0, cfg["vocab_size"], (64,), generator=g, device=cx.dev, dtype=torch.int32)
+    got, _ = greedy_tokens(model, ids, n, kv_bits, chunk)  # every rank takes the same collective steps
+    res = None
+    if cx.rank == 0:
+        full = build_model(cx, cfg, seed, chunk, sharded=False)
+        ref, margins = greedy_tokens(full, ids, n, kv_bits, chunk)
+        del full
+        torch.cuda.empty_cache()
+        k = next((i for i, (x, y) in enumerate(zip(got, ref)) if x != y), n)
+        res = {"tokens": n, "equal_prefix": k, "match": k == n,
+               "first_diff_margin": None if k == n else round(margins[k], 4),
+               "pass": k == n or margins[k] < 0.02}
+    cx.barrier()
+    return res
+
+
+def decode_bench(cx: Ctx, model, cfg: dict, ctx: int, kv_bits: int, batch: int, steps: int, warmup: int,
+                 chunk: int, seed: int, clocks: bool = False, e2e: bool = False) -> dict:
+    """Timed prefill of a `ctx`-token prompt, then `steps` graph-replayed
+    decode steps after `warmup` untimed ones (device time, max over ranks)."""
+    import torch
+
+    from myinfer_b200 import _lib
+    from myinfer_b200.generate import DecodeGraph
+    B = batch
+    g = torch.Generator(device=cx.dev).manual_seed(seed + 7)
+    ids = torch.randint(0, cfg["vocab_size"], (ctx,), generator=g, device=cx.dev, dtype=torch.int32)
+    prefill(model, new_cache(model, chunk, kv_bits), ids[:chunk], chunk)  # warm the prefill kernels
+    cache = new_cache(model, ctx + warmup + steps * 2 + 8, kv_bits, B)
+    torch.cuda.synchronize()
+    cx.barrier()
     ps, pe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ps.record()
     if B == 1:
-        prefill(model, cache, ids, args.chunk)
+        prefill(model, cache, ids, chunk)
     else:  # the timed prompt fills sequence 0; the other sequences get copies of its KV
-        model.prefill_sequence(ids, cache, 0, args.chunk)
+        model.prefill_sequence(ids, cache, 0, chunk)
     pe.record()
     torch.cuda.synchronize()
-    prefill_ms = max_over_ranks(ps.elapsed_time(pe))
+    prefill_ms = cx.max_over_ranks(ps.elapsed_time(pe))
     if B > 1:
         for c in cache:
             for t in c._tensors():
                 t[1:].copy_(t[:1].expand_as(t[1:]))
             c.offset = ctx
-
-    # ---- decode on the prefilled cache: one eager step, then the captured graph
     if B == 1:
-        tok = torch.tensor([1], dtype=torch.int32, device=dev)
+        tok = torch.tensor([1], dtype=torch.int32, device=cx.dev)
         model.forward(tok, cache, _lib.M5_LOGITS_NONE, None, tok)
         graph = DecodeGraph(model, cache, with_logits=False)
         graph.tok.copy_(tok)
     else:
         graph = BatchDecodeGraph(model, cache)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         graph.step()
     torch.cuda.synchronize()
-    barrier()
+    cx.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        start.record()
-        for _ in range(args.steps):
-            graph.step()
-        end.record()
+    clk = ClockSampler(cx.local) if clocks else None
+    if clk:
+        clk.__enter__()
+    start.record()
+    for _ in range(steps):
+        graph.step()
+    end.record()
+    torch.cuda.synchronize()
+    if clk:
+        clk.__exit__()
+    ms_step = cx.max_over_ranks(start.elapsed_time(end)) / steps
+    out = {"ms_step": ms_step, "prefill_ms": prefill_ms, "mean_ctx": ctx + 1 + warmup + steps / 2,
+           "clocks": clk.summary() if clk else None}
+    if e2e:  # the public decode step with pinned host tokens in and out, every step
+        host = torch.ones(B, dtype=torch.int32, pin_memory=True)
         torch.cuda.synchronize()
-    ms_step = max_over_ranks(start.elapsed_time(end)) / args.steps
-    mean_ctx = ctx + args.warmup + args.steps / 2
+        cx.barrier()
+        e_steps = max(4, steps // 2)
+        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        es.record()
+        for _ in range(e_steps):
+            graph.tok.copy_(host, non_blocking=True)
+            graph.step()
+            host.copy_(graph.tok, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        ee.record()
+        torch.cuda.synchronize()
+        out["e2e_ms"] = cx.max_over_ranks(es.elapsed_time(ee)) / e_steps
+    del graph, cache
+    torch.cuda.empty_cache()
+    return out
+
+
+def moe_block(cx: Ctx, name: str, args, steps: int) -> dict:
+    """Batch-1 decode of a MoE config at its BASELINE prompt and KV bits,
+    expert parallel over all ranks (attention, router and lm_head replicated;
+    each rank streams its own routed experts)."""
+    import torch
+    cfg = CONFIGS[name]
+    ctx, kv_bits = DEFAULTS[name]
+    t0 = time.perf_counter()
+    model = build_model(cx, cfg, args.seed, args.chunk)
+    load_s = time.perf_counter() - t0
+    r = decode_bench(cx, model, cfg, ctx, kv_bits, 1, steps, 3, args.chunk, args.seed)
+    check = n1_token_check(cx, model, cfg, args.seed, kv_bits, args.chunk) \
+        if cx.world > 1 and name != "qwen3-235b-a22b" else None
+    del model
+    torch.cuda.empty_cache()
+    # per-rank bytes of one token: the replicated part (attention, router,
+    # embedding row, lm_head, KV) plus this rank's share of the k routed experts
+    H, E, k, I = cfg["hidden_size"], cfg["num_experts"], cfg["num_experts_per_tok"], cfg["moe_intermediate_size"]
+    expert_bytes = cfg["num_hidden_layers"] * k * 3 * I * H * 0.5625
+    replicated = weight_bytes_per_token(cfg) - expert_bytes + kv_bytes_per_token(cfg, int(r["mean_ctx"]), kv_bits)
+    per_rank = replicated + expert_bytes / cx.world
+    peaks = measured_peaks()
+    return {"model": name, "parallelism": f"ep{cx.world}" if cx.world > 1 else "single", "prompt_tokens": ctx,
+            "kv_bits": kv_bits, "value": round(1000.0 / r["ms_step"], 2), "unit": "tok/s",
+            "ms_per_step": round(r["ms_step"], 4), "steps": steps,
+            "prefill_tok_s": round(ctx / (r["prefill_ms"] * 1e-3), 1),
+            "bytes_per_token_per_rank": int(per_rank),
+            "hbm_frac_of_measured": round(per_rank / (r["ms_step"] * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+            "tokens_match_n1": check, "load_seconds": round(load_s, 1)}
+
+
+def run_gpu(args) -> dict:
+    import torch
+    cx = Ctx()
+    cfg = CONFIGS[args.config]
+    t0 = time.perf_counter()
+    model = build_model(cx, cfg, args.seed, args.chunk)
+    load_s = time.perf_counter() - t0
+    a = model.args
+    B, ctx, world = args.batch, args.ctx, cx.world
+    r = decode_bench(cx, model, cfg, ctx, args.kv_bits, B, args.steps, args.warmup, args.chunk, args.seed,
+                     clocks=True, e2e=True)
+    ms_step = r["ms_step"]
     # bytes one step streams: the weights once, the KV of every sequence
-    bytes_step = weight_bytes_per_token(cfg) + B * kv_bytes_per_token(cfg, int(mean_ctx), args.kv_bits)
-    bytes_tok = bytes_step / B
+    bytes_step = weight_bytes_per_token(cfg) + B * kv_bytes_per_token(cfg, int(r["mean_ctx"]), args.kv_bits)
     peaks = measured_peaks()
     tok_s = B * 1000.0 / ms_step  # every rank works on the same B tokens
-
-    # e2e through the public decode step: pinned host tokens in, tokens out, every step
-    host = torch.ones(B, dtype=torch.int32, pin_memory=True)
-    torch.cuda.synchronize()
-    barrier()
-    e_steps = max(4, args.steps // 2)
-    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    es.record()
-    for _ in range(e_steps):
-        graph.tok.copy_(host, non_blocking=True)
-        graph.step()
-        host.copy_(graph.tok, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-    ee.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e_steps
     roof = gemv_roofline(model, cfg, peaks["hbm_gbs"], peaks["source"],
                          "mlp.up_proj" if not a.num_experts else "self_attn.q_proj")
+    check = n1_token_check(cx, model, cfg, args.seed, args.kv_bits, args.chunk) if world > 1 else None
     per_rank = bytes_step / world
     par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}" if world > 1 else "single")
     prefill_flops = 2.0 * ctx * (weight_bytes_per_token(cfg) / 0.5625) + 4.0 * a.num_hidden_layers * \
         a.num_attention_heads * a.head_dim * ctx * ctx / 2
+    prefill_ms = r["prefill_ms"]
     out = {
         "metric": f"batch-{B} decode tok/s ({NAMES[args.config]}-shaped, w4g64, {args.kv_bits}-bit KV) + HBM TB/s "
                   "vs peak; prefill tok/s",
@@ -425,10 +539,10 @@ def run_gpu(args) -> dict:
         "data": "synthetic (seeded random weights and prompt ids)",
         "config": {"workload": f"{args.config} batch-{B} decode after a {ctx}-token prefill"
                                + (" (one prompt prefilled, its KV copied to every sequence)" if B > 1 else ""),
-                   "model": args.config, "global_batch": B, "seq_len": ctx, "parallelism": par_name, "prefill_chunk": args.chunk,
-                   "kv_bits": args.kv_bits,
+                   "model": args.config, "global_batch": B, "seq_len": ctx, "parallelism": par_name,
+                   "prefill_chunk": args.chunk, "kv_bits": args.kv_bits,
                    "l2": f"inputs larger than L2 ({bytes_step / 1e9:.1f} GB streamed per decode step)"},
-        "hbm": {"bytes_per_step": bytes_step, "bytes_per_token": round(bytes_tok),
+        "hbm": {"bytes_per_step": bytes_step, "bytes_per_token": round(bytes_step / B),
                 "achieved_gbs": round(bytes_step / (ms_step * 1e-3) / 1e9, 1),
                 "achieved_gbs_per_gpu": round(per_rank / (ms_step * 1e-3) / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
                 "frac_of_measured": round(per_rank / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
@@ -437,10 +551,11 @@ def run_gpu(args) -> dict:
                     "ms": round(prefill_ms, 1), "flops": prefill_flops,
                     "tflops": round(prefill_flops / (prefill_ms * 1e-3) / 1e12, 1)},
         "roofline": roof,
-        "e2e": {"value": round(B * 1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+        "e2e": {"value": round(B * 1000.0 / r["e2e_ms"], 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B},
         "gpu_launches": None,
-        "clocks": clk.summary(),
+        "clocks": r["clocks"],
+        "tokens_match_n1": check,
         "load_seconds": round(load_s, 1),
     }
     # kernels per decode step: per layer qkv, rope/append, attention (+ combine), o, gate/up, down
@@ -448,16 +563,19 @@ def run_gpu(args) -> dict:
     # MoE: q|k|v, rope/append, attention, combine, o, router, top-k, expert gate/up, expert down
     per_layer = (9 + (1 if world > 1 else 0)) if a.num_experts else (7 + (2 if world > 1 else 0))
     out["gpu_launches"] = args.steps * (a.num_hidden_layers * per_layer + 4)
-    if rank == 0 and not args.no_cpu:
-        out["cpu_baseline"] = cpu_decode_sample(cfg, min(ctx, 4096), layers=1, threads=os.cpu_count() or 1,
-                                                kv_bits=args.kv_bits)
-    del graph
+    del model
+    torch.cuda.empty_cache()
+    if not args.no_moe and args.config == "qwen3-32b" and B == 1:
+        out["moe"] = [moe_block(cx, "qwen3-30b-a3b", args, min(args.steps, 32))]
+        if world >= 4:  # 132 GB of weights: 33 GB per rank at EP4
+            out["moe"].append(moe_block(cx, "qwen3-235b-a22b", args, min(args.steps, 16)))
+    if cx.rank == 0 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_decode_sample(cfg, ctx, args.kv_bits, threads=os.cpu_count() or 1, budget_s=15.0)
     if world > 1:
-        torch.distributed.barrier()
-        del model
-        comm.close()
+        cx.barrier()
+        cx.comm.close()
         torch.distributed.destroy_process_group()
-    return out if rank == 0 else None
+    return out if cx.rank == 0 else None
 
 
 def run_reference(args) -> dict:
@@ -467,23 +585,23 @@ def run_reference(args) -> dict:
     cfg = CONFIGS[args.config]
     vals = []
     base = None
-    for _ in range(max(1, args.steps // 8) if args.steps else 1):
-        base = cpu_decode_sample(cfg, min(args.ctx, 4096), layers=1, threads=os.cpu_count() or 1,
-                                 kv_bits=args.kv_bits)
+    for _ in range(max(1, args.steps // 10) if args.steps else 1):
+        base = cpu_decode_sample(cfg, args.ctx, args.kv_bits, threads=os.cpu_count() or 1, budget_s=10.0)
         vals.append(base["value"])
     v = statistics.mean(vals)
     return {"impl": "reference",
             "metric": f"batch-1 decode tok/s ({NAMES[args.config]}-shaped, w4g64, {args.kv_bits}-bit KV) + HBM TB/s "
                       "vs peak; prefill tok/s",
-            "value": round(v, 5), "unit": "tok/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
+            "value": round(v, 6), "unit": "tok/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / v, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (CPU oracle)",
             "data": "synthetic (seeded random weights and KV)",
-            "config": {"workload": f"{args.config} decode, batch 1, context {args.ctx}", "model": args.config},
-            "cpu_baseline": dict(base, value=round(v, 5)),
-            "e2e": {"value": round(v, 5), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "config": {"workload": f"{args.config} batch-1 decode after a {args.ctx}-token prefill",
+                       "model": args.config, "global_batch": 1, "seq_len": args.ctx, "kv_bits": args.kv_bits},
+            "cpu_baseline": dict(base, value=round(v, 6)),
+            "e2e": {"value": round(v, 6), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "MLX/mlx-lm (the reference's own CPU path) is not installable here; the CPU restatement "
-                    "in oracle/ stands in for it"}
+                    "in oracle/ stands in for it, sampled at the stated context (see cpu_baseline.sample)"}
 
 
 def main():
@@ -499,6 +617,7 @@ def main():
     ap.add_argument("--chunk", type=int, default=2048, help="prefill chunk (prefill_step_size)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-moe", action="store_true", help="skip the expert-parallel MoE block")
     args = ap.parse_args()
     if args.ctx is None:
         args.ctx = DEFAULTS[args.config][0]

@@ -92,14 +92,15 @@ M5_API int m5_quantized_matmul(const void* x, int64_t M, int64_t K, const uint32
                         int bits, void* y, void* stream);
 
 /* Same result as m5_quantized_matmul, for callers that cannot allocate device
- * memory (graph capture in progress, a host that owns the whole device pool).
- * It never calls cudaMalloc/cudaFree: its scratch is an 8 MiB array built into
- * the library (held by every GPU that loads it) whose address is looked up on
- * the first call on each device, so that first call must come before any
- * stream capture.  Limit: N <= 262144 weight rows (M and K as for
- * m5_quantized_matmul).  All calls share the array; calls that overlap on the
- * GPU race and must not be issued.  This entry point has no counterpart in
- * the reference. */
+ * memory (a serving host whose own allocator owns the whole device pool, an
+ * embedder that forbids allocation after start-up).  It never calls
+ * cudaMalloc/cudaFree: its scratch is an 8 MiB array built into the library
+ * (held by every GPU that loads it) whose address is looked up on the first
+ * call on each device, so that first call should come before any stream
+ * capture.  Limit: N <= 262144 weight rows (M and K as for
+ * m5_quantized_matmul).  All calls share the array, which keeps the last
+ * call's contents; calls that overlap on the GPU race and must not be issued.
+ * This entry point has no counterpart in the reference. */
 M5_API int m5_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K, const uint32_t* wq,
                                        const void* scales, const void* biases, int64_t N,
                                        int group_size, int bits, void* y, void* stream);

@@ -574,11 +574,8 @@ bool attn_mma_eligible(const AttnArgs& a) {
 template <int BITS, int NB>
 static int am_launch_t(const AttnArgs& a, cudaStream_t stream) {
   const size_t smem = am_smem(BITS, NB);
-  static bool conf = false;
-  if (!conf) {
-    M5_CUDA(cudaFuncSetAttribute(attn_mma_kernel<BITS, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    conf = true;
-  }
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(attn_mma_kernel<BITS, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
   dim3 grid(a.nsplit, (a.L + a.QB - 1) / a.QB, a.B * a.Hkv);
   M5_CUDA(launch_pdl(attn_mma_kernel<BITS, NB>, dim3(grid), dim3(AM_THREADS), smem, stream, a));
   return M5_OK;

@@ -460,19 +460,15 @@ void attn_pf_plan(const AttnArgs& a, int S_max, int max_split, int& QB, int& nsp
 
 int attn_pf_launch(const AttnArgs& a, cudaStream_t stream) {
   const size_t smem = apf_smem(a.bits);
-  static bool conf8 = false, conf4 = false;
+  static DeviceOnce once8, once4;  // the attribute belongs to each device's context
   dim3 grid(a.nsplit, (a.L + a.QB - 1) / a.QB, a.B * a.Hkv);
   if (a.bits == 8) {
-    if (!conf8) {
-      M5_CUDA(cudaFuncSetAttribute(apf::attn_pf_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      conf8 = true;
-    }
+    M5_CUDA(once8.run(
+        [&] { return cudaFuncSetAttribute(apf::attn_pf_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
     apf::attn_pf_kernel<8><<<grid, apf::THREADS, smem, stream>>>(a);
   } else {
-    if (!conf4) {
-      M5_CUDA(cudaFuncSetAttribute(apf::attn_pf_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      conf4 = true;
-    }
+    M5_CUDA(once4.run(
+        [&] { return cudaFuncSetAttribute(apf::attn_pf_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
     apf::attn_pf_kernel<4><<<grid, apf::THREADS, smem, stream>>>(a);
   }
   M5_LAUNCH_CHECK("prefill attention launch");

@@ -6,7 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdlib>
+#include <mutex>
 #include <string>
 #include <utility>
 
@@ -98,6 +100,31 @@ __device__ __forceinline__ float byte32768(uint32_t w) {
 }
 
 inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+// Runs a per-device set-up step (cudaFuncSetAttribute and the like, whose
+// effect belongs to the current device's context) once for each device, from
+// any number of host threads.  One instance per call site:
+//   static DeviceOnce once;
+//   M5_CUDA(once.run([&] { return cudaFuncSetAttribute(...); }));
+// A failed step is not recorded, so the next call retries it.
+struct DeviceOnce {
+  std::atomic<unsigned long long> done{0};
+  std::mutex mu;
+  template <class Fn>
+  cudaError_t run(Fn&& fn) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return fn();  // beyond the mask: set every time
+    const unsigned long long bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+    e = fn();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+    return e;
+  }
+};
 
 int sm_count();  // SMs of the current device (cached)
 

@@ -585,12 +585,9 @@ bool gemm_tc_eligible(const GemvArgs& a, int M, int epi) {
 
 template <int EPI>
 static int gtc_launch_t(const gtc::Params& p, const gtc::Maps& m, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(gtc::gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)gtc::SMEM));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gtc::gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)gtc::SMEM); }));
   const int tiles = p.n_tiles * p.m_tiles;
   const int grid = std::max(1, std::min(tiles, sm_count()));
   gtc::gemm_tc_kernel<EPI><<<grid, gtc::THREADS, gtc::SMEM, st>>>(p, m);

@@ -275,11 +275,8 @@ template <int MT, int EPI>
 static int launch_t(const GemvArgs& a_in, cudaStream_t stream) {
   GemvArgs a = a_in;
   const size_t smem = gemv_smem(MT, a.K);
-  static bool configured = false;  // per template instance; attribute is per device function
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(gemv_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
   // One wave: as many warps as fit on the device at this shared-memory size,
   // whole rows per warp.
   int per_sm = 0;

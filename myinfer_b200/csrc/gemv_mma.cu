@@ -253,11 +253,8 @@ bool gemv_mma_eligible(const GemvArgs& a, int MT, int epi) {
 template <int MT, int EPI>
 static int mma_launch_t(const GemvArgs& a, const MmaScratch& sc, cudaStream_t st) {
   const size_t smem = mma_smem(MT, a.K);
-  static bool configured = false;
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(gemv_mma_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_mma_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
   int per_sm = 0;
   M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_mma_kernel<MT, EPI>, MW * 32, smem));
   const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);

@@ -263,11 +263,8 @@ bool gemv_tma_eligible(int K, int MT, int epi) {
 template <int MT, int EPI>
 static int tma_launch_t(const GemvArgs& a, cudaStream_t st) {
   const size_t smem = tma_smem(MT, a.K, EPI == EPI_SWIGLU ? 2 : 1);
-  static bool configured = false;
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(gemv_tma_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_tma_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
   int per_sm = 0;
   M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tma_kernel<MT, EPI>, TG_THREADS, smem));
   const int ntiles = (a.total_rows + TG_CW - 1) / TG_CW;

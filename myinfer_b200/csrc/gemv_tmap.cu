@@ -451,11 +451,8 @@ bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
 template <int MT, int EPI>
 static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* acc, int* cnt, int acc_rows, cudaStream_t st) {
   const size_t smem = tp_smem(MT, a.K, a.norm_w != nullptr);
-  static bool configured = false;
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
   int per_sm = 0;
   M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tmap_kernel<MT, EPI>, TP_THREADS, smem));
   const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);

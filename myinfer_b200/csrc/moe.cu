@@ -98,12 +98,12 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) moe_down_kernel(const MoeArgs 
 int moe_launch(const MoeArgs& a, cudaStream_t st) {
   if (a.H % 64 || a.I % 64) return fail(M5_ERR_INVALID, "moe: hidden and expert sizes must be multiples of 64");
   if (a.T <= 0) return M5_OK;
-  static bool configured = false;
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(moe_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    M5_CUDA(cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attributes belong to each device's context
+  M5_CUDA(once.run([&] {
+    cudaError_t e = cudaFuncSetAttribute(moe_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  }));
   const int resident = sm_count() * 48;
   {
     const size_t smem = size_t(a.H) * 4 + size_t(a.H / 32) * 4 + 33 * 4;

@@ -394,11 +394,8 @@ __global__ void __launch_bounds__(RT_W * 32) moe_router_topk_kernel(const MoeRou
 int moe_router_topk_launch(const MoeRouterArgs& a, cudaStream_t st) {
   if (a.E > 256 || a.k <= 0 || a.k > 32 || a.k > a.E || a.H % 256) return fail(M5_ERR_INVALID, "moe router: shape");
   const size_t smem = size_t(a.H) * 4 + size_t(a.H / 32) * 4 + 33 * 4;
-  static bool configured = false;
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(moe_router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(moe_router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024); }));
   if (smem > 100 * 1024) return fail(M5_ERR_INVALID, "moe router: hidden size too large");
   M5_CUDA(launch_pdl(moe_router_topk_kernel, dim3(ceil_div(a.E, RT_W)), dim3(RT_W * 32), smem, st, a));
   M5_LAUNCH_CHECK("moe router/top-k launch");
@@ -415,13 +412,13 @@ bool moe_mma_eligible(const MoeArgs& a) {
 }
 
 int moe_mma_launch(const MoeArgs& a, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    M5_CUDA(cudaFuncSetAttribute(moe_gu_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    M5_CUDA(cudaFuncSetAttribute(moe_down_mma_kernel<MX_KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 200 * 1024));
-    configured = true;
-  }
+  static DeviceOnce once;  // the attributes belong to each device's context
+  M5_CUDA(once.run([&] {
+    cudaError_t e = cudaFuncSetAttribute(moe_gu_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(moe_down_mma_kernel<MX_KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024);
+  }));
   const int max_ctas = 2 * sm_count();
   {
     const long long steps = (long long)a.k * (a.I / 8) * (a.H / 64);

@@ -1,20 +1,22 @@
 // Allocation-free variant of the quantized matmul entry point.
 //
-// Some callers of this library cannot call cudaMalloc at all: code running
-// while a CUDA graph is being captured, hosts whose memory is handed out by
-// a pool they do not own (an inference server that reserved all device
-// memory up front), or embedders that forbid allocation after start-up.  The
-// regular m5_quantized_matmul lazily grows a per-device cudaMalloc'd scratch
-// for the split-tile partial sums of its tensor-core GEMV; this entry point
-// uses a fixed array compiled into the library instead.
+// Some callers of this library cannot call cudaMalloc at all: hosts whose
+// device memory is handed out by a pool they do not own (an inference server
+// that reserved all device memory for its own allocator at start-up), or
+// embedders that forbid any allocation once they are running.  The regular
+// m5_quantized_matmul lazily grows a per-device cudaMalloc'd scratch for the
+// split-tile partial sums of its tensor-core GEMV; this entry point uses a
+// fixed array compiled into the library instead.
 //
 // The scratch is a file-scope __device__ array (every GPU that loads the
 // library holds it until the process exits).  Its device address is looked
 // up once per device with cudaGetSymbolAddress on the first call made on that
-// device (so that first call must not happen during stream capture), and the
-// region a call uses is cleared on the stream before the GEMV runs.  All
-// calls share the one array: calls that overlap on the GPU (different
-// streams, no ordering between them) race on it and must not be issued.
+// device, so that first call should come before any stream capture.  The
+// rows a call uses ([8][N rounded up to 16] partial sums and N/16 counters)
+// are cleared on the stream before the GEMV runs.  All calls share the one
+// array and it keeps the last call's contents: calls that overlap on the GPU
+// (different streams, no ordering between them) race on it and must not be
+// issued.
 #include <mutex>
 
 #include "gemv.cuh"
@@ -65,10 +67,13 @@ extern "C" int m5_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K, 
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   const int rows16 = int((N + 15) / 16 * 16);
+  // This call's layout inside the array: partial sums [8][rows16], then one
+  // counter per 16-row tile.  The split-tile protocol needs both zeroed; a
+  // finished launch leaves them zeroed, but an earlier call that stopped on
+  // an error may not have.
   float* acc = reinterpret_cast<float*>(base);
   int* cnt = reinterpret_cast<int*>(base + size_t(8) * kNoAllocMaxRows * sizeof(float));
-  // the split-tile protocol needs zeroed partial sums and counters
-  M5_CUDA(cudaMemsetAsync(acc, 0, size_t(8) * kNoAllocMaxRows * sizeof(float), st));
+  M5_CUDA(cudaMemsetAsync(acc, 0, size_t(8) * rows16 * sizeof(float), st));
   M5_CUDA(cudaMemsetAsync(cnt, 0, size_t(rows16 / 16) * sizeof(int), st));
   GemvArgs a{};
   a.x = (const bf16*)x;
@@ -84,7 +89,7 @@ extern "C" int m5_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K, 
   a.total_rows = (int)N;
   a.mma_acc = acc;
   a.mma_cnt = cnt;
-  a.mma_rows = kNoAllocMaxRows;
+  a.mma_rows = rows16;
   const int cap = gemv_max_tokens((int)K);
   for (int64_t t0 = 0; t0 < M;) {
     int mt = (int)std::min<int64_t>(8, M - t0);

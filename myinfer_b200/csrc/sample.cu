@@ -665,13 +665,9 @@ extern "C" int m5_sample_bf16(void* logits, int rows, int64_t vocab, int64_t ld,
   a.state = reinterpret_cast<unsigned long long*>(state);
   a.append = (p->flags & M5_SAMPLE_APPEND_HISTORY) ? 1 : 0;
   a.vec = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && (ld % 8 == 0);
-  int dev = 0;
-  M5_CUDA(cudaGetDevice(&dev));
-  static bool configured[64] = {false};  // once per device, normally before any graph capture
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    M5_CUDA(cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmpSmem));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
+  static DeviceOnce once;  // once per device, normally before any graph capture
+  M5_CUDA(once.run(
+      [&] { return cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmpSmem); }));
   sample_rows_kernel<<<rows, kSmpThreads, kSmpSmem, static_cast<cudaStream_t>(stream)>>>(a);
   M5_LAUNCH_CHECK("sample_rows_kernel");
   return M5_OK;

@@ -20,6 +20,7 @@ import json
 import logging
 import threading
 import time
+import warnings
 from dataclasses import asdict, dataclass, field, replace
 from pathlib import Path
 from typing import Any, Dict, Iterator, List, Optional
@@ -178,14 +179,19 @@ def _load_model(opts: LoadOptions):
                 v = v.view(torch.int32)
             weights[k] = v.to(dev)
     model = Model(args, weights, dev, max_tokens=min(opts.prefill_step, 2048))
+    tok_files = [f for f in ("tokenizer.json", "tokenizer_config.json", "tokenizer.model", "vocab.json")
+                 if (path / f).exists()]
+    if not tok_files:  # weights only: ids in, ids out, text as raw bytes
+        warnings.warn(f"{path} has no tokenizer files; using the byte tokenizer")
+        return model, ByteTokenizer(args.vocab_size), config
     try:
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(str(path), local_files_only=True,
                                             trust_remote_code=opts.trust_remote_code)
-        tok.eos_token_ids = [config.get("eos_token_id")] if isinstance(config.get("eos_token_id"), int) \
-            else list(config.get("eos_token_id") or [])
-    except Exception:
-        tok = ByteTokenizer(args.vocab_size)
+    except Exception as e:  # a checkpoint's own tokenizer that fails to load is an error, not a fallback
+        raise EngineError(f"tokenizer in {path} ({', '.join(tok_files)}) failed to load: {e}") from e
+    tok.eos_token_ids = [config.get("eos_token_id")] if isinstance(config.get("eos_token_id"), int) \
+        else list(config.get("eos_token_id") or [])
     return model, tok, config
 
 
@@ -207,6 +213,7 @@ class Engine:
         self.state = "empty"
         self.error: Optional[str] = None
         self.last: RequestMetrics = RequestMetrics()
+        self.last_tokens: List[int] = []  # token ids the last request generated
         self.totals = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0, "cached_tokens": 0}
         self._native = 0
         self._plain_limit = 0
@@ -434,6 +441,7 @@ class Engine:
                 m.finish_reason = finish
                 m.peak_memory_gb = round(torch.cuda.max_memory_allocated(self.model.device) / GB, 2)
                 self.last = m
+                self.last_tokens = list(generated)
                 self.totals["requests"] += 1
                 self.totals["prompt_tokens"] += m.prompt_tokens
                 self.totals["completion_tokens"] += m.completion_tokens

@@ -94,11 +94,19 @@ def weight_specs(a: ModelArgs) -> List[tuple]:
     return specs
 
 
-def random_weights(a: ModelArgs, seed: int, device, std: float = 0.02) -> Dict[str, torch.Tensor]:
+EXPERT_BLOCK = 8  # experts of a stacked MoE projection drawn from one generator seed
+
+
+def random_weights(a: ModelArgs, seed: int, device, std: float = 0.02,
+                   experts: Optional[tuple] = None) -> Dict[str, torch.Tensor]:
     """Random-init MLX-layout weights generated and quantized on the device.
 
     Linear/embedding weights N(0, std) in bf16 -> 4-bit g64 (libm5cuda quantizer);
-    norm weights 1 + N(0, std) in bf16.  Tensor i draws from seed*1000003 + i.
+    norm weights 1 + N(0, std) in bf16.  Tensor i draws from seed*1000003 + i;
+    a stacked expert projection ([E, rows, K]) draws each block of
+    EXPERT_BLOCK experts from its own seed, so ``experts=(first, count)``
+    generates only that range of every stack (an expert-parallel rank's
+    shard) with the values the full stack holds there.
     """
     from .ops import quantize
     out: Dict[str, torch.Tensor] = {}
@@ -107,6 +115,22 @@ def random_weights(a: ModelArgs, seed: int, device, std: float = 0.02) -> Dict[s
         g.manual_seed(seed * 1000003 + idx)
         if kind == "norm":
             out[name + ".weight"] = (1.0 + std * torch.randn(shape, generator=g, device=device)).to(torch.bfloat16)
+            continue
+        if ".switch_mlp." in name:
+            E = shape[0]
+            e0, n = experts if experts is not None else (0, E)
+            if e0 < 0 or n <= 0 or e0 + n > E:
+                raise ValueError(f"expert range {experts} outside 0..{E}")
+            parts = []
+            for blk in range(e0 // EXPERT_BLOCK, (e0 + n + EXPERT_BLOCK - 1) // EXPERT_BLOCK):
+                g.manual_seed((seed * 1000003 + idx) * 1009 + blk)
+                lo, hi = blk * EXPERT_BLOCK, min(E, (blk + 1) * EXPERT_BLOCK)
+                w = (std * torch.randn((hi - lo,) + tuple(shape[1:]), generator=g, device=device))
+                w = w[max(lo, e0) - lo:min(hi, e0 + n) - lo].to(torch.bfloat16)
+                parts.append(quantize(w, a.group_size, a.bits))
+                del w
+            for j, suf in enumerate((".weight", ".scales", ".biases")):
+                out[name + suf] = torch.cat([p[j] for p in parts]) if len(parts) > 1 else parts[0][j]
             continue
         # Quantize in slices to bound the bf16 temporary of large stacks.
         rows = shape[0]

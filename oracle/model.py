@@ -32,7 +32,7 @@ from typing import Dict, List, Optional
 import numpy as np
 import torch
 
-from .quant import affine_dequantize, affine_quantize, bf16_bits_to_f32, f32_to_bf16_bits
+from .quant import affine_dequantize_torch, affine_quantize, bf16_bits_to_f32, f32_to_bf16_bits
 from .rope import rope_table
 from .sdpa import blocked_quantized_sdpa, dense_quantized_sdpa, rb
 
@@ -246,11 +246,20 @@ class Model:
         t = self._deq.get(name)
         if t is None:
             w = self.w
-            t = torch.from_numpy(affine_dequantize(w[name + ".weight"], w[name + ".scales"],
-                                                   w[name + ".biases"], self.cfg.group_size,
-                                                   self.cfg.bits))
+            t = affine_dequantize_torch(w[name + ".weight"], w[name + ".scales"], w[name + ".biases"],
+                                        self.cfg.group_size, self.cfg.bits)
             self._deq[name] = t
         return t
+
+    def deq_expert(self, name: str, e: int) -> torch.Tensor:
+        """Expert ``e`` of a stacked [E, rows, K] projection, dequantized alone
+        (a whole stack of a large MoE would not fit in host memory)."""
+        t = self._deq.get(name)
+        if t is not None:
+            return t[e]
+        w = self.w
+        return affine_dequantize_torch(w[name + ".weight"][e], w[name + ".scales"][e], w[name + ".biases"][e],
+                                       self.cfg.group_size, self.cfg.bits)
 
     def norm_w(self, name: str) -> torch.Tensor:
         return torch.from_numpy(bf16_bits_to_f32(self.w[name + ".weight"]))
@@ -315,12 +324,14 @@ class Model:
         inds, scores, gates = self.route(i, x)
         L, k = inds.shape
         y = torch.zeros(L, k, x.shape[-1])
-        for t in range(L):
-            for j in range(k):
-                e = int(inds[t, j])
-                g = rb(x[t] @ self.deq(p + "gate_proj")[e].T)
-                u = rb(x[t] @ self.deq(p + "up_proj")[e].T)
-                y[t, j] = rb(silu_mul(g, u) @ self.deq(p + "down_proj")[e].T)
+        # each routed (token, slot) pair through its expert's SwiGLU; an expert's
+        # weights are dequantized once per call for all pairs routed to it
+        for e in sorted(set(inds.reshape(-1).tolist())):
+            wg, wu, wd = (self.deq_expert(p + n, e) for n in ("gate_proj", "up_proj", "down_proj"))
+            for t, j in (inds == e).nonzero().tolist():
+                g = rb(x[t] @ wg.T)
+                u = rb(x[t] @ wu.T)
+                y[t, j] = rb(silu_mul(g, u) @ wd.T)
         out = rb((rb(y * scores[..., None])).sum(dim=1))
         return out, inds, scores, gates
 

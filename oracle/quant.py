@@ -112,3 +112,23 @@ def affine_dequantize(wq, scales_bits, biases_bits, group_size: int = 64, bits: 
     qg = q.reshape(*q.shape[:-1], K // group_size, group_size)
     w = qg * s[..., None] + b[..., None]
     return w.reshape(q.shape).astype(F32)
+
+
+def affine_dequantize_torch(wq: np.ndarray, scales_bits: np.ndarray, biases_bits: np.ndarray,
+                            group_size: int = 64, bits: int = 4):
+    """``affine_dequantize`` with torch CPU kernels (multithreaded), same values:
+    the code times the fp32 scale, rounded, plus the fp32 bias, rounded (two
+    IEEE steps, no fused multiply-add), as the numpy version computes them."""
+    import torch
+    per = 32 // bits
+    w = torch.from_numpy(np.ascontiguousarray(wq, dtype=np.uint32).view(np.int32)).long() & 0xFFFFFFFF
+    shifts = torch.arange(per, dtype=torch.long) * bits
+    q = ((w[..., None] >> shifts) & ((1 << bits) - 1)).to(torch.float32)
+    q = q.reshape(*w.shape[:-1], w.shape[-1] * per)
+    K = q.shape[-1]
+    s = torch.from_numpy(bf16_bits_to_f32(scales_bits))
+    b = torch.from_numpy(bf16_bits_to_f32(biases_bits))
+    qg = q.reshape(*q.shape[:-1], K // group_size, group_size)
+    out = torch.mul(qg, s[..., None])
+    out = torch.add(out, b[..., None])
+    return out.reshape(q.shape)

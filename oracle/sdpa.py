@@ -24,7 +24,7 @@ from typing import Optional, Union
 import numpy as np
 import torch
 
-from .quant import affine_dequantize
+from .quant import affine_dequantize_torch
 
 SCORE_BUDGET_BYTES = 512 * 1024**2      # attention.py:21
 MIN_BLOCK = 256                         # attention.py:22
@@ -41,8 +41,7 @@ def dequant_kv(kv, group_size: int = 64, bits: int = 8) -> torch.Tensor:
     if isinstance(kv, torch.Tensor):
         return kv.float()
     wq, s, b = kv
-    return torch.from_numpy(affine_dequantize(np.asarray(wq), np.asarray(s), np.asarray(b),
-                                              group_size, bits))
+    return affine_dequantize_torch(np.asarray(wq), np.asarray(s), np.asarray(b), group_size, bits)
 
 
 def _causal(L: int, S: int) -> torch.Tensor:
@@ -70,22 +69,23 @@ def dense_quantized_sdpa(queries: torch.Tensor, keys, values, scale: float,
     B, Hq, L, D = queries.shape
     K = dequant_kv(keys, group_size, bits)
     V = dequant_kv(values, group_size, bits)
-    Hkv = K.shape[-3]
+    Hkv, S = K.shape[-3], K.shape[-2]
     rep = Hq // Hkv
     q = rb(queries * scale)
-    if rep > 1:
-        K = K.repeat_interleave(rep, dim=-3)
-        V = V.repeat_interleave(rep, dim=-3)
-    scores = rb(q @ K.transpose(-1, -2))
+    # The `rep` query heads of a GQA group share kv head h // rep (mlx-lm
+    # repeats K/V per group); the group's rows are stacked against one K/V
+    # instead of materialising the repeated tensors (same products).
+    qg = q.reshape(B, Hkv, rep * L, D)
+    scores = rb(qg @ K.transpose(-1, -2)).reshape(B, Hq, L, S)
     if mask is not None:
         if isinstance(mask, str):
-            mask = _causal(L, scores.shape[-1])
+            mask = _causal(L, S)
         if mask.dtype == torch.bool:
             scores = torch.where(mask, scores, torch.tensor(BF16_MIN))
         else:
             scores = rb(scores + mask.float())
     p = rb(torch.softmax(scores, dim=-1))
-    return rb(p @ V)
+    return rb(p.reshape(B, Hkv, rep * L, S) @ V).reshape(B, Hq, L, D)
 
 
 def blocked_quantized_sdpa(queries: torch.Tensor, keys, values, scale: float,

@@ -1,10 +1,17 @@
 """Quantized-KV attention (m5_quantized_sdpa through blocked_quantized_sdpa)
 against the CPU restatement of m5engine/attention.py.
 
-Tolerances: the device kernel rounds scores and p to bf16 at the reference's
-points but accumulates in a different order and block size, and rounds the
-output to bf16, so it is compared at max-abs 2e-2 on N(0,1) data (output
-values are O(1); one bf16 step at 1.0 is 7.8e-3)."""
+Bar: the device rounds scores and p to bf16 at the reference's points
+(attention.py:66-69, 87-90) but normalises p only at the end of its split-KV
+merge, sums in another order and over other key blocks, and rounds the output
+to bf16.  Each of those moves an output by a fraction of a bf16 step, so the
+test asks, per element, |d| <= 2^-7 |ref| + 1e-2 std(ref) (two bf16 steps of
+the value itself, plus a floor of 1 % of the output's spread for values near
+zero), and cosine >= 0.9999 over the whole output.  The grid covers the
+reference's own test (tests/test_core.py:23-40), every GQA shape of the
+configs, and the attention microbenchmark's shapes (64 q / 8 kv heads,
+8- and 4-bit keys and values, decode at 4K / 32K / 128K keys, a 2048-token
+causal prefill chunk over 4K keys)."""
 
 import numpy as np
 import pytest
@@ -32,6 +39,17 @@ def _kv(rng, B, Hkv, S, D, bits):
     return qk, qv, None, None
 
 
+def _check(out, ref):
+    """|d| <= 2^-7 |ref| + 1e-2 std(ref) everywhere, cosine >= 0.9999."""
+    out, ref = out.float().cpu().reshape(-1), ref.float().cpu().reshape(-1)
+    err = (out - ref).abs()
+    bound = ref.abs() * 2 ** -7 + 1e-2 * ref.std()
+    worst = int((err - bound).argmax())
+    assert bool((err <= bound).all()), (float(err[worst]), float(ref[worst]), float(ref.std()))
+    cos = torch.nn.functional.cosine_similarity(out, ref, dim=0).item()
+    assert cos >= 0.9999, cos
+
+
 def _dev(t):
     wq, s, b = t
     return (torch.from_numpy(wq.view(np.int32)).cuda(), torch.from_numpy(s.view(np.int16)).view(torch.bfloat16).cuda(),
@@ -56,7 +74,10 @@ def test_reference_grid(hq, hk, mask_kind):
     kd = torch.from_numpy(affine_dequantize(*qk, 64, 8)).repeat_interleave(hq // hk, dim=1)
     vd = torch.from_numpy(affine_dequantize(*qv, 64, 8)).repeat_interleave(hq // hk, dim=1)
     dense = reference_attention(torch.from_numpy(q), kd, vd, 0.125, None if mask_kind is None else causal)
-    assert (out - oracle).abs().max().item() < 2e-2
+    _check(out, oracle)
+    # the reference's own test compares blocked with dense fp32 attention (no
+    # bf16 rounding at all) at 1e-4; with the bf16 rounding points of the
+    # real op the distance to fp32 is a bf16-sized one
     assert (out - dense).abs().max().item() < 2e-2
 
 
@@ -76,7 +97,7 @@ def test_decode(bits, hq, hk, S):
     else:
         out = blocked_quantized_sdpa(qd, kt.to(torch.bfloat16).cuda(), vt.to(torch.bfloat16).cuda(), D ** -0.5, None)
         oracle = ref_dense(torch.from_numpy(q), kt, vt, D ** -0.5, None)
-    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
+    _check(out, oracle)
 
 
 @pytest.mark.parametrize("bits", [8, 4])
@@ -91,7 +112,7 @@ def test_prefill_chunk_causal(bits):
                                  "causal", 64, bits)
     oracle = ref_blocked(torch.from_numpy(q), k, v, D ** -0.5, "causal", 64, bits, score_budget_bytes=1,
                          min_block=256)
-    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
+    _check(out, oracle)
 
 
 def test_additive_mask():
@@ -104,7 +125,7 @@ def test_additive_mask():
     out = blocked_quantized_sdpa(torch.from_numpy(q).to(torch.bfloat16).cuda(), _dev(k), _dev(v), D ** -0.5,
                                  add.cuda(), 64, 8)
     oracle = ref_blocked(torch.from_numpy(q), k, v, D ** -0.5, add, 64, 8, score_budget_bytes=1, min_block=128)
-    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
+    _check(out, oracle)
 
 
 @pytest.mark.parametrize("bits", [8, 4])
@@ -123,4 +144,48 @@ def test_prefill_tensor_core(bits, hq, hk, L, S, mask):
                                  mask, 64, bits)
     oracle = ref_blocked(torch.from_numpy(q), k, v, D ** -0.5, mask, 64, bits, score_budget_bytes=1,
                          min_block=256)
-    assert (out.float().cpu() - oracle).abs().max().item() < 2e-2
+    _check(out, oracle)
+
+
+_LONG = {}
+
+
+def _long_kv(S, bits):
+    """Seeded N(0,1) bf16 keys / values [1, 8, S, 128] quantized to `bits`
+    (generated once per length and shared by the 8- and 4-bit cases)."""
+    if S not in _LONG:
+        _LONG.clear()
+        rng = np.random.default_rng(S)
+        _LONG[S] = {"k": _bf16(rng.standard_normal((1, 8, S, 128), dtype=np.float32)),
+                    "v": _bf16(rng.standard_normal((1, 8, S, 128), dtype=np.float32))}
+    d = _LONG[S]
+    if bits not in d:
+        d[bits] = (affine_quantize(d["k"], 64, bits), affine_quantize(d["v"], 64, bits))
+    return d[bits]
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("S", [32768, 131072])
+def test_decode_long_context(S, bits):
+    """The attention microbenchmark's decode shapes: 64 q / 8 kv heads at 32K
+    and 128K keys, 8- and 4-bit cache (one query row, split-KV + merge)."""
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    k, v = _long_kv(S, bits)
+    q = _bf16(np.random.default_rng(S + bits).standard_normal((1, 64, 1, 128), dtype=np.float32))
+    out = blocked_quantized_sdpa(torch.from_numpy(q).to(torch.bfloat16).cuda(), _dev(k), _dev(v), 128 ** -0.5,
+                                 None, 64, bits)
+    _check(out, ref_dense(torch.from_numpy(q), k, v, 128 ** -0.5, None, 64, bits))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_prefill_chunk_2048(bits):
+    """The microbenchmark's prefill shape: a causal 2048-token chunk at the end
+    of 4096 keys, 64 q / 8 kv heads (the reference's blocked loop, 341-key
+    blocks at this size)."""
+    from myinfer_b200.attention import blocked_quantized_sdpa
+    S, L = 4096, 2048
+    k, v = _long_kv(S, bits)
+    q = _bf16(np.random.default_rng(L + bits).standard_normal((1, 64, L, 128), dtype=np.float32))
+    out = blocked_quantized_sdpa(torch.from_numpy(q).to(torch.bfloat16).cuda(), _dev(k), _dev(v), 128 ** -0.5,
+                                 "causal", 64, bits)
+    _check(out, ref_blocked(torch.from_numpy(q), k, v, 128 ** -0.5, "causal", 64, bits))

@@ -86,3 +86,49 @@ def test_sampling_and_benchmark(engine):
     assert b["prompt_tokens"] == 256 and b["completion_tokens"] == 16 and b["decode_tps"] > 0
     info = engine.info()
     assert info["totals"]["requests"] >= 1 and info["model"]["type"] == "qwen3"
+
+
+def _oracle_greedy(model, prompt, n, prefill_step=64):
+    """The oracle's greedy tokens and per-step logits for the engine's own
+    (device-generated) weights, copied to the host."""
+    import numpy as np
+    from oracle import model as om
+    host = {}
+    for k, t in model.weights.items():
+        c = t.cpu()
+        host[k] = c.numpy().view(np.uint32) if c.dtype == torch.int32 else c.view(torch.int16).numpy().view(np.uint16)
+    ora = om.Model(om.Config.from_dict(model.args.to_dict()), host)
+    toks, _, logits = om.generate(ora, prompt, n, prefill_step=prefill_step, kv_bits=8, quantized_kv_start=0,
+                                  return_logits=True)
+    return toks, logits
+
+
+def _agree_with_oracle(got, toks_o, logits_o):
+    """Equal to the oracle's greedy tokens up to the first step where the
+    oracle's own top-2 logits are within 0.02 (a numerical near-tie)."""
+    for i, (a, b) in enumerate(zip(got, toks_o)):
+        if a != b:
+            top2 = logits_o[i].topk(2).values
+            assert (top2[0] - top2[1]).item() < 0.02, (i, got, toks_o)
+            return i
+    assert len(got) == len(toks_o)
+    return len(got)
+
+
+def test_prefix_reuse_matches_oracle(engine):
+    """A follow-up request that reuses a trimmed cached prefix (move-not-copy)
+    generates the oracle's greedy tokens for the whole prompt, as does the
+    same request with a fresh prefill."""
+    engine.prefix.clear()
+    base = engine.encode_text("Shared context for a two-turn conversation about caches. " * 2)
+    follow = base + engine.encode_text(" Second turn: what is reused?")
+    _run(engine, base, 8)
+    _, m = _run(engine, follow, 10)
+    assert m.cached_tokens == len(base)
+    reused = list(engine.last_tokens)
+    _, m_fresh = _run(engine, follow, 10, use_prefix_cache=False)
+    assert m_fresh.cached_tokens == 0
+    fresh = list(engine.last_tokens)
+    toks_o, logits_o = _oracle_greedy(engine.model, follow, 10)
+    _agree_with_oracle(reused, toks_o, logits_o)
+    _agree_with_oracle(fresh, toks_o, logits_o)

@@ -1,0 +1,71 @@
+"""Two-layer slices of the benchmark models at their true layer dimensions,
+through the device token loop against the oracle (same bar as
+test_model_gpu.py: teacher-forced logits cosine >= 0.9999 median and >= 0.9995
+per step, max-abs <= 0.05, greedy tokens identical except at near-ties; the
+4-bit KV bars of that file for the 4-bit cache).
+
+* Qwen3-32B layers: hidden 5120, 64 q / 8 kv heads, intermediate 25600, YaRN
+  factor 4, 8-bit KV.  A 64-token prefill chunk runs every projection on the
+  tensor-core GEMM, o_proj and down_proj split over K into fp32 slice
+  products (40 output tiles at 64 rows), then a 5-token chunk and the decode
+  tokens on the GEMV (down_proj at K = 25600).
+* Qwen3-30B-A3B layers: hidden 2048, 32 q / 4 kv heads, 128 experts, top-8,
+  expert intermediate 768, 8-bit KV: a 64-token chunk through the per-expert
+  grouped GEMMs, a 5-token chunk through the per-token expert GEMVs, decode
+  tokens through the tensor-core expert path.
+* Qwen3-235B-A22B layers: hidden 4096, 64 q / 4 kv heads, 128 experts, top-8,
+  expert intermediate 1536, 4-bit KV.
+
+The vocabulary is cut to 4096 rows (the lm_head shape is covered by the
+Qwen3-0.6B test).  Weights come from the device generator (N(0, 0.02) bf16
+quantized by the device quantizer, which test_quant_gpu.py holds bit-exact to
+the oracle's rule) and are copied to the host for the oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as om
+from test_model_gpu import _check, _run
+
+pytestmark = pytest.mark.gpu
+
+BASE = dict(head_dim=128, num_hidden_layers=2, vocab_size=4096, tie_word_embeddings=False,
+            max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
+C3 = dict(BASE, model_type="qwen3", hidden_size=5120, num_attention_heads=64, num_key_value_heads=8,
+          intermediate_size=25600)
+C4 = dict(BASE, model_type="qwen3_moe", hidden_size=2048, num_attention_heads=32, num_key_value_heads=4,
+          intermediate_size=6144, moe_intermediate_size=768, num_experts=128, num_experts_per_tok=8,
+          norm_topk_prob=True)
+C5 = dict(BASE, model_type="qwen3_moe", hidden_size=4096, num_attention_heads=64, num_key_value_heads=4,
+          intermediate_size=12288, moe_intermediate_size=1536, num_experts=128, num_experts_per_tok=8,
+          norm_topk_prob=True)
+
+
+def _build(cfg, seed):
+    from myinfer_b200.model import Model, ModelArgs, random_weights
+    a = ModelArgs.from_dict(cfg)
+    w = random_weights(a, seed, "cuda")
+    host = {}
+    for k, t in w.items():
+        c = t.cpu()
+        host[k] = c.numpy().view(np.uint32) if c.dtype == torch.int32 else c.view(torch.int16).numpy().view(np.uint16)
+    return Model(a, w, "cuda", max_tokens=64), om.Model(om.Config.from_dict(cfg), host)
+
+
+def test_qwen3_32b_layers():
+    dev, ora = _build(C3, seed=41)
+    prompt = np.random.default_rng(41).integers(0, C3["vocab_size"], 70).tolist()
+    _check(*_run(dev, ora, prompt, 6, 64, 8, 0, yarn=4.0), n_equal=6)
+
+
+def test_qwen3_30b_a3b_layers():
+    dev, ora = _build(C4, seed=42)
+    prompt = np.random.default_rng(42).integers(0, C4["vocab_size"], 70).tolist()
+    _check(*_run(dev, ora, prompt, 6, 64, 8, 0), n_equal=6)
+
+
+def test_qwen3_235b_a22b_layers():
+    dev, ora = _build(C5, seed=43)
+    prompt = np.random.default_rng(43).integers(0, C5["vocab_size"], 12).tolist()
+    _check(*_run(dev, ora, prompt, 4, 8, 4, 0), n_equal=4, cos_min=0.999, cos_median=0.9995, max_abs=0.08)

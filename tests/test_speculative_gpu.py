@@ -1,5 +1,6 @@
 """Speculative decoding with a draft model (speculative_generate_step, the
-engine's draft_model option) against the main model's plain greedy decode.
+engine's draft_model option) against the main model's plain greedy decode and
+the oracle's greedy tokens for the main model.
 
 With greedy sampling the accepted tokens are the main model's own choices, so
 the streams are equal.  The verify call scores 1 + k tokens at once (an
@@ -21,11 +22,12 @@ MAIN = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attent
 DRAFT = dict(MAIN, hidden_size=256, num_hidden_layers=2, num_attention_heads=4, intermediate_size=512)
 
 
-def _model(cfg, seed):
+def _model(cfg, seed, with_oracle=False):
     from myinfer_b200.model import Model, ModelArgs, upload_weights
     from oracle import model as om
     host = om.generate_weights(om.Config.from_dict(cfg), seed)
-    return Model(ModelArgs.from_dict(cfg), upload_weights(host, "cuda"), "cuda", max_tokens=64)
+    m = Model(ModelArgs.from_dict(cfg), upload_weights(host, "cuda"), "cuda", max_tokens=64)
+    return (m, om.Model(om.Config.from_dict(cfg), host)) if with_oracle else m
 
 
 def _plain(model, prompt, n):
@@ -49,7 +51,8 @@ def _agree(spec, plain, logits):
 def test_speculative_equals_greedy(k):
     from myinfer_b200.generate import speculative_generate_step
     from myinfer_b200.cache import make_prompt_cache
-    main, draft = _model(MAIN, 31), _model(DRAFT, 32)
+    from oracle import model as om
+    (main, ora), draft = _model(MAIN, 31, with_oracle=True), _model(DRAFT, 32)
     prompt = np.random.default_rng(k).integers(0, MAIN["vocab_size"], 30).tolist()
     n = 24
     plain, logits = _plain(main, prompt, n)
@@ -58,6 +61,10 @@ def test_speculative_equals_greedy(k):
                                          prefill_step_size=16, kv_bits=8, quantized_kv_start=0))
     assert len(got) == n
     _agree([t for t, _ in got], plain, logits)
+    # and the oracle's greedy tokens for the main model, up to its first near-tie
+    toks_o, _, logits_o = om.generate(ora, prompt, n, prefill_step=16, kv_bits=8, quantized_kv_start=0,
+                                      return_logits=True)
+    _agree([t for t, _ in got], toks_o, list(logits_o))
 
 
 def test_self_draft_accepts_everything():
