@@ -271,11 +271,31 @@ M5_API int m5_moe_route(const void* x, int T, int H, const uint32_t* gate_w, con
  * every rank returns the full logits and the same argmax. */
 #define M5_COMM_ID_BYTES 128
 M5_API int m5_comm_unique_id(void* out, size_t len);
+/* Set-up is non-blocking and bounded (M5_COMM_INIT_TIMEOUT_S, default 300 s):
+ * if a rank never joins, the call aborts the communicator and returns
+ * M5_ERR_TIMEOUT instead of hanging. */
 M5_API int m5_comm_init(const void* id, size_t len, int nranks, int rank, void** comm);
 M5_API int m5_comm_destroy(void* comm);
 M5_API int m5_model_set_comm(void* model, void* comm);
 /* In-place fp32 sum over the communicator's ranks (stream-ordered). */
 M5_API int m5_allreduce_f32(void* comm, float* buf, int64_t n, void* stream);
+/* Failure detection (the reference's counterpart is its error state:
+ * EngineError and the load/generate error handling, m5engine/engine.py:47-56,
+ * 192-205).  m5_comm_check returns M5_ERR_COMM when NCCL reports an
+ * asynchronous error on the communicator (M5_ERR_STATE once aborted);
+ * m5_comm_abort aborts it (every later collective fails fast) so a rank that
+ * learned of a failed peer can leave without waiting on it;
+ * m5_comm_set_wait_ms bounds the peer all-reduce's wait for the other ranks
+ * (default 2000 ms; on expiry the call records a device error read by
+ * m5_device_status and leaves the residual stream unchanged). */
+M5_API int m5_comm_check(void* comm);
+M5_API int m5_comm_abort(void* comm);
+M5_API int m5_comm_set_wait_ms(void* comm, int ms);
+/* Runs the peer all-reduce kernel on the current GPU against a stand-in
+ * second rank that never arrives, with a `wait_ms` bound: returns the device
+ * error word it left (*device_code), the call's wall time and whether the
+ * residual stream was left unchanged.  Diagnostic; needs no communicator. */
+M5_API int m5_comm_peer_wait_selftest(int wait_ms, int* device_code, double* elapsed_ms, int* h_unchanged);
 
 #ifdef __cplusplus
 }

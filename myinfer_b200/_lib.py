@@ -91,6 +91,10 @@ _SIGS = {
     "m5_comm_destroy": (c_int, [c_void_p]),
     "m5_model_set_comm": (c_int, [c_void_p, c_void_p]),
     "m5_allreduce_f32": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "m5_comm_check": (c_int, [c_void_p]),
+    "m5_comm_abort": (c_int, [c_void_p]),
+    "m5_comm_set_wait_ms": (c_int, [c_void_p, c_int]),
+    "m5_comm_peer_wait_selftest": (c_int, [c_int, POINTER(c_int), POINTER(ctypes.c_double), POINTER(c_int)]),
 }
 M5_COMM_ID_BYTES = 128
 
@@ -131,3 +135,14 @@ def check(rc: int) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(lib(), name)(*args))
+
+
+def device_check() -> None:
+    """Raise if a kernel on the current device recorded an error: a bounded
+    wait that ran out (a TMA copy or a peer rank that never arrived).  The
+    error words are cleared when read, so each failure is reported once."""
+    code = c_int(0)
+    call("m5_device_status", ctypes.byref(code), 1)
+    if code.value:
+        raise M5CudaError(M5_ERR_TIMEOUT, f"device reported error code {code.value}: a bounded wait ran out "
+                                          "(a copy that never landed or a peer rank that never arrived)")

@@ -114,6 +114,21 @@ class Communicator:
                   ctypes.byref(h))
         self.handle = h
 
+    def check(self) -> None:
+        """Raise M5CudaError if NCCL reported an asynchronous error (or the
+        communicator was aborted)."""
+        _lib.call("m5_comm_check", self.handle)
+
+    def abort(self) -> None:
+        """Abort the communicator: every later collective fails fast instead of
+        waiting on a peer that is gone."""
+        if self.handle is not None and self.handle.value:
+            _lib.call("m5_comm_abort", self.handle)
+
+    def set_wait_ms(self, ms: int) -> None:
+        """Bound on the peer all-reduce's wait for the other ranks."""
+        _lib.call("m5_comm_set_wait_ms", self.handle, int(ms))
+
     def allreduce_(self, t: torch.Tensor) -> torch.Tensor:
         """In-place fp32 sum over the ranks (testing / host utilities)."""
         from .ops import _stream

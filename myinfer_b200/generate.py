@@ -14,6 +14,12 @@ reads the previous token and the cache length from device memory and writes
 the next token back (the argmax, or the device sampler's draw, which also
 applies the logits processors and rolls their token window on the device), so
 the host only copies 4 bytes per token out.
+
+Every kernel wait is bounded: a wait that runs out (a copy that never landed,
+a peer rank that never arrived) records a device error word instead of
+hanging.  The loop reads those words after the prompt, every
+``STATUS_EVERY`` decode steps and at the end, and raises ``M5CudaError``
+(M5_ERR_TIMEOUT) so a failed step never passes silently as tokens.
 """
 
 from __future__ import annotations
@@ -28,6 +34,8 @@ from . import _lib
 from .attention import safe_maybe_quantize_kv_cache
 from .cache import PromptCache, make_prompt_cache, trim_prompt_cache
 from .sample import DeviceSampler, with_processors
+
+STATUS_EVERY = 64  # decode steps between reads of the device error words
 
 
 @dataclass
@@ -150,6 +158,7 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
     if stats is not None:
         stats["prompt_time"] = time.perf_counter() - t0
         stats["prompt_tokens"] = n
+    _lib.device_check()
     y = int(host[0])
     y_logits = logits
     graph: Optional[DecodeGraph] = None
@@ -183,7 +192,10 @@ def generate_step(prompt: List[int], model, max_tokens: int = 256, sampler: Opti
         ev.record()
         yield y, y_logits
         ev.synchronize()
+        if (i + 1) % STATUS_EVERY == 0:
+            _lib.device_check()
         y, y_logits = int(host[slot]), nxt_logits
+    _lib.device_check()
     if stats is not None:
         stats["decode_time"] = time.perf_counter() - t1
 

@@ -135,3 +135,27 @@ def test_communicator_id_exchange_gloo():
     for p in procs:
         p.join(timeout=60)
     assert res == [(0, True, 2, 0, 1234), (1, True, 2, 1, 1235)]
+
+
+def test_device_check_maps_error_word(monkeypatch):
+    """_lib.device_check raises M5_ERR_TIMEOUT when the device error word is
+    set (faked status call; no GPU involved) and passes when it is clear."""
+    from myinfer_b200 import _lib
+
+    class FakeLib:
+        def __init__(self, word):
+            self.word = word
+
+        def m5_device_status(self, code_ptr, reset):
+            code_ptr._obj.value = self.word
+            return _lib.M5_OK
+
+        def m5_last_error(self, buf, n):
+            return 0
+
+    monkeypatch.setattr(_lib, "lib", lambda: FakeLib(0))
+    _lib.device_check()
+    monkeypatch.setattr(_lib, "lib", lambda: FakeLib(1))
+    with pytest.raises(_lib.M5CudaError) as e:
+        _lib.device_check()
+    assert e.value.code == _lib.M5_ERR_TIMEOUT
