@@ -297,4 +297,134 @@ __device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int6
   return ok;
 }
 
+
+// Activation staging for the int8 tensor-core GEMV (mma.sync m16n8k32, u8
+// weight codes against s8 / u8 activation planes), with the same bulk copy,
+// RMSNorm and bf16 rounding points as stage_frag_bulk.  Per token t and
+// 64-element group G the normalised bf16 values become 16-bit fixed point
+//   v = rint(x * 2^(14 - E)),  E = exponent of the group's largest |x|,
+// so |v| < 2^15 and every value at or above 2^-7 of the group's maximum is
+// exact (bf16 keeps 8 significant bits); v = 256 hi + lo with hi s8, lo u8.
+// xs[t * NG + G] = 2^(E - 14) undoes the scale, xg[t * NG + G] is the fp32
+// sum of the group's bf16 values (the bias term).  Layout of the planes,
+// 32 words per (t, G) like the fp16 pairs:
+//   xq[(t*NG + G)*32 + tq*8 + plane*4 + m*2 + r],  plane 0 = hi, 1 = lo,
+//   m = MMA (k 16tq..16tq+7 or 16tq+8..16tq+15), r = 0 even / 1 odd elements
+// of that 8-element block, 4 bytes each -- the B fragment (b0, b1) of the
+// MMA in which lane quad tq reads the weight word 2tq + m of the group.
+// Each warp converts whole groups (8 lanes per group, one 8-element block
+// each) and reads its 32 raw blocks into registers before any lane writes,
+// so the conversion is in place.  Requirements as for stage_frag_bulk.
+template <int MT, int NT>
+__device__ __forceinline__ bool stage_i8_bulk(const bf16* __restrict__ x, int64_t ldx, int K,
+                                              const bf16* __restrict__ norm_w, float eps, uint32_t* xq,
+                                              uint32_t* nbuf, float* xg, float* xs, float* red, int bar,
+                                              uint64_t* xbar, int* err) {
+  static_assert(NT % 32 == 0 && NT / 32 <= 8, "int8 staging by whole warps");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NG = K >> 6, K8 = K >> 3;
+  auto sync = [&]() {
+    if (bar == 0) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(NT) : "memory");
+  };
+  if (tid == 0) {
+    const uint32_t row = uint32_t(K) * 2u;
+    mbar_arrive_expect_tx(xbar, MT * row + (norm_w ? row : 0u));
+#pragma unroll
+    for (int t = 0; t < MT; ++t) bulk_g2s(xq + size_t(t) * NG * 32, x + size_t(t) * ldx, row, xbar);
+    if (norm_w) bulk_g2s(nbuf, norm_w, row, xbar);
+  }
+  const bool ok = mbar_wait(xbar, 0, err);
+  const uint4* nw = reinterpret_cast<const uint4*>(nbuf);
+  float inv[MT];
+  if (norm_w) {
+    float* rs = red + 8;  // [NT/32][MT] sums of squares
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const uint4* blk = reinterpret_cast<const uint4*>(xq + size_t(t) * NG * 32);
+      float ss = 0.f;
+      for (int c = tid; c < K8; c += NT) {
+        const uint4 v = blk[c];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float a = bf16_lo(w[q]), b = bf16_hi(w[q]);
+          ss = fmaf(a, a, fmaf(b, b, ss));
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) rs[warp * MT + t] = ss;
+    }
+    sync();
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < NT / 32; ++w) tot += rs[w * MT + t];
+      inv[t] = __frsqrt_rn(__fadd_rn(tot / float(K), eps));
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < MT; ++t) inv[t] = 1.f;
+  }
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    uint4* blk = reinterpret_cast<uint4*>(xq + size_t(t) * NG * 32);
+    for (int c0 = tid - lane; c0 < K8; c0 += NT) {  // K8 % 32 == 0: whole warps, whole groups
+      const int c = c0 + lane;
+      const uint4 v = blk[c];
+      float e[8];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        e[2 * q] = bf16_lo(w[q]);
+        e[2 * q + 1] = bf16_hi(w[q]);
+      }
+      if (norm_w) {
+        const uint4 nv = nw[c];
+        const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          e[2 * q] = rbf(__fmul_rn(bf16_lo(n[q]), rbf(__fmul_rn(e[2 * q], inv[t]))));
+          e[2 * q + 1] = rbf(__fmul_rn(bf16_hi(n[q]), rbf(__fmul_rn(e[2 * q + 1], inv[t]))));
+        }
+      }
+      float gs = 0.f, gm = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        gs += e[q];
+        gm = fmaxf(gm, fabsf(e[q]));
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        gs += __shfl_xor_sync(0xffffffffu, gs, o);
+        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+      }
+      const int G = c >> 3, cb = c & 7;  // group, block inside it
+      const int E = int((__float_as_uint(gm) >> 23) & 0xFFu);  // biased exponent of the group max
+      const int sh = gm > 0.f ? 141 - E : 0;                   // 2^(14 - (E - 127))
+      const float up = __uint_as_float(uint32_t(max(1, min(254, sh + 127))) << 23);
+      if (cb == 0) {
+        xg[t * NG + G] = gs;
+        xs[t * NG + G] = __uint_as_float(uint32_t(max(1, min(254, 127 - sh))) << 23);
+      }
+      uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};  // r = 0 even, 1 odd elements
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int iv = __float2int_rn(e[q] * up);
+        const uint32_t hb = uint32_t(iv >> 8) & 0xFFu, lb = uint32_t(iv) & 0xFFu;
+        hi[q & 1] |= hb << (8 * (q >> 1));
+        lo[q & 1] |= lb << (8 * (q >> 1));
+      }
+      __syncwarp();  // every raw block of this warp's groups is in registers
+      const int tq = cb >> 1, m = cb & 1;
+      uint32_t* dst = xq + (size_t(t) * NG + G) * 32 + tq * 8 + m * 2;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
+      *reinterpret_cast<uint2*>(dst + 4) = make_uint2(lo[0], lo[1]);
+    }
+  }
+  sync();
+  return ok;
+}
+
 }  // namespace m5

@@ -81,6 +81,24 @@ __device__ __forceinline__ void tp_codes_f16(uint32_t w, uint32_t (&p)[4]) {
   p[3] = tp_hsub2(f13, l13);
 }
 
+// Integer MMAs of the int8 variant: u8 weight codes (0..15) against the s8
+// high plane and the u8 low plane of the 16-bit fixed-point activations;
+// exact int32 sums.
+__device__ __forceinline__ void tp_imma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void tp_imma_u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ void tp_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -106,7 +124,12 @@ __device__ __forceinline__ void tp_half(const GemvArgs& a, int tile, int h, int&
   }
 }
 
-template <int MT, int EPI>
+// I8 selects the consumer: false = fp16 MMAs on exact codes against the
+// activations scaled per token (stage_frag_bulk), true = int8 MMAs (u8 codes
+// as they sit in the word, one mask or shift-and-mask per 4 codes) against
+// per-group 16-bit fixed-point activation planes (stage_i8_bulk), int32 group
+// sums folded as s * 2^(E - 14) * D + b * sum(x).
+template <int MT, int EPI, bool I8>
 __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs a, const __grid_constant__ TmapSet tm,
                                                                float* acc_buf, int* cnt_buf, int acc_rows) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -121,7 +144,8 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
   uint32_t* xf = reinterpret_cast<uint32_t*>(full + TP_BARS);     // [MT][NG][4][8] pairs
   uint32_t* nbuf = xf + MT * NG * 32;                             // [K] bf16 norm weight (if any)
   float* xg = reinterpret_cast<float*>(nbuf + (a.norm_w ? K / 2 : 0));  // [MT][NG]
-  float* red = xg + MT * NG;                                      // [8]
+  float* xsc = xg + MT * NG;                                      // [MT][NG] group scales (I8)
+  float* red = xsc + (I8 ? MT * NG : 0);                          // [8]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
@@ -183,8 +207,11 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
   // The next kernel may launch only now: launched earlier, its CTAs could take
   // the SM slots this grid's own CTAs still wait for.
   pdl_launch_dependents();
-  stage_frag_bulk<MT, TP_CW * 32, true>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, red, 1, xinv, xbar,
-                                        &g_gemv_tmap_err);
+  if constexpr (I8)
+    stage_i8_bulk<MT, TP_CW * 32>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, xsc, red, 1, xbar, &g_gemv_tmap_err);
+  else
+    stage_frag_bulk<MT, TP_CW * 32, true>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, red, 1, xinv, xbar,
+                                          &g_gemv_tmap_err);
 
   const int g = lane >> 2, tq = lane & 3;
   const int tok = g < MT ? g : MT - 1;
@@ -192,7 +219,9 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
   const uint32_t* xfl = xf + tok * NG * 32 + tq * 8;
   const float* xg0 = xg + t0c * NG;
   const float* xg1 = xg + t1c * NG;
-  const float xi0 = xinv[t0c], xi1 = xinv[t1c];
+  const float* xs0 = xsc + t0c * NG;
+  const float* xs1 = xsc + t1c * NG;
+  const float xi0 = I8 ? 1.f : xinv[t0c], xi1 = I8 ? 1.f : xinv[t1c];
   // per-thread smem offsets of this warp's four groups inside a stage (the
   // 128-byte swizzle of the weight boxes depends only on g, tq and the group)
   uint32_t woff[TP_UG / TP_CW];
@@ -331,6 +360,45 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
       const float X0a[4] = {X0.x, X0.y, X0.z, X0.w}, X1a[4] = {X1.x, X1.y, X1.z, X1.w};
       const uint32_t sw0[2] = {sv0.x, sv0.y}, sw8[2] = {sv8.x, sv8.y}, bw0[2] = {bv0.x, bv0.y},
                      bw8[2] = {bv8.x, bv8.y};
+      if constexpr (I8) {
+        const float4 F0 = *reinterpret_cast<const float4*>(xs0 + G0);
+        const float4 F1 = *reinterpret_cast<const float4*>(xs1 + G0);
+        const float F0a[4] = {F0.x, F0.y, F0.z, F0.w}, F1a[4] = {F1.x, F1.y, F1.z, F1.w};
+#pragma unroll
+        for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
+          const uint2 w0 = *reinterpret_cast<const uint2*>(ws + woff[jj]);
+          const uint2 w8 = *reinterpret_cast<const uint2*>(ws + 4096 + woff[jj]);
+          const uint4 xh = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32);      // s8 plane
+          const uint4 xl = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32 + 4);  // u8 plane
+          int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+          {
+            const uint32_t A[4] = {w0.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, (w0.x >> 4) & 0x0F0F0F0Fu,
+                                   (w8.x >> 4) & 0x0F0F0F0Fu};
+            tp_imma_s8(dh, A, xh.x, xh.y);
+            tp_imma_u8(dl, A, xl.x, xl.y);
+          }
+          {
+            const uint32_t A[4] = {w0.y & 0x0F0F0F0Fu, w8.y & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu,
+                                   (w8.y >> 4) & 0x0F0F0F0Fu};
+            tp_imma_s8(dh, A, xh.z, xh.w);
+            tp_imma_u8(dl, A, xl.z, xl.w);
+          }
+          const uint32_t s0w = sw0[jj >> 1], s8w = sw8[jj >> 1], b0w = bw0[jj >> 1], b8w = bw8[jj >> 1];
+          const float sA = (jj & 1) ? bf16_hi(s0w) : bf16_lo(s0w), sB = (jj & 1) ? bf16_hi(s8w) : bf16_lo(s8w);
+          const float bA = (jj & 1) ? bf16_hi(b0w) : bf16_lo(b0w), bB = (jj & 1) ? bf16_hi(b8w) : bf16_lo(b8w);
+          // exact: |256 dh + dl| < 2^25 (64 codes <= 15 times |v| < 2^15)
+          totD[0] = fmaf(sA * F0a[jj], float(dh[0] * 256 + dl[0]), totD[0]);
+          totD[2] = fmaf(sB * F0a[jj], float(dh[2] * 256 + dl[2]), totD[2]);
+          totB[0] = fmaf(bA, X0a[jj], totB[0]);
+          totB[2] = fmaf(bB, X0a[jj], totB[2]);
+          if constexpr (MT > 1) {  // the odd columns hold other tokens only when there are any
+            totD[1] = fmaf(sA * F1a[jj], float(dh[1] * 256 + dl[1]), totD[1]);
+            totD[3] = fmaf(sB * F1a[jj], float(dh[3] * 256 + dl[3]), totD[3]);
+            totB[1] = fmaf(bA, X1a[jj], totB[1]);
+            totB[3] = fmaf(bB, X1a[jj], totB[3]);
+          }
+        }
+      } else {
 #pragma unroll
       for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
         const uint2 w0 = *reinterpret_cast<const uint2*>(ws + woff[jj]);
@@ -370,6 +438,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
         totB[1] = fmaf(bA, X1a[jj], totB[1]);
         totB[2] = fmaf(bB, X0a[jj], totB[2]);
         totB[3] = fmaf(bB, X1a[jj], totB[3]);
+      }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
@@ -428,14 +497,24 @@ static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i) {
   return M5_OK;
 }
 
-static size_t tp_smem(int MT, int K, bool norm) {
+static size_t tp_smem(int MT, int K, bool norm, bool i8) {
   return TP_STAGES * (TP_W_STAGE + 2 * TP_SB_STAGE) + TP_BARS * 8 + size_t(MT) * (K / 64) * 32 * 4 +
-         (norm ? size_t(K) * 2 : 0) + size_t(MT) * (K / 64) * 4 + 8 * 4 + size_t(TP_CW) * MT * 16 * 4 + 1024;
+         (norm ? size_t(K) * 2 : 0) + size_t(MT) * (K / 64) * 4 * (i8 ? 2 : 1) + 8 * 4 +
+         size_t(TP_CW) * MT * 16 * 4 + 1024;
+}
+
+// The int8 consumer is the default; M5_GEMV_I8=0 selects the fp16 one.
+static bool tp_use_i8() {
+  static const bool on = [] {
+    const char* e = getenv("M5_GEMV_I8");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
   if (MT < 1 || MT > 8 || a.K % (64 * TP_UG)) return false;
-  if (tp_smem(MT, a.K, a.norm_w != nullptr) > 200 * 1024) return false;
+  if (tp_smem(MT, a.K, a.norm_w != nullptr, tp_use_i8()) > 200 * 1024) return false;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   // activation rows and the norm weight arrive by bulk copy: 16-byte aligned
   if (!al(a.x) || (a.ldx % 8) || (a.norm_w && !al(a.norm_w))) return false;
@@ -448,29 +527,29 @@ bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
   return encode_fn() != nullptr;
 }
 
-template <int MT, int EPI>
+template <int MT, int EPI, bool I8>
 static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* acc, int* cnt, int acc_rows, cudaStream_t st) {
-  const size_t smem = tp_smem(MT, a.K, a.norm_w != nullptr);
+  const size_t smem = tp_smem(MT, a.K, a.norm_w != nullptr, I8);
   static DeviceOnce once;  // the attribute belongs to each device's context
-  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
   int per_sm = 0;
-  M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tmap_kernel<MT, EPI>, TP_THREADS, smem));
+  M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tmap_kernel<MT, EPI, I8>, TP_THREADS, smem));
   const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
   const long long units = (long long)(vrows / 16) * (a.K / (64 * TP_UG));
   const long long max_ctas = (long long)std::max(1, per_sm) * sm_count();
   const int grid = (int)std::max(1LL, std::min(max_ctas, units));
-  M5_CUDA(launch_pdl(gemv_tmap_kernel<MT, EPI>, dim3(grid), dim3(TP_THREADS), smem, st, a, ts, acc, cnt, acc_rows));
+  M5_CUDA(launch_pdl(gemv_tmap_kernel<MT, EPI, I8>, dim3(grid), dim3(TP_THREADS), smem, st, a, ts, acc, cnt, acc_rows));
   return M5_OK;
 }
 
-template <int MT>
+template <int MT, bool I8>
 static int tp_launch_epi(const GemvArgs& a, int epi, const TmapSet& ts, float* acc, int* cnt, int rows,
                          cudaStream_t st) {
   switch (epi) {
-    case EPI_STORE: return tp_launch_t<MT, EPI_STORE>(a, ts, acc, cnt, rows, st);
-    case EPI_RESIDUAL: return tp_launch_t<MT, EPI_RESIDUAL>(a, ts, acc, cnt, rows, st);
-    case EPI_SWIGLU: return tp_launch_t<MT, EPI_SWIGLU>(a, ts, acc, cnt, rows, st);
-    case EPI_F32: return tp_launch_t<MT, EPI_F32>(a, ts, acc, cnt, rows, st);
+    case EPI_STORE: return tp_launch_t<MT, EPI_STORE, I8>(a, ts, acc, cnt, rows, st);
+    case EPI_RESIDUAL: return tp_launch_t<MT, EPI_RESIDUAL, I8>(a, ts, acc, cnt, rows, st);
+    case EPI_SWIGLU: return tp_launch_t<MT, EPI_SWIGLU, I8>(a, ts, acc, cnt, rows, st);
+    case EPI_F32: return tp_launch_t<MT, EPI_F32, I8>(a, ts, acc, cnt, rows, st);
   }
   return fail(M5_ERR_INVALID, "gemv_tmap: bad epilogue");
 }
@@ -484,15 +563,24 @@ int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, i
     int rc = make_maps(a.seg[i], a.K, ts, i);
     if (rc) return rc;
   }
+  const bool i8 = tp_use_i8();
   switch (MT) {
-    case 1: return tp_launch_epi<1>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 2: return tp_launch_epi<2>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 3: return tp_launch_epi<3>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 4: return tp_launch_epi<4>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 5: return tp_launch_epi<5>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 6: return tp_launch_epi<6>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 7: return tp_launch_epi<7>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 8: return tp_launch_epi<8>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 1: return i8 ? tp_launch_epi<1, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<1, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 2: return i8 ? tp_launch_epi<2, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<2, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 3: return i8 ? tp_launch_epi<3, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<3, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 4: return i8 ? tp_launch_epi<4, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<4, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 5: return i8 ? tp_launch_epi<5, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<5, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 6: return i8 ? tp_launch_epi<6, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<6, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 7: return i8 ? tp_launch_epi<7, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<7, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 8: return i8 ? tp_launch_epi<8, true>(a, epi, ts, acc, cnt, acc_rows, st)
+                 : tp_launch_epi<8, false>(a, epi, ts, acc, cnt, acc_rows, st);
   }
   return fail(M5_ERR_INVALID, "gemv_tmap: MT must be 1..8");
 }

@@ -364,10 +364,12 @@ def greedy(logits_row: torch.Tensor) -> int:
 
 def generate(model: Model, prompt: List[int], max_tokens: int, prefill_step: int = 2048,
              kv_bits: Optional[int] = 8, kv_group_size: int = 64, quantized_kv_start: int = 0,
-             cache: Optional[list] = None, return_logits: bool = False):
+             cache: Optional[list] = None, return_logits: bool = False, feed: Optional[List[int]] = None):
     """Greedy token loop of mlx-lm ``generate_step`` as the reference drives it.
 
-    Returns (tokens, cache[, per-step last-position logits]).
+    Returns (tokens, cache[, per-step last-position logits]).  ``feed``
+    (teacher forcing, for comparing two runs step by step) replaces the token
+    fed at decode step i with feed[i]; the returned tokens stay the greedy ones.
     """
     cache = cache if cache is not None else [KVCache() for _ in range(model.cfg.num_hidden_layers)]
     prompt = list(prompt)
@@ -380,10 +382,10 @@ def generate(model: Model, prompt: List[int], max_tokens: int, prefill_step: int
     maybe_quantize(cache, quantized_kv_start, kv_group_size, kv_bits)
     out, all_logits = [], []
     y = greedy(logits)
-    for _ in range(max_tokens):
+    for i in range(max_tokens):
         # generate_step evaluates the next step before yielding y, so the cache
         # ends holding prompt + max_tokens positions.
-        nxt = model([y], cache, last_only=True)[-1]
+        nxt = model([y if feed is None else int(feed[i])], cache, last_only=True)[-1]
         maybe_quantize(cache, quantized_kv_start, kv_group_size, kv_bits)
         out.append(y)
         all_logits.append(logits)

@@ -86,13 +86,24 @@ def _margins(logits):
 
 
 def _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal, cos_min=0.9995, cos_median=0.9999,
-           max_abs=0.05):
+           max_abs=0.05, after_tie=False):
     """North-star bar: logits cosine >= 0.9999 (asserted on the median step;
     every step must clear `cos_min`, the measured bf16 rounding-chaos floor of
     a random-init model), max-abs error <= 0.05, greedy tokens identical.
     Steps in `ties` (MoE router near-ties, where expert ids may legitimately
-    differ) are exempt from the per-step bounds but count in the median."""
+    differ) are exempt from the per-step bounds but count in the median.
+    With `after_tie`, every step from the first tie on is exempt from all
+    bounds: the tie step wrote a legitimately different KV entry, which every
+    later step attends over."""
     cos = torch.nn.functional.cosine_similarity(logits_f, logits_o, dim=-1)
+    if after_tie and ties:
+        first = min(ties)
+        ties = set(range(first, len(cos)))
+        cos, logits_f, logits_o = cos[:first], logits_f[:first], logits_o[:first]
+        toks_o, toks_f, free = toks_o[:first], toks_f[:first], free[:first]
+        n_equal = min(n_equal, first)
+        if first == 0:
+            return
     keep = [i for i in range(len(cos)) if i not in ties]
     print(f"logits cosine min {cos.min().item():.6f} median {cos.median().item():.6f}; "
           f"max-abs {(logits_f - logits_o).abs().max().item():.4f}; router-tie steps {sorted(ties)}")
@@ -206,9 +217,9 @@ def test_qwen3_06b_config():
     toks_o, logits_o, free, toks_f, logits_f, ties = _run(dev_model, ora, prompt, n, 2048, 8, 0)
     ora64 = Fp64Model(ora.cfg, ora.w)
     ora64._deq = ora._deq
-    toks_64, _, logits_64 = om.generate(ora64, prompt, n, prefill_step=2048, kv_bits=8, quantized_kv_start=0,
-                                        return_logits=True)
-    assert toks_64 == toks_o
+    # teacher-forced on the fp32 oracle's tokens, so every step compares like for like
+    _, _, logits_64 = om.generate(ora64, prompt, n, prefill_step=2048, kv_bits=8, quantized_kv_start=0,
+                                  return_logits=True, feed=toks_o)
     cos = torch.nn.functional.cosine_similarity
     floor = 1 - cos(logits_o, logits_64, dim=-1).min().item()
     dev64 = 1 - cos(logits_f, logits_64, dim=-1).min().item()

@@ -16,6 +16,16 @@ per step, max-abs <= 0.05, greedy tokens identical except at near-ties; the
 * Qwen3-235B-A22B layers: hidden 4096, 64 q / 4 kv heads, 128 experts, top-8,
   expert intermediate 1536, 4-bit KV.
 
+At the Qwen3-32B shape two correct fp32 implementations are already about
+0.05 apart in max-abs (the oracle with fp32 matmuls against the same oracle
+accumulating in fp64, measured in the test: logits of std ~1.4 and |max| ~6,
+where one bf16 step is 0.03), so that test holds the device to the cosine
+bar as stated, to 3x the oracle's own cosine distance from its fp64 twin, and
+to twice the twin's max-abs distance (at least 0.05).  The MoE slices exempt
+every step from the first router near-tie on (k-th and (k+1)-th expert
+probability within 1e-3 in the oracle): the tie step writes a legitimately
+different KV entry that later steps attend over.
+
 The vocabulary is cut to 4096 rows (the lm_head shape is covered by the
 Qwen3-0.6B test).  Weights come from the device generator (N(0, 0.02) bf16
 quantized by the device quantizer, which test_quant_gpu.py holds bit-exact to
@@ -26,6 +36,7 @@ import pytest
 import torch
 
 from oracle import model as om
+from parity_floor import Fp64Model
 from test_model_gpu import _check, _run
 
 pytestmark = pytest.mark.gpu
@@ -56,16 +67,30 @@ def _build(cfg, seed):
 def test_qwen3_32b_layers():
     dev, ora = _build(C3, seed=41)
     prompt = np.random.default_rng(41).integers(0, C3["vocab_size"], 70).tolist()
-    _check(*_run(dev, ora, prompt, 6, 64, 8, 0, yarn=4.0), n_equal=6)
+    n = 6
+    toks_o, logits_o, free, toks_f, logits_f, ties = _run(dev, ora, prompt, n, 64, 8, 0, yarn=4.0)
+    ora64 = Fp64Model(ora.cfg, ora.w)
+    ora64._deq = ora._deq
+    ora64.set_rope(4.0, 32768)
+    _, _, logits_64 = om.generate(ora64, prompt, n, prefill_step=64, kv_bits=8, quantized_kv_start=0,
+                                  return_logits=True, feed=toks_o)
+    cos = torch.nn.functional.cosine_similarity
+    floor_abs = (logits_o - logits_64).abs().max().item()
+    floor = 1 - cos(logits_o, logits_64, dim=-1).min().item()
+    dev64 = 1 - cos(logits_f, logits_64, dim=-1).min().item()
+    print(f"oracle32 vs oracle64: 1-cos {floor:.3e}, max-abs {floor_abs:.4f}; device vs oracle64 1-cos {dev64:.3e}")
+    assert dev64 <= 3 * floor + 1e-6, (dev64, floor)
+    _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal=n, max_abs=max(0.05, 2 * floor_abs))
 
 
 def test_qwen3_30b_a3b_layers():
     dev, ora = _build(C4, seed=42)
     prompt = np.random.default_rng(42).integers(0, C4["vocab_size"], 70).tolist()
-    _check(*_run(dev, ora, prompt, 6, 64, 8, 0), n_equal=6)
+    _check(*_run(dev, ora, prompt, 6, 64, 8, 0), n_equal=6, after_tie=True)
 
 
 def test_qwen3_235b_a22b_layers():
     dev, ora = _build(C5, seed=43)
     prompt = np.random.default_rng(43).integers(0, C5["vocab_size"], 12).tolist()
-    _check(*_run(dev, ora, prompt, 4, 8, 4, 0), n_equal=4, cos_min=0.999, cos_median=0.9995, max_abs=0.08)
+    _check(*_run(dev, ora, prompt, 4, 8, 4, 0), n_equal=4, cos_min=0.999, cos_median=0.9995, max_abs=0.08,
+           after_tie=True)
