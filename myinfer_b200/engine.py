@@ -171,13 +171,8 @@ def _load_model(opts: LoadOptions):
         raise EngineError(f"model path {path} not found (no network: pass a local MLX checkpoint directory)")
     config = json.loads((path / "config.json").read_text())
     args = ModelArgs.from_dict(config)
-    from safetensors.torch import load_file
-    weights: Dict[str, torch.Tensor] = {}
-    for f in sorted(path.glob("*.safetensors")):
-        for k, v in load_file(str(f)).items():
-            if v.dtype == torch.uint32:
-                v = v.view(torch.int32)
-            weights[k] = v.to(dev)
+    from .loader import load_mlx_checkpoint
+    weights = load_mlx_checkpoint(path, dev, tie_word_embeddings=args.tie_word_embeddings)
     model = Model(args, weights, dev, max_tokens=min(opts.prefill_step, 2048))
     tok_files = [f for f in ("tokenizer.json", "tokenizer_config.json", "tokenizer.model", "vocab.json")
                  if (path / f).exists()]

@@ -132,3 +132,31 @@ def test_prefix_reuse_matches_oracle(engine):
     toks_o, logits_o = _oracle_greedy(engine.model, follow, 10)
     _agree_with_oracle(reused, toks_o, logits_o)
     _agree_with_oracle(fresh, toks_o, logits_o)
+
+
+def test_engine_loads_mlx_checkpoint_directory(tmp_path):
+    """Engine.load on an MLX-style checkpoint directory (weights written by
+    loader.save_mlx_checkpoint in two files with an index, no tokenizer files)
+    generates the oracle's greedy tokens for those weights."""
+    import numpy as np
+    import warnings
+    from myinfer_b200.engine import Engine, LoadOptions
+    from myinfer_b200.loader import save_mlx_checkpoint
+    from oracle import model as om
+    cfg = dict(TINY, quantization={"group_size": 64, "bits": 4})
+    host = om.generate_weights(om.Config.from_dict(cfg), seed=9)
+    w = {k: torch.from_numpy(v.view(np.int32)) if v.dtype == np.uint32 else
+         torch.from_numpy(v.view(np.int16)).view(torch.bfloat16) for k, v in host.items()}
+    save_mlx_checkpoint(tmp_path, cfg, w, files=2)
+    eng = Engine()
+    with warnings.catch_warnings(record=True):
+        eng.load(LoadOptions(model=str(tmp_path), kv_bits=8, quantized_kv_start=0, memory_budget_gb=4.0,
+                             prefill_step=64, seed=5))
+    try:
+        prompt = list(np.random.default_rng(4).integers(3, 250, 40))
+        _run(eng, prompt, 8, use_prefix_cache=False)
+        toks_o, _, logits_o = om.generate(om.Model(om.Config.from_dict(cfg), host), prompt, 8, prefill_step=64,
+                                          kv_bits=8, quantized_kv_start=0, return_logits=True)
+        _agree_with_oracle(list(eng.last_tokens), toks_o, logits_o)
+    finally:
+        eng.unload()
