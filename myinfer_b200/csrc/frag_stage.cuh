@@ -20,7 +20,8 @@ namespace m5 {
 // chosen so the token's largest |x| lands in [2^14, 2^15): exact for every
 // value above max|x| * 2^-29 (bf16 has 8 significant bits, fp16 11), and
 // 2^-e_t is written to xinv[t] for the caller to undo after the dot product.
-template <int MT, int NT, bool FP16 = false>
+// CG: read x through L2 only (rows another CTA of the same launch wrote).
+template <int MT, int NT, bool FP16 = false, bool CG = false>
 __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t ldx, int K,
                                            const bf16* __restrict__ norm_w, float eps, uint32_t* xf, float* xg,
                                            float* red, int bar, float* xinv = nullptr) {
@@ -44,7 +45,7 @@ __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t l
         uint4 v[CH];
 #pragma unroll
         for (int k = 0; k < CH; ++k)
-          if (c0 + k * NT < K8) v[k] = xr[c0 + k * NT];
+          if (c0 + k * NT < K8) v[k] = CG ? __ldcg(xr + c0 + k * NT) : xr[c0 + k * NT];
 #pragma unroll
         for (int k = 0; k < CH; ++k)
           if (c0 + k * NT < K8) {
@@ -71,7 +72,7 @@ __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t l
 #pragma unroll
       for (int k = 0; k < CH; ++k)
         if (c0 + k * NT < K8) {
-          v[k] = xr[c0 + k * NT];
+          v[k] = CG ? __ldcg(xr + c0 + k * NT) : xr[c0 + k * NT];
           if (norm_w) wv[k] = nw[c0 + k * NT];
         }
 #pragma unroll

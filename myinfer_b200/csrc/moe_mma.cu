@@ -161,19 +161,18 @@ __device__ __forceinline__ void mx_range(long long steps, long long& b, long lon
   e = steps * (wid + 1) / nw;
 }
 
-__global__ void __launch_bounds__(MX_W * 32, 2) moe_gu_mma_kernel(const MoeArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
+// Gate/up of the token's local slots (nl of them, slot / local expert lists in
+// shared memory) over this CTA's share of the (slot, 8-row tile, group) steps.
+__device__ __forceinline__ void mx_gu_body(const MoeArgs& a, int nl, const int* s_slot, const int* s_eid,
+                                           unsigned char* smem_raw) {
   const int H = a.H, I = a.I, NG = H >> 6;
+  const int tpe = I / 8;  // tiles per expert
   uint32_t* xf = reinterpret_cast<uint32_t*>(smem_raw);  // [NG][4][8] bf16 pairs
   float* xg = reinterpret_cast<float*>(xf + NG * 32);    // [NG]
   float* red = xg + NG;                                  // [33]
-  const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
-  if (nl == 0) return;
+  // every thread of the CTA stages (the staging synchronises the CTA), before
+  // the per-warp step ranges let idle warps leave
   stage_frag<1, MX_W * 32>(a.x, H, H, a.norm_w, a.eps, xf, xg, red, 0);
-  const int tpe = I / 8;  // tiles per expert
   long long sb, se;
   mx_range((long long)nl * tpe * NG, sb, se);
   if (sb >= se) return;
@@ -207,6 +206,7 @@ __global__ void __launch_bounds__(MX_W * 32, 2) moe_gu_mma_kernel(const MoeArgs 
         const int ls = tile / tpe, rt = tile % tpe;
         a.act[size_t(s_slot[ls]) * I + rt * 8 + lane] = f2bf(rbf(gv * sg) * uv);
       }
+      __threadfence();
       __syncwarp();
       if (lane == 0) a.cnt[tile] = 0;
     }
@@ -214,24 +214,18 @@ __global__ void __launch_bounds__(MX_W * 32, 2) moe_gu_mma_kernel(const MoeArgs 
   mx_walk<1>(sb, se, H, xf, xg, row_of, flush);
 }
 
-template <int MT>
-__global__ void __launch_bounds__(MX_W * 32, 2) moe_down_mma_kernel(const MoeArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
+// Down projection of the nl local slots, the k SwiGLU rows staged as the MMA's
+// B columns (CG: read through L2, rows written by other CTAs of this launch),
+// then the score-weighted slot combine into h (or the fp32 partial).
+template <int MT, bool CG>
+__device__ __forceinline__ void mx_down_body(const MoeArgs& a, int nl, const int* s_slot, const int* s_eid,
+                                             unsigned char* smem_raw) {
   const int H = a.H, I = a.I, NG = I >> 6;
-  const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
-  if (nl == 0) {  // no expert of this token is local: this rank's share is zero
-    if (a.partial)
-      for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < H; n += gridDim.x * blockDim.x) a.partial[n] = 0.f;
-    return;
-  }
+  const int tpe = H / 16;
   uint32_t* xf = reinterpret_cast<uint32_t*>(smem_raw);  // [MT][NG][4][8]
   float* xg = reinterpret_cast<float*>(xf + MT * NG * 32);  // [MT][NG]
   float* red = xg + MT * NG;
-  stage_frag<MT, MX_W * 32>(a.act, I, I, nullptr, 0.f, xf, xg, red, 0);
-  const int tpe = H / 16;
+  stage_frag<MT, MX_W * 32, false, CG>(a.act, I, I, nullptr, 0.f, xf, xg, red, 0);  // whole CTA, as above
   long long sb, se;
   mx_range((long long)nl * tpe * NG, sb, se);
   if (sb >= se) return;
@@ -257,7 +251,7 @@ __global__ void __launch_bounds__(MX_W * 32, 2) moe_down_mma_kernel(const MoeArg
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) return;
     __threadfence();
-    const float sj = bf2f(a.scores[j]);
+    const float sj = bf2f(__ldcg(a.scores + j));
     if (lane < 16) {
       float* p = &acc[base + lane];
       const float y = rbf(__ldcg(p));
@@ -289,6 +283,31 @@ __global__ void __launch_bounds__(MX_W * 32, 2) moe_down_mma_kernel(const MoeArg
     if (lane == 0) a.ncnt[nb] = 0;
   };
   mx_walk<MT>(sb, se, I, xf, xg, row_of, flush);
+}
+
+__global__ void __launch_bounds__(MX_W * 32, 2) moe_gu_mma_kernel(const MoeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
+  const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
+  if (nl == 0) return;
+  mx_gu_body(a, nl, s_slot, s_eid, smem_raw);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(MX_W * 32, 2) moe_down_mma_kernel(const MoeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
+  const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
+  if (nl == 0) {  // no expert of this token is local: this rank's share is zero
+    if (a.partial)
+      for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < a.H; n += gridDim.x * blockDim.x) a.partial[n] = 0.f;
+    return;
+  }
+  mx_down_body<MT, false>(a, nl, s_slot, s_eid, smem_raw);
 }
 
 // Softmax (fp32, rounded to bf16) and top-k of the E router logits by one
@@ -403,6 +422,7 @@ int moe_router_topk_launch(const MoeRouterArgs& a, cudaStream_t st) {
 }
 
 static size_t mx_smem(int MT, int K) { return size_t(MT) * (K / 64) * 32 * 4 + size_t(MT) * (K / 64) * 4 + 33 * 4; }
+
 
 bool moe_mma_eligible(const MoeArgs& a) {
   return a.T == 1 && a.k == MX_KMAX && a.acc && a.cnt && a.ybuf && a.ncnt && a.H % 64 == 0 && a.I % 64 == 0 &&

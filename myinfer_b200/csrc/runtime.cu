@@ -113,6 +113,7 @@ constexpr int kGemmMinRows = 16;
 // tokens on (below, the per-token expert GEMVs: too few rows per expert).
 constexpr int kMoeGroupedMinTokens = 64;
 
+
 static bool parse_layer(const char* name, int& idx, const char*& rest) {
   const char* p = "model.layers.";
   if (strncmp(name, p, strlen(p)) != 0) return false;
@@ -556,11 +557,11 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
       g.norm_w = ly.post_norm;
       g.eps = c.rms_norm_eps;
       attach(m, g);
+      MoeRouterArgs ra{m->h,          ly.post_norm,      c.rms_norm_eps,  ly.router.w,
+                       ly.router.s,   ly.router.b,       H,               c.num_experts,
+                       c.experts_per_tok, c.norm_topk_prob, m->rlogits,   m->rids,
+                       m->rscores,    m->moe_ncnt + H / 16};
       if (T == 1 && m->moe_ncnt && c.num_experts <= 256 && H % 256 == 0) {  // one launch for a decode token
-        MoeRouterArgs ra{m->h,          ly.post_norm,      c.rms_norm_eps,  ly.router.w,
-                         ly.router.s,   ly.router.b,       H,               c.num_experts,
-                         c.experts_per_tok, c.norm_topk_prob, m->rlogits,   m->rids,
-                         m->rscores,    m->moe_ncnt + H / 16};
         if ((rc = moe_router_topk_launch(ra, st))) return rc;
       } else {
         if ((rc = linear_auto(m, g, T, EPI_STORE, st))) return rc;

@@ -235,6 +235,10 @@ class Model:
         self.w = weights
         self._deq: Dict[str, torch.Tensor] = {}
         self.route_log: Optional[list] = None  # set to a list to record router margins
+        # attention in key blocks of this size at every length (the blocked
+        # loop of attention.py:29-103 without its dense fallback); None = as
+        # the reference dispatches
+        self.attn_block: Optional[int] = None
         self.set_rope(yarn_factor, native_ctx)
 
     def set_rope(self, factor: float, native: int = 32768):
@@ -286,11 +290,17 @@ class Model:
         mask = "causal" if L > 1 else None
         scale = D ** -0.5
         if isinstance(cache, QuantizedKVCache):
-            o = blocked_quantized_sdpa(q[None], tuple(a[None] for a in keys),
-                                       tuple(a[None] for a in values), scale, mask,
-                                       cache.group_size, cache.bits)
+            kq, vq = tuple(a[None] for a in keys), tuple(a[None] for a in values)
+            gs, bits = cache.group_size, cache.bits
         else:
-            o = dense_quantized_sdpa(q[None], keys[None], values[None], scale, mask)
+            kq, vq, gs, bits = keys[None], values[None], 64, 8
+        if self.attn_block:
+            o = blocked_quantized_sdpa(q[None], kq, vq, scale, mask, gs, bits, score_budget_bytes=1,
+                                       min_block=self.attn_block, force_blocks=True)
+        elif isinstance(cache, QuantizedKVCache):
+            o = blocked_quantized_sdpa(q[None], kq, vq, scale, mask, gs, bits)
+        else:
+            o = dense_quantized_sdpa(q[None], kq, vq, scale, mask)
         o = o[0].transpose(0, 1).reshape(L, Hq * D)
         return self.linear(o, p + "o_proj")
 

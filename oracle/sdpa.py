@@ -91,7 +91,11 @@ def dense_quantized_sdpa(queries: torch.Tensor, keys, values, scale: float,
 def blocked_quantized_sdpa(queries: torch.Tensor, keys, values, scale: float,
                            mask: Union[None, str, torch.Tensor], group_size: int = 64,
                            bits: int = 8, score_budget_bytes: int = SCORE_BUDGET_BYTES,
-                           min_block: int = MIN_BLOCK, dtype: str = "bf16") -> torch.Tensor:
+                           min_block: int = MIN_BLOCK, dtype: str = "bf16",
+                           force_blocks: bool = False) -> torch.Tensor:
+    """``force_blocks`` runs the block loop even where attention.py:42-45 falls
+    back to the dense op (short caches, single queries): the same algorithm
+    at any length, for measuring how far its rounding points move a result."""
     rb = _rounder(dtype)
     B, Hq, L, D = queries.shape
     K = dequant_kv(keys, group_size, bits)
@@ -99,7 +103,7 @@ def blocked_quantized_sdpa(queries: torch.Tensor, keys, values, scale: float,
     S = K.shape[-2]
     per_key = B * Hq * L * 4 * 3
     block = max(min_block, score_budget_bytes // max(per_key, 1))
-    if S <= block or L == 1:
+    if not force_blocks and (S <= block or L == 1):
         return dense_quantized_sdpa(queries, keys, values, scale, mask, group_size, bits, dtype)
     Hkv = K.shape[-3]
     rep = Hq // Hkv

@@ -8,7 +8,12 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-TINY = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=2,
+# Hidden and intermediate sizes of 1024: every decode GEMV tile (16 rows x K)
+# stays inside one CTA and reduces in shared memory in a fixed order, so two
+# runs of the same request are bitwise equal and a seed reproduces its
+# sampled text.  (Where a tile is split over CTAs the partial sums meet in
+# fp32 atomics in no fixed order, and logits may differ in the last bit.)
+TINY = dict(model_type="qwen3", hidden_size=1024, num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=2,
             head_dim=128, intermediate_size=1024, vocab_size=4096, tie_word_embeddings=False,
             max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6)
 

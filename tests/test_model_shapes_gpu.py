@@ -16,14 +16,19 @@ per step, max-abs <= 0.05, greedy tokens identical except at near-ties; the
 * Qwen3-235B-A22B layers: hidden 4096, 64 q / 4 kv heads, 128 experts, top-8,
   expert intermediate 1536, 4-bit KV.
 
-At the Qwen3-32B shape two correct fp32 implementations are already about
-0.05 apart in max-abs (the oracle with fp32 matmuls against the same oracle
-accumulating in fp64, measured in the test: logits of std ~1.4 and |max| ~6,
-where one bf16 step is 0.03), so that test holds the device to the cosine
-bar as stated, to 3x the oracle's own cosine distance from its fp64 twin, and
-to twice the twin's max-abs distance (at least 0.05).  The MoE slices exempt
-every step from the first router near-tie on (k-th and (k+1)-th expert
-probability within 1e-3 in the oracle): the tie step writes a legitimately
+Bars.  The reference computes attention two ways (attention.py:42-45): the
+dense op for short caches and single queries, the blocked loop otherwise;
+the device's split-KV kernels round p to bf16 per key tile, like the blocked
+loop.  At these shapes the two reference paths are themselves ~0.08 apart in
+max-abs (logits of std ~1.4 and |max| ~6, one bf16 step 0.03) and 8e-5 in
+1-cos.  Each test therefore measures a floor: the oracle against its twin
+with fp64 matmul accumulation and the blocked loop at every length (64-key
+blocks), teacher-forced on the same tokens.  The device is held to the north
+star's median cosine (0.9999 with 8-bit KV; 0.9995 with 4-bit KV, where one
+bf16 step of a key flips a 4-bit code), to twice the floor's 1-cos and to
+1.5 times its max-abs (at least 0.05 / 0.08), per step.  The MoE slices use
+only the steps before the oracle's first router near-tie (k-th and (k+1)-th
+expert probability within 1e-3): the tie step writes a legitimately
 different KV entry that later steps attend over.
 
 The vocabulary is cut to 4096 rows (the lm_head shape is covered by the
@@ -64,33 +69,53 @@ def _build(cfg, seed):
     return Model(a, w, "cuda", max_tokens=64), om.Model(om.Config.from_dict(cfg), host)
 
 
+def _floor_twin(ora, prompt, n, prefill_step, kv_bits, toks_o, yarn=None):
+    tw = Fp64Model(ora.cfg, ora.w)
+    tw._deq = ora._deq
+    tw.attn_block = 64
+    if yarn:
+        tw.set_rope(yarn, 32768)
+    _, _, lt = om.generate(tw, prompt, n, prefill_step=prefill_step, kv_bits=kv_bits, quantized_kv_start=0,
+                           return_logits=True, feed=toks_o)
+    return lt
+
+
+def _check_floor(run, lt, n, kv_bits):
+    toks_o, logits_o, free, toks_f, logits_f, ties = run
+    keep = min(ties) if ties else n  # steps before the first router near-tie
+    assert keep > 0, "router near-tie at the first step: nothing comparable"
+    cos = torch.nn.functional.cosine_similarity
+    floor = 1 - cos(logits_o[:keep], lt[:keep], dim=-1).min().item()
+    floor_abs = (logits_o[:keep] - lt[:keep]).abs().max().item()
+    dev = 1 - cos(logits_o[:keep], logits_f[:keep], dim=-1).min().item()
+    print(f"floor (oracle vs fp64 + blocked twin): 1-cos {floor:.3e}, max-abs {floor_abs:.4f}; "
+          f"device 1-cos {dev:.3e}; steps compared {keep}")
+    assert dev <= 2 * floor + 1e-6, (dev, floor)
+    four = kv_bits == 4
+    _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal=n, cos_min=0.999 if four else 0.9995,
+           cos_median=0.9995 if four else 0.9999, max_abs=max(0.08 if four else 0.05, 1.5 * floor_abs),
+           after_tie=True)
+
+
 def test_qwen3_32b_layers():
     dev, ora = _build(C3, seed=41)
     prompt = np.random.default_rng(41).integers(0, C3["vocab_size"], 70).tolist()
     n = 6
-    toks_o, logits_o, free, toks_f, logits_f, ties = _run(dev, ora, prompt, n, 64, 8, 0, yarn=4.0)
-    ora64 = Fp64Model(ora.cfg, ora.w)
-    ora64._deq = ora._deq
-    ora64.set_rope(4.0, 32768)
-    _, _, logits_64 = om.generate(ora64, prompt, n, prefill_step=64, kv_bits=8, quantized_kv_start=0,
-                                  return_logits=True, feed=toks_o)
-    cos = torch.nn.functional.cosine_similarity
-    floor_abs = (logits_o - logits_64).abs().max().item()
-    floor = 1 - cos(logits_o, logits_64, dim=-1).min().item()
-    dev64 = 1 - cos(logits_f, logits_64, dim=-1).min().item()
-    print(f"oracle32 vs oracle64: 1-cos {floor:.3e}, max-abs {floor_abs:.4f}; device vs oracle64 1-cos {dev64:.3e}")
-    assert dev64 <= 3 * floor + 1e-6, (dev64, floor)
-    _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal=n, max_abs=max(0.05, 2 * floor_abs))
+    run = _run(dev, ora, prompt, n, 64, 8, 0, yarn=4.0)
+    _check_floor(run, _floor_twin(ora, prompt, n, 64, 8, run[0], yarn=4.0), n, 8)
 
 
 def test_qwen3_30b_a3b_layers():
     dev, ora = _build(C4, seed=42)
     prompt = np.random.default_rng(42).integers(0, C4["vocab_size"], 70).tolist()
-    _check(*_run(dev, ora, prompt, 6, 64, 8, 0), n_equal=6, after_tie=True)
+    n = 6
+    run = _run(dev, ora, prompt, n, 64, 8, 0)
+    _check_floor(run, _floor_twin(ora, prompt, n, 64, 8, run[0]), n, 8)
 
 
 def test_qwen3_235b_a22b_layers():
     dev, ora = _build(C5, seed=43)
     prompt = np.random.default_rng(43).integers(0, C5["vocab_size"], 12).tolist()
-    _check(*_run(dev, ora, prompt, 4, 8, 4, 0), n_equal=4, cos_min=0.999, cos_median=0.9995, max_abs=0.08,
-           after_tie=True)
+    n = 4
+    run = _run(dev, ora, prompt, n, 8, 4, 0)
+    _check_floor(run, _floor_twin(ora, prompt, n, 8, 4, run[0]), n, 4)
