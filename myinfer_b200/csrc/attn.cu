@@ -392,8 +392,13 @@ int attn_launch(const AttnArgs& a, cudaStream_t stream) {
     // prefill: 128 rows per CTA; the caller's scratch holds a.nsplit partials per row
     AttnArgs p = a;
     const int S_max = a.d_S ? a.k.head_stride : a.S_host;
-    attn_pf_plan(a, (int)std::min<int64_t>(S_max, 1 << 30), std::max(1, a.nsplit), p.QB, p.nsplit);
-    if ((rc = attn_pf_launch(p, stream))) return rc;
+    if (attn_tc_eligible(a)) {
+      attn_tc_plan(a, (int)std::min<int64_t>(S_max, 1 << 30), std::max(1, a.nsplit), p.QB, p.nsplit);
+      if ((rc = attn_tc_launch(p, stream))) return rc;
+    } else {
+      attn_pf_plan(a, (int)std::min<int64_t>(S_max, 1 << 30), std::max(1, a.nsplit), p.QB, p.nsplit);
+      if ((rc = attn_pf_launch(p, stream))) return rc;
+    }
     if (p.nsplit > 1) {
       const int rows = a.B * a.Hq * a.L;
       M5_CUDA(launch_pdl(attn_combine_kernel, dim3(rows, 4), dim3(CMB_WARPS * 32), 0, stream, p.part_o, p.part_ml,

@@ -1,0 +1,583 @@
+// Prefill flash attention over an 8/4-bit KV cache on the fifth-generation
+// tensor cores (kernel K4p, tcgen05 + TMEM): chunks of L queries, rows = GQA
+// group x queries = 128 per CTA, one kv head and one key range per CTA.
+//
+// Roles (one CTA per SM, 320 threads):
+//   warp 9      producer: 1-D bulk copies of 64-key tiles of packed K / V and
+//               their bf16 scales / biases into a 3-stage ring;
+//   warps 4-7   dequant: the tile's codes become exact fp16 values in shared
+//               memory, written in the 128-byte-swizzled K-major layout the
+//               MMA reads (K as [key][dim], V transposed to [dim][key]), one
+//               64-dim scale group per operand; the tile's scales and biases
+//               are copied beside them so the packed slot frees at once;
+//   warp 8      MMA issuer (one thread): per tile and scale group g
+//                 S_g[128 x 64 keys] = Q_g (TMEM, fp16) * K_g^T   (4 MMAs)
+//               into one of two S buffers, and after the softmax
+//                 O[:, 64g..] += P'_g (TMEM, fp16) * V_g           (4 MMAs)
+//   warps 0-3   softmax: thread = query row = TMEM lane.  Per key
+//                 s = rb(kscale_0 * S_0 + kbias_0 * sum(q_0)
+//                      + kscale_1 * S_1 + kbias_1 * sum(q_1))
+//               (the dequantized dot product, rounded to bf16 like
+//               attention.py:66-69), causal / range mask, fp32 online softmax
+//               with the running max of the row (no shuffles: the row is the
+//               thread's), p rounded to bf16 for PV (attention.py:87-90) with
+//               the value scale folded in, P'_g = rb(p) * vscale_g * 2^6 in
+//               fp16, the value bias as an fp32 side sum, fp32 p in the
+//               denominator; O in TMEM is rescaled in place when a row's max
+//               moves.  The arithmetic is the mma.sync prefill kernel's
+//               (attn_pf.cu); only the data movement differs.
+// TMEM columns: S buffers [0,128) [128,256) (group g at +64g), O [256,384),
+// Q [384,448) (fp16 pairs), P' [448,512).  Every mbarrier wait is bounded; a
+// timeout sets a CTA-wide failure flag that ends every role, records a device
+// error and still frees TMEM.
+#include <algorithm>
+#include <cmath>
+
+#include "attn.cuh"
+#include "tcgen05.cuh"
+
+namespace m5 {
+
+static __device__ int g_attn_tc_err = 0;
+
+namespace atc {
+
+constexpr int TK = 64;            // keys per tile
+constexpr int STAGES = 3;         // packed ring
+constexpr int ROWS = 128;         // query rows per CTA (MMA M)
+constexpr int THREADS = 10 * 32;
+constexpr float PSCALE = 64.f;    // p * vscale kept in fp16 scaled by 2^6
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t S_COL = 0, O_COL = 256, Q_COL = 384, P_COL = 448;
+
+template <int BITS>
+struct Packed {  // one ring stage: K codes, K scales, K biases, V codes, V scales, V biases
+  static constexpr int KROW = 128 * BITS / 8;
+  static constexpr int K_OFF = 0;
+  static constexpr int KS_OFF = K_OFF + TK * KROW;
+  static constexpr int KB_OFF = KS_OFF + TK * 4;
+  static constexpr int V_OFF = KB_OFF + TK * 4;
+  static constexpr int VS_OFF = V_OFF + TK * KROW;
+  static constexpr int VB_OFF = VS_OFF + TK * 4;
+  static constexpr int STAGE = (VB_OFF + TK * 4 + 1023) / 1024 * 1024;
+};
+
+// fp16 operand buffer (two per CTA): K groups 0/1 then V^T groups 0/1, 8 KB
+// each (64 rows x 128 bytes, 128-byte swizzle), then the tile's scales and
+// biases as fp32 [4][64] (kscale g0/g1 interleaved per key, see below).
+constexpr int OP_BYTES = 8192;
+constexpr int OP_K = 0, OP_V = 2 * OP_BYTES;
+constexpr int SB_OFF = 4 * OP_BYTES;        // float kscale[64][2], kbias[64][2], vscale[64][2], vbias[64][2]
+constexpr int OPBUF = SB_OFF + 4 * TK * 2 * 4;
+
+template <int BITS>
+constexpr size_t smem_bytes() {
+  return 1024 + size_t(STAGES) * Packed<BITS>::STAGE + 2 * size_t(OPBUF) + 256;
+}
+
+// Byte offset of 16-byte chunk j of row n in a 128-byte-swizzled K-major tile.
+__device__ __forceinline__ uint32_t sw128(int n, int j) {
+  return uint32_t((n >> 3) * 1024 + (n & 7) * 128 + ((j ^ (n & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t hsub1024(uint32_t x) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0x64006400u));
+  return r;
+}
+// fp16 pair of the 8-bit codes at bytes (i, i + 1) of w, exactly
+__device__ __forceinline__ uint32_t c8(uint32_t w, int i) {
+  return hsub1024(__byte_perm(w, 0x64u, i == 0 ? 0x4140 : 0x4342));
+}
+// fp16 pair of two 4-bit / 8-bit codes given as small integers
+__device__ __forceinline__ uint32_t cpair(uint32_t lo, uint32_t hi) {
+  return hsub1024(0x64006400u | lo | (hi << 16));
+}
+// Generic-proxy shared-memory writes become visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Instruction descriptor of kind::f16 with fp16 A and B (K-major), fp32 D.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint64_t atc_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait by one thread (~2 s), failure shared through `fail`.
+__device__ __forceinline__ bool wait1(uint64_t* bar, uint32_t par, volatile int* fail) {
+  if (mbar_try_wait_fast(bar, par)) return true;
+  const uint64_t t0 = atc_now();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_fast(bar, par)) return true;
+    if (*fail) return false;
+    if ((i & 255) == 0 && atc_now() - t0 > 2000000000ull) break;
+  }
+  *fail = 1;
+  atomicExch(&g_attn_tc_err, M5_DEV_ERR_WAIT_TIMEOUT);
+  return false;
+}
+// Bounded wait by a whole warp with a warp-uniform result.
+__device__ __forceinline__ bool waitw(uint64_t* bar, uint32_t par, volatile int* fail, int lane) {
+  bool ok = true;
+  if (lane == 0) ok = wait1(bar, par, fail);
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_try_wait_fast(bar, par);  // acquire for every lane (the phase is complete)
+  return ok;
+}
+
+
+template <int BITS>
+__global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
+  using PK = Packed<BITS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;
+  uint8_t* opb = ring + size_t(STAGES) * PK::STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(opb + 2 * size_t(OPBUF));
+  uint64_t* full = bars;
+  uint64_t* empty = full + STAGES;
+  uint64_t* op_full = empty + STAGES;
+  uint64_t* op_empty = op_full + 2;
+  uint64_t* s_full = op_empty + 2;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* q_ready = pv_done + 1;
+  uint64_t* mma_idle = q_ready + 1;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_fail;
+  volatile int* fail = &s_fail;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x;
+  const int b = blockIdx.z / a.Hkv, hk = blockIdx.z % a.Hkv;
+  const int rep = a.Hq / a.Hkv;
+  const int S = a.d_S ? (*a.d_S + a.S_add) : a.S_host;
+  const int q0 = blockIdx.y * a.QB;
+  const int nq = min(a.QB, a.L - q0);
+  const int rows = nq * rep;
+  const bool causal = a.mask_kind == M5_MASK_CAUSAL;
+  int chunk = a.chunk;
+  if (chunk <= 0) chunk = ((S + a.nsplit - 1) / a.nsplit + TK - 1) / TK * TK;
+  const int k_begin = split * chunk;
+  int k_end = min(S, k_begin + chunk);
+  if (causal) k_end = min(k_end, S - a.L + q0 + nq);
+  const int ntiles = k_end > k_begin ? (k_end - k_begin + TK - 1) / TK : 0;
+
+  if (tid == 0) {
+    s_fail = 0;
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&op_full[i], 4);
+      mbar_init(&op_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(q_ready, 4);
+    mbar_init(mma_idle, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&s_tmem, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      const size_t kbase = size_t(b) * a.k.batch_stride + size_t(hk) * a.k.head_stride;
+      const size_t vbase = size_t(b) * a.v.batch_stride + size_t(hk) * a.v.head_stride;
+      const uint8_t* kd = reinterpret_cast<const uint8_t*>(a.k.data);
+      const uint8_t* vd = reinterpret_cast<const uint8_t*>(a.v.data);
+      const uint8_t* ksd = reinterpret_cast<const uint8_t*>(a.k.scales);
+      const uint8_t* kbd = reinterpret_cast<const uint8_t*>(a.k.biases);
+      const uint8_t* vsd = reinterpret_cast<const uint8_t*>(a.v.scales);
+      const uint8_t* vbd = reinterpret_cast<const uint8_t*>(a.v.biases);
+      int issued = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        const int st = t % STAGES;
+        if (!wait1(&empty[st], ((t / STAGES) & 1) ^ 1, fail)) break;
+        const int key0 = k_begin + t * TK;
+        const int nk = (min(TK, k_end - key0) + 3) & ~3;  // whole 16-byte scale rows
+        uint8_t* sb = ring + size_t(st) * PK::STAGE;
+        const uint32_t rowb = nk * PK::KROW, sclb = nk * 4;
+        mbar_arrive_expect_tx(&full[st], 2 * rowb + 4 * sclb);
+        bulk_g2s(sb + PK::K_OFF, kd + (kbase + key0) * PK::KROW, rowb, &full[st]);
+        bulk_g2s(sb + PK::KS_OFF, ksd + (kbase + key0) * 4, sclb, &full[st]);
+        bulk_g2s(sb + PK::KB_OFF, kbd + (kbase + key0) * 4, sclb, &full[st]);
+        bulk_g2s(sb + PK::V_OFF, vd + (vbase + key0) * PK::KROW, rowb, &full[st]);
+        bulk_g2s(sb + PK::VS_OFF, vsd + (vbase + key0) * 4, sclb, &full[st]);
+        bulk_g2s(sb + PK::VB_OFF, vbd + (vbase + key0) * 4, sclb, &full[st]);
+        issued = t + 1;
+      }
+      // the copies in flight land before the CTA may exit
+      for (int t = std::max(0, issued - STAGES); t < issued; ++t) (void)wait1(&full[t % STAGES], (t / STAGES) & 1, fail);
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(ROWS, TK);
+      bool ok = ntiles > 0 && wait1(q_ready, 0, fail);
+      auto issue_s = [&](int t) -> bool {
+        const int bb = t & 1;
+        if (!wait1(&op_full[bb], (t >> 1) & 1, fail) || !wait1(&s_empty[bb], ((t >> 1) & 1) ^ 1, fail)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_K + g * OP_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_ts(tmem + S_COL + 128u * bb + 64u * g, tmem + Q_COL + 32u * g + 8u * kk, bdesc + 2u * kk, idesc,
+                      kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[bb]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int t = 0; t < ntiles && ok; ++t) {
+        if (t + 1 < ntiles && !(ok = issue_s(t + 1))) break;
+        if (!(ok = wait1(p_full, t & 1, fail))) break;
+        tc_fence_after();
+        const int bb = t & 1;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_V + g * OP_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_ts(tmem + O_COL + 64u * g, tmem + P_COL + 32u * g + 8u * kk, bdesc + 2u * kk, idesc,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(pv_done);
+        tc_commit(&op_empty[bb]);
+      }
+      // every MMA issued has completed before TMEM may be freed
+      tc_commit(mma_idle);
+      (void)wait1(mma_idle, 0, fail);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- dequant
+    const int d = tid - 128;  // 0..127
+    for (int t = 0; t < ntiles; ++t) {
+      const int st = t % STAGES, bb = t & 1;
+      if (!waitw(&full[st], (t / STAGES) & 1, fail, lane) || !waitw(&op_empty[bb], ((t >> 1) & 1) ^ 1, fail, lane))
+        break;
+      const uint8_t* sb = ring + size_t(st) * PK::STAGE;
+      uint8_t* ob = opb + size_t(bb) * OPBUF;
+      // K: 64 keys x 2 groups x 8 chunks of 8 dims
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = d + 128 * i, n = c >> 4, g = (c >> 3) & 1, j = c & 7;
+        uint4 o;
+        if constexpr (BITS == 8) {
+          const uint2 w = *reinterpret_cast<const uint2*>(sb + PK::K_OFF + n * 128 + 64 * g + 8 * j);
+          o = make_uint4(c8(w.x, 0), c8(w.x, 1), c8(w.y, 0), c8(w.y, 1));
+        } else {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(sb + PK::K_OFF + n * 64 + 32 * g + 4 * j);
+          o = make_uint4(cpair(w & 15u, (w >> 4) & 15u), cpair((w >> 8) & 15u, (w >> 12) & 15u),
+                         cpair((w >> 16) & 15u, (w >> 20) & 15u), cpair((w >> 24) & 15u, w >> 28));
+        }
+        *reinterpret_cast<uint4*>(ob + OP_K + g * OP_BYTES + sw128(n, j)) = o;
+      }
+      // V^T: row = dim of the group, chunk j = keys 8j .. 8j + 7
+      if constexpr (BITS == 8) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int task = d + 128 * i, kb = task >> 5, dw = task & 31;  // 8 keys x dims 4dw .. 4dw + 3
+          uint32_t w[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) w[q] = *reinterpret_cast<const uint32_t*>(sb + PK::V_OFF + (8 * kb + q) * 128 + 4 * dw);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int dim = 4 * dw + e, g = dim >> 6, n = dim & 63;
+            uint32_t cd[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) cd[q] = (w[q] >> (8 * e)) & 0xFFu;
+            const uint4 o = make_uint4(cpair(cd[0], cd[1]), cpair(cd[2], cd[3]), cpair(cd[4], cd[5]), cpair(cd[6], cd[7]));
+            *reinterpret_cast<uint4*>(ob + OP_V + g * OP_BYTES + sw128(n, kb)) = o;
+          }
+        }
+      } else {
+        const int kb = d >> 4, dw = d & 15;  // 8 keys x dims 8dw .. 8dw + 7
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) w[q] = *reinterpret_cast<const uint32_t*>(sb + PK::V_OFF + (8 * kb + q) * 64 + 4 * dw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int dim = 8 * dw + e, g = dim >> 6, n = dim & 63;
+          uint32_t cd[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) cd[q] = (w[q] >> (4 * e)) & 0xFu;
+          const uint4 o = make_uint4(cpair(cd[0], cd[1]), cpair(cd[2], cd[3]), cpair(cd[4], cd[5]), cpair(cd[6], cd[7]));
+          *reinterpret_cast<uint4*>(ob + OP_V + g * OP_BYTES + sw128(n, kb)) = o;
+        }
+      }
+      // scales / biases of the tile as fp32 (zero past the tile's last key)
+      if (d < TK) {
+        const int valid = k_end - (k_begin + t * TK);
+        float* sbf = reinterpret_cast<float*>(ob + SB_OFF);
+        const uint32_t ks = *reinterpret_cast<const uint32_t*>(sb + PK::KS_OFF + 4 * d);
+        const uint32_t kbv = *reinterpret_cast<const uint32_t*>(sb + PK::KB_OFF + 4 * d);
+        const uint32_t vs = *reinterpret_cast<const uint32_t*>(sb + PK::VS_OFF + 4 * d);
+        const uint32_t vbv = *reinterpret_cast<const uint32_t*>(sb + PK::VB_OFF + 4 * d);
+        const bool in = d < valid;
+        sbf[2 * d + 0] = in ? bf16_lo(ks) : 0.f;
+        sbf[2 * d + 1] = in ? bf16_hi(ks) : 0.f;
+        sbf[2 * TK + 2 * d + 0] = in ? bf16_lo(kbv) : 0.f;
+        sbf[2 * TK + 2 * d + 1] = in ? bf16_hi(kbv) : 0.f;
+        sbf[4 * TK + 2 * d + 0] = in ? bf16_lo(vs) : 0.f;
+        sbf[4 * TK + 2 * d + 1] = in ? bf16_hi(vs) : 0.f;
+        sbf[6 * TK + 2 * d + 0] = in ? bf16_lo(vbv) : 0.f;
+        sbf[6 * TK + 2 * d + 1] = in ? bf16_hi(vbv) : 0.f;
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&op_full[bb]);
+        mbar_arrive(&empty[st]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int r = 32 * warp + lane;  // query row = TMEM lane
+    const uint32_t lrow = uint32_t(32 * warp) << 16;
+    const bool row_ok = r < rows;
+    const int qi = q0 + (row_ok ? r / rep : 0), h = hk * rep + (row_ok ? r % rep : 0);
+    const int qp = S - a.L + qi;  // query position (causal mask)
+    // Q row: bf16-rounded q * scale (attention.py:49), exact in fp16, into TMEM
+    float qsum[2] = {0.f, 0.f};
+    {
+      const bf16* qr = a.q + ((size_t(b) * a.Hq + h) * a.L + qi) * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {  // 32 dims per 16 TMEM columns
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0 = 0.f, x1 = 0.f;
+          if (row_ok) {
+            const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(qr + 32 * c + 2 * i);
+            x0 = rbf(__low2float(p2) * a.scale);
+            x1 = rbf(__high2float(p2) * a.scale);
+          }
+          qsum[c >> 1] += x0 + x1;
+          v[i] = pack_h2(x0, x1);
+        }
+        tmem_st16(tmem + lrow + Q_COL + 16u * c, v);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    float m_run = -INFINITY, l_run = 0.f, vb_acc[2] = {0.f, 0.f};
+    bool ok = true;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int bb = t & 1;
+      if (!(ok = waitw(&s_full[bb], (t >> 1) & 1, fail, lane))) break;
+      if (!(ok = waitw(&op_full[bb], (t >> 1) & 1, fail, lane))) break;  // scales of the tile
+      tc_fence_after();
+      const float* sbf = reinterpret_cast<const float*>(opb + size_t(bb) * OPBUF + SB_OFF);
+      const int key0 = k_begin + t * TK;
+      float sc[TK];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float s0[32], s1[32];
+        tmem_ld32(tmem + lrow + S_COL + 128u * bb + 32u * half, s0);
+        tmem_ld32(tmem + lrow + S_COL + 128u * bb + 64u + 32u * half, s1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int k = 32 * half + i, key = key0 + k;
+          const float ks0 = sbf[2 * k], ks1 = sbf[2 * k + 1];
+          const float kb0 = sbf[2 * TK + 2 * k], kb1 = sbf[2 * TK + 2 * k + 1];
+          const float v = fmaf(ks0, s0[i], kb0 * qsum[0]) + fmaf(ks1, s1[i], kb1 * qsum[1]);
+          const bool valid = key < k_end && (!causal || key <= qp);
+          sc[k] = valid ? rbf(v) : -INFINITY;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[bb]);  // the S buffer may take tile t + 2
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < TK; ++k) tmax = fmaxf(tmax, sc[k]);
+      const float mn = fmaxf(m_run, tmax);
+      const float corr = (m_run == mn) ? 1.f : (m_run == -INFINITY ? 0.f : expf(m_run - mn));
+      m_run = mn;
+      float psum = 0.f;
+#pragma unroll
+      for (int k = 0; k < TK; ++k) {
+        const float pv = (sc[k] == -INFINITY) ? 0.f : expf(sc[k] - mn);
+        psum += pv;
+        sc[k] = pv;
+      }
+      l_run = l_run * corr + psum;
+      vb_acc[0] *= corr;
+      vb_acc[1] *= corr;
+      // the previous tile's PV has finished: O is stable and P' is free
+      if (t > 0 && !(ok = waitw(pv_done, (t - 1) & 1, fail, lane))) break;
+      tc_fence_after();
+      if (t > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tmem_ld32(tmem + lrow + O_COL + 32u * c, o);
+          tmem_ld_wait();
+          uint32_t u0[16], u1[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            u0[i] = __float_as_uint(o[i] * corr);
+            u1[i] = __float_as_uint(o[16 + i] * corr);
+          }
+          tmem_st16(tmem + lrow + O_COL + 32u * c, u0);
+          tmem_st16(tmem + lrow + O_COL + 32u * c + 16u, u1);
+        }
+      }
+      // P'_g = rb(p) * vscale_g * 2^6 (fp16 pairs of keys), value-bias side sums
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k = 32 * c + 2 * i;
+            const float r0 = rbf(sc[k]), r1 = rbf(sc[k + 1]);
+            const float vs0 = sbf[4 * TK + 2 * k + g], vs1 = sbf[4 * TK + 2 * (k + 1) + g];
+            const float vb0 = sbf[6 * TK + 2 * k + g], vb1 = sbf[6 * TK + 2 * (k + 1) + g];
+            vb_acc[g] += r0 * vb0 + r1 * vb1;
+            v[i] = pack_h2(r0 * (vs0 * PSCALE), r1 * (vs1 * PSCALE));
+          }
+          tmem_st16(tmem + lrow + P_COL + 32u * g + 16u * c, v);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ---- finish: wait for the last PV, normalise, write the row
+    if (ok && ntiles > 0) ok = waitw(pv_done, (ntiles - 1) & 1, fail, lane);
+    tc_fence_after();
+    if (ok) {
+      const size_t orow = (size_t(b) * a.Hq + h) * a.L + qi;
+      const float inv = 1.f / fmaxf(l_run, 1e-30f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        if (ntiles > 0) {
+          tmem_ld32(tmem + lrow + O_COL + 32u * c, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (!row_ok) continue;
+        const int g = c >> 1;
+        float n[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) n[i] = o[i] / PSCALE + vb_acc[g];
+        if (a.nsplit == 1) {
+          const size_t od = a.out_tokens_major ? ((size_t(b) * a.L + qi) * a.Hq + h) : orow;
+          uint4* dst = reinterpret_cast<uint4*>(a.out + od * 128 + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const __nv_bfloat162 v2 = __floats2bfloat162_rn(n[8 * i + 2 * j] * inv, n[8 * i + 2 * j + 1] * inv);
+              w[j] = *reinterpret_cast<const uint32_t*>(&v2);
+            }
+            dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        } else {
+          float4* po = reinterpret_cast<float4*>(a.part_o + (orow * a.nsplit + split) * 128 + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) po[i] = make_float4(n[4 * i], n[4 * i + 1], n[4 * i + 2], n[4 * i + 3]);
+        }
+      }
+      if (row_ok && a.nsplit > 1) {
+        a.part_ml[(orow * a.nsplit + split) * 2 + 0] = m_run;
+        a.part_ml[(orow * a.nsplit + split) * 2 + 1] = l_run;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace atc
+
+// M5_ATTN_TC=1 selects the tcgen05 kernel for prefill attention; otherwise
+// the mma.sync kernel (attn_pf.cu) runs.
+static bool attn_tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("M5_ATTN_TC");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+bool attn_tc_eligible(const AttnArgs& a) {
+  return attn_tc_enabled() && attn_pf_eligible(a);  // same shapes, masks and alignment as the mma.sync kernel
+}
+
+void attn_tc_plan(const AttnArgs& a, int S_max, int max_split, int& QB, int& nsplit) {
+  const int rep = a.Hq / a.Hkv;
+  QB = std::max(1, std::min(a.L, atc::ROWS / rep));
+  const long long ctas = (long long)a.B * a.Hkv * ((a.L + QB - 1) / QB);
+  const int tiles = std::max(1, (S_max + atc::TK - 1) / atc::TK);
+  const long long want = ((long long)sm_count() + ctas - 1) / ctas;  // one CTA per SM
+  nsplit = (int)std::max(1LL, std::min<long long>(std::min<long long>(want, tiles), max_split));
+}
+
+int attn_tc_launch(const AttnArgs& a, cudaStream_t stream) {
+  dim3 grid(a.nsplit, (a.L + a.QB - 1) / a.QB, a.B * a.Hkv);
+  if (a.bits == 8) {
+    constexpr size_t smem = atc::smem_bytes<8>();
+    static DeviceOnce once;  // the attribute belongs to each device's context
+    M5_CUDA(once.run(
+        [&] { return cudaFuncSetAttribute(atc::attn_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
+    atc::attn_tc_kernel<8><<<grid, atc::THREADS, smem, stream>>>(a);
+  } else {
+    constexpr size_t smem = atc::smem_bytes<4>();
+    static DeviceOnce once;
+    M5_CUDA(once.run(
+        [&] { return cudaFuncSetAttribute(atc::attn_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
+    atc::attn_tc_kernel<4><<<grid, atc::THREADS, smem, stream>>>(a);
+  }
+  M5_LAUNCH_CHECK("prefill attention (tcgen05) launch");
+  return M5_OK;
+}
+
+int attn_tc_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_attn_tc_err, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_attn_tc_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace m5

@@ -667,9 +667,10 @@ extern "C" int m5_device_status(int* code, int reset) {
   const int gm = gemm_tc_error(reset);
   const int ap = attn_pf_error(reset);
   const int ar = comm_ar_error(reset);
-  if (g < 0 || gt < 0 || at < 0 || gm < 0 || ap < 0 || ar < 0)
+  const int atc = attn_tc_error(reset);
+  if (g < 0 || gt < 0 || at < 0 || gm < 0 || ap < 0 || ar < 0 || atc < 0)
     return fail(M5_ERR_CUDA, "m5_device_status: cannot read the device error words");
-  *code = g | gt | at | gm | ap | ar;
+  *code = g | gt | at | gm | ap | ar | atc;
   return M5_OK;
 }
 
