@@ -98,7 +98,7 @@ def _tops(logits):
 
 
 def _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal, cos_min=0.9995, cos_median=0.9999,
-           max_abs=0.05, after_tie=False):
+           max_abs=0.05, after_tie=False, tie_margin=0.0):
     """North-star bar: logits cosine >= 0.9999 (asserted on the median step;
     every step must clear `cos_min`, the measured bf16 rounding-chaos floor of
     a random-init model), max-abs error <= 0.05, greedy tokens identical.
@@ -124,13 +124,17 @@ def _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal, cos_min=0.99
     err = (logits_f - logits_o)[keep].abs().max().item()
     assert err <= max_abs, err
     marg, tops = _margins(logits_o), _tops(logits_o)
+    # `tie_margin`: a measured gap below which two correct implementations may
+    # order the top two differently (callers pass twice the oracle's own
+    # fp32-vs-fp64 max-abs distance)
+    near = [_near_tie(m, t) or m < tie_margin for m, t in zip(marg, tops)]
     # teacher-forced argmax equals the oracle's wherever the oracle is not at a near-tie
     for i, (a, b) in enumerate(zip(toks_f, toks_o)):
-        assert a == b or _near_tie(marg[i], tops[i]) or i in ties, (i, a, b, marg[i])
+        assert a == b or near[i] or i in ties, (i, a, b, marg[i])
     # free-running greedy tokens identical up to n_equal, unless a near-tie comes first
     for i in range(n_equal):
         if free[i] != toks_o[i]:
-            assert _near_tie(marg[i], tops[i]) or i in ties, (i, free, toks_o, marg[:i + 1])
+            assert near[i] or i in ties, (i, free, toks_o, marg[:i + 1])
             break
 
 
@@ -234,8 +238,11 @@ def test_qwen3_06b_config():
                                   return_logits=True, feed=toks_o)
     cos = torch.nn.functional.cosine_similarity
     floor = 1 - cos(logits_o, logits_64, dim=-1).min().item()
+    floor_abs = (logits_o - logits_64).abs().max().item()
     dev64 = 1 - cos(logits_f, logits_64, dim=-1).min().item()
-    print(f"1-cos: oracle32 vs oracle64 {floor:.3e}, device vs oracle64 {dev64:.3e}")
+    print(f"1-cos: oracle32 vs oracle64 {floor:.3e} (max-abs {floor_abs:.4f}), device vs oracle64 {dev64:.3e}")
     assert dev64 <= 1.5 * floor + 1e-6, (dev64, floor)
+    # greedy order may differ where the top two are closer than the two
+    # oracles' own logit distance allows them to agree on (twice its max-abs)
     _check(toks_o, logits_o, free, toks_f, logits_f, ties, n_equal=n, cos_min=0.9998, cos_median=0.9998,
-           max_abs=0.07)
+           max_abs=0.07, tie_margin=2 * floor_abs)
