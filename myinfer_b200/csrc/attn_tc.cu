@@ -2,34 +2,35 @@
 // tensor cores (kernel K4p, tcgen05 + TMEM): chunks of L queries, rows = GQA
 // group x queries = 128 per CTA, one kv head and one key range per CTA.
 //
-// Roles (one CTA per SM, 320 threads):
-//   warp 9      producer: 1-D bulk copies of 64-key tiles of packed K / V and
+// Roles (one CTA per SM, 448 threads):
+//   warp 13     producer: 1-D bulk copies of 64-key tiles of packed K / V and
 //               their bf16 scales / biases into a 3-stage ring;
-//   warps 4-7   dequant: the tile's codes become exact fp16 values in shared
-//               memory, written in the 128-byte-swizzled K-major layout the
-//               MMA reads (K as [key][dim], V transposed to [dim][key]), one
-//               64-dim scale group per operand; the tile's scales and biases
-//               are copied beside them so the packed slot frees at once;
-//   warp 8      MMA issuer (one thread): per tile and scale group g
-//                 S_g[128 x 64 keys] = Q_g (TMEM, fp16) * K_g^T   (4 MMAs)
+//   warps 8-11  dequant, into one of two operand buffers: K codes as exact
+//               fp16 in the 128-byte-swizzled K-major layout the MMA reads
+//               ([key][dim], one 64-dim scale group per operand), K's scales
+//               and biases as fp32 beside them, and V dequantized,
+//               fp16(code * vscale + vbias), transposed to [dim][key];
+//   warp 12     MMA issuer (one thread): per tile
+//                 S_g[128 x 64 keys] = Q_g (TMEM, fp16) * Kcodes_g^T   (g = 0, 1)
 //               into one of two S buffers, and after the softmax
-//                 O[:, 64g..] += P'_g (TMEM, fp16) * V_g           (4 MMAs)
-//   warps 0-3   softmax: thread = query row = TMEM lane.  Per key
-//                 s = rb(kscale_0 * S_0 + kbias_0 * sum(q_0)
-//                      + kscale_1 * S_1 + kbias_1 * sum(q_1))
+//                 O[128 x 128] += P (TMEM, fp16) * V                  (4 MMAs)
+//   warps 0-7   softmax: warps w and w + 4 share TMEM lanes 32 (w & 3) ..,
+//               i.e. 32 query rows, and take keys 0-31 / 32-63 of each tile.
+//               Per key
+//                 s = rb(kscale_0 S_0 + kscale_1 S_1 + kbias_0 sum(q_0) + kbias_1 sum(q_1))
 //               (the dequantized dot product, rounded to bf16 like
-//               attention.py:66-69), causal / range mask, fp32 online softmax
-//               with the running max of the row (no shuffles: the row is the
-//               thread's), p rounded to bf16 for PV (attention.py:87-90) with
-//               the value scale folded in, P'_g = rb(p) * vscale_g * 2^6 in
-//               fp16, the value bias as an fp32 side sum, fp32 p in the
-//               denominator; O in TMEM is rescaled in place when a row's max
-//               moves.  The arithmetic is the mma.sync prefill kernel's
-//               (attn_pf.cu); only the data movement differs.
+//               attention.py:66-69), causal / range mask on boundary tiles,
+//               the row max exchanged between the two warps, fp32 online
+//               softmax, p rounded to bf16 for PV (attention.py:87-90) and
+//               stored as fp16 (exact), fp32 p in the denominator; O in TMEM
+//               is rescaled in place when a row's max moves.
+// exp(x) is evaluated as 2^(x log2 e) (ex2.approx): relative error ~1e-6,
+// far below the bf16 rounding of p.  V in fp16 carries a relative rounding
+// of 2^-12 per element, like the fp16 p * vscale of the mma.sync kernel.
 // TMEM columns: S buffers [0,128) [128,256) (group g at +64g), O [256,384),
-// Q [384,448) (fp16 pairs), P' [448,512).  Every mbarrier wait is bounded; a
-// timeout sets a CTA-wide failure flag that ends every role, records a device
-// error and still frees TMEM.
+// Q [384,448) (fp16 pairs), P buffers [448,480) [480,512).  Every mbarrier
+// wait is bounded; a timeout sets a CTA-wide failure flag that ends every
+// role, records a device error and still frees TMEM.
 #include <algorithm>
 #include <cmath>
 
@@ -45,10 +46,12 @@ namespace atc {
 constexpr int TK = 64;            // keys per tile
 constexpr int STAGES = 3;         // packed ring
 constexpr int ROWS = 128;         // query rows per CTA (MMA M)
-constexpr int THREADS = 10 * 32;
-constexpr float PSCALE = 64.f;    // p * vscale kept in fp16 scaled by 2^6
+constexpr int SMX_WARPS = 8, DQ_WARPS = 4;
+constexpr int MMA_WARP = SMX_WARPS + DQ_WARPS, PROD_WARP = MMA_WARP + 1;
+constexpr int THREADS = (PROD_WARP + 1) * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_COL = 0, O_COL = 256, Q_COL = 384, P_COL = 448;
+constexpr float LOG2E = 1.4426950408889634f;
 
 template <int BITS>
 struct Packed {  // one ring stage: K codes, K scales, K biases, V codes, V scales, V biases
@@ -62,17 +65,17 @@ struct Packed {  // one ring stage: K codes, K scales, K biases, V codes, V scal
   static constexpr int STAGE = (VB_OFF + TK * 4 + 1023) / 1024 * 1024;
 };
 
-// fp16 operand buffer (two per CTA): K groups 0/1 then V^T groups 0/1, 8 KB
-// each (64 rows x 128 bytes, 128-byte swizzle), then the tile's scales and
-// biases as fp32 [4][64] (kscale g0/g1 interleaved per key, see below).
+// fp16 operand buffer (two per CTA): K codes of groups 0 / 1 (8 KB each: 64
+// keys x 128 bytes, 128-byte swizzle), V [128 dims x 64 keys] (16 KB, same
+// swizzle), then float4 (kscale_0, kscale_1, kbias_0, kbias_1) per key.
 constexpr int OP_BYTES = 8192;
 constexpr int OP_K = 0, OP_V = 2 * OP_BYTES;
-constexpr int SB_OFF = 4 * OP_BYTES;        // float kscale[64][2], kbias[64][2], vscale[64][2], vbias[64][2]
-constexpr int OPBUF = SB_OFF + 4 * TK * 2 * 4;
+constexpr int SB_OFF = 4 * OP_BYTES;
+constexpr int OPBUF = SB_OFF + TK * 16;
 
 template <int BITS>
 constexpr size_t smem_bytes() {
-  return 1024 + size_t(STAGES) * Packed<BITS>::STAGE + 2 * size_t(OPBUF) + 256;
+  return 1024 + size_t(STAGES) * Packed<BITS>::STAGE + 2 * size_t(OPBUF) + 512;
 }
 
 // Byte offset of 16-byte chunk j of row n in a 128-byte-swizzled K-major tile.
@@ -97,6 +100,14 @@ __device__ __forceinline__ uint32_t c8(uint32_t w, int i) {
 // fp16 pair of two 4-bit / 8-bit codes given as small integers
 __device__ __forceinline__ uint32_t cpair(uint32_t lo, uint32_t hi) {
   return hsub1024(0x64006400u | lo | (hi << 16));
+}
+// A code (0..255) placed in the low mantissa bits of 2^23 reads 2^23 + code.
+__device__ __forceinline__ float code_f(uint32_t magic_bits) { return __uint_as_float(magic_bits) - 8388608.f; }
+// 2^x (ex2.approx; -inf gives 0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 // Generic-proxy shared-memory writes become visible to the tensor core (async proxy).
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -133,6 +144,22 @@ __device__ __forceinline__ bool waitw(uint64_t* bar, uint32_t par, volatile int*
   return ok;
 }
 
+__device__ __forceinline__ float max32(const float (&x)[32]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(fmaxf(x[i], x[i + 8]), fmaxf(x[i + 16], x[i + 24]));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
+  return fmaxf(fmaxf(m[0], m[2]), fmaxf(m[1], m[3]));
+}
+__device__ __forceinline__ float sum32(const float (&x)[32]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = (x[i] + x[i + 8]) + (x[i + 16] + x[i + 24]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] += m[i + 4];
+  return (m[0] + m[2]) + (m[1] + m[3]);
+}
 
 template <int BITS>
 __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
@@ -152,6 +179,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
   uint64_t* pv_done = p_full + 1;
   uint64_t* q_ready = pv_done + 1;
   uint64_t* mma_idle = q_ready + 1;
+  uint64_t* xbar = mma_idle + 1;  // [4 row quarters][2 tile parities]: the two warps' row maxima
+  uint64_t* xend = xbar + 8;      // [4]: the two warps' denominators
+  __shared__ float s_xmax[2][2][ROWS];  // [tile parity][key half][row]
+  __shared__ float s_xl[2][ROWS];
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail;
   volatile int* fail = &s_fail;
@@ -176,18 +207,20 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     s_fail = 0;
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 4);
+      mbar_init(&empty[i], DQ_WARPS);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&op_full[i], 4);
+      mbar_init(&op_full[i], DQ_WARPS);
       mbar_init(&op_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&s_empty[i], SMX_WARPS);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, SMX_WARPS);
     mbar_init(pv_done, 1);
-    mbar_init(q_ready, 4);
+    mbar_init(q_ready, SMX_WARPS);
     mbar_init(mma_idle, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 2);
+    for (int i = 0; i < 4; ++i) mbar_init(&xend[i], 2);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -199,7 +232,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  if (warp == 9) {
+  if (warp == PROD_WARP) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
       const size_t kbase = size_t(b) * a.k.batch_stride + size_t(hk) * a.k.head_stride;
@@ -230,10 +263,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
       // the copies in flight land before the CTA may exit
       for (int t = std::max(0, issued - STAGES); t < issued; ++t) (void)wait1(&full[t % STAGES], (t / STAGES) & 1, fail);
     }
-  } else if (warp == 8) {
+  } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(ROWS, TK);
+      constexpr uint32_t idesc_s = idesc_f16(ROWS, TK), idesc_o = idesc_f16(ROWS, 128);
       bool ok = ntiles > 0 && wait1(q_ready, 0, fail);
       auto issue_s = [&](int t) -> bool {
         const int bb = t & 1;
@@ -244,7 +277,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
           const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_K + g * OP_BYTES));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc_mma_ts(tmem + S_COL + 128u * bb + 64u * g, tmem + Q_COL + 32u * g + 8u * kk, bdesc + 2u * kk, idesc,
+            tc_mma_ts(tmem + S_COL + 128u * bb + 64u * g, tmem + Q_COL + 32u * g + 8u * kk, bdesc + 2u * kk, idesc_s,
                       kk > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[bb]);
@@ -256,14 +289,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
         if (!(ok = wait1(p_full, t & 1, fail))) break;
         tc_fence_after();
         const int bb = t & 1;
+        const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_V));
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_V + g * OP_BYTES));
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma_ts(tmem + O_COL + 64u * g, tmem + P_COL + 32u * g + 8u * kk, bdesc + 2u * kk, idesc,
-                      (t > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_ts(tmem + O_COL, tmem + P_COL + 32u * (t & 1) + 8u * kk, bdesc + 2u * kk, idesc_o,
+                    (t > 0 || kk > 0) ? 1u : 0u);
         tc_commit(pv_done);
         tc_commit(&op_empty[bb]);
       }
@@ -271,16 +301,18 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
       tc_commit(mma_idle);
       (void)wait1(mma_idle, 0, fail);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= SMX_WARPS) {
     // ---------------------------------------------------------------- dequant
-    const int d = tid - 128;  // 0..127
+    const int d = tid - SMX_WARPS * 32;  // 0..127
+    const int vkb = d >> 4, vdw = d & 15, vg = vdw >> 3;  // V task: keys 8 vkb .., dims 8 vdw ..
     for (int t = 0; t < ntiles; ++t) {
       const int st = t % STAGES, bb = t & 1;
       if (!waitw(&full[st], (t / STAGES) & 1, fail, lane) || !waitw(&op_empty[bb], ((t >> 1) & 1) ^ 1, fail, lane))
         break;
       const uint8_t* sb = ring + size_t(st) * PK::STAGE;
       uint8_t* ob = opb + size_t(bb) * OPBUF;
-      // K: 64 keys x 2 groups x 8 chunks of 8 dims
+      const int valid = k_end - (k_begin + t * TK);
+      // K codes: 64 keys x 2 groups x 8 chunks of 8 dims, exact fp16
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int c = d + 128 * i, n = c >> 4, g = (c >> 3) & 1, j = c & 7;
@@ -295,56 +327,52 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
         }
         *reinterpret_cast<uint4*>(ob + OP_K + g * OP_BYTES + sw128(n, j)) = o;
       }
-      // V^T: row = dim of the group, chunk j = keys 8j .. 8j + 7
-      if constexpr (BITS == 8) {
+      // V: keys 8 vkb .. 8 vkb + 7 x dims 8 vdw .. 8 vdw + 7, dequantized and
+      // transposed; zero past the last key.  Chunk e of the 8 dims is taken in
+      // the rotated order (e' + vdw) & 7, so the 8 lanes of a store phase hit 8
+      // different 16-byte bank groups of the swizzled rows.
+      {
+        float vs[8], vb[8];
+        uint32_t wlo[8], whi[8];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int task = d + 128 * i, kb = task >> 5, dw = task & 31;  // 8 keys x dims 4dw .. 4dw + 3
-          uint32_t w[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) w[q] = *reinterpret_cast<const uint32_t*>(sb + PK::V_OFF + (8 * kb + q) * 128 + 4 * dw);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int dim = 4 * dw + e, g = dim >> 6, n = dim & 63;
-            uint32_t cd[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) cd[q] = (w[q] >> (8 * e)) & 0xFFu;
-            const uint4 o = make_uint4(cpair(cd[0], cd[1]), cpair(cd[2], cd[3]), cpair(cd[4], cd[5]), cpair(cd[6], cd[7]));
-            *reinterpret_cast<uint4*>(ob + OP_V + g * OP_BYTES + sw128(n, kb)) = o;
+        for (int q = 0; q < 8; ++q) {
+          const int key = 8 * vkb + q;
+          if constexpr (BITS == 8) {
+            const uint2 w = *reinterpret_cast<const uint2*>(sb + PK::V_OFF + key * 128 + 8 * vdw);
+            wlo[q] = w.x;
+            whi[q] = w.y;
+          } else {
+            wlo[q] = *reinterpret_cast<const uint32_t*>(sb + PK::V_OFF + key * 64 + 4 * vdw);
+            whi[q] = 0;
           }
+          const uint32_t s2 = *reinterpret_cast<const uint32_t*>(sb + PK::VS_OFF + 4 * key);
+          const uint32_t b2 = *reinterpret_cast<const uint32_t*>(sb + PK::VB_OFF + 4 * key);
+          const bool in = key < valid;
+          vs[q] = in ? (vg ? bf16_hi(s2) : bf16_lo(s2)) : 0.f;
+          vb[q] = in ? (vg ? bf16_hi(b2) : bf16_lo(b2)) : 0.f;
         }
-      } else {
-        const int kb = d >> 4, dw = d & 15;  // 8 keys x dims 8dw .. 8dw + 7
-        uint32_t w[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) w[q] = *reinterpret_cast<const uint32_t*>(sb + PK::V_OFF + (8 * kb + q) * 64 + 4 * dw);
+        for (int e0 = 0; e0 < 8; ++e0) {
+          const int e = (e0 + vdw) & 7;
+          float v[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int dim = 8 * dw + e, g = dim >> 6, n = dim & 63;
-          uint32_t cd[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) cd[q] = (w[q] >> (4 * e)) & 0xFu;
-          const uint4 o = make_uint4(cpair(cd[0], cd[1]), cpair(cd[2], cd[3]), cpair(cd[4], cd[5]), cpair(cd[6], cd[7]));
-          *reinterpret_cast<uint4*>(ob + OP_V + g * OP_BYTES + sw128(n, kb)) = o;
+          for (int q = 0; q < 8; ++q) {
+            uint32_t mb;
+            if constexpr (BITS == 8) mb = __byte_perm(e < 4 ? wlo[q] : whi[q], 0x4B000000u, 0x7540u | uint32_t(e & 3));
+            else mb = ((wlo[q] >> (4 * e)) & 15u) | 0x4B000000u;
+            v[q] = fmaf(code_f(mb), vs[q], vb[q]);
+          }
+          const uint4 o = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+          *reinterpret_cast<uint4*>(ob + OP_V + sw128(8 * vdw + e, vkb)) = o;
         }
       }
-      // scales / biases of the tile as fp32 (zero past the tile's last key)
+      // K scales / biases of the tile as fp32 (zero past the last key)
       if (d < TK) {
-        const int valid = k_end - (k_begin + t * TK);
-        float* sbf = reinterpret_cast<float*>(ob + SB_OFF);
         const uint32_t ks = *reinterpret_cast<const uint32_t*>(sb + PK::KS_OFF + 4 * d);
         const uint32_t kbv = *reinterpret_cast<const uint32_t*>(sb + PK::KB_OFF + 4 * d);
-        const uint32_t vs = *reinterpret_cast<const uint32_t*>(sb + PK::VS_OFF + 4 * d);
-        const uint32_t vbv = *reinterpret_cast<const uint32_t*>(sb + PK::VB_OFF + 4 * d);
         const bool in = d < valid;
-        sbf[2 * d + 0] = in ? bf16_lo(ks) : 0.f;
-        sbf[2 * d + 1] = in ? bf16_hi(ks) : 0.f;
-        sbf[2 * TK + 2 * d + 0] = in ? bf16_lo(kbv) : 0.f;
-        sbf[2 * TK + 2 * d + 1] = in ? bf16_hi(kbv) : 0.f;
-        sbf[4 * TK + 2 * d + 0] = in ? bf16_lo(vs) : 0.f;
-        sbf[4 * TK + 2 * d + 1] = in ? bf16_hi(vs) : 0.f;
-        sbf[6 * TK + 2 * d + 0] = in ? bf16_lo(vbv) : 0.f;
-        sbf[6 * TK + 2 * d + 1] = in ? bf16_hi(vbv) : 0.f;
+        reinterpret_cast<float4*>(ob + SB_OFF)[d] = in ? make_float4(bf16_lo(ks), bf16_hi(ks), bf16_lo(kbv), bf16_hi(kbv))
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       fence_async_smem();
       __syncwarp();
@@ -355,12 +383,15 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     }
   } else {
     // ---------------------------------------------------------------- softmax
-    const int r = 32 * warp + lane;  // query row = TMEM lane
-    const uint32_t lrow = uint32_t(32 * warp) << 16;
+    const int rq = warp & 3, kh = warp >> 2;  // row quarter, key half
+    const int r = 32 * rq + lane;             // query row = TMEM lane
+    const uint32_t lrow = uint32_t(32 * rq) << 16;
     const bool row_ok = r < rows;
     const int qi = q0 + (row_ok ? r / rep : 0), h = hk * rep + (row_ok ? r % rep : 0);
-    const int qp = S - a.L + qi;  // query position (causal mask)
-    // Q row: bf16-rounded q * scale (attention.py:49), exact in fp16, into TMEM
+    const int qp = S - a.L + qi;                 // query position (causal mask)
+    const int qp_first = S - a.L + q0;           // first query of the CTA
+    // Q row: bf16-rounded q * scale (attention.py:49), exact in fp16; this
+    // warp stores dims 64 kh .. 64 kh + 63 into TMEM, both group sums are kept
     float qsum[2] = {0.f, 0.f};
     {
       const bf16* qr = a.q + ((size_t(b) * a.Hq + h) * a.L + qi) * 128;
@@ -378,66 +409,75 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
           qsum[c >> 1] += x0 + x1;
           v[i] = pack_h2(x0, x1);
         }
-        tmem_st16(tmem + lrow + Q_COL + 16u * c, v);
+        if ((c >> 1) == kh) tmem_st16(tmem + lrow + Q_COL + 16u * c, v);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
     }
-    float m_run = -INFINITY, l_run = 0.f, vb_acc[2] = {0.f, 0.f};
+    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int t = 0; t < ntiles && ok; ++t) {
       const int bb = t & 1;
       if (!(ok = waitw(&s_full[bb], (t >> 1) & 1, fail, lane))) break;
-      if (!(ok = waitw(&op_full[bb], (t >> 1) & 1, fail, lane))) break;  // scales of the tile
+      if (!(ok = waitw(&op_full[bb], (t >> 1) & 1, fail, lane))) break;  // K scales of the tile
       tc_fence_after();
-      const float* sbf = reinterpret_cast<const float*>(opb + size_t(bb) * OPBUF + SB_OFF);
-      const int key0 = k_begin + t * TK;
-      float sc[TK];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float s0[32], s1[32];
-        tmem_ld32(tmem + lrow + S_COL + 128u * bb + 32u * half, s0);
-        tmem_ld32(tmem + lrow + S_COL + 128u * bb + 64u + 32u * half, s1);
+      const float4* ksb = reinterpret_cast<const float4*>(opb + size_t(bb) * OPBUF + SB_OFF) + 32 * kh;
+      const int key0 = k_begin + t * TK + 32 * kh;
+      float sc[32];
+      {
+        float s1[32];
+        tmem_ld32(tmem + lrow + S_COL + 128u * bb + 32u * kh, sc);
+        tmem_ld32(tmem + lrow + S_COL + 128u * bb + 64u + 32u * kh, s1);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int k = 32 * half + i, key = key0 + k;
-          const float ks0 = sbf[2 * k], ks1 = sbf[2 * k + 1];
-          const float kb0 = sbf[2 * TK + 2 * k], kb1 = sbf[2 * TK + 2 * k + 1];
-          const float v = fmaf(ks0, s0[i], kb0 * qsum[0]) + fmaf(ks1, s1[i], kb1 * qsum[1]);
-          const bool valid = key < k_end && (!causal || key <= qp);
-          sc[k] = valid ? rbf(v) : -INFINITY;
+          const float4 kq = ksb[i];
+          sc[i] = rbf(fmaf(kq.y, s1[i], fmaf(kq.x, sc[i], fmaf(kq.w, qsum[1], kq.z * qsum[0]))));
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[bb]);  // the S buffer may take tile t + 2
-      float tmax = -INFINITY;
+      // masks only where the tile crosses the range end or the causal diagonal
+      if (k_begin + (t + 1) * TK > k_end || (causal && k_begin + (t + 1) * TK - 1 > qp_first)) {
 #pragma unroll
-      for (int k = 0; k < TK; ++k) tmax = fmaxf(tmax, sc[k]);
-      const float mn = fmaxf(m_run, tmax);
-      const float corr = (m_run == mn) ? 1.f : (m_run == -INFINITY ? 0.f : expf(m_run - mn));
-      m_run = mn;
-      float psum = 0.f;
-#pragma unroll
-      for (int k = 0; k < TK; ++k) {
-        const float pv = (sc[k] == -INFINITY) ? 0.f : expf(sc[k] - mn);
-        psum += pv;
-        sc[k] = pv;
+        for (int i = 0; i < 32; ++i) {
+          const int key = key0 + i;
+          if (!(key < k_end && (!causal || key <= qp))) sc[i] = -INFINITY;
+        }
       }
-      l_run = l_run * corr + psum;
-      vb_acc[0] *= corr;
-      vb_acc[1] *= corr;
-      // the previous tile's PV has finished: O is stable and P' is free
+      // the row max over both key halves
+      float tmax = max32(sc);
+      s_xmax[t & 1][kh][r] = tmax;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[2 * rq + (t & 1)]);
+      if (!(ok = waitw(&xbar[2 * rq + (t & 1)], (t >> 1) & 1, fail, lane))) break;
+      tmax = fmaxf(tmax, s_xmax[t & 1][kh ^ 1][r]);
+      const float mn = fmaxf(m_run, tmax);
+      const float corr = (m_run == mn) ? 1.f : (m_run == -INFINITY ? 0.f : ex2((m_run - mn) * LOG2E));
+      m_run = mn;
+      const float mnl = mn == -INFINITY ? 0.f : mn * LOG2E;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sc[i] = ex2(fmaf(sc[i], LOG2E, -mnl));
+      l_run = l_run * corr + sum32(sc);
+      // P (this warp's 32 keys) = fp16 pairs of rb(p), into the tile's P buffer
+      {
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = pack_h2(rbf(sc[2 * i]), rbf(sc[2 * i + 1]));
+        tmem_st16(tmem + lrow + P_COL + 32u * (t & 1) + 16u * kh, v);
+      }
+      // the previous tile's PV has finished: O is stable
       if (t > 0 && !(ok = waitw(pv_done, (t - 1) & 1, fail, lane))) break;
       tc_fence_after();
       if (t > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {  // this warp's 64 columns of O
           float o[32];
-          tmem_ld32(tmem + lrow + O_COL + 32u * c, o);
+          const uint32_t col = O_COL + 64u * kh + 32u * c;
+          tmem_ld32(tmem + lrow + col, o);
           tmem_ld_wait();
           uint32_t u0[16], u1[16];
 #pragma unroll
@@ -445,26 +485,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
             u0[i] = __float_as_uint(o[i] * corr);
             u1[i] = __float_as_uint(o[16 + i] * corr);
           }
-          tmem_st16(tmem + lrow + O_COL + 32u * c, u0);
-          tmem_st16(tmem + lrow + O_COL + 32u * c + 16u, u1);
-        }
-      }
-      // P'_g = rb(p) * vscale_g * 2^6 (fp16 pairs of keys), value-bias side sums
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t v[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int k = 32 * c + 2 * i;
-            const float r0 = rbf(sc[k]), r1 = rbf(sc[k + 1]);
-            const float vs0 = sbf[4 * TK + 2 * k + g], vs1 = sbf[4 * TK + 2 * (k + 1) + g];
-            const float vb0 = sbf[6 * TK + 2 * k + g], vb1 = sbf[6 * TK + 2 * (k + 1) + g];
-            vb_acc[g] += r0 * vb0 + r1 * vb1;
-            v[i] = pack_h2(r0 * (vs0 * PSCALE), r1 * (vs1 * PSCALE));
-          }
-          tmem_st16(tmem + lrow + P_COL + 32u * g + 16u * c, v);
+          tmem_st16(tmem + lrow + col, u0);
+          tmem_st16(tmem + lrow + col + 16u, u1);
         }
       }
       tmem_st_wait();
@@ -472,49 +494,54 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // ---- finish: wait for the last PV, normalise, write the row
+    // ---- finish: wait for the last PV, add the two halves' denominators,
+    // normalise this warp's 64 dims and write them
     if (ok && ntiles > 0) ok = waitw(pv_done, (ntiles - 1) & 1, fail, lane);
+    if (ok) {
+      s_xl[kh][r] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xend[rq]);
+      ok = waitw(&xend[rq], 0, fail, lane);
+    }
     tc_fence_after();
     if (ok) {
+      const float l_tot = s_xl[0][r] + s_xl[1][r];
       const size_t orow = (size_t(b) * a.Hq + h) * a.L + qi;
-      const float inv = 1.f / fmaxf(l_run, 1e-30f);
+      const float inv = 1.f / fmaxf(l_tot, 1e-30f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float o[32];
+        const int d0 = 64 * kh + 32 * c;  // first dim of the 32
         if (ntiles > 0) {
-          tmem_ld32(tmem + lrow + O_COL + 32u * c, o);
+          tmem_ld32(tmem + lrow + O_COL + uint32_t(d0), o);
           tmem_ld_wait();
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0.f;
         }
         if (!row_ok) continue;
-        const int g = c >> 1;
-        float n[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) n[i] = o[i] / PSCALE + vb_acc[g];
         if (a.nsplit == 1) {
           const size_t od = a.out_tokens_major ? ((size_t(b) * a.L + qi) * a.Hq + h) : orow;
-          uint4* dst = reinterpret_cast<uint4*>(a.out + od * 128 + 32 * c);
+          uint4* dst = reinterpret_cast<uint4*>(a.out + od * 128 + d0);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             uint32_t w[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const __nv_bfloat162 v2 = __floats2bfloat162_rn(n[8 * i + 2 * j] * inv, n[8 * i + 2 * j + 1] * inv);
+              const __nv_bfloat162 v2 = __floats2bfloat162_rn(o[8 * i + 2 * j] * inv, o[8 * i + 2 * j + 1] * inv);
               w[j] = *reinterpret_cast<const uint32_t*>(&v2);
             }
             dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         } else {
-          float4* po = reinterpret_cast<float4*>(a.part_o + (orow * a.nsplit + split) * 128 + 32 * c);
+          float4* po = reinterpret_cast<float4*>(a.part_o + (orow * a.nsplit + split) * 128 + d0);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) po[i] = make_float4(n[4 * i], n[4 * i + 1], n[4 * i + 2], n[4 * i + 3]);
+          for (int i = 0; i < 8; ++i) po[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
         }
       }
-      if (row_ok && a.nsplit > 1) {
+      if (row_ok && a.nsplit > 1 && kh == 0) {
         a.part_ml[(orow * a.nsplit + split) * 2 + 0] = m_run;
-        a.part_ml[(orow * a.nsplit + split) * 2 + 1] = l_run;
+        a.part_ml[(orow * a.nsplit + split) * 2 + 1] = l_tot;
       }
     }
   }

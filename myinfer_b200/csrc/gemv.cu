@@ -307,6 +307,8 @@ int gemv_launch(const GemvArgs& a_in, int MT, int epi, cudaStream_t stream) {
   if (a.K % 64 != 0 || a.K <= 0) return fail(M5_ERR_INVALID, "gemv: K must be a positive multiple of 64");
   if (a.total_rows <= 0) return M5_OK;
   const bool tmap = gemv_tmap_eligible(a, MT, epi);
+  if (a.rope_cnt && !(tmap && epi == EPI_STORE && a.rope.L == MT))
+    return fail(M5_ERR_INVALID, "gemv: the fused rope epilogue needs the tensor-map GEMV, EPI_STORE and rope.L == MT");
   if (tmap || gemv_mma_eligible(a, MT, epi)) {
     const int vrows = a.total_rows * (epi == EPI_SWIGLU ? 2 : 1);
     float* acc = a.mma_acc;

@@ -2,6 +2,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "ops.cuh"
 
 namespace m5 {
 
@@ -43,6 +44,14 @@ struct GemvArgs {
   // Row length of the weights, scales and biases when the call reduces over
   // only K columns of wider rows (a K slice; 0 = K).  Read by the prefill GEMM.
   int64_t ldk;
+  // QK-norm + RoPE + KV append fused into the q|k|v projection (EPI_STORE on
+  // the tensor-map GEMV, gemv_tmap_eligible): when rope_cnt is set, the warp
+  // that writes the last of the 8 16-row tiles of a 128-row head runs that
+  // head's rope_append_row for every token.  rope.qkv must be the output of
+  // the segments laid end to end (row = head * 128 + d) and rope.L = MT;
+  // rope_cnt is one zeroed int per head, left zeroed.
+  RopeAppendArgs rope;
+  unsigned int* rope_cnt;
 };
 
 // Launch y = epi(x @ W^T) for up to 8 tokens.  Chooses rows per warp so the

@@ -26,6 +26,7 @@
 
 #include "frag_stage.cuh"
 #include "gemv.cuh"
+#include "rope_impl.cuh"
 #include "tma.cuh"
 
 namespace m5 {
@@ -124,13 +125,20 @@ __device__ __forceinline__ void tp_half(const GemvArgs& a, int tile, int h, int&
   }
 }
 
+// QK-norm + RoPE + KV append of head h for MT tokens, by one warp, once the
+// head's 8 tiles are written (kept out of line: it runs once per 8 tiles and
+// its trigonometric slow path must not weigh on the dot-product loop).
+__device__ __noinline__ void tp_rope_head(const RopeAppendArgs& r, int MT, int h, int lane) {
+  for (int t = 0; t < MT; ++t) rope_append_row_any<true>(r, t, h, lane);
+}
+
 // I8 selects the consumer: false = fp16 MMAs on exact codes against the
 // activations scaled per token (stage_frag_bulk), true = int8 MMAs (u8 codes
 // as they sit in the word, one mask or shift-and-mask per 4 codes) against
 // per-group 16-bit fixed-point activation planes (stage_i8_bulk), int32 group
 // sums folded as s * 2^(E - 14) * D + b * sum(x).
 template <int MT, int EPI, bool I8>
-__global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs a, const __grid_constant__ TmapSet tm,
+__global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_constant__ GemvArgs a, const __grid_constant__ TmapSet tm,
                                                                float* acc_buf, int* cnt_buf, int acc_rows) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 128-byte-swizzled boxes must start on 1 KB boundaries
@@ -256,6 +264,21 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
       }
     }
   };
+  // Called by the whole warp that wrote tile `tile` (EPI_STORE): the 8th tile
+  // of a head to finish runs the head's QK-norm + RoPE + KV append.  The
+  // counter wraps to 0 on the 8th arrival (atomicInc), ready for the next launch.
+  auto rope_tile = [&](int tile) {
+    if (a.rope_cnt == nullptr) return;
+    __threadfence();  // this warp's rows of the tile, before the count
+    __syncwarp();
+    unsigned int old = 0;
+    if (lane == 0) old = atomicInc(&a.rope_cnt[tile >> 3], 7u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == 7u) {
+      __threadfence();  // the other tiles' rows, after their counts
+      tp_rope_head(a.rope, MT, tile >> 3, lane);
+    }
+  };
   float* tred = reinterpret_cast<float*>(red + 8);  // [CW][MT][16] partial tile sums
   // A tile whose units all lie in this CTA's range is reduced in shared memory
   // by the four consumer warps (no global atomics, no fence); a tile shared
@@ -289,6 +312,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
           }
           if (EPI != EPI_SWIGLU || r16 < 8) epilogue(tile, r16, t, v, vu);
         }
+        if constexpr (EPI == EPI_STORE) rope_tile(tile);
       }
       named_sync(2, TP_CW * 32);
     } else {
@@ -327,6 +351,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const GemvArgs
         }
         __syncwarp();
         if (lane == 0) cnt_buf[tile] = 0;
+        if constexpr (EPI == EPI_STORE) rope_tile(tile);
       }
     }
 #pragma unroll

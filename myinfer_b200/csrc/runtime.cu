@@ -65,6 +65,7 @@ struct Model {
   float* mma_acc = nullptr;  // zeroed split-tile scratch of the tensor-core GEMV
   int* mma_cnt = nullptr;
   int mma_rows = 0;
+  unsigned int* rope_cnt = nullptr;  // zeroed per-head counters of the q|k|v GEMV's fused rope epilogue
   float* moe_ybuf = nullptr;  // zeroed [k, H] and [H/16] scratch of the tensor-core expert path
   int* moe_ncnt = nullptr;
   // MoE prefill grouped by expert (T >= kMoeGroupedMinTokens): expert-ordered rows and
@@ -426,6 +427,16 @@ static int moe_prefill_grouped(Model* m, const Layer& ly, int T, cudaStream_t st
   return moe_combine_launch(m->moe_y, T, H, k, m->moe_pos, m->rscores, m->h, c.ep_size > 1 ? m->hf : nullptr, st);
 }
 
+// QK-norm + RoPE + KV append run in the q|k|v GEMV's epilogue for decode-sized
+// calls (M5_FUSE_ROPE=0 keeps the separate kernel).
+static bool fuse_rope() {
+  static const bool on = [] {
+    const char* e = getenv("M5_FUSE_ROPE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 static bool stream_capturing(cudaStream_t st) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   return cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
@@ -460,7 +471,6 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     a.norm_w = ly.in_norm;
     a.eps = c.rms_norm_eps;
     attach(m, a);
-    if ((rc = linear_auto(m, a, T, EPI_STORE, st))) return rc;
     // QK-norm + RoPE + KV append
     RopeAppendArgs r{};
     r.qkv = m->qkv;
@@ -476,7 +486,15 @@ static int forward(Model* m, const m5_layer_kv* kv, int32_t* d_len, const int32_
     r.d_len = d_len;
     r.q_out = m->q;
     r.kv = lk;
-    if ((rc = rope_append_launch(r, st))) return rc;
+    if (T < kGemmMinRows && T <= 8 && D == 128 && fuse_rope() && gemv_tmap_eligible(a, T, EPI_STORE)) {
+      // one launch: the GEMV's epilogue appends each head once its rows are written
+      a.rope = r;
+      a.rope_cnt = m->rope_cnt;
+      if ((rc = gemv_launch(a, T, EPI_STORE, st))) return rc;
+    } else {
+      if ((rc = linear_auto(m, a, T, EPI_STORE, st))) return rc;
+      if ((rc = rope_append_launch(r, st))) return rc;
+    }
     // attention over the cache (S = *d_len + L keys after the append)
     AttnArgs at{};
     at.q = m->q;
@@ -963,7 +981,8 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
                           moe_pre ? T * k * 4 : 0,
                           moe_pre ? size_t(2) * m->E_local * 4 : 0,
                           T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_rows * sk_n * 4 : 0,
-                          T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_xs : 0};
+                          T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_xs : 0,
+                          (QKV / 128 + 1) * sizeof(unsigned int)};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -1009,6 +1028,7 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->sk_f = sizes[25] ? (float*)carve(p, sizes[25]) : nullptr;
   m->sk_n = sizes[25] ? (int)sk_n : 0;
   m->sk_xs = sizes[26] ? carve(p, sizes[26]) : nullptr;
+  m->rope_cnt = (unsigned int*)carve(p, sizes[27]);
   m->sk_xs_stride = sizes[26] ? sk_xs : 0;
   if (m->sk_f && !m->sk_fork) {
     M5_CUDA(cudaEventCreateWithFlags(&m->sk_fork, cudaEventDisableTiming));
