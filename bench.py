@@ -75,9 +75,25 @@ def weight_bytes_per_token(cfg: dict) -> int:
     return int(L * per_layer + head + H * 2)
 
 
-def kv_bytes_per_token(cfg: dict, ctx: int, bits: int = 8) -> int:
+def kv_bytes_per_token(cfg: dict, ctx: int, bits: int = 8, kv_heads: int = 0) -> int:
     per_elem = bits / 8 + 4 / 64
-    return int(2 * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * per_elem * ctx)
+    n = kv_heads or cfg["num_key_value_heads"]
+    return int(2 * cfg["num_hidden_layers"] * n * cfg["head_dim"] * per_elem * ctx)
+
+
+def moe_bytes_per_rank(cfg: dict, world: int, ctx: int, bits: int) -> int:
+    """Bytes one rank streams for a batch-1 MoE decode token with the heads
+    sharded over `world` ranks (kv heads replicated where there are fewer
+    than ranks), the router replicated, the lm_head split by rows and the k
+    routed experts spread evenly (their expected share)."""
+    from myinfer_b200.distributed import kv_heads_local
+    H, L, D = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["head_dim"]
+    Hq, V, E = cfg["num_attention_heads"], cfg["vocab_size"], cfg["num_experts"]
+    hkv = kv_heads_local(cfg["num_key_value_heads"], world)
+    attn = (2 * (Hq // world) * D * H + 2 * hkv * D * H) * 0.5625
+    experts = cfg["num_experts_per_tok"] * 3 * cfg["moe_intermediate_size"] * H * 0.5625 / world
+    per_layer = attn + E * H * 0.5625 + experts + (2 * H + 2 * D) * 2
+    return int(L * per_layer + V // world * H * 0.5625 + H * 2 + kv_bytes_per_token(cfg, ctx, bits, hkv))
 
 
 class ClockSampler:
@@ -329,10 +345,12 @@ class Ctx:
 
 
 def build_model(cx: Ctx, cfg: dict, seed: int, chunk: int, sharded: bool = True):
-    """This rank's shard of the seeded random model (dense: tensor parallel,
-    MoE: expert parallel over all ranks), or the whole model on this GPU."""
+    """This rank's shard of the seeded random model (dense: tensor parallel;
+    MoE: expert parallel over all ranks with the attention heads sharded over
+    the same ranks), or the whole model on this GPU."""
     import torch
 
+    from myinfer_b200.distributed import shard_weights
     from myinfer_b200.model import Model, ModelArgs, random_weights
     a = ModelArgs.from_dict(cfg)
     world = cx.world if sharded else 1
@@ -340,11 +358,12 @@ def build_model(cx: Ctx, cfg: dict, seed: int, chunk: int, sharded: bool = True)
     if world > 1 and a.num_experts:
         El = a.num_experts // world
         w = random_weights(a, seed=seed, device=cx.dev, experts=(cx.rank * El, El))  # this rank's experts only
-        par = dict(ep_size=world, ep_rank=cx.rank)
+        par = dict(ep_size=world, ep_rank=cx.rank, tp_size=world, tp_rank=cx.rank)
+        w = shard_weights(w, a, experts_local=True, **par)
+        torch.cuda.empty_cache()
     else:
         w = random_weights(a, seed=seed, device=cx.dev)
         if world > 1:
-            from myinfer_b200.distributed import shard_weights
             par = dict(tp_size=world, tp_rank=cx.rank)
             w = shard_weights(w, a, **par)
             torch.cuda.empty_cache()
@@ -496,8 +515,9 @@ def decode_bench(cx: Ctx, model, cfg: dict, ctx: int, kv_bits: int, batch: int, 
 
 def moe_block(cx: Ctx, name: str, args, steps: int) -> dict:
     """Batch-1 decode of a MoE config at its BASELINE prompt and KV bits,
-    expert parallel over all ranks (attention, router and lm_head replicated;
-    each rank streams its own routed experts)."""
+    expert parallel over all ranks with the attention heads, their KV and the
+    lm_head rows sharded over the same ranks (router replicated; each rank
+    streams its own routed experts)."""
     import torch
     cfg = CONFIGS[name]
     ctx, kv_bits = DEFAULTS[name]
@@ -509,14 +529,9 @@ def moe_block(cx: Ctx, name: str, args, steps: int) -> dict:
         if cx.world > 1 and name != "qwen3-235b-a22b" else None
     del model
     torch.cuda.empty_cache()
-    # per-rank bytes of one token: the replicated part (attention, router,
-    # embedding row, lm_head, KV) plus this rank's share of the k routed experts
-    H, E, k, I = cfg["hidden_size"], cfg["num_experts"], cfg["num_experts_per_tok"], cfg["moe_intermediate_size"]
-    expert_bytes = cfg["num_hidden_layers"] * k * 3 * I * H * 0.5625
-    replicated = weight_bytes_per_token(cfg) - expert_bytes + kv_bytes_per_token(cfg, int(r["mean_ctx"]), kv_bits)
-    per_rank = replicated + expert_bytes / cx.world
+    per_rank = moe_bytes_per_rank(cfg, cx.world, int(r["mean_ctx"]), kv_bits)
     peaks = measured_peaks()
-    return {"model": name, "parallelism": f"ep{cx.world}" if cx.world > 1 else "single", "prompt_tokens": ctx,
+    return {"model": name, "parallelism": f"ep{cx.world}+tp{cx.world}-attention" if cx.world > 1 else "single", "prompt_tokens": ctx,
             "kv_bits": kv_bits, "value": round(1000.0 / r["ms_step"], 2), "unit": "tok/s",
             "ms_per_step": round(r["ms_step"], 4), "steps": steps,
             "prefill_tok_s": round(ctx / (r["prefill_ms"] * 1e-3), 1),
@@ -545,7 +560,7 @@ def run_gpu(args) -> dict:
                          "mlp.up_proj" if not a.num_experts else "self_attn.q_proj")
     check = n1_token_check(cx, model, cfg, args.seed, args.kv_bits, args.chunk) if world > 1 else None
     per_rank = bytes_step / world
-    par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}" if world > 1 else "single")
+    par_name = f"tp{world}" if world > 1 and not a.num_experts else (f"ep{world}+tp{world}-attention" if world > 1 else "single")
     prefill_flops = 2.0 * ctx * (weight_bytes_per_token(cfg) / 0.5625) + 4.0 * a.num_hidden_layers * \
         a.num_attention_heads * a.head_dim * ctx * ctx / 2
     prefill_ms = r["prefill_ms"]

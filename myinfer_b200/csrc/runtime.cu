@@ -842,13 +842,16 @@ extern "C" int m5_model_create(const m5_model_cfg* cfg, void** out) {
   M5_CHECK_ARG(c.vocab_size > 0, "m5_model_create: vocab_size");
   const int tp = std::max(1, c.tp_size), ep = std::max(1, c.ep_size);
   M5_CHECK_ARG(c.tp_rank >= 0 && c.tp_rank < tp && c.ep_rank >= 0 && c.ep_rank < ep, "m5_model_create: rank");
-  M5_CHECK_ARG(c.num_heads % tp == 0 && c.num_kv_heads % tp == 0, "m5_model_create: heads not divisible by tp_size");
+  // kv heads split over the ranks, or (fewer kv heads than ranks) each
+  // replicated on tp / Hkv consecutive ranks, which hold its group's q heads
+  M5_CHECK_ARG(c.num_heads % tp == 0 && (c.num_kv_heads % tp == 0 || tp % c.num_kv_heads == 0),
+               "m5_model_create: heads neither split over nor replicate onto tp_size ranks");
   Model* m = new Model();
   m->cfg = c;
   m->cfg.tp_size = tp;
   m->cfg.ep_size = ep;
   m->Hq = c.num_heads / tp;
-  m->Hkv = c.num_kv_heads / tp;
+  m->Hkv = c.num_kv_heads % tp == 0 ? c.num_kv_heads / tp : 1;
   if (c.num_experts > 0) {
     if (c.num_experts % ep || c.moe_intermediate_size % 64 || c.experts_per_tok <= 0) {
       delete m;
@@ -864,9 +867,11 @@ extern "C" int m5_model_create(const m5_model_cfg* cfg, void** out) {
     }
     m->I = c.intermediate_size / tp;
   }
-  if (c.num_experts > 0 && tp > 1) {
+  // a MoE model shards its attention heads only over the ranks that hold its
+  // experts: one group, one communicator, two partial-sum reductions per layer
+  if (c.num_experts > 0 && tp > 1 && (ep != tp || c.ep_rank != c.tp_rank)) {
     delete m;
-    return fail(M5_ERR_UNSUPPORTED, "m5_model_create: MoE models split experts (ep_size), not heads (tp_size)");
+    return fail(M5_ERR_UNSUPPORTED, "m5_model_create: a MoE model shards heads only with tp_size == ep_size on the same ranks");
   }
   if (c.num_experts == 0 && ep > 1) {
     delete m;

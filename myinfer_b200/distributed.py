@@ -4,9 +4,15 @@ One process per GPU.  Dense Qwen3 runs tensor parallel over ``tp`` ranks
 (q/k/v heads, gate/up rows, o_proj/down columns and lm_head rows split; the
 C++ forward all-reduces the o_proj and down partial sums and all-gathers the
 vocabulary shards).  Qwen3-MoE runs expert parallel over ``ep`` ranks (the
-stacked ``switch_mlp`` experts split, attention and router replicated; the
-MoE partial sums are all-reduced).  The reference (m5engine) is single-device;
-this is the B200 build's own partitioning.
+stacked ``switch_mlp`` experts split, the router replicated; the MoE partial
+sums are all-reduced), with attention either replicated (``tp_size`` 1) or
+head-sharded over the same ranks (``tp_size == ep_size``: q/k/v heads,
+o_proj columns and lm_head rows split as for a dense model, one more
+all-reduce per layer).  Where a model has fewer kv heads than ranks
+(Qwen3-235B-A22B: 4 kv heads, 8 ranks) each kv head is replicated on
+``tp / Hkv`` consecutive ranks, which hold the q heads of its group.  The
+reference (m5engine) is single-device; this is the B200 build's own
+partitioning.
 
 ``shard_weights`` works on any tensors (CPU or device) in the MLX layout:
 packed ``*.weight`` [rows, K/8] int32, ``*.scales`` / ``*.biases`` [rows, K/64].
@@ -50,28 +56,61 @@ def _rows(w: Dict[str, torch.Tensor], name: str, n: int, r: int, out: Dict[str, 
         out[name + suf] = _row_slice(w[src + suf], n, r, axis)
 
 
-def shard_weights(w: Dict[str, torch.Tensor], args, tp_size: int = 1, tp_rank: int = 0, ep_size: int = 1,
-                  ep_rank: int = 0) -> Dict[str, torch.Tensor]:
-    """This rank's tensors (new contiguous tensors; the full set is not modified)."""
-    if tp_size > 1 and ep_size > 1:
-        raise ValueError("use tensor parallel for dense models and expert parallel for MoE models")
-    if tp_size == 1 and ep_size == 1:
-        return dict(w)
-    out: Dict[str, torch.Tensor] = {}
+def kv_heads_local(n_kv_heads: int, tp_size: int) -> int:
+    """kv heads a rank holds: Hkv / tp, or 1 (replicated) when tp is a multiple of Hkv."""
+    if n_kv_heads % tp_size == 0:
+        return n_kv_heads // tp_size
+    if tp_size % n_kv_heads == 0:
+        return 1
+    raise ValueError(f"{n_kv_heads} kv heads neither split over nor replicate onto {tp_size} ranks")
+
+
+def kv_head_first(n_kv_heads: int, tp_size: int, tp_rank: int) -> int:
+    """First kv head of rank tp_rank (the group of its q heads)."""
+    return tp_rank * kv_heads_local(n_kv_heads, tp_size) if n_kv_heads % tp_size == 0 \
+        else tp_rank * n_kv_heads // tp_size
+
+
+def check_parallel(args, tp_size: int, tp_rank: int, ep_size: int, ep_rank: int) -> None:
+    """The partitions the C++ model accepts (m5_model_create)."""
     moe = args.num_experts > 0
-    if moe and tp_size > 1:
-        raise ValueError("MoE models split experts (ep_size), not heads")
     if not moe and ep_size > 1:
         raise ValueError("ep_size > 1 needs a MoE model")
+    if tp_size > 1 and ep_size > 1 and (tp_size != ep_size or tp_rank != ep_rank):
+        raise ValueError("head-sharded attention with expert parallelism uses the same ranks for both")
+    if moe and tp_size > 1 and ep_size != tp_size:
+        raise ValueError("a MoE model shards heads only together with its experts (tp_size == ep_size)")
+    if args.num_attention_heads % tp_size:
+        raise ValueError("num_attention_heads not divisible by tp_size")
+    kv_heads_local(args.num_key_value_heads, tp_size)
+
+
+def shard_weights(w: Dict[str, torch.Tensor], args, tp_size: int = 1, tp_rank: int = 0, ep_size: int = 1,
+                  ep_rank: int = 0, experts_local: bool = False) -> Dict[str, torch.Tensor]:
+    """This rank's tensors (new contiguous tensors; the full set is not modified).
+    ``experts_local``: the expert stacks in ``w`` already hold only this rank's
+    experts (``random_weights(experts=...)``) and are taken as they are."""
+    if tp_size == 1 and ep_size == 1:
+        return dict(w)
+    check_parallel(args, tp_size, tp_rank, ep_size, ep_rank)
+    out: Dict[str, torch.Tensor] = {}
     D = args.head_dim
+    Hkv = args.num_key_value_heads
     for name, t in w.items():
         if name in out:
             continue
         base = name.rsplit(".", 1)[0]
         if ".switch_mlp." in name and ep_size > 1:
-            _rows(w, base, ep_size, ep_rank, out)  # experts are the leading axis
-        elif tp_size > 1 and base.endswith(("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
-                                             "mlp.gate_proj", "mlp.up_proj")):
+            if experts_local:
+                out[name] = t
+            else:
+                _rows(w, base, ep_size, ep_rank, out)  # experts are the leading axis
+        elif tp_size > 1 and base.endswith(("self_attn.k_proj", "self_attn.v_proj")):
+            n = kv_heads_local(Hkv, tp_size)
+            r0 = kv_head_first(Hkv, tp_size, tp_rank) * D
+            for suf in (".weight", ".scales", ".biases"):
+                out[base + suf] = w[base + suf].narrow(0, r0, n * D).contiguous()
+        elif tp_size > 1 and base.endswith(("self_attn.q_proj", "mlp.gate_proj", "mlp.up_proj")):
             _rows(w, base, tp_size, tp_rank, out)  # whole heads / intermediate rows per rank
         elif tp_size > 1 and base.endswith(("self_attn.o_proj", "mlp.down_proj")):
             _col_slice(w, base, tp_size, tp_rank, out)

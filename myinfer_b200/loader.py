@@ -13,8 +13,9 @@ Here every tensor goes to the device once, and a rank of a tensor- or
 expert-parallel group reads only its own part from the file (through the
 safetensors slice API, which maps the file and copies just the requested
 rows): q/k/v and gate/up rows, o_proj/down columns in whole scale groups,
-lm_head rows (tensor parallel); its experts of every ``switch_mlp`` stack
-(expert parallel).  The result equals ``distributed.shard_weights`` applied
+lm_head rows (tensor parallel; k/v rows of the rank's kv head when kv heads
+are replicated over the ranks); its experts of every ``switch_mlp`` stack
+(expert parallel; both at once for head-sharded MoE attention).  The result equals ``distributed.shard_weights`` applied
 to the whole checkpoint, without the whole checkpoint ever being in host or
 device memory.
 """
@@ -52,9 +53,11 @@ def checkpoint_files(path: Path) -> Dict[str, Path]:
 
 
 def _part(name: str, shape: List[int], tp_size: int, tp_rank: int, ep_size: int,
-          ep_rank: int) -> Tuple[Optional[Tuple[int, int]], Optional[Tuple[int, int]]]:
+          ep_rank: int, n_kv_heads: int = 0) -> Tuple[Optional[Tuple[int, int]], Optional[Tuple[int, int]]]:
     """(row range on the leading axis, column range on the last axis) of this
-    rank's part of tensor `name` (None = whole axis)."""
+    rank's part of tensor `name` (None = whole axis).  `n_kv_heads` (the
+    model's) decides the k/v rows under tensor parallelism."""
+    from .distributed import kv_head_first, kv_heads_local
     base, suffix = name.rsplit(".", 1)
     if ep_size > 1 and ".switch_mlp." in name:
         E = shape[0]
@@ -62,6 +65,11 @@ def _part(name: str, shape: List[int], tp_size: int, tp_rank: int, ep_size: int,
             raise ValueError(f"{name}: {E} experts do not split over {ep_size} ranks")
         k = E // ep_size
         return (ep_rank * k, (ep_rank + 1) * k), None
+    if tp_size > 1 and n_kv_heads and base.endswith(("self_attn.k_proj", "self_attn.v_proj")) \
+            and suffix in ("weight", "scales", "biases"):
+        D = shape[0] // n_kv_heads
+        r0 = kv_head_first(n_kv_heads, tp_size, tp_rank) * D
+        return (r0, r0 + kv_heads_local(n_kv_heads, tp_size) * D), None
     if tp_size > 1 and suffix in ("weight", "scales", "biases"):
         if base.endswith(TP_ROWS) or base == "lm_head":
             R = shape[0]
@@ -87,12 +95,14 @@ def load_mlx_checkpoint(path, device, tp_size: int = 1, tp_rank: int = 0, ep_siz
     layout libm5cuda binds).  Under tensor parallelism a model with tied
     embeddings also gets ``lm_head.*``: its vocabulary rows of the embedding."""
     from safetensors import safe_open
-    if tp_size > 1 and ep_size > 1:
-        raise ValueError("use tensor parallel for dense models and expert parallel for MoE models")
+    if tp_size > 1 and ep_size > 1 and (tp_size != ep_size or tp_rank != ep_rank):
+        raise ValueError("head-sharded attention with expert parallelism uses the same ranks for both")
     path = Path(path)
+    cfg_path = path / "config.json"
+    cfg = json.loads(cfg_path.read_text()) if cfg_path.exists() else {}
     if tie_word_embeddings is None:
-        cfg = json.loads((path / "config.json").read_text())
         tie_word_embeddings = bool(cfg.get("tie_word_embeddings", False))
+    n_kv_heads = int(cfg.get("num_key_value_heads", 0))
     by_file: Dict[Path, List[str]] = {}
     for name, f in checkpoint_files(path).items():
         by_file.setdefault(f, []).append(name)
@@ -103,7 +113,7 @@ def load_mlx_checkpoint(path, device, tp_size: int = 1, tp_rank: int = 0, ep_siz
             for name in sorted(names):
                 sl = h.get_slice(name)
                 shape = list(sl.get_shape())
-                rows, cols = _part(name, shape, tp_size, tp_rank, ep_size, ep_rank)
+                rows, cols = _part(name, shape, tp_size, tp_rank, ep_size, ep_rank, n_kv_heads)
                 if rows is not None:
                     t = sl[rows[0]:rows[1]]
                 elif cols is not None:

@@ -22,6 +22,7 @@ import torch
 from . import _lib
 from ._lib import M5ModelCfg, call
 from .cache import PromptCache, make_prompt_cache
+from .distributed import kv_heads_local
 from .ops import _stream
 
 
@@ -200,7 +201,7 @@ class Model:
         self.device = torch.device(device)
         self.weights = weights
         self.tp_size, self.tp_rank, self.ep_size, self.ep_rank = tp_size, tp_rank, ep_size, ep_rank
-        self.n_kv_heads_local = args.num_key_value_heads // tp_size
+        self.n_kv_heads_local = kv_heads_local(args.num_key_value_heads, tp_size)
         self.layers = [None] * args.num_hidden_layers
         cfg = M5ModelCfg(
             hidden_size=args.hidden_size, num_layers=args.num_hidden_layers, num_heads=args.num_attention_heads,

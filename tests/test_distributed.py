@@ -39,7 +39,14 @@ def test_tensor_parallel_shards_recompose(tp):
     shards = [shard_weights(full, args, tp_size=tp, tp_rank=r) for r in range(tp)]
     p = "model.layers.1."
     for name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "mlp.gate_proj", "mlp.up_proj"):
+        kv = name in ("self_attn.k_proj", "self_attn.v_proj")
         for suf in (".weight", ".scales", ".biases"):
+            if kv and args.num_key_value_heads < tp:  # each kv head replicated on tp / Hkv ranks
+                per = tp // args.num_key_value_heads
+                for r, s in enumerate(shards):
+                    h = r // per
+                    assert torch.equal(s[p + name + suf], full[p + name + suf][h * 128:(h + 1) * 128]), name
+                continue
             cat = torch.cat([s[p + name + suf] for s in shards], dim=0)
             assert torch.equal(cat, full[p + name + suf]), name
     for name in ("self_attn.o_proj", "mlp.down_proj"):
@@ -95,7 +102,14 @@ def test_shard_errors():
         shard_weights(full, args, ep_size=2, ep_rank=0)  # dense model
     moe = ModelArgs.from_dict(TINY_MOE)
     with pytest.raises(ValueError):
-        shard_weights(_host(TINY_MOE), moe, tp_size=2, tp_rank=0)
+        shard_weights(_host(TINY_MOE), moe, tp_size=2, tp_rank=0)  # heads without the experts
+    with pytest.raises(ValueError):
+        shard_weights(_host(TINY_MOE), moe, tp_size=2, tp_rank=0, ep_size=2, ep_rank=1)  # different ranks
+    with pytest.raises(ValueError):
+        shard_weights(_host(TINY_MOE), moe, tp_size=2, tp_rank=0, ep_size=4, ep_rank=0)  # different groups
+    with pytest.raises(ValueError):  # 3 kv heads neither split over nor replicate onto 2 ranks
+        shard_weights(full, ModelArgs.from_dict(dict(TINY, num_attention_heads=12, num_key_value_heads=3)),
+                      tp_size=2, tp_rank=0)
 
 
 def _exchange_worker(rank, world, port, q):
@@ -159,3 +173,49 @@ def test_device_check_maps_error_word(monkeypatch):
     with pytest.raises(_lib.M5CudaError) as e:
         _lib.device_check()
     assert e.value.code == _lib.M5_ERR_TIMEOUT
+
+
+def test_kv_head_placement():
+    from myinfer_b200.distributed import kv_head_first, kv_heads_local
+    assert [kv_heads_local(8, t) for t in (1, 2, 4, 8)] == [8, 4, 2, 1]
+    assert [kv_heads_local(4, t) for t in (2, 4, 8)] == [2, 1, 1]  # 8 ranks: each kv head on 2 ranks
+    assert [kv_head_first(4, 8, r) for r in range(8)] == [0, 0, 1, 1, 2, 2, 3, 3]
+    assert [kv_head_first(8, 4, r) for r in range(4)] == [0, 2, 4, 6]
+    with pytest.raises(ValueError):
+        kv_heads_local(4, 3)
+    with pytest.raises(ValueError):
+        kv_heads_local(3, 2)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_moe_head_sharded_with_experts(world):
+    """MoE with attention heads sharded over the expert-parallel ranks: q rows
+    and o_proj columns split by heads, k/v rows of the rank's kv head (each of
+    the 4 kv heads replicated on world / 4 ranks at 8), lm_head rows split,
+    experts split, router replicated; every rank's q heads belong to the kv
+    head it holds (GQA group = heads // kv_heads)."""
+    cfg = dict(TINY_MOE, num_attention_heads=16, num_key_value_heads=4, num_experts=16)
+    args = ModelArgs.from_dict(cfg)
+    full = _host(cfg)
+    D, Hq, Hkv = 128, 16, 4
+    shards = [shard_weights(full, args, tp_size=world, tp_rank=r, ep_size=world, ep_rank=r) for r in range(world)]
+    p = "model.layers.1."
+    for suf in (".weight", ".scales", ".biases"):
+        assert torch.equal(torch.cat([s[p + "self_attn.q_proj" + suf] for s in shards]), full[p + "self_attn.q_proj" + suf])
+        assert torch.equal(torch.cat([s[p + "self_attn.o_proj" + suf] for s in shards], dim=-1),
+                           full[p + "self_attn.o_proj" + suf])
+        assert torch.equal(torch.cat([s["lm_head" + suf] for s in shards]), full["lm_head" + suf])
+        ex = p + "mlp.switch_mlp.up_proj" + suf
+        assert torch.equal(torch.cat([s[ex] for s in shards]), full[ex])
+    for r, s in enumerate(shards):
+        hq0 = r * Hq // world                       # first q head of the rank
+        kv = hq0 // (Hq // Hkv)                      # its group's kv head
+        n_kv = max(1, Hkv // world)
+        assert (hq0 + Hq // world - 1) // (Hq // Hkv) < kv + n_kv  # all the rank's q heads map into its kv heads
+        for name in ("self_attn.k_proj", "self_attn.v_proj"):
+            assert torch.equal(s[p + name + ".weight"], full[p + name + ".weight"][kv * D:(kv + n_kv) * D])
+        assert torch.equal(s[p + "mlp.gate.weight"], full[p + "mlp.gate.weight"])
+    # experts generated per rank are taken as they are
+    local = {k: (v[:16 // world] if ".switch_mlp." in k else v) for k, v in full.items()}
+    s0 = shard_weights(local, args, tp_size=world, tp_rank=0, ep_size=world, ep_rank=0, experts_local=True)
+    assert torch.equal(s0[p + "mlp.switch_mlp.down_proj.weight"], shards[0][p + "mlp.switch_mlp.down_proj.weight"])

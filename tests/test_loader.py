@@ -64,6 +64,18 @@ def test_expert_parallel_rank_reads_its_experts(tmp_path, ep):
               shard_weights(w, args, ep_size=ep, ep_rank=r))
 
 
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_sharded_moe_rank_reads_its_shard(tmp_path, world):
+    """Attention heads and experts over the same ranks (kv heads replicated at
+    4 ranks: 2 kv heads)."""
+    w = _weights(MOE)
+    save_mlx_checkpoint(tmp_path, MOE, w, files=3)
+    args = ModelArgs.from_dict(MOE)
+    for r in range(world):
+        _same(load_mlx_checkpoint(tmp_path, "cpu", tp_size=world, tp_rank=r, ep_size=world, ep_rank=r),
+              shard_weights(w, args, tp_size=world, tp_rank=r, ep_size=world, ep_rank=r))
+
+
 def test_uneven_split_is_rejected(tmp_path):
     w = _weights(MOE)
     save_mlx_checkpoint(tmp_path, MOE, w)

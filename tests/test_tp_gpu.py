@@ -1,7 +1,7 @@
-"""Tensor-parallel (dense) and expert-parallel (MoE) decode on 2 GPUs against
-the same model on one GPU: the ranks' fp32 partial sums are all-reduced, so
-logits agree to fp32 summation-order noise and greedy tokens are identical.
-For MoE that noise can flip a router tie (the router's probabilities are bf16,
+"""Tensor-parallel (dense), expert-parallel (MoE) and expert-parallel MoE with
+head-sharded attention decode on 2 GPUs against the same model on one GPU:
+the ranks' fp32 partial sums are all-reduced, so logits agree to fp32
+summation-order noise and greedy tokens are identical.  For MoE that noise can flip a router tie (the router's probabilities are bf16,
 so the k-th and (k+1)-th expert often tie exactly): the runs may part from the
 first step whose routing the oracle finds within 1e-3 of a tie, the allowance
 the single-GPU model tests make too.  Skipped with fewer than two GPUs."""
@@ -23,7 +23,7 @@ TINY_MOE = dict(TINY, model_type="qwen3_moe", num_experts=16, num_experts_per_to
 TINY_MOE8 = dict(TINY_MOE, num_experts=32, num_experts_per_tok=8, moe_intermediate_size=192)
 
 
-def _run(cfg, rank, world, prompt, n, prefill_step):
+def _run(cfg, rank, world, prompt, n, prefill_step, heads=False):
     from myinfer_b200.cache import make_prompt_cache
     from myinfer_b200.distributed import Communicator, shard_weights
     from myinfer_b200.generate import generate_step
@@ -38,6 +38,8 @@ def _run(cfg, rank, world, prompt, n, prefill_step):
     if world > 1:
         comm = Communicator(world, rank)
         kw = dict(ep_size=world, ep_rank=rank) if moe else dict(tp_size=world, tp_rank=rank)
+        if moe and heads:  # attention heads sharded over the expert-parallel ranks
+            kw.update(tp_size=world, tp_rank=rank)
         w = shard_weights(full, args, **kw)
     else:
         kw, w = {}, full
@@ -52,7 +54,7 @@ def _run(cfg, rank, world, prompt, n, prefill_step):
     return toks, logits
 
 
-def _worker(rank, world, port, cfg, prompt, n, step, q):
+def _worker(rank, world, port, cfg, prompt, n, step, q, heads=False):
     import datetime
 
     import torch.distributed as dist
@@ -61,7 +63,7 @@ def _worker(rank, world, port, cfg, prompt, n, step, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        q.put((rank, _run(cfg, rank, world, prompt, n, step)))
+        q.put((rank, _run(cfg, rank, world, prompt, n, step, heads)))
     finally:
         dist.destroy_process_group()
 
@@ -80,16 +82,17 @@ def _router_tie_rows(cfg, prompt, n, step):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("cfg", [TINY, TINY_MOE, TINY_MOE8], ids=["tp2-dense", "ep2-moe", "ep2-moe-top8"])
+@pytest.mark.parametrize("cfg,heads", [(TINY, False), (TINY_MOE, False), (TINY_MOE8, False), (TINY_MOE8, True)],
+                         ids=["tp2-dense", "ep2-moe", "ep2-moe-top8", "ep2-tp2-attention-moe-top8"])
 @pytest.mark.parametrize("step", [8, 64], ids=["gemv-prefill", "gemm-prefill"])
-def test_two_rank_matches_one(cfg, step):
+def test_two_rank_matches_one(cfg, heads, step):
     import torch.multiprocessing as mp
     prompt = np.random.default_rng(4).integers(0, cfg["vocab_size"], 80).tolist()
     n = 8
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29400 + os.getpid() % 500
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, cfg, prompt, n, step, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, cfg, prompt, n, step, q, heads)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
