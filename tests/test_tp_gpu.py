@@ -1,10 +1,11 @@
 """Tensor-parallel (dense), expert-parallel (MoE) and expert-parallel MoE with
 head-sharded attention decode on 2 GPUs against the same model on one GPU:
 the ranks' fp32 partial sums are all-reduced, so logits agree to fp32
-summation-order noise and greedy tokens are identical.  For MoE that noise can flip a router tie (the router's probabilities are bf16,
-so the k-th and (k+1)-th expert often tie exactly): the runs may part from the
-first step whose routing the oracle finds within 1e-3 of a tie, the allowance
-the single-GPU model tests make too.  Skipped with fewer than two GPUs."""
+summation-order noise and greedy tokens are identical.  For MoE that noise
+can flip a router tie (the router's probabilities are bf16, so the k-th and
+(k+1)-th expert often tie exactly): the runs may part from the first step
+whose routing the oracle finds within 1e-3 of a tie, the allowance the
+single-GPU model tests make too.  Skipped with fewer than two GPUs."""
 
 import os
 
