@@ -149,8 +149,30 @@ def measured_peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops", 1590.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def attention_block() -> list:
+    """The attention op alone: 64 q / 8 kv heads, D 128,
+    bf16 q, K/V N(0, 1) quantized to 8 and 4 bits, at 4K / 32K / 128K keys;
+    decode (one query) against HBM, a causal 2048-query prefill chunk against
+    bf16 tensor throughput.  Device time per call, graph-replayed; several
+    KV sets rotate where they fit so the decode reads come from HBM."""
+    from myinfer_b200.microbench import bench_attention
+    peaks = measured_peaks()
+    out = []
+    for s in (4096, 32768, 131072):
+        for bits in (8, 4):
+            for l in (1, 2048):
+                r = bench_attention(s, l, bits, 64, 8, 20 if l == 1 else 3)
+                row = {"keys": s, "queries": l, "kv_bits": bits, "us": r["us"]}
+                if l == 1:
+                    row.update(gbs=r["gbs"], hbm_frac_of_measured=round(r["gbs"] / peaks["hbm_gbs"], 4))
+                else:
+                    row.update(tflops=r["tflops"], tensor_frac_of_measured=round(r["tflops"] / peaks["bf16_tflops"], 4))
+                out.append(row)
+    return out
 
 
 # ----------------------------------------------------------------- CPU legs
@@ -592,10 +614,12 @@ def run_gpu(args) -> dict:
         "tokens_match_n1": check,
         "load_seconds": round(load_s, 1),
     }
-    # kernels per decode step: per layer qkv, rope/append, attention (+ combine), o, gate/up, down
-    # (+ 2 residual adds under tensor parallelism); embed, lm_head, argmax, length update
-    # MoE: q|k|v, rope/append, attention, combine, o, router, top-k, expert gate/up, expert down
-    per_layer = (9 + (1 if world > 1 else 0)) if a.num_experts else (7 + (2 if world > 1 else 0))
+    # kernels per decode step: per layer q|k|v (QK-norm, RoPE and KV append in its
+    # epilogue), attention, combine, o, gate/up, down (+ 2 peer all-reduces under
+    # tensor parallelism); embed, lm_head, argmax, length update.
+    # MoE: q|k|v, attention, combine, o, router + top-k, expert gate/up, expert down
+    # (+ the o_proj and expert all-reduces when sharded)
+    per_layer = (7 + (2 if world > 1 else 0)) if a.num_experts else (6 + (2 if world > 1 else 0))
     out["gpu_launches"] = args.steps * (a.num_hidden_layers * per_layer + 4)
     del model
     torch.cuda.empty_cache()
@@ -603,6 +627,8 @@ def run_gpu(args) -> dict:
         out["moe"] = [moe_block(cx, "qwen3-30b-a3b", args, min(args.steps, 32))]
         if world >= 4:  # 132 GB of weights: 33 GB per rank at EP4
             out["moe"].append(moe_block(cx, "qwen3-235b-a22b", args, min(args.steps, 16)))
+    if world == 1 and not args.no_attention:
+        out["attention_op"] = attention_block()
     if cx.rank == 0 and not args.no_cpu:
         out["cpu_baseline"] = cpu_decode_sample(cfg, ctx, args.kv_bits, threads=os.cpu_count() or 1, budget_s=15.0)
     if world > 1:
@@ -652,6 +678,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-moe", action="store_true", help="skip the expert-parallel MoE block")
+    ap.add_argument("--no-attention", action="store_true", help="skip the attention-op block (1 GPU)")
     args = ap.parse_args()
     if args.ctx is None:
         args.ctx = DEFAULTS[args.config][0]

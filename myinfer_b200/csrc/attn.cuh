@@ -50,7 +50,7 @@ int attn_pf_launch(const AttnArgs& a, cudaStream_t stream);
 int attn_pf_error(int reset);
 
 // Prefill kernel on tcgen05 / TMEM (attn_tc.cu): the shapes of attn_pf, one
-// CTA of 128 rows per SM; used where attn_pf is eligible when M5_ATTN_TC=1.
+// CTA of 128 rows per SM; used where attn_pf is eligible unless M5_ATTN_TC=0.
 bool attn_tc_eligible(const AttnArgs& a);
 void attn_tc_plan(const AttnArgs& a, int S_max, int max_split, int& QB, int& nsplit);
 int attn_tc_launch(const AttnArgs& a, cudaStream_t stream);

@@ -88,6 +88,15 @@ __device__ __forceinline__ uint32_t hsixteenth(uint32_t x) {
   return r;
 }
 
+// 2^x (ex2.approx; -inf gives 0).  exp(x) is taken as 2^(x log2 e): relative
+// error ~1e-6, far below the bf16 rounding p goes through.
+__device__ __forceinline__ float am_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float AM_LOG2E = 1.4426950408889634f;
+
 // fp16 pair (code_a, code_b) exactly, from 8-bit codes at bytes ia, ib of w.
 template <int SEL>
 __device__ __forceinline__ uint32_t code8_pair(uint32_t w) {
@@ -264,6 +273,7 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
       qp[nb][e] = qpos[r];
     }
   const bool causal = a.mask_kind == M5_MASK_CAUSAL;
+  const int qp_first = S - a.L + q0;  // position of the CTA's first query
 
   // O^T accumulators: block (G, jj) rows g / g+8 are dims 64G + 8g + 2jj (+1),
   // columns 2t, 2t+1 are query rows 2t + 8nb, 2t + 1 + 8nb
@@ -334,6 +344,10 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
     const float sk[2][2] = {{bf16_lo(ksA), bf16_hi(ksA)}, {bf16_lo(ksB), bf16_hi(ksB)}};
     const float bk[2][2] = {{bf16_lo(kbA), bf16_hi(kbA)}, {bf16_lo(kbB), bf16_hi(kbB)}};
     const int keyA = key_base + g, keyB = key_base + 8 + g;
+    // a tile that reaches past the range end or across the causal diagonal
+    // masks per key and row; inside ones skip the tests (warp-uniform)
+    const int tile_end = k_begin + (it + 1) * AM_TK;
+    const bool edge = tile_end > k_end || (causal && tile_end - 1 > qp_first);
     float sc[NB][4];
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb)
@@ -342,9 +356,11 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
         const int kk = i >> 1, e = i & 1;
         const float s = fmaf(sk[kk][0], dG[nb][0][i], bk[kk][0] * qsr[nb][e][0]) +
                         fmaf(sk[kk][1], dG[nb][1][i], bk[kk][1] * qsr[nb][e][1]);
-        const int key = kk ? keyB : keyA;
-        const bool valid = key < k_end && (!causal || key <= qp[nb][e]);
-        sc[nb][i] = valid ? rbf(s) : -INFINITY;
+        sc[nb][i] = rbf(s);
+        if (edge) {
+          const int key = kk ? keyB : keyA;
+          if (!(key < k_end && (!causal || key <= qp[nb][e]))) sc[nb][i] = -INFINITY;
+        }
       }
 
     // ---------------- online softmax: column (row) maxima over the 8 key lanes
@@ -360,7 +376,7 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
         pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
         pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
         const float mn = fmaxf(m_run[nb][e], pm);
-        corr[nb][e] = (m_run[nb][e] == mn) ? 1.f : (m_run[nb][e] == -INFINITY ? 0.f : expf(m_run[nb][e] - mn));
+        corr[nb][e] = (m_run[nb][e] == mn) ? 1.f : (m_run[nb][e] == -INFINITY ? 0.f : am_ex2((m_run[nb][e] - mn) * AM_LOG2E));
         changed |= corr[nb][e] != 1.f;
         m_run[nb][e] = mn;
       }
@@ -383,20 +399,29 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
       }
     }
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
+    for (int nb = 0; nb < NB; ++nb) {
+      float ml[2];  // m log2 e (0 while a row has seen no key: its scores are -inf and p = 0)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) ml[e] = m_run[nb][e] == -INFINITY ? 0.f : m_run[nb][e] * AM_LOG2E;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        p[nb][i] = (sc[nb][i] == -INFINITY) ? 0.f : expf(sc[nb][i] - m_run[nb][i & 1]);
+        p[nb][i] = am_ex2(fmaf(sc[nb][i], AM_LOG2E, -ml[i & 1]));
         l_run[nb][i & 1] += p[nb][i];
       }
+    }
 
     // ---------------- O^T += V^T P^T
-    const uint32_t vsA = *reinterpret_cast<const uint32_t*>(sb + LY::VS_OFF + (kw0 + g) * 4);
-    const uint32_t vsB = *reinterpret_cast<const uint32_t*>(sb + LY::VS_OFF + (kw0 + 8 + g) * 4);
-    const uint32_t vbA = *reinterpret_cast<const uint32_t*>(sb + LY::VB_OFF + (kw0 + g) * 4);
-    const uint32_t vbB = *reinterpret_cast<const uint32_t*>(sb + LY::VB_OFF + (kw0 + 8 + g) * 4);
-    // masked keys have p == 0; their stage bytes may be stale, so never multiply them
-    auto mul = [](float r, float x) { return r == 0.f ? 0.f : r * x; };
+    uint32_t vsA = *reinterpret_cast<const uint32_t*>(sb + LY::VS_OFF + (kw0 + g) * 4);
+    uint32_t vsB = *reinterpret_cast<const uint32_t*>(sb + LY::VS_OFF + (kw0 + 8 + g) * 4);
+    uint32_t vbA = *reinterpret_cast<const uint32_t*>(sb + LY::VB_OFF + (kw0 + g) * 4);
+    uint32_t vbB = *reinterpret_cast<const uint32_t*>(sb + LY::VB_OFF + (kw0 + 8 + g) * 4);
+    // keys past the range end have p == 0 but stale stage bytes (possibly NaN
+    // scales): their scales become 0 so no product with them is formed
+    if (edge) {
+      if (keyA >= k_end) vsA = vbA = 0u;
+      if (keyB >= k_end) vsB = vbB = 0u;
+    }
+    auto mul = [](float r, float x) { return r * x; };
     // B fragments per value group: p * vscale * 2^6 of this lane's keys, moved
     // to the (keys 2t, 2t+1 ; row g) layout with one transpose per 8 keys
     uint32_t pb[NB][2][2];  // [nb][group][b0 / b1]

@@ -33,6 +33,7 @@
 // role, records a device error and still frees TMEM.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "attn.cuh"
 #include "tcgen05.cuh"
@@ -122,23 +123,36 @@ __device__ __forceinline__ uint64_t atc_now() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes (or the hint runs out) instead of issuing poll instructions that
+// take slots from the working warps of its sub-partition.
+__device__ __forceinline__ bool try_wait_hint(uint64_t* bar, uint32_t par, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(par), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait by one thread (~2 s), failure shared through `fail`.
-__device__ __forceinline__ bool wait1(uint64_t* bar, uint32_t par, volatile int* fail) {
+// hint_ns = 0 polls without suspending.
+__device__ __forceinline__ bool wait1(uint64_t* bar, uint32_t par, volatile int* fail, uint32_t hint_ns) {
   if (mbar_try_wait_fast(bar, par)) return true;
   const uint64_t t0 = atc_now();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_fast(bar, par)) return true;
+    if (hint_ns ? try_wait_hint(bar, par, hint_ns) : mbar_try_wait_fast(bar, par)) return true;
     if (*fail) return false;
-    if ((i & 255) == 0 && atc_now() - t0 > 2000000000ull) break;
+    if ((hint_ns || (i & 255) == 0) && atc_now() - t0 > 2000000000ull) break;
   }
   *fail = 1;
   atomicExch(&g_attn_tc_err, M5_DEV_ERR_WAIT_TIMEOUT);
   return false;
 }
 // Bounded wait by a whole warp with a warp-uniform result.
-__device__ __forceinline__ bool waitw(uint64_t* bar, uint32_t par, volatile int* fail, int lane) {
+__device__ __forceinline__ bool waitw(uint64_t* bar, uint32_t par, volatile int* fail, int lane, uint32_t hint_ns) {
   bool ok = true;
-  if (lane == 0) ok = wait1(bar, par, fail);
+  if (lane == 0) ok = wait1(bar, par, fail, hint_ns);
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (ok) (void)mbar_try_wait_fast(bar, par);  // acquire for every lane (the phase is complete)
   return ok;
@@ -162,7 +176,7 @@ __device__ __forceinline__ float sum32(const float (&x)[32]) {
 }
 
 template <int BITS>
-__global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, const uint32_t hint_ns) {
   using PK = Packed<BITS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
       int issued = 0;
       for (int t = 0; t < ntiles; ++t) {
         const int st = t % STAGES;
-        if (!wait1(&empty[st], ((t / STAGES) & 1) ^ 1, fail)) break;
+        if (!wait1(&empty[st], ((t / STAGES) & 1) ^ 1, fail, hint_ns)) break;
         const int key0 = k_begin + t * TK;
         const int nk = (min(TK, k_end - key0) + 3) & ~3;  // whole 16-byte scale rows
         uint8_t* sb = ring + size_t(st) * PK::STAGE;
@@ -261,16 +275,16 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
         issued = t + 1;
       }
       // the copies in flight land before the CTA may exit
-      for (int t = std::max(0, issued - STAGES); t < issued; ++t) (void)wait1(&full[t % STAGES], (t / STAGES) & 1, fail);
+      for (int t = std::max(0, issued - STAGES); t < issued; ++t) (void)wait1(&full[t % STAGES], (t / STAGES) & 1, fail, hint_ns);
     }
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(ROWS, TK), idesc_o = idesc_f16(ROWS, 128);
-      bool ok = ntiles > 0 && wait1(q_ready, 0, fail);
+      bool ok = ntiles > 0 && wait1(q_ready, 0, fail, hint_ns);
       auto issue_s = [&](int t) -> bool {
         const int bb = t & 1;
-        if (!wait1(&op_full[bb], (t >> 1) & 1, fail) || !wait1(&s_empty[bb], ((t >> 1) & 1) ^ 1, fail)) return false;
+        if (!wait1(&op_full[bb], (t >> 1) & 1, fail, hint_ns) || !wait1(&s_empty[bb], ((t >> 1) & 1) ^ 1, fail, hint_ns)) return false;
         tc_fence_after();
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
@@ -286,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
       if (ok) ok = issue_s(0);
       for (int t = 0; t < ntiles && ok; ++t) {
         if (t + 1 < ntiles && !(ok = issue_s(t + 1))) break;
-        if (!(ok = wait1(p_full, t & 1, fail))) break;
+        if (!(ok = wait1(p_full, t & 1, fail, hint_ns))) break;
         tc_fence_after();
         const int bb = t & 1;
         const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_V));
@@ -299,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
       }
       // every MMA issued has completed before TMEM may be freed
       tc_commit(mma_idle);
-      (void)wait1(mma_idle, 0, fail);
+      (void)wait1(mma_idle, 0, fail, hint_ns);
     }
   } else if (warp >= SMX_WARPS) {
     // ---------------------------------------------------------------- dequant
@@ -307,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     const int vkb = d >> 4, vdw = d & 15, vg = vdw >> 3;  // V task: keys 8 vkb .., dims 8 vdw ..
     for (int t = 0; t < ntiles; ++t) {
       const int st = t % STAGES, bb = t & 1;
-      if (!waitw(&full[st], (t / STAGES) & 1, fail, lane) || !waitw(&op_empty[bb], ((t >> 1) & 1) ^ 1, fail, lane))
+      if (!waitw(&full[st], (t / STAGES) & 1, fail, lane, hint_ns) || !waitw(&op_empty[bb], ((t >> 1) & 1) ^ 1, fail, lane, hint_ns))
         break;
       const uint8_t* sb = ring + size_t(st) * PK::STAGE;
       uint8_t* ob = opb + size_t(bb) * OPBUF;
@@ -420,8 +434,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     bool ok = true;
     for (int t = 0; t < ntiles && ok; ++t) {
       const int bb = t & 1;
-      if (!(ok = waitw(&s_full[bb], (t >> 1) & 1, fail, lane))) break;
-      if (!(ok = waitw(&op_full[bb], (t >> 1) & 1, fail, lane))) break;  // K scales of the tile
+      if (!(ok = waitw(&s_full[bb], (t >> 1) & 1, fail, lane, hint_ns))) break;
+      if (!(ok = waitw(&op_full[bb], (t >> 1) & 1, fail, lane, hint_ns))) break;  // K scales of the tile
       tc_fence_after();
       const float4* ksb = reinterpret_cast<const float4*>(opb + size_t(bb) * OPBUF + SB_OFF) + 32 * kh;
       const int key0 = k_begin + t * TK + 32 * kh;
@@ -453,7 +467,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
       s_xmax[t & 1][kh][r] = tmax;
       __syncwarp();
       if (lane == 0) mbar_arrive(&xbar[2 * rq + (t & 1)]);
-      if (!(ok = waitw(&xbar[2 * rq + (t & 1)], (t >> 1) & 1, fail, lane))) break;
+      if (!(ok = waitw(&xbar[2 * rq + (t & 1)], (t >> 1) & 1, fail, lane, hint_ns))) break;
       tmax = fmaxf(tmax, s_xmax[t & 1][kh ^ 1][r]);
       const float mn = fmaxf(m_run, tmax);
       const float corr = (m_run == mn) ? 1.f : (m_run == -INFINITY ? 0.f : ex2((m_run - mn) * LOG2E));
@@ -470,7 +484,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
         tmem_st16(tmem + lrow + P_COL + 32u * (t & 1) + 16u * kh, v);
       }
       // the previous tile's PV has finished: O is stable
-      if (t > 0 && !(ok = waitw(pv_done, (t - 1) & 1, fail, lane))) break;
+      if (t > 0 && !(ok = waitw(pv_done, (t - 1) & 1, fail, lane, hint_ns))) break;
       tc_fence_after();
       if (t > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
@@ -496,12 +510,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     }
     // ---- finish: wait for the last PV, add the two halves' denominators,
     // normalise this warp's 64 dims and write them
-    if (ok && ntiles > 0) ok = waitw(pv_done, (ntiles - 1) & 1, fail, lane);
+    if (ok && ntiles > 0) ok = waitw(pv_done, (ntiles - 1) & 1, fail, lane, hint_ns);
     if (ok) {
       s_xl[kh][r] = l_run;
       __syncwarp();
       if (lane == 0) mbar_arrive(&xend[rq]);
-      ok = waitw(&xend[rq], 0, fail, lane);
+      ok = waitw(&xend[rq], 0, fail, lane, hint_ns);
     }
     tc_fence_after();
     if (ok) {
@@ -555,12 +569,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a) {
 
 }  // namespace atc
 
-// M5_ATTN_TC=1 selects the tcgen05 kernel for prefill attention; otherwise
-// the mma.sync kernel (attn_pf.cu) runs.
+// The tcgen05 kernel runs prefill attention; M5_ATTN_TC=0 selects the
+// mma.sync kernel (attn_pf.cu) instead.
 static bool attn_tc_enabled() {
   static const bool on = [] {
     const char* e = getenv("M5_ATTN_TC");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   return on;
 }
@@ -578,20 +592,30 @@ void attn_tc_plan(const AttnArgs& a, int S_max, int max_split, int& QB, int& nsp
   nsplit = (int)std::max(1LL, std::min<long long>(std::min<long long>(want, tiles), max_split));
 }
 
+// Suspend-time hint of the kernel's mbarrier waits (M5_ATTN_TC_HINT_NS, 0 = poll).
+static uint32_t attn_tc_hint_ns() {
+  static const uint32_t v = [] {
+    const char* e = getenv("M5_ATTN_TC_HINT_NS");
+    return e ? uint32_t(strtoul(e, nullptr, 10)) : 1000000u;
+  }();
+  return v;
+}
+
 int attn_tc_launch(const AttnArgs& a, cudaStream_t stream) {
   dim3 grid(a.nsplit, (a.L + a.QB - 1) / a.QB, a.B * a.Hkv);
+  const uint32_t hint = attn_tc_hint_ns();
   if (a.bits == 8) {
     constexpr size_t smem = atc::smem_bytes<8>();
     static DeviceOnce once;  // the attribute belongs to each device's context
     M5_CUDA(once.run(
         [&] { return cudaFuncSetAttribute(atc::attn_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
-    atc::attn_tc_kernel<8><<<grid, atc::THREADS, smem, stream>>>(a);
+    atc::attn_tc_kernel<8><<<grid, atc::THREADS, smem, stream>>>(a, hint);
   } else {
     constexpr size_t smem = atc::smem_bytes<4>();
     static DeviceOnce once;
     M5_CUDA(once.run(
         [&] { return cudaFuncSetAttribute(atc::attn_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
-    atc::attn_tc_kernel<4><<<grid, atc::THREADS, smem, stream>>>(a);
+    atc::attn_tc_kernel<4><<<grid, atc::THREADS, smem, stream>>>(a, hint);
   }
   M5_LAUNCH_CHECK("prefill attention (tcgen05) launch");
   return M5_OK;
