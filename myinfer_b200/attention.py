@@ -90,11 +90,3 @@ def safe_maybe_quantize_kv_cache(prompt_cache, quantized_kv_start: int, kv_group
         if type(c) is KVCache and c.offset >= quantized_kv_start:
             prompt_cache[i] = c.to_quantized(group_size=kv_group_size, bits=kv_bits)
 
-
-_installed = False
-
-
-def install() -> None:
-    """Make the token loop use these two operators (idempotent)."""
-    global _installed
-    _installed = True

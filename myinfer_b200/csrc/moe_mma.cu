@@ -1,24 +1,23 @@
 // Routed experts of one decode token on the tensor cores (kernel K6, T = 1).
 //
-// The CUDA-core expert GEMVs (moe.cu) spend ~2.5 issue slots per 4-bit
-// weight and stay near 0.5 TB/s whatever their grid; here the expert
-// projections run the register-prefetch MMA scheme of gemv_mma.cu
+// The expert projections run the register-prefetch MMA scheme of gemv_mma.cu
 // (mma.sync m16n8k16 bf16, codes as exact (128 + q) pairs, per-group fold
-// s*D + (b - 128 s)*sum(x), fine-grained (tile, group) steps dealt to every
-// warp, split tiles through the zeroed fp32 scratch with a last-arriver
-// epilogue), over the rows of the routed experts only:
+// s*D + (b - 128 s)*sum(x), up to MX_PIPE (tile, group) steps of loads in
+// flight per warp) over the rows of the routed experts only, and every tile
+// is finished inside one CTA: the CTA's 8 warps split its tiles' steps, write
+// their partial sums to shared memory and the tile is their sum in warp order
+// (no global atomics, no fences, a fixed summation order):
 //   gate/up - tile = 8 gate rows + the 8 matching up rows of one routed
-//             expert; input RMSNorm(h) staged once per CTA; the tile's last
-//             arriver writes bf16(bf16(g * bf16(sigmoid g)) * u) (mlx-lm
-//             SwiGLU) into act[slot][I];
-//   down    - the k SwiGLU rows are staged as the k B-columns of the MMA, so
-//             a tile (16 rows of one routed expert) computes every slot's
-//             column and keeps its own; its last arriver writes the row's
-//             bf16(bf16(y) * score) into ybuf[slot][H], and the last slot to
-//             finish a 16-row block adds the slots in slot order,
-//             h += bf16(sum_j bf16(bf16(y_j) * score_j)) (mlx-lm
-//             Qwen3MoeSparseMoeBlock), or writes the fp32 sum as this rank's
-//             partial under expert parallelism.
+//             expert, a few whole tiles per CTA (about two CTAs per SM);
+//             input RMSNorm(h) staged once per CTA; the tile's SwiGLU rows
+//             bf16(bf16(g * bf16(sigmoid g)) * u) (mlx-lm) go to
+//             act[slot][I];
+//   down    - one CTA per 16 output rows, all local slots: the k SwiGLU rows
+//             are staged as the k B-columns of the MMA, tile ls (16 rows of
+//             slot ls's expert) keeps its own column, and the CTA adds the
+//             slots in slot order, h += bf16(sum_j bf16(bf16(y_j) * score_j))
+//             (mlx-lm Qwen3MoeSparseMoeBlock), or writes the fp32 sum as this
+//             rank's partial under expert parallelism.
 // Only experts in [e_first, e_first + e_local) are streamed; each CTA lists
 // the token's local slots from the router ids, so no host sync is needed.
 #include <algorithm>
@@ -154,145 +153,116 @@ __device__ __forceinline__ void mx_walk(long long s_begin, long long s_end, int 
   if (c_done) flush(c_tile, tot, c_done);
 }
 
-// warp's range of `steps` steps over the grid's warps
-__device__ __forceinline__ void mx_range(long long steps, long long& b, long long& e) {
-  const long long nw = (long long)gridDim.x * MX_W, wid = (long long)blockIdx.x * MX_W + (threadIdx.x >> 5);
-  b = steps * wid / nw;
-  e = steps * (wid + 1) / nw;
+// This CTA's whole tiles [tile0, tile0 + ntile) of NG steps each: the warps
+// split the steps evenly (contiguous ranges), and each warp's partial sum of
+// a tile lands in part[(tile - tile0) * MX_W + warp][16] (rows; the B column
+// col_of(tile) of the MMA).  Slots no warp writes stay zero.  After the
+// trailing barrier every tile's rows are the sum of its MX_W partials, added
+// by the caller in warp order: no global atomics, a fixed summation order.
+template <int MT, class RowOf, class ColOf>
+__device__ __forceinline__ void mx_cta_tiles(int tile0, int ntile, int K, const uint32_t* xf, const float* xg,
+                                             float* part, RowOf row_of, ColOf col_of) {
+  const int NG = K >> 6, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  for (int i = threadIdx.x; i < ntile * MX_W * 16; i += blockDim.x) part[i] = 0.f;
+  __syncthreads();
+  const long long steps = (long long)ntile * NG;
+  const long long b = (long long)tile0 * NG + steps * warp / MX_W, e = (long long)tile0 * NG + steps * (warp + 1) / MX_W;
+  auto flush = [&](int tile, const float (&tot)[4], int) {
+    const int j = col_of(tile);
+    if ((j >> 1) == tq) {
+      float* p = part + ((tile - tile0) * MX_W + warp) * 16;
+      p[g] = tot[j & 1];
+      p[g + 8] = tot[2 + (j & 1)];
+    }
+  };
+  if (b < e) mx_walk<MT>(b, e, K, xf, xg, row_of, flush);
+  __syncthreads();
+}
+
+// Sum of the MX_W warp partials of local tile t, row r (warp order).
+__device__ __forceinline__ float mx_tile_sum(const float* part, int t, int r) {
+  float v = 0.f;
+#pragma unroll
+  for (int w = 0; w < MX_W; ++w) v += part[(t * MX_W + w) * 16 + r];
+  return v;
 }
 
 // Gate/up of the token's local slots (nl of them, slot / local expert lists in
-// shared memory) over this CTA's share of the (slot, 8-row tile, group) steps.
-__device__ __forceinline__ void mx_gu_body(const MoeArgs& a, int nl, const int* s_slot, const int* s_eid,
+// shared memory): this CTA takes `tpc` whole (slot, 8-row) tiles; the tile's
+// SwiGLU rows bf16(bf16(g * bf16(sigmoid g)) * u) (mlx-lm) go to act[slot][I].
+__device__ __forceinline__ void mx_gu_body(const MoeArgs& a, int nl, const int* s_slot, const int* s_eid, int tpc,
                                            unsigned char* smem_raw) {
   const int H = a.H, I = a.I, NG = H >> 6;
   const int tpe = I / 8;  // tiles per expert
   uint32_t* xf = reinterpret_cast<uint32_t*>(smem_raw);  // [NG][4][8] bf16 pairs
   float* xg = reinterpret_cast<float*>(xf + NG * 32);    // [NG]
   float* red = xg + NG;                                  // [33]
-  // every thread of the CTA stages (the staging synchronises the CTA), before
-  // the per-warp step ranges let idle warps leave
+  float* part = red + 33;                                // [tpc][MX_W][16]
+  // every thread of the CTA stages (the staging synchronises the CTA)
   stage_frag<1, MX_W * 32>(a.x, H, H, a.norm_w, a.eps, xf, xg, red, 0);
-  long long sb, se;
-  mx_range((long long)nl * tpe * NG, sb, se);
-  if (sb >= se) return;
-  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int tile0 = blockIdx.x * tpc;
+  const int ntile = min(tpc, nl * tpe - tile0);
+  if (ntile <= 0) return;  // CTA-uniform
   auto row_of = [&](int tile, int r16, QW& m, size_t& rr) {
     const int ls = tile / tpe, rt = tile % tpe;
     m = r16 < 8 ? a.gate : a.up;
     rr = size_t(s_eid[ls]) * I + rt * 8 + (r16 & 7);
   };
-  auto flush = [&](int tile, const float (&tot)[4], int done) {
-    float* acc = a.acc;
-    const int base = tile * 16;
-    if (tq == 0) {  // token column 0
-      atomicAdd(&acc[base + g], tot[0]);
-      atomicAdd(&acc[base + g + 8], tot[2]);
+  mx_cta_tiles<1>(tile0, ntile, H, xf, xg, part, row_of, [](int) { return 0; });
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < ntile; t += MX_W) {
+    if (lane < 8) {
+      const float gv = rbf(mx_tile_sum(part, t, lane)), uv = rbf(mx_tile_sum(part, t, lane + 8));
+      const float sg = rbf(1.f / (1.f + expf(-gv)));
+      const int tile = tile0 + t, ls = tile / tpe, rt = tile % tpe;
+      a.act[size_t(s_slot[ls]) * I + rt * 8 + lane] = f2bf(rbf(gv * sg) * uv);
     }
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = (atomicAdd(&a.cnt[tile], done) + done == NG);
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      __threadfence();
-      if (lane < 8) {
-        float* p = &acc[base + lane];
-        const float v = __ldcg(p), u = __ldcg(p + 8);
-        p[0] = 0.f;
-        p[8] = 0.f;
-        const float gv = rbf(v), uv = rbf(u);
-        const float sg = rbf(1.f / (1.f + expf(-gv)));
-        const int ls = tile / tpe, rt = tile % tpe;
-        a.act[size_t(s_slot[ls]) * I + rt * 8 + lane] = f2bf(rbf(gv * sg) * uv);
-      }
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) a.cnt[tile] = 0;
-    }
-  };
-  mx_walk<1>(sb, se, H, xf, xg, row_of, flush);
+  }
 }
 
-// Down projection of the nl local slots, the k SwiGLU rows staged as the MMA's
-// B columns (CG: read through L2, rows written by other CTAs of this launch),
-// then the score-weighted slot combine into h (or the fp32 partial).
-template <int MT, bool CG>
+// Down projection of the nl local slots for the 16 output rows nb * 16 ..
+// (nb = blockIdx.x): the k SwiGLU rows are staged as the MMA's B columns and
+// tile ls (16 rows of local slot ls's expert) keeps column s_slot[ls]; then
+// h += bf16(sum_j bf16(bf16(y_j) * score_j)) over the slots in slot order
+// (mlx-lm Qwen3MoeSparseMoeBlock), or the fp32 sum as this rank's partial
+// under expert parallelism.
+template <int MT>
 __device__ __forceinline__ void mx_down_body(const MoeArgs& a, int nl, const int* s_slot, const int* s_eid,
                                              unsigned char* smem_raw) {
   const int H = a.H, I = a.I, NG = I >> 6;
-  const int tpe = H / 16;
   uint32_t* xf = reinterpret_cast<uint32_t*>(smem_raw);  // [MT][NG][4][8]
   float* xg = reinterpret_cast<float*>(xf + MT * NG * 32);  // [MT][NG]
-  float* red = xg + MT * NG;
-  stage_frag<MT, MX_W * 32, false, CG>(a.act, I, I, nullptr, 0.f, xf, xg, red, 0);  // whole CTA, as above
-  long long sb, se;
-  mx_range((long long)nl * tpe * NG, sb, se);
-  if (sb >= se) return;
-  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  float* red = xg + MT * NG;                                // [33]
+  float* part = red + 33;                                   // [nl][MX_W][16]
+  stage_frag<MT, MX_W * 32>(a.act, I, I, nullptr, 0.f, xf, xg, red, 0);
+  const int nb = blockIdx.x;
   auto row_of = [&](int tile, int r16, QW& m, size_t& rr) {
-    const int ls = tile / tpe, nb = tile % tpe;
     m = a.down;
-    rr = size_t(s_eid[ls]) * H + nb * 16 + r16;
+    rr = size_t(s_eid[tile]) * H + nb * 16 + r16;
   };
-  auto flush = [&](int tile, const float (&tot)[4], int done) {
-    float* acc = a.acc;
-    const int base = tile * 16;
-    const int ls = tile / tpe, nb = tile % tpe;
-    const int j = s_slot[ls];  // this tile's own B column
-    if ((j >> 1) == tq) {
-      atomicAdd(&acc[base + g], tot[j & 1]);
-      atomicAdd(&acc[base + g + 8], tot[2 + (j & 1)]);
+  mx_cta_tiles<MT>(0, nl, I, xf, xg, part, row_of, [&](int tile) { return s_slot[tile]; });
+  if (threadIdx.x < 16) {
+    const int r = threadIdx.x, n = nb * 16 + r;
+    float sum = 0.f;
+    for (int ls = 0; ls < nl; ++ls)
+      sum += rbf(rbf(mx_tile_sum(part, ls, r)) * bf2f(a.scores[s_slot[ls]]));
+    if (a.partial) {
+      a.partial[n] = sum;
+    } else {
+      bf16* o = a.h + n;
+      *o = f2bf(bf2f(*o) + rbf(sum));
     }
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = (atomicAdd(&a.cnt[tile], done) + done == NG);
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    const float sj = bf2f(__ldcg(a.scores + j));
-    if (lane < 16) {
-      float* p = &acc[base + lane];
-      const float y = rbf(__ldcg(p));
-      *p = 0.f;
-      a.ybuf[size_t(j) * H + nb * 16 + lane] = rbf(y * sj);
-    }
-    __threadfence();
-    __syncwarp();
-    int blk_last = 0;
-    if (lane == 0) {
-      a.cnt[tile] = 0;
-      blk_last = (atomicAdd(&a.ncnt[nb], 1) + 1 == nl);
-    }
-    blk_last = __shfl_sync(0xffffffffu, blk_last, 0);
-    if (!blk_last) return;
-    __threadfence();
-    if (lane < 16) {
-      const int n = nb * 16 + lane;
-      float sum = 0.f;
-      for (int q = 0; q < nl; ++q) sum += __ldcg(&a.ybuf[size_t(s_slot[q]) * H + n]);
-      if (a.partial) {
-        a.partial[n] = sum;
-      } else {
-        bf16* o = a.h + n;
-        *o = f2bf(bf2f(*o) + rbf(sum));
-      }
-    }
-    __syncwarp();
-    if (lane == 0) a.ncnt[nb] = 0;
-  };
-  mx_walk<MT>(sb, se, I, xf, xg, row_of, flush);
+  }
 }
 
-__global__ void __launch_bounds__(MX_W * 32, 2) moe_gu_mma_kernel(const MoeArgs a) {
+__global__ void __launch_bounds__(MX_W * 32, 2) moe_gu_mma_kernel(const MoeArgs a, const int tpc) {
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
   const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
   if (nl == 0) return;
-  mx_gu_body(a, nl, s_slot, s_eid, smem_raw);
+  mx_gu_body(a, nl, s_slot, s_eid, tpc, smem_raw);
 }
 
 template <int MT>
@@ -303,11 +273,10 @@ __global__ void __launch_bounds__(MX_W * 32, 2) moe_down_mma_kernel(const MoeArg
   __shared__ int s_slot[MX_KMAX], s_eid[MX_KMAX], s_n;
   const int nl = mx_local_slots(a, s_slot, s_eid, &s_n);
   if (nl == 0) {  // no expert of this token is local: this rank's share is zero
-    if (a.partial)
-      for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < a.H; n += gridDim.x * blockDim.x) a.partial[n] = 0.f;
+    if (a.partial && threadIdx.x < 16) a.partial[blockIdx.x * 16 + threadIdx.x] = 0.f;
     return;
   }
-  mx_down_body<MT, false>(a, nl, s_slot, s_eid, smem_raw);
+  mx_down_body<MT>(a, nl, s_slot, s_eid, smem_raw);
 }
 
 // Softmax (fp32, rounded to bf16) and top-k of the E router logits by one
@@ -421,14 +390,20 @@ int moe_router_topk_launch(const MoeRouterArgs& a, cudaStream_t st) {
   return M5_OK;
 }
 
-static size_t mx_smem(int MT, int K) { return size_t(MT) * (K / 64) * 32 * 4 + size_t(MT) * (K / 64) * 4 + 33 * 4; }
+// staged activations, group sums, staging scratch, then the tile partials
+static size_t mx_smem(int MT, int K, int tiles) {
+  return size_t(MT) * (K / 64) * 32 * 4 + size_t(MT) * (K / 64) * 4 + 33 * 4 + size_t(tiles) * MX_W * 16 * 4;
+}
+// Whole (slot, 8-row) gate/up tiles per CTA: about two CTAs per SM.
+static int mx_gu_tpc(const MoeArgs& a) {
+  const long long tiles = (long long)a.k * (a.I / 8);
+  return (int)std::max(1LL, (tiles + 2LL * sm_count() - 1) / (2LL * sm_count()));
+}
 
 
 bool moe_mma_eligible(const MoeArgs& a) {
-  return a.T == 1 && a.k == MX_KMAX && a.acc && a.cnt && a.ybuf && a.ncnt && a.H % 64 == 0 && a.I % 64 == 0 &&
-         a.I % 8 == 0 && a.H % 16 == 0 && size_t(a.k) * a.I * 2 <= size_t(a.acc_rows) &&
-         size_t(a.k) * a.H <= size_t(a.acc_rows) && mx_smem(MX_KMAX, a.I) <= 200 * 1024 &&
-         mx_smem(1, a.H) <= 200 * 1024;
+  return a.T == 1 && a.k == MX_KMAX && a.H % 64 == 0 && a.I % 64 == 0 && a.I % 8 == 0 && a.H % 16 == 0 &&
+         mx_smem(MX_KMAX, a.I, MX_KMAX) <= 200 * 1024 && mx_smem(1, a.H, mx_gu_tpc(a)) <= 200 * 1024;
 }
 
 int moe_mma_launch(const MoeArgs& a, cudaStream_t st) {
@@ -439,17 +414,17 @@ int moe_mma_launch(const MoeArgs& a, cudaStream_t st) {
     return cudaFuncSetAttribute(moe_down_mma_kernel<MX_KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  200 * 1024);
   }));
-  const int max_ctas = 2 * sm_count();
   {
-    const long long steps = (long long)a.k * (a.I / 8) * (a.H / 64);
-    const int grid = (int)std::max(1LL, std::min<long long>(max_ctas, (steps + MX_W * 4 - 1) / (MX_W * 4)));
-    M5_CUDA(launch_pdl(moe_gu_mma_kernel, dim3(grid), dim3(MX_W * 32), mx_smem(1, a.H), st, a));
+    // grid for all k slots; CTAs past the local slots' tiles leave at once
+    const int tpc = mx_gu_tpc(a);
+    const int grid = (int)std::max(1LL, ((long long)a.k * (a.I / 8) + tpc - 1) / tpc);
+    M5_CUDA(launch_pdl(moe_gu_mma_kernel, dim3(grid), dim3(MX_W * 32), mx_smem(1, a.H, tpc), st, a, tpc));
     M5_LAUNCH_CHECK("moe gate/up (tensor core) launch");
   }
   {
-    const long long steps = (long long)a.k * (a.H / 16) * (a.I / 64);
-    const int grid = (int)std::max(1LL, std::min<long long>(max_ctas, (steps + MX_W * 4 - 1) / (MX_W * 4)));
-    M5_CUDA(launch_pdl(moe_down_mma_kernel<MX_KMAX>, dim3(grid), dim3(MX_W * 32), mx_smem(MX_KMAX, a.I), st, a));
+    const int grid = a.H / 16;  // one CTA per 16 output rows, every local slot
+    M5_CUDA(launch_pdl(moe_down_mma_kernel<MX_KMAX>, dim3(grid), dim3(MX_W * 32), mx_smem(MX_KMAX, a.I, MX_KMAX), st,
+                       a));
     M5_LAUNCH_CHECK("moe down (tensor core) launch");
   }
   return M5_OK;

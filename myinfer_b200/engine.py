@@ -27,7 +27,7 @@ from typing import Any, Dict, Iterator, List, Optional
 
 import torch
 
-from . import attention, sample
+from . import sample
 from .cache import PromptCache, make_prompt_cache
 from .context import (GB, MAX_YARN_FACTOR, ContextPlan, KVFootprint, apply_yarn, kv_estimate_per_token,
                       measure_kv_footprint, native_context, plan_context, reserve_bytes, yarn_capable,
@@ -192,7 +192,6 @@ def _load_model(opts: LoadOptions):
 
 class Engine:
     def __init__(self):
-        attention.install()
         self._lock = threading.RLock()
         self._gen_lock = threading.Lock()
         self.model = None
