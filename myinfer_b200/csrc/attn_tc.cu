@@ -74,9 +74,9 @@ constexpr int OP_K = 0, OP_V = 2 * OP_BYTES;
 constexpr int SB_OFF = 4 * OP_BYTES;
 constexpr int OPBUF = SB_OFF + TK * 16;
 
-template <int BITS>
+template <int BITS, int OPB>
 constexpr size_t smem_bytes() {
-  return 1024 + size_t(STAGES) * Packed<BITS>::STAGE + 2 * size_t(OPBUF) + 512;
+  return 1024 + size_t(STAGES) * Packed<BITS>::STAGE + OPB * size_t(OPBUF) + 512;
 }
 
 // Byte offset of 16-byte chunk j of row n in a 128-byte-swizzled K-major tile.
@@ -102,8 +102,12 @@ __device__ __forceinline__ uint32_t c8(uint32_t w, int i) {
 __device__ __forceinline__ uint32_t cpair(uint32_t lo, uint32_t hi) {
   return hsub1024(0x64006400u | lo | (hi << 16));
 }
-// A code (0..255) placed in the low mantissa bits of 2^23 reads 2^23 + code.
-__device__ __forceinline__ float code_f(uint32_t magic_bits) { return __uint_as_float(magic_bits) - 8388608.f; }
+// fp16 pair a * b + c, one rounding
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 // 2^x (ex2.approx; -inf gives 0)
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -175,19 +179,21 @@ __device__ __forceinline__ float sum32(const float (&x)[32]) {
   return (m[0] + m[2]) + (m[1] + m[3]);
 }
 
-template <int BITS>
+// OPB operand buffers: dequant runs up to OPB - 1 tiles ahead of the PV that
+// frees a buffer.
+template <int BITS, int OPB>
 __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, const uint32_t hint_ns) {
   using PK = Packed<BITS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base;
   uint8_t* opb = ring + size_t(STAGES) * PK::STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(opb + 2 * size_t(OPBUF));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(opb + OPB * size_t(OPBUF));
   uint64_t* full = bars;
   uint64_t* empty = full + STAGES;
   uint64_t* op_full = empty + STAGES;
-  uint64_t* op_empty = op_full + 2;
-  uint64_t* s_full = op_empty + 2;
+  uint64_t* op_empty = op_full + OPB;
+  uint64_t* s_full = op_empty + OPB;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
   uint64_t* pv_done = p_full + 1;
@@ -223,9 +229,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, c
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], DQ_WARPS);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < OPB; ++i) {
       mbar_init(&op_full[i], DQ_WARPS);
       mbar_init(&op_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], SMX_WARPS);
     }
@@ -283,12 +291,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, c
       constexpr uint32_t idesc_s = idesc_f16(ROWS, TK), idesc_o = idesc_f16(ROWS, 128);
       bool ok = ntiles > 0 && wait1(q_ready, 0, fail, hint_ns);
       auto issue_s = [&](int t) -> bool {
-        const int bb = t & 1;
-        if (!wait1(&op_full[bb], (t >> 1) & 1, fail, hint_ns) || !wait1(&s_empty[bb], ((t >> 1) & 1) ^ 1, fail, hint_ns)) return false;
+        const int bb = t & 1, ob = t % OPB;  // S buffer, operand buffer
+        if (!wait1(&op_full[ob], (t / OPB) & 1, fail, hint_ns) || !wait1(&s_empty[bb], ((t >> 1) & 1) ^ 1, fail, hint_ns)) return false;
         tc_fence_after();
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
-          const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_K + g * OP_BYTES));
+          const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(ob) * OPBUF + OP_K + g * OP_BYTES));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             tc_mma_ts(tmem + S_COL + 128u * bb + 64u * g, tmem + Q_COL + 32u * g + 8u * kk, bdesc + 2u * kk, idesc_s,
@@ -297,19 +305,23 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, c
         tc_commit(&s_full[bb]);
         return true;
       };
+      // S runs two tiles ahead (both S buffers), and PV(t) goes out as soon as
+      // P(t) is in TMEM: S(t + 2) needs the softmax to have read S(t), which it
+      // did before publishing P(t)
       if (ok) ok = issue_s(0);
+      if (ok && ntiles > 1) ok = issue_s(1);
       for (int t = 0; t < ntiles && ok; ++t) {
-        if (t + 1 < ntiles && !(ok = issue_s(t + 1))) break;
         if (!(ok = wait1(p_full, t & 1, fail, hint_ns))) break;
         tc_fence_after();
-        const int bb = t & 1;
-        const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(bb) * OPBUF + OP_V));
+        const int ob = t % OPB;
+        const uint64_t bdesc = tc_sdesc_sw128(smem_addr(opb + size_t(ob) * OPBUF + OP_V));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           tc_mma_ts(tmem + O_COL, tmem + P_COL + 32u * (t & 1) + 8u * kk, bdesc + 2u * kk, idesc_o,
                     (t > 0 || kk > 0) ? 1u : 0u);
         tc_commit(pv_done);
-        tc_commit(&op_empty[bb]);
+        tc_commit(&op_empty[ob]);
+        if (t + 2 < ntiles && !(ok = issue_s(t + 2))) break;
       }
       // every MMA issued has completed before TMEM may be freed
       tc_commit(mma_idle);
@@ -320,8 +332,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, c
     const int d = tid - SMX_WARPS * 32;  // 0..127
     const int vkb = d >> 4, vdw = d & 15, vg = vdw >> 3;  // V task: keys 8 vkb .., dims 8 vdw ..
     for (int t = 0; t < ntiles; ++t) {
-      const int st = t % STAGES, bb = t & 1;
-      if (!waitw(&full[st], (t / STAGES) & 1, fail, lane, hint_ns) || !waitw(&op_empty[bb], ((t >> 1) & 1) ^ 1, fail, lane, hint_ns))
+      const int st = t % STAGES, bb = t % OPB;
+      if (!waitw(&full[st], (t / STAGES) & 1, fail, lane, hint_ns) || !waitw(&op_empty[bb], ((t / OPB) & 1) ^ 1, fail, lane, hint_ns))
         break;
       const uint8_t* sb = ring + size_t(st) * PK::STAGE;
       uint8_t* ob = opb + size_t(bb) * OPBUF;
@@ -341,13 +353,15 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, c
         }
         *reinterpret_cast<uint4*>(ob + OP_K + g * OP_BYTES + sw128(n, j)) = o;
       }
-      // V: keys 8 vkb .. 8 vkb + 7 x dims 8 vdw .. 8 vdw + 7, dequantized and
-      // transposed; zero past the last key.  Chunk e of the 8 dims is taken in
-      // the rotated order (e' + vdw) & 7, so the 8 lanes of a store phase hit 8
-      // different 16-byte bank groups of the swizzled rows.
+      // V: keys 8 vkb .. 8 vkb + 7 x dims 8 vdw .. 8 vdw + 7, transposed and
+      // dequantized two keys at a time in fp16: the exact code pair (keys 2m,
+      // 2m + 1 at one dim) times the pair's scales plus their biases, one
+      // fp16 rounding (scales and biases are bf16 values, exact in fp16 within
+      // its normal range); zero past the last key.  Chunk e of the 8 dims is
+      // taken in the rotated order (e' + vdw) & 7, so the 8 lanes of a store
+      // phase hit 8 different 16-byte bank groups of the swizzled rows.
       {
-        float vs[8], vb[8];
-        uint32_t wlo[8], whi[8];
+        uint32_t wlo[8], whi[8], vs2[4], vb2[4];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const int key = 8 * vkb + q;
@@ -359,25 +373,40 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, c
             wlo[q] = *reinterpret_cast<const uint32_t*>(sb + PK::V_OFF + key * 64 + 4 * vdw);
             whi[q] = 0;
           }
-          const uint32_t s2 = *reinterpret_cast<const uint32_t*>(sb + PK::VS_OFF + 4 * key);
-          const uint32_t b2 = *reinterpret_cast<const uint32_t*>(sb + PK::VB_OFF + 4 * key);
-          const bool in = key < valid;
-          vs[q] = in ? (vg ? bf16_hi(s2) : bf16_lo(s2)) : 0.f;
-          vb[q] = in ? (vg ? bf16_hi(b2) : bf16_lo(b2)) : 0.f;
+        }
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int k0 = 8 * vkb + 2 * m;
+          float sv[2], bv[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint32_t s2 = *reinterpret_cast<const uint32_t*>(sb + PK::VS_OFF + 4 * (k0 + i));
+            const uint32_t b2 = *reinterpret_cast<const uint32_t*>(sb + PK::VB_OFF + 4 * (k0 + i));
+            const bool in = k0 + i < valid;
+            sv[i] = in ? (vg ? bf16_hi(s2) : bf16_lo(s2)) : 0.f;
+            bv[i] = in ? (vg ? bf16_hi(b2) : bf16_lo(b2)) : 0.f;
+          }
+          vs2[m] = pack_h2(sv[0], sv[1]);
+          vb2[m] = pack_h2(bv[0], bv[1]);
         }
 #pragma unroll
         for (int e0 = 0; e0 < 8; ++e0) {
           const int e = (e0 + vdw) & 7;
-          float v[8];
+          uint32_t o[4];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            uint32_t mb;
-            if constexpr (BITS == 8) mb = __byte_perm(e < 4 ? wlo[q] : whi[q], 0x4B000000u, 0x7540u | uint32_t(e & 3));
-            else mb = ((wlo[q] >> (4 * e)) & 15u) | 0x4B000000u;
-            v[q] = fmaf(code_f(mb), vs[q], vb[q]);
+          for (int m = 0; m < 4; ++m) {
+            uint32_t cp;  // fp16 pair (code of key 2m, code of key 2m + 1) at dim e, exact
+            if constexpr (BITS == 8) {
+              const uint32_t wa = e < 4 ? wlo[2 * m] : whi[2 * m], wb = e < 4 ? wlo[2 * m + 1] : whi[2 * m + 1];
+              const uint32_t ab = __byte_perm(wa, wb, uint32_t(e & 3) | (uint32_t(4 + (e & 3)) << 4));
+              cp = c8(ab, 0);
+            } else {
+              const uint32_t ab = __byte_perm(wlo[2 * m], wlo[2 * m + 1], uint32_t(e >> 1) | (uint32_t(4 + (e >> 1)) << 8));
+              cp = hsub1024(((ab >> (4 * (e & 1))) & 0x000F000Fu) | 0x64006400u);
+            }
+            o[m] = hfma2(cp, vs2[m], vb2[m]);
           }
-          const uint4 o = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
-          *reinterpret_cast<uint4*>(ob + OP_V + sw128(8 * vdw + e, vkb)) = o;
+          *reinterpret_cast<uint4*>(ob + OP_V + sw128(8 * vdw + e, vkb)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       // K scales / biases of the tile as fp32 (zero past the last key)
@@ -435,9 +464,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const AttnArgs a, c
     for (int t = 0; t < ntiles && ok; ++t) {
       const int bb = t & 1;
       if (!(ok = waitw(&s_full[bb], (t >> 1) & 1, fail, lane, hint_ns))) break;
-      if (!(ok = waitw(&op_full[bb], (t >> 1) & 1, fail, lane, hint_ns))) break;  // K scales of the tile
+      if (!(ok = waitw(&op_full[t % OPB], (t / OPB) & 1, fail, lane, hint_ns))) break;  // K scales of the tile
       tc_fence_after();
-      const float4* ksb = reinterpret_cast<const float4*>(opb + size_t(bb) * OPBUF + SB_OFF) + 32 * kh;
+      const float4* ksb = reinterpret_cast<const float4*>(opb + size_t(t % OPB) * OPBUF + SB_OFF) + 32 * kh;
       const int key0 = k_begin + t * TK + 32 * kh;
       float sc[32];
       {
@@ -601,22 +630,35 @@ static uint32_t attn_tc_hint_ns() {
   return v;
 }
 
+// Operand buffers of the kernel (M5_ATTN_TC_OPB, 2 or 3).
+static int attn_tc_opb() {
+  static const int v = [] {
+    const char* e = getenv("M5_ATTN_TC_OPB");
+    return e && e[0] == '2' ? 2 : 3;
+  }();
+  return v;
+}
+
+template <int BITS, int OPB>
+static cudaError_t attn_tc_launch_t(const AttnArgs& a, dim3 grid, uint32_t hint, cudaStream_t stream) {
+  constexpr size_t smem = atc::smem_bytes<BITS, OPB>();
+  static DeviceOnce once;  // the attribute belongs to each device's context
+  cudaError_t e = once.run([&] {
+    return cudaFuncSetAttribute(atc::attn_tc_kernel<BITS, OPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  if (e != cudaSuccess) return e;
+  atc::attn_tc_kernel<BITS, OPB><<<grid, atc::THREADS, smem, stream>>>(a, hint);
+  return cudaSuccess;
+}
+
 int attn_tc_launch(const AttnArgs& a, cudaStream_t stream) {
   dim3 grid(a.nsplit, (a.L + a.QB - 1) / a.QB, a.B * a.Hkv);
   const uint32_t hint = attn_tc_hint_ns();
-  if (a.bits == 8) {
-    constexpr size_t smem = atc::smem_bytes<8>();
-    static DeviceOnce once;  // the attribute belongs to each device's context
-    M5_CUDA(once.run(
-        [&] { return cudaFuncSetAttribute(atc::attn_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
-    atc::attn_tc_kernel<8><<<grid, atc::THREADS, smem, stream>>>(a, hint);
-  } else {
-    constexpr size_t smem = atc::smem_bytes<4>();
-    static DeviceOnce once;
-    M5_CUDA(once.run(
-        [&] { return cudaFuncSetAttribute(atc::attn_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); }));
-    atc::attn_tc_kernel<4><<<grid, atc::THREADS, smem, stream>>>(a, hint);
-  }
+  const bool three = attn_tc_opb() == 3;
+  cudaError_t e;
+  if (a.bits == 8) e = three ? attn_tc_launch_t<8, 3>(a, grid, hint, stream) : attn_tc_launch_t<8, 2>(a, grid, hint, stream);
+  else e = three ? attn_tc_launch_t<4, 3>(a, grid, hint, stream) : attn_tc_launch_t<4, 2>(a, grid, hint, stream);
+  M5_CUDA(e);
   M5_LAUNCH_CHECK("prefill attention (tcgen05) launch");
   return M5_OK;
 }
