@@ -409,13 +409,18 @@ __device__ __forceinline__ bool stage_i8_bulk(const bf16* __restrict__ x, int64_
         xg[t * NG + G] = gs;
         xs[t * NG + G] = __uint_as_float(uint32_t(max(1, min(254, 127 - sh))) << 23);
       }
-      uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};  // r = 0 even, 1 odd elements
+      // v = rint(e * up) by one fma against 1.5 * 2^23 (|e * up| < 2^15, so the
+      // single round-to-nearest-even lands on the integer): the sum's low
+      // mantissa bits hold v + 2^22, whose byte 0 is v's low byte and byte 1
+      // its high byte (two's complement); byte permutes gather four of each.
+      uint32_t f[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int iv = __float2int_rn(e[q] * up);
-        const uint32_t hb = uint32_t(iv >> 8) & 0xFFu, lb = uint32_t(iv) & 0xFFu;
-        hi[q & 1] |= hb << (8 * (q >> 1));
-        lo[q & 1] |= lb << (8 * (q >> 1));
+      for (int q = 0; q < 8; ++q) f[q] = __float_as_uint(fmaf(e[q], up, 12582912.f));
+      uint32_t hi[2], lo[2];  // r = 0 even, 1 odd elements
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        lo[r] = __byte_perm(__byte_perm(f[r], f[r + 2], 0x0040), __byte_perm(f[r + 4], f[r + 6], 0x0040), 0x5410);
+        hi[r] = __byte_perm(__byte_perm(f[r], f[r + 2], 0x0051), __byte_perm(f[r + 4], f[r + 6], 0x0051), 0x5410);
       }
       __syncwarp();  // every raw block of this warp's groups is in registers
       const int tq = cb >> 1, m = cb & 1;

@@ -40,10 +40,22 @@ constexpr int TP_UG = 16;                     // 64-column scale groups per unit
 constexpr int TP_W_STAGE = 16 * TP_UG * 32;    // 16 rows x UG groups x 32 bytes (1 KB swizzled boxes)
 constexpr int TP_SB_STAGE = 16 * TP_UG * 2;    // 16 rows x UG bf16 (scales or biases)
 constexpr int TP_BARS = 2 * TP_STAGES + 2;      // full, empty, activation copy (+ pad to 16 bytes)
+// Row blocks of a unit fetched by separate boxes: the two 8-row halves of a
+// SwiGLU tile come from the gate and the up matrix; any other tile's 16 rows
+// are one block of one segment (segments are whole tiles).
+#define TP_HALVES (EPI == EPI_SWIGLU ? 2 : 1)
 
 struct TmapSet {
   CUtensorMap w[3], s[3], b[3];  // per segment
 };
+
+__device__ __forceinline__ void tma3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
 
 __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -190,15 +202,16 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
         mbar_arrive_expect_tx(&full[st], TP_W_STAGE + 2 * TP_SB_STAGE);
         unsigned char* ws = wring + st * TP_W_STAGE;
         unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
+        // one 3-D box per row block: 32 words x rows x 4 128-byte chunks (the
+        // unit's 1024 columns), landing as [chunk][row][128 B] with the
+        // 128-byte swizzle keyed by the row; scales and biases one box each
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < TP_HALVES; ++h) {
           int si, row0;
           tp_half<EPI>(a, tile, h, si, row0);
-#pragma unroll
-          for (int bx = 0; bx < TP_UG / 4; ++bx)  // 1 KB box = 8 rows x 4 groups
-            tma2d(ws + (h * (TP_UG / 4) + bx) * 1024, &tm.w[si], ch * TP_UG * 8 + bx * 32, row0, &full[st]);
-          tma2d(ss + h * (TP_SB_STAGE / 2), &tm.s[si], ch * TP_UG, row0, &full[st]);
-          tma2d(ss + TP_SB_STAGE + h * (TP_SB_STAGE / 2), &tm.b[si], ch * TP_UG, row0, &full[st]);
+          tma3d(ws + h * (TP_W_STAGE / TP_HALVES), &tm.w[si], 0, row0, ch * (TP_UG / 4), &full[st]);
+          tma2d(ss + h * (TP_SB_STAGE / TP_HALVES), &tm.s[si], ch * TP_UG, row0, &full[st]);
+          tma2d(ss + TP_SB_STAGE + h * (TP_SB_STAGE / TP_HALVES), &tm.b[si], ch * TP_UG, row0, &full[st]);
         }
         if (++ch == NCH) {
           ch = 0;
@@ -232,11 +245,14 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
   const float xi0 = I8 ? 1.f : xinv[t0c], xi1 = I8 ? 1.f : xinv[t1c];
   // per-thread smem offsets of this warp's four groups inside a stage (the
   // 128-byte swizzle of the weight boxes depends only on g, tq and the group)
+  // stage layout [half][chunk][8 rows][128 B] (SwiGLU) or [chunk][16 rows][128 B]
+  constexpr uint32_t W_CHUNK = EPI == EPI_SWIGLU ? 1024 : 2048;  // bytes per 128-byte column chunk
+  constexpr uint32_t W_ROW8 = EPI == EPI_SWIGLU ? 4096 : 1024;   // offset of rows g + 8
   uint32_t woff[TP_UG / TP_CW];
 #pragma unroll
   for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
     const int c = 2 * jj + (tq >> 1);
-    woff[jj] = warp * 1024 + g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
+    woff[jj] = warp * W_CHUNK + g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
   }
   const uint32_t soff = g * (TP_UG * 2) + warp * (TP_UG / TP_CW) * 2;  // 4 consecutive bf16 of row g
 
@@ -392,7 +408,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
 #pragma unroll
         for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
           const uint2 w0 = *reinterpret_cast<const uint2*>(ws + woff[jj]);
-          const uint2 w8 = *reinterpret_cast<const uint2*>(ws + 4096 + woff[jj]);
+          const uint2 w8 = *reinterpret_cast<const uint2*>(ws + W_ROW8 + woff[jj]);
           const uint4 xh = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32);      // s8 plane
           const uint4 xl = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32 + 4);  // u8 plane
           int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
@@ -427,7 +443,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
 #pragma unroll
       for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
         const uint2 w0 = *reinterpret_cast<const uint2*>(ws + woff[jj]);
-        const uint2 w8 = *reinterpret_cast<const uint2*>(ws + 4096 + woff[jj]);
+        const uint2 w8 = *reinterpret_cast<const uint2*>(ws + W_ROW8 + woff[jj]);
         const uint4 xa = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32);
         const uint4 xb = *reinterpret_cast<const uint4*>(xfl + (G0 + jj) * 32 + 4);
         uint32_t pa0[4], pa8[4], pb0[4], pb8[4];
@@ -495,15 +511,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i) {
+// Maps of one segment; `brows` rows per box (16, or 8 for a SwiGLU half).
+// Weights as 3-D: 32 words of a 128-byte chunk, rows (stride K/2 bytes), the
+// K/256 chunks of a row (stride 128 bytes).
+static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i, int brows) {
   auto enc = encode_fn();
   if (!enc) return fail(M5_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t rows = (cuuint64_t)sg.rows;
   {
-    cuuint64_t dims[2] = {(cuuint64_t)K / 8, rows};
-    cuuint64_t strides[1] = {(cuuint64_t)K / 2};
-    cuuint32_t box[2] = {32, 8}, es[2] = {1, 1};
-    CUresult r = enc(&ts.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(sg.w), dims, strides, box, es,
+    cuuint64_t dims[3] = {32, rows, (cuuint64_t)K / 256};
+    cuuint64_t strides[2] = {(cuuint64_t)K / 2, 128};
+    cuuint32_t box[3] = {32, (cuuint32_t)brows, TP_UG / 4}, es[3] = {1, 1, 1};
+    CUresult r = enc(&ts.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint32_t*>(sg.w), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(M5_ERR_CUDA, "tensor map (weights) encode failed");
@@ -513,7 +532,7 @@ static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i) {
   for (int k = 0; k < 2; ++k) {
     cuuint64_t dims[2] = {(cuuint64_t)K / 64, rows};
     cuuint64_t strides[1] = {(cuuint64_t)K / 32};
-    cuuint32_t box[2] = {TP_UG, 8}, es[2] = {1, 1};
+    cuuint32_t box[2] = {TP_UG, (cuuint32_t)brows}, es[2] = {1, 1};
     CUresult r = enc(m2[k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(p2[k]), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -585,7 +604,7 @@ int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, i
   TmapSet ts;
   memset(&ts, 0, sizeof(ts));
   for (int i = 0; i < a.nseg && i < 3; ++i) {
-    int rc = make_maps(a.seg[i], a.K, ts, i);
+    int rc = make_maps(a.seg[i], a.K, ts, i, epi == EPI_SWIGLU ? 8 : 16);
     if (rc) return rc;
   }
   const bool i8 = tp_use_i8();
