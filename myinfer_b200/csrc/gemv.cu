@@ -234,10 +234,11 @@ __global__ void __launch_bounds__(GW * 32, MT == 1 ? 2 : 1) gemv_kernel(const Ge
 
 // Per-device zeroed scratch for tensor-core GEMV calls that bring none
 // (standalone m5_quantized_matmul / m5_moe_route).  Grows, never shrinks.
-int gemv_default_scratch(int rows, float** acc, int** cnt, int* cap_rows) {
+int gemv_default_scratch(int rows, float** acc, int** cnt, int* cap_rows, float** part, size_t* part_floats) {
   static std::mutex mu;
   static char* buf[64] = {nullptr};
   static int cap[64] = {0};
+  static float* slots[64] = {nullptr};
   int dev = 0;
   M5_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(M5_ERR_INVALID, "device index out of range");
@@ -257,9 +258,12 @@ int gemv_default_scratch(int rows, float** acc, int** cnt, int* cap_rows) {
     buf[dev] = p;
     cap[dev] = r16;
   }
+  if (!slots[dev]) M5_CUDA(cudaMalloc(&slots[dev], gemv_part_floats() * sizeof(float)));
   *acc = reinterpret_cast<float*>(buf[dev]);
   *cnt = reinterpret_cast<int*>(buf[dev] + size_t(8) * cap[dev] * sizeof(float));
   *cap_rows = cap[dev];
+  *part = slots[dev];
+  *part_floats = gemv_part_floats();
   return M5_OK;
 }
 
@@ -314,11 +318,13 @@ int gemv_launch(const GemvArgs& a_in, int MT, int epi, cudaStream_t stream) {
     float* acc = a.mma_acc;
     int* cnt = a.mma_cnt;
     int rows = a.mma_rows;
-    if (!(acc && cnt && rows >= vrows)) {
-      int rc = gemv_default_scratch(vrows, &acc, &cnt, &rows);
+    float* part = a.mma_part;
+    size_t part_floats = a.mma_part_floats;
+    if (!(acc && cnt && rows >= vrows && (!tmap || (part && part_floats >= gemv_part_floats())))) {
+      int rc = gemv_default_scratch(vrows, &acc, &cnt, &rows, &part, &part_floats);
       if (rc) return rc;
     }
-    if (tmap) return gemv_tmap_launch(a, MT, epi, acc, cnt, rows, stream);
+    if (tmap) return gemv_tmap_launch(a, MT, epi, part, part_floats, cnt, rows, stream);
     return gemv_mma_launch(a, MT, epi, acc, cnt, rows, stream);
   }
   if (gemv_tma_eligible(a.K, MT, epi)) return gemv_tma_launch(a, MT, epi, stream);

@@ -41,6 +41,10 @@ struct GemvArgs {
   float* mma_acc;
   int* mma_cnt;
   int mma_rows;
+  // Per-CTA slots for the tensor-map GEMV's tiles shared between CTAs
+  // (gemv_part_floats() floats; no zeroing needed); null: per-device scratch.
+  float* mma_part;
+  size_t mma_part_floats;
   // Row length of the weights, scales and biases when the call reduces over
   // only K columns of wider rows (a K slice; 0 = K).  Read by the prefill GEMM.
   int64_t ldk;
@@ -61,9 +65,14 @@ int gemv_launch(const GemvArgs& a, int MT, int epi, cudaStream_t stream);
 // Largest number of tokens one launch can stage for this K (shared memory).
 int gemv_max_tokens(int K);
 
-// TMA tensor-map + tensor-core variant (gemv_tmap.cu): K % 512 == 0.
+// TMA tensor-map + tensor-core variant (gemv_tmap.cu): K % 1024 == 0.  `part`
+// holds part_floats floats of per-CTA split-tile slots, `cnt` one zeroed
+// counter per 16-row tile for cnt_rows rows (both left as found).
 bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi);
-int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, int acc_rows, cudaStream_t stream);
+int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* part, size_t part_floats, int* cnt, int cnt_rows,
+                     cudaStream_t stream);
+// Slot floats a tensor-map GEMV launch of this device may need.
+size_t gemv_part_floats();
 int gemv_tmap_error(int reset);
 
 // Tensor-core variant (gemv_mma.cu): K % 64 == 0, segments of 16-row multiples.

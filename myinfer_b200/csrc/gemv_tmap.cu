@@ -151,7 +151,7 @@ __device__ __noinline__ void tp_rope_head(const RopeAppendArgs& r, int MT, int h
 // sums folded as s * 2^(E - 14) * D + b * sum(x).
 template <int MT, int EPI, bool I8>
 __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_constant__ GemvArgs a, const __grid_constant__ TmapSet tm,
-                                                               float* acc_buf, int* cnt_buf, int acc_rows) {
+                                                               float* part, int* cnt_buf) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 128-byte-swizzled boxes must start on 1 KB boundaries
   unsigned char* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
 
   float tot[4] = {0.f, 0.f, 0.f, 0.f};
   float totD[4] = {0.f, 0.f, 0.f, 0.f}, totB[4] = {0.f, 0.f, 0.f, 0.f};
-  int cur_tile = u0 < u1 ? int(u0 / NCH) : 0, done = 0;
+  int cur_tile = u0 < u1 ? int(u0 / NCH) : 0;
   // Epilogue of one finished tile row r16 / token t with its complete sum v.
   auto epilogue = [&](int tile, int r16, int t, float v, float vu) {
     if constexpr (EPI == EPI_SWIGLU) {
@@ -296,28 +296,40 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
     }
   };
   float* tred = reinterpret_cast<float*>(red + 8);  // [CW][MT][16] partial tile sums
-  // A tile whose units all lie in this CTA's range is reduced in shared memory
-  // by the four consumer warps (no global atomics, no fence); a tile shared
-  // with a neighbouring CTA goes through the zeroed global scratch and the
-  // last contributor finishes it.
+  // Every tile is first reduced over the four consumer warps in shared memory
+  // (warp order).  A tile whose units all lie in this CTA's range is finished
+  // at once; a tile shared with neighbouring CTAs leaves this CTA's sum in its
+  // own slot of `part` (slot 0: the CTA's first tile, 1: its last), and the
+  // CTA that completes the tile's unit count adds the slots of the CTAs that
+  // cover it in CTA order.  No floating-point atomics: the result does not
+  // depend on which CTA finishes first.
+  const long long G_ = gridDim.x;
+  auto unit_begin = [&](long long c) { return total * c / G_; };
+  auto cta_of = [&](long long u) {  // the CTA whose range holds unit u
+    long long c = u * G_ / total;
+    while (c + 1 < G_ && unit_begin(c + 1) <= u) ++c;
+    while (c > 0 && unit_begin(c) > u) --c;
+    return int(c);
+  };
   auto flush = [&](int tile) {
     tot[0] = fmaf(totD[0], xi0, totB[0]);
     tot[1] = fmaf(totD[1], xi1, totB[1]);
     tot[2] = fmaf(totD[2], xi0, totB[2]);
     tot[3] = fmaf(totD[3], xi1, totB[3]);
     const int t0 = 2 * tq, t1 = 2 * tq + 1;
-    const bool whole = (long long)tile * NCH >= u0 && (long long)(tile + 1) * NCH <= u1;
-    if (whole) {
-      if (t0 < MT) {
-        tred[(warp * MT + t0) * 16 + g] = tot[0];
-        tred[(warp * MT + t0) * 16 + g + 8] = tot[2];
-      }
-      if (t1 < MT) {
-        tred[(warp * MT + t1) * 16 + g] = tot[1];
-        tred[(warp * MT + t1) * 16 + g + 8] = tot[3];
-      }
-      named_sync(2, TP_CW * 32);
-      if (warp == 0) {
+    const long long tb = (long long)tile * NCH, te = tb + NCH;  // the tile's units
+    const bool whole = tb >= u0 && te <= u1;
+    if (t0 < MT) {
+      tred[(warp * MT + t0) * 16 + g] = tot[0];
+      tred[(warp * MT + t0) * 16 + g + 8] = tot[2];
+    }
+    if (t1 < MT) {
+      tred[(warp * MT + t1) * 16 + g] = tot[1];
+      tred[(warp * MT + t1) * 16 + g + 8] = tot[3];
+    }
+    named_sync(2, TP_CW * 32);
+    if (warp == 0) {
+      if (whole) {
         for (int q = lane; q < 16 * MT; q += 32) {
           const int r16 = q & 15, t = q >> 4;
           float v = 0.f, vu = 0.f;
@@ -329,50 +341,53 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
           if (EPI != EPI_SWIGLU || r16 < 8) epilogue(tile, r16, t, v, vu);
         }
         if constexpr (EPI == EPI_STORE) rope_tile(tile);
-      }
-      named_sync(2, TP_CW * 32);
-    } else {
-      const int base = tile * 16;
-      if (t0 < MT) {
-        atomicAdd(&acc_buf[t0 * acc_rows + base + g], tot[0]);
-        atomicAdd(&acc_buf[t0 * acc_rows + base + g + 8], tot[2]);
-      }
-      if (t1 < MT) {
-        atomicAdd(&acc_buf[t1 * acc_rows + base + g], tot[1]);
-        atomicAdd(&acc_buf[t1 * acc_rows + base + g + 8], tot[3]);
-      }
-      __threadfence();
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) last = (atomicAdd(&cnt_buf[tile], done) + done == NG);
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence();
+      } else {
+        float* mine = part + (size_t(blockIdx.x) * 2 + (tb <= u0 ? 0 : 1)) * (MT * 16);
         for (int q = lane; q < 16 * MT; q += 32) {
           const int r16 = q & 15, t = q >> 4;
-          float* p = &acc_buf[t * acc_rows + base + r16];
-          if (EPI == EPI_SWIGLU) {
-            if (r16 < 8) {
-              float* pu = &acc_buf[t * acc_rows + base + r16 + 8];
-              const float v = __ldcg(p), u = __ldcg(pu);
-              *p = 0.f;
-              *pu = 0.f;
-              epilogue(tile, r16, t, v, u);
-            }
-          } else {
-            const float v = __ldcg(p);
-            *p = 0.f;
-            epilogue(tile, r16, t, v, 0.f);
-          }
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < TP_CW; ++w) v += tred[(w * MT + t) * 16 + r16];
+          mine[q] = v;
         }
+        __threadfence();  // the slot, before the count
         __syncwarp();
-        if (lane == 0) cnt_buf[tile] = 0;
-        if constexpr (EPI == EPI_STORE) rope_tile(tile);
+        const int here = int(min(u1, te) - max(u0, tb));
+        int last = 0;
+        if (lane == 0) last = (atomicAdd(&cnt_buf[tile], here) + here == NCH);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();  // the other CTAs' slots, after their counts
+          const int c_lo = cta_of(tb), c_hi = cta_of(te - 1);
+          constexpr int QN = (16 * MT + 31) / 32;  // rows x tokens per lane
+          float v[QN], vu[QN];
+#pragma unroll
+          for (int k = 0; k < QN; ++k) v[k] = vu[k] = 0.f;
+          for (int c = c_lo; c <= c_hi; ++c) {  // CTA order
+            const float* p = part + (size_t(c) * 2 + (unit_begin(c) >= tb ? 0 : 1)) * (MT * 16);
+#pragma unroll
+            for (int k = 0; k < QN; ++k) {
+              const int q = lane + 32 * k;
+              if (q < 16 * MT) {
+                v[k] += __ldcg(p + q);
+                if (EPI == EPI_SWIGLU && (q & 15) < 8) vu[k] += __ldcg(p + q + 8);
+              }
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < QN; ++k) {
+            const int q = lane + 32 * k, r16 = q & 15, t = q >> 4;
+            if (q < 16 * MT && (EPI != EPI_SWIGLU || r16 < 8)) epilogue(tile, r16, t, v[k], vu[k]);
+          }
+          __syncwarp();
+          if (lane == 0) cnt_buf[tile] = 0;
+          if constexpr (EPI == EPI_STORE) rope_tile(tile);
+        }
       }
     }
+    named_sync(2, TP_CW * 32);
 #pragma unroll
     for (int i = 0; i < 4; ++i) tot[i] = totD[i] = totB[i] = 0.f;
-    done = 0;
   };
 
   bool failed = false;
@@ -484,7 +499,6 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
-    done += TP_UG / TP_CW;
     if (++ch == NCH) {
       ch = 0;
       ++tile;
@@ -571,36 +585,46 @@ bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
   return encode_fn() != nullptr;
 }
 
+// CTAs per SM the kernel may keep resident, at most (sizing of the slots).
+constexpr int TP_MAX_CTAS_PER_SM = 8;
+
+size_t gemv_part_floats() { return size_t(2) * 8 * 16 * TP_MAX_CTAS_PER_SM * sm_count(); }
+
 template <int MT, int EPI, bool I8>
-static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* acc, int* cnt, int acc_rows, cudaStream_t st) {
+static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* part, size_t part_floats, int* cnt,
+                       cudaStream_t st) {
   const size_t smem = tp_smem(MT, a.K, a.norm_w != nullptr, I8);
   static DeviceOnce once;  // the attribute belongs to each device's context
   M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
   int per_sm = 0;
   M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tmap_kernel<MT, EPI, I8>, TP_THREADS, smem));
+  per_sm = std::min(std::max(1, per_sm), TP_MAX_CTAS_PER_SM);
   const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
   const long long units = (long long)(vrows / 16) * (a.K / (64 * TP_UG));
-  const long long max_ctas = (long long)std::max(1, per_sm) * sm_count();
+  const long long max_ctas = (long long)per_sm * sm_count();
   const int grid = (int)std::max(1LL, std::min(max_ctas, units));
-  M5_CUDA(launch_pdl(gemv_tmap_kernel<MT, EPI, I8>, dim3(grid), dim3(TP_THREADS), smem, st, a, ts, acc, cnt, acc_rows));
+  if (size_t(grid) * 2 * MT * 16 > part_floats) return fail(M5_ERR_INVALID, "gemv_tmap: split-tile slots too small");
+  M5_CUDA(launch_pdl(gemv_tmap_kernel<MT, EPI, I8>, dim3(grid), dim3(TP_THREADS), smem, st, a, ts, part, cnt));
   return M5_OK;
 }
 
 template <int MT, bool I8>
-static int tp_launch_epi(const GemvArgs& a, int epi, const TmapSet& ts, float* acc, int* cnt, int rows,
+static int tp_launch_epi(const GemvArgs& a, int epi, const TmapSet& ts, float* part, size_t pf, int* cnt,
                          cudaStream_t st) {
   switch (epi) {
-    case EPI_STORE: return tp_launch_t<MT, EPI_STORE, I8>(a, ts, acc, cnt, rows, st);
-    case EPI_RESIDUAL: return tp_launch_t<MT, EPI_RESIDUAL, I8>(a, ts, acc, cnt, rows, st);
-    case EPI_SWIGLU: return tp_launch_t<MT, EPI_SWIGLU, I8>(a, ts, acc, cnt, rows, st);
-    case EPI_F32: return tp_launch_t<MT, EPI_F32, I8>(a, ts, acc, cnt, rows, st);
+    case EPI_STORE: return tp_launch_t<MT, EPI_STORE, I8>(a, ts, part, pf, cnt, st);
+    case EPI_RESIDUAL: return tp_launch_t<MT, EPI_RESIDUAL, I8>(a, ts, part, pf, cnt, st);
+    case EPI_SWIGLU: return tp_launch_t<MT, EPI_SWIGLU, I8>(a, ts, part, pf, cnt, st);
+    case EPI_F32: return tp_launch_t<MT, EPI_F32, I8>(a, ts, part, pf, cnt, st);
   }
   return fail(M5_ERR_INVALID, "gemv_tmap: bad epilogue");
 }
 
-int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, int acc_rows, cudaStream_t st) {
+int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* part, size_t part_floats, int* cnt, int cnt_rows,
+                     cudaStream_t st) {
   const int vrows = a.total_rows * (epi == EPI_SWIGLU ? 2 : 1);
-  if (vrows > acc_rows) return fail(M5_ERR_INVALID, "gemv_tmap: scratch too small for this matrix");
+  if (vrows > cnt_rows) return fail(M5_ERR_INVALID, "gemv_tmap: scratch too small for this matrix");
+  if (!part) return fail(M5_ERR_INVALID, "gemv_tmap: no split-tile slots");
   TmapSet ts;
   memset(&ts, 0, sizeof(ts));
   for (int i = 0; i < a.nseg && i < 3; ++i) {
@@ -609,22 +633,22 @@ int gemv_tmap_launch(const GemvArgs& a, int MT, int epi, float* acc, int* cnt, i
   }
   const bool i8 = tp_use_i8();
   switch (MT) {
-    case 1: return i8 ? tp_launch_epi<1, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<1, false>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 2: return i8 ? tp_launch_epi<2, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<2, false>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 3: return i8 ? tp_launch_epi<3, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<3, false>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 4: return i8 ? tp_launch_epi<4, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<4, false>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 5: return i8 ? tp_launch_epi<5, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<5, false>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 6: return i8 ? tp_launch_epi<6, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<6, false>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 7: return i8 ? tp_launch_epi<7, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<7, false>(a, epi, ts, acc, cnt, acc_rows, st);
-    case 8: return i8 ? tp_launch_epi<8, true>(a, epi, ts, acc, cnt, acc_rows, st)
-                 : tp_launch_epi<8, false>(a, epi, ts, acc, cnt, acc_rows, st);
+    case 1: return i8 ? tp_launch_epi<1, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<1, false>(a, epi, ts, part, part_floats, cnt, st);
+    case 2: return i8 ? tp_launch_epi<2, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<2, false>(a, epi, ts, part, part_floats, cnt, st);
+    case 3: return i8 ? tp_launch_epi<3, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<3, false>(a, epi, ts, part, part_floats, cnt, st);
+    case 4: return i8 ? tp_launch_epi<4, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<4, false>(a, epi, ts, part, part_floats, cnt, st);
+    case 5: return i8 ? tp_launch_epi<5, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<5, false>(a, epi, ts, part, part_floats, cnt, st);
+    case 6: return i8 ? tp_launch_epi<6, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<6, false>(a, epi, ts, part, part_floats, cnt, st);
+    case 7: return i8 ? tp_launch_epi<7, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<7, false>(a, epi, ts, part, part_floats, cnt, st);
+    case 8: return i8 ? tp_launch_epi<8, true>(a, epi, ts, part, part_floats, cnt, st)
+                 : tp_launch_epi<8, false>(a, epi, ts, part, part_floats, cnt, st);
   }
   return fail(M5_ERR_INVALID, "gemv_tmap: MT must be 1..8");
 }

@@ -25,7 +25,11 @@ namespace m5 {
 
 // Largest output dimension N (weight rows) the array covers.
 constexpr int kNoAllocMaxRows = 1 << 18;  // 262144 rows: every Qwen3 projection and the 151936-row vocabulary
-constexpr size_t kNoAllocBytes = size_t(8) * kNoAllocMaxRows * sizeof(float) + size_t(kNoAllocMaxRows / 16) * sizeof(int);
+// Split-tile slots of the tensor-map GEMV: 2 x 8 tokens x 16 rows per CTA, for
+// up to 8 CTAs on each of up to 256 SMs.
+constexpr size_t kNoAllocPartFloats = size_t(2) * 8 * 16 * 8 * 256;
+constexpr size_t kNoAllocBytes = size_t(8) * kNoAllocMaxRows * sizeof(float) + size_t(kNoAllocMaxRows / 16) * sizeof(int) +
+                                 kNoAllocPartFloats * sizeof(float);
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
@@ -68,9 +72,10 @@ extern "C" int m5_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K, 
   cudaStream_t st = (cudaStream_t)stream;
   const int rows16 = int((N + 15) / 16 * 16);
   // This call's layout inside the array: partial sums [8][rows16], then one
-  // counter per 16-row tile.  The split-tile protocol needs both zeroed; a
-  // finished launch leaves them zeroed, but an earlier call that stopped on
-  // an error may not have.
+  // counter per 16-row tile, then the per-CTA split-tile slots.  The partial
+  // sums and the counters must be zero; a finished launch leaves them zeroed,
+  // but an earlier call that stopped on an error may not have.  The slots are
+  // written before they are read.
   float* acc = reinterpret_cast<float*>(base);
   int* cnt = reinterpret_cast<int*>(base + size_t(8) * kNoAllocMaxRows * sizeof(float));
   M5_CUDA(cudaMemsetAsync(acc, 0, size_t(8) * rows16 * sizeof(float), st));
@@ -90,6 +95,9 @@ extern "C" int m5_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K, 
   a.mma_acc = acc;
   a.mma_cnt = cnt;
   a.mma_rows = rows16;
+  a.mma_part = reinterpret_cast<float*>(base + size_t(8) * kNoAllocMaxRows * sizeof(float) +
+                                        size_t(kNoAllocMaxRows / 16) * sizeof(int));
+  a.mma_part_floats = kNoAllocPartFloats;
   const int cap = gemv_max_tokens((int)K);
   for (int64_t t0 = 0; t0 < M;) {
     int mt = (int)std::min<int64_t>(8, M - t0);

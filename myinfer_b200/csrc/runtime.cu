@@ -66,6 +66,7 @@ struct Model {
   int* mma_cnt = nullptr;
   int mma_rows = 0;
   unsigned int* rope_cnt = nullptr;  // zeroed per-head counters of the q|k|v GEMV's fused rope epilogue
+  float* gemv_part = nullptr;        // split-tile slots of the tensor-map GEMV (gemv_part_floats())
   float* moe_ybuf = nullptr;  // zeroed [k, H] and [H/16] scratch of the tensor-core expert path
   int* moe_ncnt = nullptr;
   // MoE prefill grouped by expert (T >= kMoeGroupedMinTokens): expert-ordered rows and
@@ -233,6 +234,8 @@ static void attach(const Model* m, GemvArgs& a) {
   a.mma_acc = m->mma_acc;
   a.mma_cnt = m->mma_cnt;
   a.mma_rows = m->mma_rows;
+  a.mma_part = m->gemv_part;
+  a.mma_part_floats = m->gemv_part ? gemv_part_floats() : 0;
 }
 
 // One projection of T tokens: the tensor-core GEMM for prefill-sized T (with
@@ -987,7 +990,7 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
                           moe_pre ? size_t(2) * m->E_local * 4 : 0,
                           T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_rows * sk_n * 4 : 0,
                           T >= kGemmMinTokens ? size_t(Model::kSplitK) * sk_xs : 0,
-                          (QKV / 128 + 1) * sizeof(unsigned int)};
+                          (QKV / 128 + 1) * sizeof(unsigned int), gemv_part_floats() * sizeof(float)};
   for (size_t s : sizes) total += (s + 255) & ~size_t(255);
   char* buf = nullptr;
   M5_CUDA(cudaMalloc(&buf, total));
@@ -1034,6 +1037,7 @@ extern "C" int m5_model_reserve(void* model, int max_tokens) {
   m->sk_n = sizes[25] ? (int)sk_n : 0;
   m->sk_xs = sizes[26] ? carve(p, sizes[26]) : nullptr;
   m->rope_cnt = (unsigned int*)carve(p, sizes[27]);
+  m->gemv_part = (float*)carve(p, sizes[28]);
   m->sk_xs_stride = sizes[26] ? sk_xs : 0;
   if (m->sk_f && !m->sk_fork) {
     M5_CUDA(cudaEventCreateWithFlags(&m->sk_fork, cudaEventDisableTiming));
