@@ -424,14 +424,22 @@ def greedy_tokens(model, ids, n: int, kv_bits: int, chunk: int, feed=None):
     return out, margins, torch.stack(logits)
 
 
+N1_COS_FLOOR = 0.995  # teacher-forced logits cosine, N GPUs vs one (see n1_token_check)
+
+
 def n1_token_check(cx: Ctx, model, cfg: dict, seed: int, kv_bits: int, chunk: int, n: int = 16) -> dict:
     """The N-GPU model against the same seeded model on one GPU (rank 0), at a
     64-token prompt: the 1-GPU greedy tokens, the N-GPU greedy tokens (how
     long they agree), and the N-GPU logits teacher-forced on the 1-GPU tokens
     (per-step cosine and max-abs).  The ranks add their fp32 partial sums in
     another order than one GPU, so over dozens of layers the logits drift by
-    bf16 rounding and a close top two may swap; `pass` asks for a logits
-    cosine >= 0.999 at every step, which a wrong partial sum would not meet."""
+    bf16 rounding and a close top two may swap.  How far such a change moves
+    this random-weight model was measured on one GPU: the 64-layer 32B shape
+    run with the GEMV's fp16 consumer instead of its int8 one (both valid,
+    both within one bf16 step per projection) gives a teacher-forced logits
+    cosine of 0.9975 (max-abs 0.48) against the default, and the same run
+    twice gives identical logits.  `pass` asks for a cosine >= 0.995 at every
+    step; a missing or doubled rank partial in any layer falls far below it."""
     import torch
     g = torch.Generator(device=cx.dev).manual_seed(seed + 11)
     ids = torch.randint(0, cfg["vocab_size"], (64,), generator=g, device=cx.dev, dtype=torch.int32)
@@ -456,7 +464,7 @@ def n1_token_check(cx: Ctx, model, cfg: dict, seed: int, kv_bits: int, chunk: in
                "first_diff_margin": None if k == n else round(margins[k], 4),
                "forced_logits_cos_min": round(cos.min().item(), 6),
                "forced_logits_max_abs": round((forced - ref_logits).abs().max().item(), 4),
-               "pass": cos.min().item() >= 0.999}
+               "pass": cos.min().item() >= N1_COS_FLOOR}
     cx.barrier()
     return res
 

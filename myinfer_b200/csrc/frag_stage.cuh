@@ -176,16 +176,16 @@ __device__ __forceinline__ void stage_frag(const bf16* __restrict__ x, int64_t l
 // The raw bf16 row of token t is copied to xf + t * NG * 32: the uint4 of raw
 // 8-element block c sits exactly where the pairs of block c go, so every
 // thread converts its blocks in place.  Requirements: x rows and norm_w
-// 16-byte aligned (ldx % 8 == 0), K % 1024 == 0, nbuf holds K bf16 when
+// 16-byte aligned (ldx % 8 == 0), K % 256 == 0, nbuf holds K bf16 when
 // norm_w is set, xbar is an initialised, unused mbarrier, red has room for
-// 8 + 16 * MT floats.  Returns false (and records a device error) if the copy
+// 8 + 32 * MT floats (up to 16 staging warps).  Returns false (and records a device error) if the copy
 // did not land in time.
 template <int MT, int NT, bool FP16>
 __device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int64_t ldx, int K,
                                                 const bf16* __restrict__ norm_w, float eps, uint32_t* xf,
                                                 uint32_t* nbuf, float* xg, float* red, int bar, float* xinv,
                                                 uint64_t* xbar, int* err) {
-  static_assert(FP16 && NT % 32 == 0 && NT / 32 <= 8, "fp16 staging by whole warps");
+  static_assert(FP16 && NT % 32 == 0 && NT / 32 <= 16, "fp16 staging by whole warps");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NG = K >> 6, K8 = K >> 3;
   auto sync = [&]() {
@@ -205,7 +205,7 @@ __device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int6
   // red[0..MT) receives xinv while other threads still read the partials:
   // the partials live past it
   float* rs = red + 8;           // [NT/32][MT] sums of squares
-  float* rm = red + 8 + 8 * MT;  // [NT/32][MT] maxima
+  float* rm = red + 8 + 16 * MT;  // [NT/32][MT] maxima
 #pragma unroll
   for (int t = 0; t < MT; ++t) {
     const uint4* blk = reinterpret_cast<const uint4*>(xf + size_t(t) * NG * 32);
@@ -299,6 +299,53 @@ __device__ __forceinline__ bool stage_frag_bulk(const bf16* __restrict__ x, int6
 }
 
 
+// Block c (8 values e, already normalised and bf16-rounded) of token t in
+// the int8 plane layout described below; the 8 lanes of a group (lanes
+// 8j..8j+7 hold its blocks) reduce its sum and maximum by shuffles, and every
+// lane of the warp must call this with its own block.  The planes are written
+// over the raw block's words after a __syncwarp, so a warp whose 32 raw
+// blocks are all in registers converts them in place.
+__device__ __forceinline__ void i8_block(const float (&e)[8], int c, int t, int NG, uint32_t* xq, float* xg,
+                                         float* xs, int lane) {
+  float gs = 0.f, gm = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    gs += e[q];
+    gm = fmaxf(gm, fabsf(e[q]));
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    gs += __shfl_xor_sync(0xffffffffu, gs, o);
+    gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+  }
+  const int G = c >> 3, cb = c & 7;  // group, block inside it
+  const int E = int((__float_as_uint(gm) >> 23) & 0xFFu);  // biased exponent of the group max
+  const int sh = gm > 0.f ? 141 - E : 0;                   // 2^(14 - (E - 127))
+  const float up = __uint_as_float(uint32_t(max(1, min(254, sh + 127))) << 23);
+  if (cb == 0) {
+    xg[t * NG + G] = gs;
+    xs[t * NG + G] = __uint_as_float(uint32_t(max(1, min(254, 127 - sh))) << 23);
+  }
+  // v = rint(e * up) by one fma against 1.5 * 2^23 (|e * up| < 2^15, so the
+  // single round-to-nearest-even lands on the integer): the sum's low
+  // mantissa bits hold v + 2^22, whose byte 0 is v's low byte and byte 1
+  // its high byte (two's complement); byte permutes gather four of each.
+  uint32_t f[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) f[q] = __float_as_uint(fmaf(e[q], up, 12582912.f));
+  uint32_t hi[2], lo[2];  // r = 0 even, 1 odd elements
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    lo[r] = __byte_perm(__byte_perm(f[r], f[r + 2], 0x0040), __byte_perm(f[r + 4], f[r + 6], 0x0040), 0x5410);
+    hi[r] = __byte_perm(__byte_perm(f[r], f[r + 2], 0x0051), __byte_perm(f[r + 4], f[r + 6], 0x0051), 0x5410);
+  }
+  __syncwarp();  // every raw block of this warp's groups is in registers
+  const int tq = cb >> 1, m = cb & 1;
+  uint32_t* dst = xq + (size_t(t) * NG + G) * 32 + tq * 8 + m * 2;
+  *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
+  *reinterpret_cast<uint2*>(dst + 4) = make_uint2(lo[0], lo[1]);
+}
+
 // Activation staging for the int8 tensor-core GEMV (mma.sync m16n8k32, u8
 // weight codes against s8 / u8 activation planes), with the same bulk copy,
 // RMSNorm and bf16 rounding points as stage_frag_bulk.  Per token t and
@@ -321,7 +368,7 @@ __device__ __forceinline__ bool stage_i8_bulk(const bf16* __restrict__ x, int64_
                                               const bf16* __restrict__ norm_w, float eps, uint32_t* xq,
                                               uint32_t* nbuf, float* xg, float* xs, float* red, int bar,
                                               uint64_t* xbar, int* err) {
-  static_assert(NT % 32 == 0 && NT / 32 <= 8, "int8 staging by whole warps");
+  static_assert(NT % 32 == 0 && NT / 32 <= 16, "int8 staging by whole warps");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NG = K >> 6, K8 = K >> 3;
   auto sync = [&]() {
@@ -390,43 +437,7 @@ __device__ __forceinline__ bool stage_i8_bulk(const bf16* __restrict__ x, int64_
           e[2 * q + 1] = rbf(__fmul_rn(bf16_hi(n[q]), rbf(__fmul_rn(e[2 * q + 1], inv[t]))));
         }
       }
-      float gs = 0.f, gm = 0.f;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        gs += e[q];
-        gm = fmaxf(gm, fabsf(e[q]));
-      }
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        gs += __shfl_xor_sync(0xffffffffu, gs, o);
-        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
-      }
-      const int G = c >> 3, cb = c & 7;  // group, block inside it
-      const int E = int((__float_as_uint(gm) >> 23) & 0xFFu);  // biased exponent of the group max
-      const int sh = gm > 0.f ? 141 - E : 0;                   // 2^(14 - (E - 127))
-      const float up = __uint_as_float(uint32_t(max(1, min(254, sh + 127))) << 23);
-      if (cb == 0) {
-        xg[t * NG + G] = gs;
-        xs[t * NG + G] = __uint_as_float(uint32_t(max(1, min(254, 127 - sh))) << 23);
-      }
-      // v = rint(e * up) by one fma against 1.5 * 2^23 (|e * up| < 2^15, so the
-      // single round-to-nearest-even lands on the integer): the sum's low
-      // mantissa bits hold v + 2^22, whose byte 0 is v's low byte and byte 1
-      // its high byte (two's complement); byte permutes gather four of each.
-      uint32_t f[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) f[q] = __float_as_uint(fmaf(e[q], up, 12582912.f));
-      uint32_t hi[2], lo[2];  // r = 0 even, 1 odd elements
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        lo[r] = __byte_perm(__byte_perm(f[r], f[r + 2], 0x0040), __byte_perm(f[r + 4], f[r + 6], 0x0040), 0x5410);
-        hi[r] = __byte_perm(__byte_perm(f[r], f[r + 2], 0x0051), __byte_perm(f[r + 4], f[r + 6], 0x0051), 0x5410);
-      }
-      __syncwarp();  // every raw block of this warp's groups is in registers
-      const int tq = cb >> 1, m = cb & 1;
-      uint32_t* dst = xq + (size_t(t) * NG + G) * 32 + tq * 8 + m * 2;
-      *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
-      *reinterpret_cast<uint2*>(dst + 4) = make_uint2(lo[0], lo[1]);
+      i8_block(e, c, t, NG, xq, xg, xs, lane);
     }
   }
   sync();

@@ -21,7 +21,11 @@ def _weights(N, K, seed):
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 13])
-@pytest.mark.parametrize("N,K", [(256, 1024), (1000, 2048), (384, 5120), (96, 25600), (4096, 64), (33, 1088)])
+# K % 1024 != 0 with K % 512 == 0 (1536, 2560, 12800): the tensor-map kernel's
+# partial last unit of a row, e.g. a down_proj sharded over 2 ranks (25600 / 2);
+# 1280 and 3328 (K % 512 != 0) take the register-fed GEMV
+@pytest.mark.parametrize("N,K", [(256, 1024), (1000, 2048), (384, 5120), (96, 25600), (4096, 64), (33, 1088),
+                                 (512, 1536), (48, 2560), (160, 12800), (512, 1280), (48, 3328)])
 def test_quantized_matmul(M, N, K):
     from myinfer_b200 import ops
     (wq, s, b), wd = _weights(N, K, seed=N * 7 + K)
