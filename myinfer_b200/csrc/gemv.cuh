@@ -65,7 +65,7 @@ int gemv_launch(const GemvArgs& a, int MT, int epi, cudaStream_t stream);
 // Largest number of tokens one launch can stage for this K (shared memory).
 int gemv_max_tokens(int K);
 
-// TMA tensor-map + tensor-core variant (gemv_tmap.cu): K % 1024 == 0.  `part`
+// TMA tensor-map + tensor-core variant (gemv_tmap.cu): K % 512 == 0.  `part`
 // holds part_floats floats of per-CTA split-tile slots, `cnt` one zeroed
 // counter per 16-row tile for cnt_rows rows (both left as found).
 bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi);

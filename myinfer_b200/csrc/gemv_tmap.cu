@@ -1,22 +1,29 @@
-// Decode dequant-GEMV: 2-D TMA tiles into shared memory + tensor-core dot
-// products (kernel K1, M <= 8 tokens, K % 1024 == 0).
+// Decode dequant-GEMV: TMA tiles into shared memory + tensor-core dot
+// products (kernel K1, M <= 8 tokens, K % 512 == 0; a row's last 1024-column
+// unit may be partial).
 //
 // The register-prefetch tensor-core GEMV (gemv_mma.cu) spends ~3.6 issue
 // slots per weight and stalls on L1 load latency with 16 warps per SM; the
 // TMA-fed CUDA-core GEMV (gemv_tma.cu) keeps enough bytes in flight but is
 // issue-bound at ~5.3 slots per weight.  This kernel takes the best of both:
-//   * a producer warp streams units of (16 weight rows x 1024 columns) with
-//     2-D tensor-map TMA loads (weights in 1 KB boxes with 128-byte swizzle so
-//     the 8 rows a fragment load touches hit different banks; bf16 scales and
-//     biases) into a 5-stage ring (~45 KB in flight per CTA, several CTAs per
-//     SM), no registers involved;
-//   * four consumer warps each take four 64-column scale groups of every unit
-//     and run mma.sync m16n8k16 fp16 dot products of the exact codes q against
-//     the activations scaled by a per-token power of two, per-group fold
-//     s * D + b * sum(x);
-//   * units are dealt to CTAs as equal contiguous ranges (stream-K); partial
-//     tile sums go through fp32 atomics into a zeroed scratch and the warp that
-//     completes a tile runs the epilogue and re-zeroes the scratch.
+//   * a ring's producer warp streams units of (16 weight rows x 1024 columns)
+//     with one 3-D tensor-map TMA box for the codes (128-byte swizzle, so the
+//     8 rows a fragment load touches hit different banks) and one box each for
+//     the bf16 scales and biases, into an mbarrier ring, no registers
+//     involved.  A CTA holds one ring (three CTAs per SM, 5 stages) when three
+//     copies of the staged activations fit an SM, else three rings (one CTA
+//     per SM) that share one copy and take the memory it frees as deeper rings
+//     (3-8 stages; down_proj's 25600-long rows);
+//   * the consumer warps first stage the activations once per CTA (input
+//     RMSNorm, 16-bit fixed-point planes per 64-column group), then four warps
+//     per ring each take four 64-column scale groups of every unit of their
+//     ring and run int8 mma.sync m16n8k32 products of the exact codes against
+//     the planes (or, with M5_GEMV_I8=0, fp16 m16n8k16 products against
+//     per-token scaled activations), folding s * D + b * sum(x) per group;
+//   * units are dealt to rings as equal contiguous ranges (stream-K); a tile
+//     shared by neighbouring rings is summed from their per-ring slots in ring
+//     order by the ring that completes it (no floating-point atomics, so the
+//     result is bitwise repeatable), which then runs the epilogue.
 // All mbarrier waits are bounded (tma.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -33,13 +40,15 @@ namespace m5 {
 
 static __device__ int g_gemv_tmap_err = 0;
 
-constexpr int TP_CW = 4;                       // consumer warps
-constexpr int TP_THREADS = (TP_CW + 1) * 32;
-constexpr int TP_STAGES = 5;
+constexpr int TP_CW = 4;                       // consumer warps of a ring
+constexpr int TP_MAX_STAGES = 8;
 constexpr int TP_UG = 16;                     // 64-column scale groups per unit (1024 columns)
 constexpr int TP_W_STAGE = 16 * TP_UG * 32;    // 16 rows x UG groups x 32 bytes (1 KB swizzled boxes)
 constexpr int TP_SB_STAGE = 16 * TP_UG * 2;    // 16 rows x UG bf16 (scales or biases)
-constexpr int TP_BARS = 2 * TP_STAGES + 2;      // full, empty, activation copy (+ pad to 16 bytes)
+// Rings per CTA: 1 (three CTAs per SM when their activation copies fit) or 3
+// (one CTA per SM whose rings share one activation copy).
+constexpr int tp_threads(int sub) { return sub * (TP_CW + 1) * 32; }
+constexpr int tp_bars(int sub) { return sub * 2 * TP_MAX_STAGES + 2; }  // full, empty per ring; activation copy (+ pad)
 // Row blocks of a unit fetched by separate boxes: the two 8-row halves of a
 // SwiGLU tile come from the gate and the up matrix; any other tile's 16 rows
 // are one block of one segment (segments are whole tiles).
@@ -149,52 +158,62 @@ __device__ __noinline__ void tp_rope_head(const RopeAppendArgs& r, int MT, int h
 // as they sit in the word, one mask or shift-and-mask per 4 codes) against
 // per-group 16-bit fixed-point activation planes (stage_i8_bulk), int32 group
 // sums folded as s * 2^(E - 14) * D + b * sum(x).
-template <int MT, int EPI, bool I8>
-__global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_constant__ GemvArgs a, const __grid_constant__ TmapSet tm,
-                                                               float* part, int* cnt_buf) {
+template <int MT, int EPI, bool I8, int SUB>
+__global__ void __launch_bounds__(tp_threads(SUB), SUB == 1 ? 3 : 1) gemv_tmap_kernel(const __grid_constant__ GemvArgs a, const __grid_constant__ TmapSet tm,
+                                                               float* part, int* cnt_buf, int nst) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 128-byte-swizzled boxes must start on 1 KB boundaries
   unsigned char* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
-  const int K = a.K, NG = K >> 6, NCH = NG / TP_UG;
-  unsigned char* wring = smem;                                   // [STAGES][4096], 1024-aligned boxes
-  unsigned char* sbring = wring + TP_STAGES * TP_W_STAGE;        // [STAGES][2 (s,b)][256]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sbring + TP_STAGES * 2 * TP_SB_STAGE);
-  uint64_t* empty = full + TP_STAGES;
-  uint64_t* xbar = empty + TP_STAGES;                             // activation copy
-  uint32_t* xf = reinterpret_cast<uint32_t*>(full + TP_BARS);     // [MT][NG][4][8] pairs
+  const int K = a.K, NG = K >> 6, NCH = (NG + TP_UG - 1) / TP_UG;  // the last unit of a row may be partial
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warps 0 .. 4 SUB - 1: consumers, four per ring; then one producer per ring
+  constexpr int NC = SUB * TP_CW * 32;  // consumer threads
+  const bool producer = warp >= SUB * TP_CW;
+  const int sub = producer ? warp - SUB * TP_CW : warp / TP_CW, cw = warp % TP_CW;
+  const int stage_bytes = TP_W_STAGE + 2 * TP_SB_STAGE;
+  unsigned char* wring = smem + size_t(sub) * nst * stage_bytes;  // [nst][4096], 1024-aligned boxes
+  unsigned char* sbring = wring + nst * TP_W_STAGE;               // [nst][2 (s,b)][256]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(SUB) * nst * stage_bytes);
+  uint64_t* full = bars + sub * 2 * TP_MAX_STAGES;
+  uint64_t* empty = full + TP_MAX_STAGES;
+  uint64_t* xbar = bars + SUB * 2 * TP_MAX_STAGES;                 // activation copy
+  // activation staging, shared by the CTA's rings
+  uint32_t* xf = reinterpret_cast<uint32_t*>(bars + tp_bars(SUB));  // [MT][NG][4][8] pairs
   uint32_t* nbuf = xf + MT * NG * 32;                             // [K] bf16 norm weight (if any)
   float* xg = reinterpret_cast<float*>(nbuf + (a.norm_w ? K / 2 : 0));  // [MT][NG]
   float* xsc = xg + MT * NG;                                      // [MT][NG] group scales (I8)
-  float* red = xsc + (I8 ? MT * NG : 0);                          // [8]
+  float* red = xsc + (I8 ? MT * NG : 0);                          // [8], then the rings' tile sums
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
   const int ntiles = vrows >> 4;
   const long long total = (long long)ntiles * NCH;
-  const long long u0 = total * blockIdx.x / gridDim.x, u1 = total * (blockIdx.x + 1) / gridDim.x;
+  // ring `sub` of CTA b is virtual CTA b * SUB + sub: equal contiguous unit ranges
+  const long long G_ = (long long)gridDim.x * SUB, vid = (long long)blockIdx.x * SUB + sub;
+  const long long u0 = total * vid / G_, u1 = total * (vid + 1) / G_;
 
   if (tid == 0) {
-    for (int s = 0; s < TP_STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], TP_CW);
-    }
+    for (int r = 0; r < SUB; ++r)
+      for (int s = 0; s < nst; ++s) {
+        mbar_init(&bars[r * 2 * TP_MAX_STAGES + s], 1);
+        mbar_init(&bars[r * 2 * TP_MAX_STAGES + TP_MAX_STAGES + s], TP_CW);
+      }
     mbar_init(xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == TP_CW) {
+  if (producer) {
     // -------------------------------------------------------------- producer
     // streams constant weights: needs nothing from earlier kernels
     if (lane == 0) {
       int it = 0;
       int tile = int(u0 / NCH), ch = int(u0 % NCH);
       for (long long u = u0; u < u1; ++u, ++it) {
-        const int st = it % TP_STAGES;
-        const uint32_t par = (it / TP_STAGES) & 1;
+        const int st = it % nst;
+        const uint32_t par = (it / nst) & 1;
         // the ring is full: from here on the consumers gate this warp, and they
         // start only once the previous kernel has finished
-        if (it == TP_STAGES) {
+        if (it == nst) {
           pdl_wait();
           pdl_launch_dependents();
         }
@@ -229,9 +248,9 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
   // the SM slots this grid's own CTAs still wait for.
   pdl_launch_dependents();
   if constexpr (I8)
-    stage_i8_bulk<MT, TP_CW * 32>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, xsc, red, 1, xbar, &g_gemv_tmap_err);
+    stage_i8_bulk<MT, NC>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, xsc, red, 1, xbar, &g_gemv_tmap_err);
   else
-    stage_frag_bulk<MT, TP_CW * 32, true>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, red, 1, xinv, xbar,
+    stage_frag_bulk<MT, NC, true>(a.x, a.ldx, K, a.norm_w, a.eps, xf, nbuf, xg, red, 1, xinv, xbar,
                                           &g_gemv_tmap_err);
 
   const int g = lane >> 2, tq = lane & 3;
@@ -252,9 +271,9 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
 #pragma unroll
   for (int jj = 0; jj < TP_UG / TP_CW; ++jj) {
     const int c = 2 * jj + (tq >> 1);
-    woff[jj] = warp * W_CHUNK + g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
+    woff[jj] = cw * W_CHUNK + g * 128 + ((c ^ g) << 4) + 8 * (tq & 1);
   }
-  const uint32_t soff = g * (TP_UG * 2) + warp * (TP_UG / TP_CW) * 2;  // 4 consecutive bf16 of row g
+  const uint32_t soff = g * (TP_UG * 2) + cw * (TP_UG / TP_CW) * 2;  // 4 consecutive bf16 of row g
 
   float tot[4] = {0.f, 0.f, 0.f, 0.f};
   float totD[4] = {0.f, 0.f, 0.f, 0.f}, totB[4] = {0.f, 0.f, 0.f, 0.f};
@@ -295,7 +314,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
       tp_rope_head(a.rope, MT, tile >> 3, lane);
     }
   };
-  float* tred = reinterpret_cast<float*>(red + 8);  // [CW][MT][16] partial tile sums
+  float* tred = red + 8 + sub * (TP_CW * MT * 16);  // this ring's [CW][MT][16] partial tile sums
   // Every tile is first reduced over the four consumer warps in shared memory
   // (warp order).  A tile whose units all lie in this CTA's range is finished
   // at once; a tile shared with neighbouring CTAs leaves this CTA's sum in its
@@ -303,7 +322,6 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
   // CTA that completes the tile's unit count adds the slots of the CTAs that
   // cover it in CTA order.  No floating-point atomics: the result does not
   // depend on which CTA finishes first.
-  const long long G_ = gridDim.x;
   auto unit_begin = [&](long long c) { return total * c / G_; };
   auto cta_of = [&](long long u) {  // the CTA whose range holds unit u
     long long c = u * G_ / total;
@@ -320,15 +338,15 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
     const long long tb = (long long)tile * NCH, te = tb + NCH;  // the tile's units
     const bool whole = tb >= u0 && te <= u1;
     if (t0 < MT) {
-      tred[(warp * MT + t0) * 16 + g] = tot[0];
-      tred[(warp * MT + t0) * 16 + g + 8] = tot[2];
+      tred[(cw * MT + t0) * 16 + g] = tot[0];
+      tred[(cw * MT + t0) * 16 + g + 8] = tot[2];
     }
     if (t1 < MT) {
-      tred[(warp * MT + t1) * 16 + g] = tot[1];
-      tred[(warp * MT + t1) * 16 + g + 8] = tot[3];
+      tred[(cw * MT + t1) * 16 + g] = tot[1];
+      tred[(cw * MT + t1) * 16 + g + 8] = tot[3];
     }
-    named_sync(2, TP_CW * 32);
-    if (warp == 0) {
+    named_sync(2 + sub, TP_CW * 32);
+    if (cw == 0) {
       if (whole) {
         for (int q = lane; q < 16 * MT; q += 32) {
           const int r16 = q & 15, t = q >> 4;
@@ -342,7 +360,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
         }
         if constexpr (EPI == EPI_STORE) rope_tile(tile);
       } else {
-        float* mine = part + (size_t(blockIdx.x) * 2 + (tb <= u0 ? 0 : 1)) * (MT * 16);
+        float* mine = part + (size_t(vid) * 2 + (tb <= u0 ? 0 : 1)) * (MT * 16);
         for (int q = lane; q < 16 * MT; q += 32) {
           const int r16 = q & 15, t = q >> 4;
           float v = 0.f;
@@ -385,7 +403,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
         }
       }
     }
-    named_sync(2, TP_CW * 32);
+    named_sync(2 + sub, TP_CW * 32);
 #pragma unroll
     for (int i = 0; i < 4; ++i) tot[i] = totD[i] = totB[i] = 0.f;
   };
@@ -402,10 +420,13 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
     // On a timed-out wait the warp stops computing but keeps walking the units
     // so that every consumer warp still reaches the tile barriers in flush().
     if (!failed && !mbar_wait(&full[st], par, &g_gemv_tmap_err)) failed = true;
-    if (!failed) {
+    // K % 512 == 0: a warp's four groups lie all inside the row or all past
+    // its end (the partial last unit of a row: zero-filled by the copy and
+    // skipped here, though the warp still takes its turn on the stage)
+    const int G0 = ch * TP_UG + cw * (TP_UG / TP_CW);  // first global group of this warp
+    if (!failed && G0 < NG) {
       const unsigned char* ws = wring + st * TP_W_STAGE;
       const unsigned char* ss = sbring + st * 2 * TP_SB_STAGE;
-      const int G0 = ch * TP_UG + warp * (TP_UG / TP_CW);  // first global group of this warp
       // scales / biases of the warp's 4 groups, rows g and g + 8; group sums of x
       const uint2 sv0 = *reinterpret_cast<const uint2*>(ss + soff);
       const uint2 sv8 = *reinterpret_cast<const uint2*>(ss + TP_SB_STAGE / 2 + soff);
@@ -496,6 +517,8 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
         totB[3] = fmaf(bB, X1a[jj], totB[3]);
       }
       }
+    }
+    if (!failed) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
@@ -503,7 +526,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) gemv_tmap_kernel(const __grid_c
       ch = 0;
       ++tile;
     }
-    if (++st == TP_STAGES) {
+    if (++st == nst) {
       st = 0;
       par ^= 1;
     }
@@ -555,10 +578,45 @@ static int make_maps(const GemvSeg& sg, int K, TmapSet& ts, int i, int brows) {
   return M5_OK;
 }
 
-static size_t tp_smem(int MT, int K, bool norm, bool i8) {
-  return TP_STAGES * (TP_W_STAGE + 2 * TP_SB_STAGE) + TP_BARS * 8 + size_t(MT) * (K / 64) * 32 * 4 +
+// Shared memory of a CTA: its rings of nst stages, their barriers, the shared
+// activation staging (planes, norm weight, group sums and scales) and the
+// rings' tile sums (which also hold the staging's per-warp partials).
+static size_t tp_smem(int MT, int K, bool norm, bool i8, int sub, int nst) {
+  return size_t(sub) * nst * (TP_W_STAGE + 2 * TP_SB_STAGE) + tp_bars(sub) * 8 + size_t(MT) * (K / 64) * 32 * 4 +
          (norm ? size_t(K) * 2 : 0) + size_t(MT) * (K / 64) * 4 * (i8 ? 2 : 1) + 8 * 4 +
-         size_t(TP_CW) * MT * 16 * 4 + 1024;
+         size_t(sub) * TP_CW * MT * 16 * 4 + 1024;
+}
+
+constexpr size_t TP_SMEM_MAX = 227 * 1024;  // opt-in dynamic shared memory of one CTA
+constexpr size_t TP_SMEM_SM = 228 * 1024;   // shared memory of an SM (1 KB of it reserved per CTA)
+constexpr int TP_STAGES1 = 5;               // ring depth of the one-ring CTA
+
+// Launch shape of a GEMV: one-ring CTAs (5 stages) while three of them fit an
+// SM; otherwise, for the int8 consumer, one CTA of three rings sharing the
+// activation copy, as deep as the memory allows (3..8 stages).  sub = 0 when
+// neither fits.
+struct TpShape {
+  int sub = 0, nst = 0;
+  size_t smem = 0;
+};
+static TpShape tp_shape(int MT, int K, bool norm, bool i8) {
+  TpShape r;
+  const size_t one = tp_smem(MT, K, norm, i8, 1, TP_STAGES1);
+  if (3 * (one + 1024) <= TP_SMEM_SM || (!i8 && one <= TP_SMEM_MAX)) {
+    r.sub = 1;
+    r.nst = TP_STAGES1;
+    r.smem = one;
+    return r;
+  }
+  if (!i8) return r;
+  for (int n = TP_MAX_STAGES; n >= 3; --n)
+    if (tp_smem(MT, K, norm, i8, 3, n) <= TP_SMEM_MAX) {
+      r.sub = 3;
+      r.nst = n;
+      r.smem = tp_smem(MT, K, norm, i8, 3, n);
+      return r;
+    }
+  return r;
 }
 
 // The int8 consumer is the default; M5_GEMV_I8=0 selects the fp16 one.
@@ -571,8 +629,10 @@ static bool tp_use_i8() {
 }
 
 bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
-  if (MT < 1 || MT > 8 || a.K % (64 * TP_UG)) return false;
-  if (tp_smem(MT, a.K, a.norm_w != nullptr, tp_use_i8()) > 200 * 1024) return false;
+  // K % 512: the scale / bias rows' byte stride (K / 32) must be a multiple of 16
+  // for their tensor maps; the row's last 1024-column unit may be partial
+  if (MT < 1 || MT > 8 || a.K % 512 || a.K <= 0) return false;
+  if (tp_shape(MT, a.K, a.norm_w != nullptr, tp_use_i8()).sub == 0) return false;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   // activation rows and the norm weight arrive by bulk copy: 16-byte aligned
   if (!al(a.x) || (a.ldx % 8) || (a.norm_w && !al(a.norm_w))) return false;
@@ -585,27 +645,56 @@ bool gemv_tmap_eligible(const GemvArgs& a, int MT, int epi) {
   return encode_fn() != nullptr;
 }
 
-// CTAs per SM the kernel may keep resident, at most (sizing of the slots).
+// Split-tile slots are sized for up to 8 virtual CTAs (rings) per SM.
 constexpr int TP_MAX_CTAS_PER_SM = 8;
 
 size_t gemv_part_floats() { return size_t(2) * 8 * 16 * TP_MAX_CTAS_PER_SM * sm_count(); }
 
+// Resident CTAs per SM of one instantiation (setting its shared-memory
+// opt-in first: the attribute belongs to each device's context).
+template <int MT, int EPI, bool I8, int SUB>
+static int tp_occupancy(size_t smem, int& per_sm) {
+  auto kern = gemv_tmap_kernel<MT, EPI, I8, SUB>;
+  static DeviceOnce once;
+  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TP_SMEM_MAX); }));
+  per_sm = 0;
+  M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tp_threads(SUB), smem));
+  per_sm = std::min(std::max(1, per_sm), TP_MAX_CTAS_PER_SM / SUB);
+  return M5_OK;
+}
+
+// Grid of a launch: as many CTAs as stay resident, at most one ring per unit.
+static int tp_grid(int per_sm, int sub, long long units) {
+  return (int)std::max(1LL, std::min<long long>((long long)per_sm * sm_count(), (units + sub - 1) / sub));
+}
+
+static long long tp_units(const GemvArgs& a, int epi) {
+  const int vrows = a.total_rows * (epi == EPI_SWIGLU ? 2 : 1);
+  return (long long)(vrows / 16) * ((a.K / 64 + TP_UG - 1) / TP_UG);
+}
+
+template <int MT, int EPI, bool I8, int SUB>
+static int tp_launch_s(const GemvArgs& a, const TmapSet& ts, const TpShape& sh, float* part, size_t part_floats,
+                       int* cnt, cudaStream_t st) {
+  int per_sm = 0;
+  int rc = tp_occupancy<MT, EPI, I8, SUB>(sh.smem, per_sm);
+  if (rc) return rc;
+  const int grid = tp_grid(per_sm, SUB, tp_units(a, EPI));
+  if (size_t(grid) * SUB * 2 * MT * 16 > part_floats) return fail(M5_ERR_INVALID, "gemv_tmap: split-tile slots too small");
+  M5_CUDA(launch_pdl(gemv_tmap_kernel<MT, EPI, I8, SUB>, dim3(grid), dim3(tp_threads(SUB)), sh.smem, st, a, ts,
+                     part, cnt, sh.nst));
+  return M5_OK;
+}
+
 template <int MT, int EPI, bool I8>
 static int tp_launch_t(const GemvArgs& a, const TmapSet& ts, float* part, size_t part_floats, int* cnt,
                        cudaStream_t st) {
-  const size_t smem = tp_smem(MT, a.K, a.norm_w != nullptr, I8);
-  static DeviceOnce once;  // the attribute belongs to each device's context
-  M5_CUDA(once.run([&] { return cudaFuncSetAttribute(gemv_tmap_kernel<MT, EPI, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); }));
-  int per_sm = 0;
-  M5_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tmap_kernel<MT, EPI, I8>, TP_THREADS, smem));
-  per_sm = std::min(std::max(1, per_sm), TP_MAX_CTAS_PER_SM);
-  const int vrows = a.total_rows * (EPI == EPI_SWIGLU ? 2 : 1);
-  const long long units = (long long)(vrows / 16) * (a.K / (64 * TP_UG));
-  const long long max_ctas = (long long)per_sm * sm_count();
-  const int grid = (int)std::max(1LL, std::min(max_ctas, units));
-  if (size_t(grid) * 2 * MT * 16 > part_floats) return fail(M5_ERR_INVALID, "gemv_tmap: split-tile slots too small");
-  M5_CUDA(launch_pdl(gemv_tmap_kernel<MT, EPI, I8>, dim3(grid), dim3(TP_THREADS), smem, st, a, ts, part, cnt));
-  return M5_OK;
+  const TpShape sh = tp_shape(MT, a.K, a.norm_w != nullptr, I8);
+  if (sh.sub == 1) return tp_launch_s<MT, EPI, I8, 1>(a, ts, sh, part, part_floats, cnt, st);
+  if constexpr (I8) {
+    if (sh.sub == 3) return tp_launch_s<MT, EPI, I8, 3>(a, ts, sh, part, part_floats, cnt, st);
+  }
+  return fail(M5_ERR_INVALID, "gemv_tmap: activations too large for shared memory");
 }
 
 template <int MT, bool I8>
