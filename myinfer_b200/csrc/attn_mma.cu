@@ -63,6 +63,38 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], u
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Integer MMAs for S^T = K Q^T: u8 key codes against the s8 high and u8 low
+// planes of the 16-bit fixed-point queries; exact int32 sums.
+__device__ __forceinline__ void am_imma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void am_imma_u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Physical dim of byte e (0..3) of the A register `half` (0: a0/a1, 1: a2/a3)
+// in k32 step j of group G for lane quad t, as the int8 S path reads the
+// codes: 8-bit rows give a lane 16 contiguous bytes per group (words 2j,
+// 2j+1); 4-bit rows 8 bytes per group, word j split into its even-dim (low
+// nibble) and odd-dim (high nibble) codes.
+template <int BITS>
+__device__ __forceinline__ int i8s_dim(int G, int t, int j, int half, int e) {
+  if constexpr (BITS == 8) return 64 * G + 16 * t + 8 * j + 4 * half + e;
+  else return 64 * G + 16 * t + 8 * j + 2 * e + half;
+}
+
+// S^T on integer MMAs (no code conversion) instead of fp16 MMAs on codes
+// converted in registers (decode: one 8-row block of query rows).
+constexpr bool AM_I8S = false;
+
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
@@ -134,6 +166,8 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
   pdl_wait();
   pdl_launch_dependents();
   using LY = AmLayout<BITS>;
+  // integer S for one 8-row block (two blocks would spill at 2 CTAs per SM)
+  constexpr bool I8S = AM_I8S && NB == 1;
   constexpr int STAGES = AmCfg<NB>::STAGES;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * LY::STAGE);
@@ -230,22 +264,48 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
   if (tid < 16) qpos[tid] = S - a.L + q0 + (tid < rows ? tid / rep : 0);
   named_sync(1, AM_CW * 32);
 
-  // B fragments of q^T for the 8 contraction slices: column g of n-block nb is
-  // query row g + 8 nb (contraction dims permuted as the K codes are read)
-  uint32_t qb[NB][8][2];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int d0 = qk_dim<BITS>(j, t, 2 * t), d1 = qk_dim<BITS>(j, t, 2 * t + 1);
-    const int d8 = qk_dim<BITS>(j, t, 2 * t + 8), d9 = qk_dim<BITS>(j, t, 2 * t + 9);
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const float* r = q_s + (g + 8 * nb) * 128;
-      qb[nb][j][0] = pack_h2(r[d0], r[d1]);
-      qb[nb][j][1] = pack_h2(r[d8], r[d9]);
-    }
-  }
   // per-(row, group) sums of q: 4 threads x 16 elements per (row, group)
   float* qsum_s = reinterpret_cast<float*>(qpos + 16);  // [16][2]
+  float* qxs_s = qsum_s + 32;                           // [16] 2^-sh of a row's fixed-point planes
+  if constexpr (I8S) {
+    // Each query row becomes 16-bit fixed point v = rint(q * 2^sh), sh set by
+    // the row's largest |q| so |v| < 2^15 (every value at or above 2^-7 of
+    // the row's maximum exact: q is bf16), split into an s8 high and a u8 low
+    // plane; 8 threads per row.
+    const int r = tid >> 3, part = tid & 7;
+    const float4* src = reinterpret_cast<const float4*>(q_s + r * 128 + part * 16);
+    float mx = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 f = src[k];
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    if (part == 0) {
+      const int E = int((__float_as_uint(mx) >> 23) & 0xFFu);
+      const int sh = mx > 0.f ? 141 - E : 0;
+      qxs_s[r] = __uint_as_float(uint32_t(max(1, min(254, 127 - sh))) << 23);
+    }
+  }
+  // B fragments of q^T: column g of n-block nb is query row g + 8 nb, the
+  // contraction dims permuted as the K codes are read.  fp16 path: 8 k16
+  // slices; int8 path: per group and k32 step, the high and low planes.
+  uint32_t qb[NB][8][2];
+  if constexpr (!I8S) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d0 = qk_dim<BITS>(j, t, 2 * t), d1 = qk_dim<BITS>(j, t, 2 * t + 1);
+      const int d8 = qk_dim<BITS>(j, t, 2 * t + 8), d9 = qk_dim<BITS>(j, t, 2 * t + 9);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const float* r = q_s + (g + 8 * nb) * 128;
+        qb[nb][j][0] = pack_h2(r[d0], r[d1]);
+        qb[nb][j][1] = pack_h2(r[d8], r[d9]);
+      }
+    }
+  }
   {
     const int pair = tid >> 2, part = tid & 3;  // 32 (row, group) pairs
     const float4* src = reinterpret_cast<const float4*>(q_s + (pair >> 1) * 128 + (pair & 1) * 64 + part * 16);
@@ -260,8 +320,34 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
     if (part == 0) qsum_s[pair] = sum;
   }
   named_sync(1, AM_CW * 32);
+  if constexpr (I8S) {
+    // planes of this lane's B fragments: qb[nb][4 G + 2 j + plane][b0 / b1]
+    // (plane 0 high, 1 low); v + 2^22 sits in the low mantissa bits of
+    // fma(q, 2^sh, 1.5 * 2^23), byte 0 its low byte, byte 1 its high byte
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const int r = g + 8 * nb;
+      const float* qr = q_s + r * 128;
+      const float up = 1.f / qxs_s[r];
+#pragma unroll
+      for (int G = 0; G < 2; ++G)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t f[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) f[e] = __float_as_uint(fmaf(qr[i8s_dim<BITS>(G, t, j, hf, e)], up, 12582912.f));
+            qb[nb][4 * G + 2 * j + 0][hf] =
+                __byte_perm(__byte_perm(f[0], f[1], 0x0051), __byte_perm(f[2], f[3], 0x0051), 0x5410);
+            qb[nb][4 * G + 2 * j + 1][hf] =
+                __byte_perm(__byte_perm(f[0], f[1], 0x0040), __byte_perm(f[2], f[3], 0x0040), 0x5410);
+          }
+    }
+  }
   // this lane's score columns: rows 2t + e + 8 nb
   float qsr[NB][2][2];  // [nb][e][group]
+  float qxr[NB][2];     // [nb][e] 2^-sh of the row's planes (int8 S path)
   int qp[NB][2];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
@@ -270,6 +356,7 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
       const int r = 2 * t + e + 8 * nb;
       qsr[nb][e][0] = qsum_s[r * 2];
       qsr[nb][e][1] = qsum_s[r * 2 + 1];
+      qxr[nb][e] = I8S ? qxs_s[r] : 1.f;
       qp[nb][e] = qpos[r];
     }
   const bool causal = a.mask_kind == M5_MASK_CAUSAL;
@@ -305,13 +392,53 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
 
     // ---------------- S^T = K Q^T: A rows g / g+8 are keys kw0 + g / kw0 + 8 + g
     float dG[NB][2][4];
+    int dh[NB][2][4], dl[NB][2][4];  // int8 path: high / low plane sums per group
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-      for (int G = 0; G < 2; ++G) dG[nb][G][0] = dG[nb][G][1] = dG[nb][G][2] = dG[nb][G][3] = 0.f;
+      for (int G = 0; G < 2; ++G)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          dG[nb][G][i] = 0.f;
+          dh[nb][G][i] = dl[nb][G][i] = 0;
+        }
 #pragma unroll
     for (int G = 0; G < 2; ++G) {
-      if constexpr (BITS == 8) {
+      if constexpr (I8S) {
+        // the codes are the A operand as they lie: 8-bit rows 16 bytes per
+        // lane and group, 4-bit rows 8 bytes split into even / odd dims
+        uint32_t A[2][4];  // [k32 step j]
+        if constexpr (BITS == 8) {
+          const uint4 c0 = *reinterpret_cast<const uint4*>(sb + LY::K_OFF + (kw0 + g) * 128 + 64 * G + 16 * t);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(sb + LY::K_OFF + (kw0 + 8 + g) * 128 + 64 * G + 16 * t);
+          A[0][0] = c0.x;
+          A[0][1] = c1.x;
+          A[0][2] = c0.y;
+          A[0][3] = c1.y;
+          A[1][0] = c0.z;
+          A[1][1] = c1.z;
+          A[1][2] = c0.w;
+          A[1][3] = c1.w;
+        } else {
+          const uint2 c0 = *reinterpret_cast<const uint2*>(sb + LY::K_OFF + (kw0 + g) * 64 + 32 * G + 8 * t);
+          const uint2 c1 = *reinterpret_cast<const uint2*>(sb + LY::K_OFF + (kw0 + 8 + g) * 64 + 32 * G + 8 * t);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t wa = j ? c0.y : c0.x, wb = j ? c1.y : c1.x;
+            A[j][0] = wa & 0x0F0F0F0Fu;
+            A[j][1] = wb & 0x0F0F0F0Fu;
+            A[j][2] = (wa >> 4) & 0x0F0F0F0Fu;
+            A[j][3] = (wb >> 4) & 0x0F0F0F0Fu;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) {
+            am_imma_s8(dh[nb][G], A[j], qb[nb][4 * G + 2 * j][0], qb[nb][4 * G + 2 * j][1]);
+            am_imma_u8(dl[nb][G], A[j], qb[nb][4 * G + 2 * j + 1][0], qb[nb][4 * G + 2 * j + 1][1]);
+          }
+      } else if constexpr (BITS == 8) {
         const uint4 c0 = *reinterpret_cast<const uint4*>(sb + LY::K_OFF + (kw0 + g) * 128 + 64 * G + 16 * t);
         const uint4 c1 = *reinterpret_cast<const uint4*>(sb + LY::K_OFF + (kw0 + 8 + g) * 128 + 64 * G + 16 * t);
         const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w}, w1[4] = {c1.x, c1.y, c1.z, c1.w};
@@ -354,8 +481,17 @@ __global__ void __launch_bounds__(AM_THREADS, AmCfg<NB>::MINB) attn_mma_kernel(c
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int kk = i >> 1, e = i & 1;
-        const float s = fmaf(sk[kk][0], dG[nb][0][i], bk[kk][0] * qsr[nb][e][0]) +
-                        fmaf(sk[kk][1], dG[nb][1][i], bk[kk][1] * qsr[nb][e][1]);
+        float s;
+        if constexpr (I8S) {
+          // exact: |256 dh + dl| < 2^30 (64 codes <= 255 times |v| < 2^15)
+          const float a0 = float(dh[nb][0][i] * 256 + dl[nb][0][i]);
+          const float a1 = float(dh[nb][1][i] * 256 + dl[nb][1][i]);
+          s = fmaf(qxr[nb][e], fmaf(sk[kk][0], a0, sk[kk][1] * a1),
+                   fmaf(bk[kk][0], qsr[nb][e][0], bk[kk][1] * qsr[nb][e][1]));
+        } else {
+          s = fmaf(sk[kk][0], dG[nb][0][i], bk[kk][0] * qsr[nb][e][0]) +
+              fmaf(sk[kk][1], dG[nb][1][i], bk[kk][1] * qsr[nb][e][1]);
+        }
         sc[nb][i] = rbf(s);
         if (edge) {
           const int key = kk ? keyB : keyA;
@@ -569,7 +705,7 @@ static size_t am_smem(int bits, int nb) {
   const int stages = nb == 1 ? AmCfg<1>::STAGES : AmCfg<2>::STAGES;
   const size_t main = stages * stage;
   const size_t merge = size_t(AM_CW) * 16 * (2 + 128 + 2) * 4;
-  return std::max(main, merge) + 2 * stages * 8 + 16 * 128 * 4 + 16 * 4 + 32 * 4;
+  return std::max(main, merge) + 2 * stages * 8 + 16 * 128 * 4 + 16 * 4 + 32 * 4 + 16 * 4;
 }
 
 int attn_mma_rows(const AttnArgs& a) { return std::min(a.QB, a.L) * (a.Hq / a.Hkv); }
