@@ -93,7 +93,7 @@ __device__ __forceinline__ int i8s_dim(int G, int t, int j, int half, int e) {
 
 // S^T on integer MMAs (no code conversion) instead of fp16 MMAs on codes
 // converted in registers (decode: one 8-row block of query rows).
-constexpr bool AM_I8S = false;
+constexpr bool AM_I8S = true;
 
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
