@@ -359,12 +359,44 @@ __global__ void __launch_bounds__(RT_W * 32) moe_router_topk_kernel(const MoeRou
   float* xs = rsm;
   float* xsum = xs + H;
   float* red = xsum + (H >> 5);
-  stage_rows<1>(a.x, H, H, a.norm_w, a.eps, xs, xsum, red);
   const int lane = threadIdx.x & 31, row = blockIdx.x * RT_W + (threadIdx.x >> 5);
+  const size_t H8 = H >> 3, H64 = H >> 6;
+  // The row's codes, scales and biases depend on nothing earlier: for rows of
+  // up to 4096 columns (4 16-byte blocks per lane) they are loaded before the
+  // staging, so their round trip overlaps it; the sum below is row_dot's, in
+  // its order.
+  constexpr int RU = 4;
+  const int K32 = H >> 5;
+  const bool pre = K32 <= 32 * RU;
+  uint4 wv[RU];
+  float sv[RU], bv[RU];
+  if (row < E && pre) {
+    const uint4* wr = reinterpret_cast<const uint4*>(a.w + row * H8);
+#pragma unroll
+    for (int u = 0; u < RU; ++u) {
+      const int i = lane + 32 * u;
+      if (i < K32) {
+        wv[u] = ldg_stream(wr + i);
+        sv[u] = bf2f(a.s[row * H64 + (i >> 1)]);
+        bv[u] = bf2f(a.b[row * H64 + (i >> 1)]);
+      }
+    }
+  }
+  stage_rows<1>(a.x, H, H, a.norm_w, a.eps, xs, xsum, red);
   if (row < E) {
     float acc[1] = {0.f};
-    const size_t H8 = H >> 3, H64 = H >> 6;
-    row_dot<1, 4>(a.w + row * H8, a.s + row * H64, a.b + row * H64, H, xs, xsum, acc);
+    if (pre) {
+#pragma unroll
+      for (int u = 0; u < RU; ++u) {
+        const int i = lane + 32 * u;
+        if (i < K32) {
+          const float off = fmaf(-128.f, sv[u], bv[u]);
+          acc[0] = fmaf(sv[u], dot32(wv[u], xs, i), fmaf(off, xsum[i], acc[0]));
+        }
+      }
+    } else {
+      row_dot<1, 4>(a.w + row * H8, a.s + row * H64, a.b + row * H64, H, xs, xsum, acc);
+    }
     const float v = rbf(warp_sum(acc[0]));
     if (lane == 0) a.logits[row] = f2bf(v);
   }
